@@ -1,0 +1,392 @@
+"""Benchmark: RealVectorSHT.forward at 512 x 1024, batch 4, FP32 (the
+reference's headline metric, README.md:79), on N GPUs of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one RealVectorSHT.forward (rfft on cuFFT + the fused vector
+Legendre kernel) over a (4, 2, 512, 1024) float32 batch resident in HBM.
+Multi-GPU: batch partition with no collective (every rank transforms its own
+batch of 4, weak scaling); the timing is device time (CUDA events), the max
+over ranks.  The L2 is flushed (256 MiB write) before every timed step.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference's
+CPU path restated by the oracle (rfft + per-order GEMMs in numpy/BLAS, all
+host cores) on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+NLAT, NLON, BATCH = 512, 1024, 4
+METRIC = "RealVectorSHT.forward ms @512x1024 b4 fp32"
+UNIT = "ms"
+PUBLISHED_GB10_MS = 6.855  # HOLYSHT RealVectorSHT.forward 512x1024 b4 on GB10
+PROFILE = ROOT / "profiles" / "legendre_vector_fwd_512x1024_b4.md"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples (100 ms) of SM clock and throttle reasons."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def mark(self, which):
+        setattr(self, which, time.time())
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for t, line in self.samples:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            rows.append((t, parts))
+        inside = [p for t, p in rows if self.t0 is not None and self.t0 - 0.15 <= t <= self.t1 + 0.15]
+        use = inside or rows
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        sm = [float(p[1]) for p in use if p[1].replace(".", "").isdigit()]
+        smax = [float(p[2]) for p in use if p[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for p in use for n, v in zip(names, p[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(use), "in_timed_region": bool(inside)}
+
+
+# ------------------------------------------------------------------ ours
+
+def _traffic_from_profile():
+    """DRAM bytes per launch of the vector kernel from the committed ncu summary."""
+    try:
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", PROFILE.read_text())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+def _peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def algorithmic_bytes(L, K, M, B, tables):
+    """Bytes one forward Legendre launch must move: the l >= m triangle of each
+    table (fp32), the spectrum read (complex64, orders < M) and the output."""
+    pairs = sum(max(L - m, 0) for m in range(M))
+    return tables * pairs * K * 4 + B * tables * K * M * 8 + B * tables * L * M * 8
+
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import holysht_b200 as hs
+    from holysht_b200 import _lib
+    from holysht_b200.ops import legendre_contract
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    vsht = hs.RealVectorSHT(NLAT, NLON).to(dev)
+    L, M = vsht.lmax, vsht.mmax
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+    x = torch.randn((BATCH, 2, NLAT, NLON), generator=gen, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        vsht(x)
+    torch.cuda.synchronize(dev)
+
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    clocks = ClockSampler(visible[local_rank].strip() if local_rank < len(visible) else local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    K = args.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks.mark("t0")
+    for i in range(K):
+        flush.zero_()
+        starts[i].record(stream)
+        vsht(x)
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks.mark("t1")
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = max_over_ranks(sum(step_ms) / K)
+    launches_per_step = 1  # one holysht_b200 kernel per RealVectorSHT.forward
+
+    # ---- the dominant kernel alone (roofline) ----
+    spec = torch.fft.rfft(x, dim=-1, norm="forward")
+    out = torch.empty((BATCH, 2, L, M), dtype=torch.complex64, device=dev)
+    W = spec.size(-1)
+
+    def kernel():
+        legendre_contract(kind=_lib.KIND_VECTOR, direction=_lib.DIR_FORWARD, input=spec, output=out,
+                          w0=vsht.w0_t, w1=vsht.w1_t, batch=BATCH, nlat=NLAT, lmax=L, mmax=M,
+                          in_strides=(2 * NLAT * W, NLAT * W, W), out_strides=(2 * L * M, L * M, M),
+                          out_cols=M, scale=2 * math.pi)
+
+    for _ in range(3):
+        kernel()
+    kn = max(20, K // 2)
+    ks = [torch.cuda.Event(enable_timing=True) for _ in range(kn)]
+    ke = [torch.cuda.Event(enable_timing=True) for _ in range(kn)]
+    for i in range(kn):
+        flush.zero_()
+        ks[i].record(stream)
+        kernel()
+        ke[i].record(stream)
+    torch.cuda.synchronize(dev)
+    kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(ks, ke))
+    kernel_ms = max_over_ranks(kernel_ms)
+    abytes = algorithmic_bytes(L, NLAT, M, BATCH, 2)
+    clocks.stop()
+
+    # ---- secondary: RealSHT.forward on the same grid ----
+    ssht = hs.RealSHT(NLAT, NLON).to(dev)
+    xs = torch.randn((BATCH, NLAT, NLON), generator=gen, device=dev)
+    for _ in range(3):
+        ssht(xs)
+    sn = max(20, K // 2)
+    ss = [torch.cuda.Event(enable_timing=True) for _ in range(sn)]
+    se = [torch.cuda.Event(enable_timing=True) for _ in range(sn)]
+    for i in range(sn):
+        flush.zero_()
+        ss[i].record(stream)
+        ssht(xs)
+        se[i].record(stream)
+    torch.cuda.synchronize(dev)
+    scalar_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(ss, se)))
+    del ssht
+
+    # ---- end to end through the public API with host buffers ----
+    xh = torch.empty((BATCH, 2, NLAT, NLON), dtype=torch.float32).pin_memory()
+    xh.copy_(x.cpu())
+    oh = torch.empty((BATCH, 2, L, M), dtype=torch.complex64).pin_memory()
+    xd = torch.empty_like(x)
+    for _ in range(3):
+        xd.copy_(xh, non_blocking=True)
+        oh.copy_(vsht(xd), non_blocking=True)
+    torch.cuda.synchronize(dev)
+    en = max(10, K // 4)
+    es = [torch.cuda.Event(enable_timing=True) for _ in range(en)]
+    ee = [torch.cuda.Event(enable_timing=True) for _ in range(en)]
+    barrier()
+    for i in range(en):
+        flush.zero_()
+        es[i].record(stream)
+        xd.copy_(xh, non_blocking=True)
+        oh.copy_(vsht(xd), non_blocking=True)
+        ee[i].record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(es, ee)))
+    h2d = xh.numel() * 4
+    d2h = oh.numel() * 8
+
+    peaks, peak_kind = _peaks()
+    achieved = abytes / (kernel_ms * 1e-3) / 1e9
+    traffic = _traffic_from_profile()
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(vsht, x)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(ms, 5),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": round(ms / PUBLISHED_GB10_MS, 5),
+        "dtype": "f32",
+        "data": "synthetic N(0,1), seed 1+rank",
+        "config": {"workload": "RealVectorSHT.forward 512x1024 equiangular lmax=512 mmax=513 ortho csphase, batch 4",
+                   "global_batch": BATCH * world, "parallelism": f"batch-partition x{world}, no collective",
+                   "l2": "flushed (256 MiB write) before every timed step; tables 2x538 MB exceed L2"},
+        "transforms_per_s": round(BATCH * world / (ms * 1e-3), 2),
+        "secondary": {"RealSHT.forward_ms": round(scalar_ms, 5)},
+        "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * K,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": traffic, "algorithmic_bytes": abytes, "kernel_ms": round(kernel_ms, 5),
+                     "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)"},
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(vsht, x):
+    """The oracle's restatement of the reference CPU path on the same workload
+    (full batch; a few repetitions, about 10-20 s of CPU work)."""
+    import numpy as np
+
+    from oracle import sht_oracle as orc
+
+    w = np.stack([vsht.w0.float().cpu().numpy(), vsht.w1.float().cpu().numpy()])
+    fn = orc.CpuForwardBaseline(w, vector=True)
+    xh = x.cpu().numpy()
+    fn(xh)
+    times = []
+    t_end = time.perf_counter() + 10.0
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 20):
+        t = time.perf_counter()
+        fn(xh)
+        times.append((time.perf_counter() - t) * 1e3)
+    return {"value": round(statistics.median(times), 3), "unit": UNIT, "cores": _blas_threads(), "kind": "port",
+            "sample": f"full workload (4,2,512,1024), median of {len(times)} runs"}
+
+
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        return max(d["num_threads"] for d in threadpool_info())
+    except Exception:
+        return os.cpu_count()
+
+
+# ------------------------------------------------------------------ reference arm
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import sht_oracle as orc
+
+    w = orc.vector_forward_tables(NLAT, NLON).astype(np.float32)
+    fn = orc.CpuForwardBaseline(w, vector=True)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((BATCH, 2, NLAT, NLON)).astype(np.float32)
+    for _ in range(max(args.warmup, 1)):
+        fn(x)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        fn(x)
+        times.append((time.perf_counter() - t) * 1e3)
+    ms = sum(times) / len(times)
+    cores = _blas_threads()
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(ms, 4),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": round(ms / PUBLISHED_GB10_MS, 5),
+        "dtype": "f32",
+        "data": "synthetic N(0,1), seed 1",
+        "config": {"workload": "RealVectorSHT.forward 512x1024 equiangular lmax=512 mmax=513 ortho csphase, batch 4",
+                   "global_batch": BATCH, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(ms, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "full workload per step: rfft + per-order fp32 GEMMs (numpy/BLAS)"},
+        "e2e": {"value": round(ms, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local_rank = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,554 @@
+"""holysht_b200: B200-native (sm_100a) Legendre kernels behind HOLYSHT's API.
+
+Drop-in replacements for the reference's public modules and functions
+(chrisvoncsefalvay/holysht ``torch-ext/holysht/__init__.py``):
+
+* ``RealSHT`` / ``InverseRealSHT`` / ``RealVectorSHT`` / ``InverseRealVectorSHT``
+  (reference :1228-1791) with the same constructor arguments
+  ``(nlat, nlon, lmax, mmax, grid, norm, csphase[, dtype])``, the same
+  buffer names (``weights``/``weight_t``, ``pct``/``pct_t``,
+  ``w0``/``w1``/``w0_t``/``w1_t``, ``d0``/``d1``/``d0_t``/``d1_t``) and autograd;
+* ``GraphedModule`` (reference :1794-1866), the function API
+  ``legendre_forward`` / ``legendre_inverse`` / ``sht_forward`` /
+  ``sht_inverse`` and the ``Fused*`` aliases (:1869-1878).
+
+Every transform runs the longitude FFT on cuFFT (``torch.fft``) and the
+Legendre stage on the kernels of ``libholysht_b200.so`` on the same stream.
+The forward kernels read the rfft output in place (no slice copy) and fold the
+2*pi spectrum scale; the inverse kernels write straight into the irfft input
+(zero padding and the DC/Nyquist imaginary parts handled in the kernel).
+There is no CPU fallback: CUDA tensors only.
+"""
+from __future__ import annotations
+
+import math
+from enum import IntEnum
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+from . import _lib, ops, weights as _weights
+from .ops import legendre_contract as _contract
+
+__all__ = [
+    "RealSHT",
+    "InverseRealSHT",
+    "RealVectorSHT",
+    "InverseRealVectorSHT",
+    "GraphedModule",
+    "legendre_forward",
+    "legendre_inverse",
+    "sht_forward",
+    "sht_inverse",
+]
+
+TWO_PI = 2.0 * math.pi
+_HAS_NATIVE_EXT = _lib.LIB_PATH.exists()
+
+
+class _ForwardBackend(IntEnum):
+    """Backend hints of the reference's ``*_ex`` operators (``__init__.py:192-197``).
+    Accepted for compatibility; all hints run the FP32 sm_100a kernel."""
+
+    AUTO = 0
+    FMA = 1
+    TMA = 2
+    TC_TF32 = 3
+    TC_BF16 = 4
+
+
+def _need_cuda(x: torch.Tensor, what: str) -> None:
+    if not x.is_cuda:
+        raise RuntimeError(f"{what}: holysht_b200 runs on CUDA tensors only (no CPU fallback)")
+
+
+def _strides3(t: torch.Tensor, vector: bool):
+    """(batch, component, row) element strides of a [B,(2),R,C] tensor."""
+    if vector:
+        return t.stride(0), t.stride(1), t.stride(2)
+    return t.stride(0), 0, t.stride(1)
+
+
+# ---------------------------------------------------------------------------
+# module-level autograd functions (spectrum in rfft layout)
+# ---------------------------------------------------------------------------
+
+class _SpectrumLegendreForward(torch.autograd.Function):
+    """coef = 2*pi * Legendre(spec[..., :mmax]) for an rfft spectrum
+    ``spec`` [B,(2),K,W]; backward is the transposed (conjugate for the
+    vector map) contraction written straight into a [B,(2),K,W] gradient."""
+
+    @staticmethod
+    def forward(ctx, spec, w0, w1, mmax: int, round_bf16: bool):
+        vector = w1 is not None
+        B, K, W = spec.size(0), spec.size(-2), spec.size(-1)
+        L = w0.size(0)
+        shape = (B, 2, L, mmax) if vector else (B, L, mmax)
+        out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
+        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_FORWARD,
+                  input=spec, output=out, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=mmax,
+                  in_strides=_strides3(spec, vector), out_strides=_strides3(out, vector),
+                  out_cols=mmax, scale=TWO_PI, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+        ctx.save_for_backward(w0, w1)
+        ctx.dims = (B, K, W, L, mmax, vector)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        w0, w1 = ctx.saved_tensors
+        B, K, W, L, mmax, vector = ctx.dims
+        g = grad.contiguous()
+        shape = (B, 2, K, W) if vector else (B, K, W)
+        gspec = torch.empty(shape, device=g.device, dtype=torch.complex64)
+        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_INVERSE,
+                  input=g, output=gspec, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=mmax,
+                  in_strides=_strides3(g, vector), out_strides=_strides3(gspec, vector),
+                  out_cols=W, scale=TWO_PI, flags=_lib.FLAG_CONJ_W1 if vector else 0)
+        return gspec, None, None, None, None
+
+
+class _SpectrumLegendreInverse(torch.autograd.Function):
+    """spec[B,(2),K,W] = irfft-ready synthesis of coef [B,(2),L,M]: columns
+    m >= M are zero and Im at m = 0 (and m = nlon/2 for even nlon) dropped."""
+
+    @staticmethod
+    def forward(ctx, coef, w0, w1, nlon: int):
+        vector = w1 is not None
+        B, L, M = coef.size(0), coef.size(-2), coef.size(-1)
+        K = w0.size(1)
+        W = nlon // 2 + 1
+        c = coef.contiguous()
+        shape = (B, 2, K, W) if vector else (B, K, W)
+        spec = torch.empty(shape, device=c.device, dtype=torch.complex64)
+        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_INVERSE,
+                  input=c, output=spec, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=M,
+                  in_strides=_strides3(c, vector), out_strides=_strides3(spec, vector),
+                  out_cols=W, scale=1.0, flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
+        ctx.save_for_backward(w0, w1)
+        ctx.dims = (B, K, W, L, M, vector)
+        ctx.nyq = nlon // 2 if nlon % 2 == 0 else None
+        return spec
+
+    @staticmethod
+    def backward(ctx, grad):
+        w0, w1 = ctx.saved_tensors
+        B, K, W, L, M, vector = ctx.dims
+        g = grad.clone(memory_format=torch.contiguous_format)
+        # adjoint of dropping Im at m = 0 / m = nlon/2: drop it from the gradient
+        g[..., 0] = g[..., 0].real.to(g.dtype)
+        if ctx.nyq is not None:
+            g[..., ctx.nyq] = g[..., ctx.nyq].real.to(g.dtype)
+        shape = (B, 2, L, M) if vector else (B, L, M)
+        gc = torch.empty(shape, device=g.device, dtype=torch.complex64)
+        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_FORWARD,
+                  input=g, output=gc, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=M,
+                  in_strides=_strides3(g, vector), out_strides=_strides3(gc, vector),
+                  out_cols=M, scale=1.0, flags=_lib.FLAG_CONJ_W1 if vector else 0)
+        return gc, None, None, None
+
+
+# ---------------------------------------------------------------------------
+# operator-level autograd functions (reference layouts, :976-1093)
+# ---------------------------------------------------------------------------
+
+def _dense_contract(kind, direction, inp, out, w0, w1, conj=False):
+    vector = kind == _lib.KIND_VECTOR
+    L, K, M = w0.shape
+    _contract(kind=kind, direction=direction, input=inp, output=out, w0=w0, w1=w1, batch=inp.size(0),
+              nlat=K, lmax=L, mmax=M, in_strides=_strides3(inp, vector),
+              out_strides=_strides3(out, vector), out_cols=M, scale=1.0,
+              flags=_lib.FLAG_CONJ_W1 if conj else 0)
+
+
+class _FusedLegendreForwardFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, input, weight_t):
+        x = input.contiguous()
+        out = torch.empty(x.size(0), weight_t.size(0), x.size(2), device=x.device, dtype=torch.complex64)
+        ops.fused_legendre_forward(out, x, weight_t)
+        ctx.save_for_backward(weight_t)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        (weight_t,) = ctx.saved_tensors
+        g = grad.contiguous()
+        gi = torch.empty(g.size(0), weight_t.size(1), g.size(2), device=g.device, dtype=torch.complex64)
+        ops.fused_legendre_inverse(gi, g, weight_t)
+        return gi, None
+
+
+class _FusedLegendreInverseFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, input, weight_t):
+        x = input.contiguous()
+        out = torch.empty(x.size(0), weight_t.size(1), x.size(2), device=x.device, dtype=torch.complex64)
+        ops.fused_legendre_inverse(out, x, weight_t)
+        ctx.save_for_backward(weight_t)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        (weight_t,) = ctx.saved_tensors
+        g = grad.contiguous()
+        gi = torch.empty(g.size(0), weight_t.size(0), g.size(2), device=g.device, dtype=torch.complex64)
+        ops.fused_legendre_forward(gi, g, weight_t)
+        return gi, None
+
+
+class _FusedLegendreForwardRealFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, input, weight_t):
+        x = input.contiguous()
+        out = torch.empty(x.size(0), weight_t.size(0), x.size(2), device=x.device, dtype=torch.float32)
+        ops.fused_legendre_forward_real(out, x, weight_t)
+        ctx.save_for_backward(weight_t)
+        ctx.in_dtype = x.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        (weight_t,) = ctx.saved_tensors
+        g = grad.contiguous().float()
+        gi = torch.empty(g.size(0), weight_t.size(1), g.size(2), device=g.device, dtype=torch.float32)
+        ops.fused_legendre_inverse_real(gi, g, weight_t)
+        return gi.to(ctx.in_dtype), None
+
+
+class _FusedVectorLegendreForwardFn(torch.autograd.Function):
+    """Backward applies the conjugate transpose A^H = [[W0, -iW1], [-iW1, -W0]]
+    (PyTorch's complex-gradient convention).  The reference applies A^T here
+    (``__init__.py:1061-1069``), which is not the adjoint."""
+
+    @staticmethod
+    def forward(ctx, input, weight0_t, weight1_t):
+        x = input.contiguous()
+        out = torch.empty(x.size(0), 2, weight0_t.size(0), x.size(3), device=x.device, dtype=torch.complex64)
+        ops.fused_vector_legendre_forward(out, x, weight0_t, weight1_t)
+        ctx.save_for_backward(weight0_t, weight1_t)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        w0, w1 = ctx.saved_tensors
+        g = grad.contiguous()
+        gi = torch.empty(g.size(0), 2, w0.size(1), g.size(3), device=g.device, dtype=torch.complex64)
+        _dense_contract(_lib.KIND_VECTOR, _lib.DIR_INVERSE, g, gi, w0, w1, conj=True)
+        return gi, None, None
+
+
+class _FusedVectorLegendreInverseFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, input, weight0_t, weight1_t):
+        x = input.contiguous()
+        out = torch.empty(x.size(0), 2, weight0_t.size(1), x.size(3), device=x.device, dtype=torch.complex64)
+        ops.fused_vector_legendre_inverse(out, x, weight0_t, weight1_t)
+        ctx.save_for_backward(weight0_t, weight1_t)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        w0, w1 = ctx.saved_tensors
+        g = grad.contiguous()
+        gi = torch.empty(g.size(0), 2, w0.size(0), g.size(3), device=g.device, dtype=torch.complex64)
+        _dense_contract(_lib.KIND_VECTOR, _lib.DIR_FORWARD, g, gi, w0, w1, conj=True)
+        return gi, None, None
+
+
+# ---------------------------------------------------------------------------
+# function API (reference :1100-1221)
+# ---------------------------------------------------------------------------
+
+def _as_weight_t(weights: torch.Tensor, weight_t: Optional[torch.Tensor]) -> torch.Tensor:
+    if weight_t is None:
+        weight_t = weights.float().permute(1, 2, 0).contiguous()
+    return weight_t
+
+
+def fused_legendre_forward(input: torch.Tensor, weights: torch.Tensor,
+                           weight_t: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[b,l,m] = sum_k weights[m,l,k] input[b,k,m]; input [B,nlat,mmax] complex64,
+    weights [mmax,lmax,nlat] (torch-harmonics layout) or weight_t [lmax,nlat,mmax]."""
+    _need_cuda(input, "fused_legendre_forward")
+    return _FusedLegendreForwardFn.apply(input, _as_weight_t(weights, weight_t))
+
+
+def fused_legendre_inverse(input: torch.Tensor, pct: torch.Tensor,
+                           pct_t: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[b,k,m] = sum_l pct[m,l,k] input[b,l,m]; input [B,lmax,mmax] complex64."""
+    _need_cuda(input, "fused_legendre_inverse")
+    return _FusedLegendreInverseFn.apply(input, _as_weight_t(pct, pct_t))
+
+
+def fused_legendre_forward_real(input: torch.Tensor, weight_t: torch.Tensor) -> torch.Tensor:
+    """Real-valued forward Legendre transform with float accumulation."""
+    _need_cuda(input, "fused_legendre_forward_real")
+    return _FusedLegendreForwardRealFn.apply(input, weight_t)
+
+
+def fused_legendre_inverse_real(input: torch.Tensor, weight_t: torch.Tensor) -> torch.Tensor:
+    """Real-valued inverse Legendre transform with float accumulation."""
+    _need_cuda(input, "fused_legendre_inverse_real")
+    x = input.contiguous().float()
+    out = torch.empty(x.size(0), weight_t.size(1), x.size(2), device=x.device, dtype=torch.float32)
+    ops.fused_legendre_inverse_real(out, x, weight_t)
+    return out
+
+
+def fused_sht_forward(x: torch.Tensor, weights: torch.Tensor, mmax: int,
+                      weight_t: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """rfft -> Legendre: [B, nlat, nlon] float32 -> [B, lmax, mmax] complex64."""
+    _need_cuda(x, "fused_sht_forward")
+    spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
+    lead = spec.shape[:-2]
+    spec = spec.reshape(-1, spec.size(-2), spec.size(-1))
+    out = _SpectrumLegendreForward.apply(spec, _as_weight_t(weights, weight_t), None, int(mmax), False)
+    return out.reshape(lead + out.shape[-2:])
+
+
+def fused_sht_inverse(coeffs: torch.Tensor, pct: torch.Tensor, nlon: int,
+                      pct_t: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Legendre -> irfft: [B, lmax, mmax] complex64 -> [B, nlat, nlon] float32."""
+    _need_cuda(coeffs, "fused_sht_inverse")
+    lead = coeffs.shape[:-2]
+    c = coeffs.reshape(-1, coeffs.size(-2), coeffs.size(-1))
+    if c.dtype != torch.complex64:
+        c = c.to(torch.complex64)
+    spec = _SpectrumLegendreInverse.apply(c, _as_weight_t(pct, pct_t), None, int(nlon))
+    y = torch.fft.irfft(spec, n=int(nlon), dim=-1, norm="forward")
+    return y.reshape(lead + y.shape[-2:])
+
+
+def _prepare_irfft_input(x: torch.Tensor, nlon: int, active_mmax: Optional[int] = None) -> torch.Tensor:
+    """Pad an rFFT-format complex tensor to nlon//2+1 and drop Im at DC/Nyquist
+    (reference ``__init__.py:949-973``), on the native kernel."""
+    _need_cuda(x, "_prepare_irfft_input")
+    active_mmax = x.size(-1) if active_mmax is None else active_mmax
+    full = nlon // 2 + 1
+    if x.size(-1) == full:
+        out = x.contiguous().clone() if x.is_contiguous() else x.contiguous()
+    else:
+        out = torch.zeros(x.shape[:-1] + (full,), dtype=x.dtype, device=x.device)
+        n = min(full, x.size(-1))
+        out[..., :n] = x[..., :n]
+    flat = out.reshape(-1, out.size(-2), out.size(-1))
+    ops.sht_prepare_irfft(flat, active_mmax, nlon)
+    return flat.reshape(out.shape)
+
+
+def _stack_vector_forward_real_inputs(input: torch.Tensor):
+    """[B,2,K,M] complex64 -> (stacked_w0, stacked_w1) [4B,K,M] (reference :429-445)."""
+    _need_cuda(input, "_stack_vector_forward_real_inputs")
+    B, _, K, M = input.shape
+    s0 = torch.empty((4 * B, K, M), device=input.device, dtype=torch.float32)
+    s1 = torch.empty_like(s0)
+    ops.fused_vector_forward_pack_real(s0, s1, input.contiguous())
+    return s0, s1
+
+
+def _recompose_vector_forward_real_outputs(out_w0, out_w1, *, batch_size: int, lmax: int, mmax: int):
+    """Inverse of the packing above on the two real outputs (reference :448-477)."""
+    _need_cuda(out_w0, "_recompose_vector_forward_real_outputs")
+    out = torch.empty((batch_size, 2, lmax, mmax), device=out_w0.device, dtype=torch.complex64)
+    ops.fused_vector_forward_recompose_real(out, out_w0.contiguous(), out_w1.contiguous())
+    return out
+
+
+# ---------------------------------------------------------------------------
+# modules (reference :1228-1791)
+# ---------------------------------------------------------------------------
+
+def _w_dtype(dtype: str) -> torch.dtype:
+    if dtype == "fp32":
+        return torch.float32
+    if dtype == "bf16":
+        return torch.bfloat16
+    if dtype == "fp16":
+        return torch.float16
+    raise ValueError(f"dtype must be 'fp32', 'bf16' or 'fp16', got {dtype!r}")
+
+
+def _check_mmax(mmax: int, nlon: int) -> None:
+    if mmax > nlon // 2 + 1:
+        raise ValueError(f"mmax={mmax} exceeds nlon//2+1={nlon // 2 + 1}")
+
+
+class RealSHT(nn.Module):
+    """Drop-in ``RealSHT``: ``x`` [..., nlat, nlon] real -> [..., lmax, mmax] complex64.
+
+    ``dtype="bf16"`` rounds the post-FFT spectrum to bfloat16 and contracts it
+    with the FP32 table in FP32 (the reference's BF16 path, ``__init__.py:1289-1337``).
+    """
+
+    def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True,
+                 dtype: str = "fp32"):
+        super().__init__()
+        w_dtype = _w_dtype(dtype)
+        w, L, M = _weights.scalar_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        _check_mmax(M, nlon)
+        self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
+        self.grid, self.norm, self.csphase = grid, norm, csphase
+        self._use_bf16 = dtype == "bf16"
+        self._use_fp16 = dtype == "fp16"
+        wt = torch.from_numpy(w)
+        self.register_buffer("weights", wt.to(w_dtype))
+        self.register_buffer("weight_t", wt.permute(1, 2, 0).contiguous())
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _need_cuda(x, "RealSHT")
+        assert x.shape[-2] == self.nlat and x.shape[-1] == self.nlon
+        spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
+        lead = spec.shape[:-2]
+        spec = spec.reshape(-1, self.nlat, spec.size(-1))
+        out = _SpectrumLegendreForward.apply(spec, self.weight_t, None, self.mmax,
+                                             self._use_bf16 or self._use_fp16)
+        return out.reshape(lead + (self.lmax, self.mmax))
+
+
+class InverseRealSHT(nn.Module):
+    """Drop-in ``InverseRealSHT``: [..., lmax, mmax] complex -> [..., nlat, nlon] real."""
+
+    def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True):
+        super().__init__()
+        p, L, M = _weights.scalar_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        _check_mmax(M, nlon)
+        self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
+        self.grid, self.norm, self.csphase = grid, norm, csphase
+        pt = torch.from_numpy(p)
+        self.register_buffer("pct", pt)
+        self.register_buffer("pct_t", pt.permute(1, 2, 0).contiguous())
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _need_cuda(x, "InverseRealSHT")
+        assert x.shape[-2] == self.lmax and x.shape[-1] == self.mmax
+        return fused_sht_inverse(x, self.pct, self.nlon, self.pct_t)
+
+
+class RealVectorSHT(nn.Module):
+    """Drop-in ``RealVectorSHT``: [..., 2, nlat, nlon] -> [..., 2, lmax, mmax] complex64
+    (spheroidal, toroidal), both tables fused in one pass."""
+
+    def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True,
+                 dtype: str = "fp32"):
+        super().__init__()
+        w_dtype = _w_dtype(dtype)
+        w, L, M = _weights.vector_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        _check_mmax(M, nlon)
+        self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
+        self.grid, self.norm, self.csphase = grid, norm, csphase
+        self._use_bf16 = dtype == "bf16"
+        self._use_fp16 = dtype == "fp16"
+        wt = torch.from_numpy(w)
+        self.register_buffer("w0", wt[0].to(w_dtype))
+        self.register_buffer("w1", wt[1].to(w_dtype))
+        self.register_buffer("w0_t", wt[0].permute(1, 2, 0).contiguous())
+        self.register_buffer("w1_t", wt[1].permute(1, 2, 0).contiguous())
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _need_cuda(x, "RealVectorSHT")
+        assert x.shape[-2] == self.nlat and x.shape[-1] == self.nlon and x.shape[-3] == 2
+        spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
+        lead = spec.shape[:-3]
+        spec = spec.reshape(-1, 2, self.nlat, spec.size(-1))
+        out = _SpectrumLegendreForward.apply(spec, self.w0_t, self.w1_t, self.mmax,
+                                             self._use_bf16 or self._use_fp16)
+        return out.reshape(lead + (2, self.lmax, self.mmax))
+
+
+class InverseRealVectorSHT(nn.Module):
+    """Drop-in ``InverseRealVectorSHT``: [..., 2, lmax, mmax] -> [..., 2, nlat, nlon]."""
+
+    def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True):
+        super().__init__()
+        d, L, M = _weights.vector_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        _check_mmax(M, nlon)
+        self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
+        self.grid, self.norm, self.csphase = grid, norm, csphase
+        dt = torch.from_numpy(d)
+        self.register_buffer("d0", dt[0].contiguous())
+        self.register_buffer("d1", dt[1].contiguous())
+        self.register_buffer("d0_t", dt[0].permute(1, 2, 0).contiguous())
+        self.register_buffer("d1_t", dt[1].permute(1, 2, 0).contiguous())
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _need_cuda(x, "InverseRealVectorSHT")
+        assert x.shape[-2] == self.lmax and x.shape[-1] == self.mmax and x.shape[-3] == 2
+        lead = x.shape[:-3]
+        c = x.reshape(-1, 2, self.lmax, self.mmax)
+        if c.dtype != torch.complex64:
+            c = c.to(torch.complex64)
+        spec = _SpectrumLegendreInverse.apply(c, self.d0_t, self.d1_t, self.nlon)
+        y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
+        return y.reshape(lead + (2, self.nlat, self.nlon))
+
+
+class GraphedModule(nn.Module):
+    """CUDA-graph capture/replay of a module's forward (reference :1794-1866).
+
+    The first call per (shape, dtype) warms the module up on a side stream and
+    captures one graph; later calls copy the input into the captured buffer,
+    replay and return a clone of the captured output.  Inputs off CUDA or
+    requiring grad run the module directly.  At most ``max_cached_shapes``
+    graphs are kept (least recently used is dropped).
+    """
+
+    def __init__(self, module: nn.Module, num_warmup: int = 3, max_cached_shapes: int = 4):
+        super().__init__()
+        self.module = module
+        self._num_warmup = num_warmup
+        self._max_cached_shapes = max_cached_shapes
+        self._graph_cache = {}
+        self._graph_lru = []
+
+    def reset_graph_cache(self) -> None:
+        self._graph_cache.clear()
+        self._graph_lru.clear()
+
+    def _capture(self, x: torch.Tensor):
+        static_in = x.detach().clone()
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):
+            for _ in range(self._num_warmup):
+                self.module(static_in)
+        torch.cuda.current_stream(x.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = self.module(static_in)
+        return static_in, static_out, graph
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda or x.requires_grad:
+            return self.module(x)
+        key = (tuple(x.shape), x.dtype, x.device)
+        entry = self._graph_cache.get(key)
+        if entry is None:
+            entry = self._capture(x)
+            self._graph_cache[key] = entry
+            self._graph_lru.append(key)
+            while len(self._graph_lru) > self._max_cached_shapes:
+                self._graph_cache.pop(self._graph_lru.pop(0), None)
+        else:
+            self._graph_lru.remove(key)
+            self._graph_lru.append(key)
+        static_in, static_out, graph = entry
+        static_in.copy_(x)
+        graph.replay()
+        return static_out.clone()
+
+
+legendre_forward = fused_legendre_forward
+legendre_inverse = fused_legendre_inverse
+sht_forward = fused_sht_forward
+sht_inverse = fused_sht_inverse
+
+FusedRealSHT = RealSHT
+FusedInverseRealSHT = InverseRealSHT
+FusedRealVectorSHT = RealVectorSHT
+FusedInverseRealVectorSHT = InverseRealVectorSHT

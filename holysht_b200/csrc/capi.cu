@@ -1,0 +1,440 @@
+// C ABI of libholysht_b200.so: argument validation, launch configuration and
+// dispatch to the sm_100a kernels.  The checks mirror the reference's
+// TORCH_CHECK set (cuda/fused_legendre.cu:3157-3335): non-null pointers,
+// non-negative extents, table/input extents that agree, and extents that fit
+// the kernels' 32-bit tile arithmetic.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <string>
+
+#include "../../include/holysht_b200.h"
+#include "contract.cuh"
+#include "elementwise.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return HOLYSHT_OK;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(HOLYSHT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+constexpr int kMaxDevices = 64;
+
+int sm_count_of_current_device() {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+int env_ksplit() {
+  static int v = [] {
+    const char* s = std::getenv("HOLYSHT_KSPLIT");
+    if (!s || !*s) return 0;
+    int k = std::atoi(s);
+    return (k == 1 || k == 2 || k == 4 || k == 8) ? k : 0;
+  }();
+  return v;
+}
+
+template <int KIND, int DIR, int NB, typename TIN>
+int launch_contract(const hsb::ContractParams& p_in, int grid_tiles, cudaStream_t stream) {
+  static std::atomic<unsigned long long> configured{0};
+  auto kernel = hsb::contract_kernel<KIND, DIR, NB, TIN>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         hsb::kSmemBytes);
+    if (e != cudaSuccess)
+      return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the Legendre kernel: %s",
+                  cudaGetErrorString(e));
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  hsb::ContractParams p = p_in;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_tiles) * static_cast<unsigned>(p.ks), 1, 1);
+  cfg.blockDim = dim3(hsb::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = hsb::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(HOLYSHT_ERR_CUDA, "Legendre kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  return ok();
+}
+
+int next_pow2_at_least(long long v, int lo, int hi) {
+  int r = lo;
+  while (r < hi && r < v) r *= 2;
+  return r;
+}
+
+bool fits_int(long long v) { return v >= 0 && v <= (INT_MAX / 4); }
+
+// Normalised description handed to the dispatcher.
+struct Job {
+  int kind, dir, in_dtype, flags;
+  const void* in;
+  void* out;
+  const float* w0;
+  const float* w1;
+  long long B, K, L, M;
+  long long in_bs, in_ps, in_rs, out_bs, out_ps, out_rs, out_cols, w_ls, w_ks, nlon;
+  float scale;
+  int ksplit;
+};
+
+template <int KIND, int DIR, typename TIN>
+int dispatch_nb(const hsb::ContractParams& p0, int nb, cudaStream_t stream) {
+  hsb::ContractParams p = p0;
+  p.n_bg = (p.B + nb - 1) / nb;
+  const long long tiles = (long long)(p.n_compute + p.n_zero) * p.n_bg;
+  if (tiles == 0) return ok();
+  if (tiles * p.ks > INT_MAX / 2) return fail(HOLYSHT_ERR_INVALID, "problem too large for one launch");
+  const int grid_tiles = static_cast<int>(tiles);
+  if constexpr (KIND == hsb::KIND_VECTOR) {
+    switch (nb) {
+      case 1: return launch_contract<KIND, DIR, 1, TIN>(p, grid_tiles, stream);
+      case 2: return launch_contract<KIND, DIR, 2, TIN>(p, grid_tiles, stream);
+      default: return launch_contract<KIND, DIR, 4, TIN>(p, grid_tiles, stream);
+    }
+  } else if constexpr (KIND == hsb::KIND_SCALAR) {
+    switch (nb) {
+      case 1: return launch_contract<KIND, DIR, 1, TIN>(p, grid_tiles, stream);
+      case 2: return launch_contract<KIND, DIR, 2, TIN>(p, grid_tiles, stream);
+      case 4: return launch_contract<KIND, DIR, 4, TIN>(p, grid_tiles, stream);
+      default: return launch_contract<KIND, DIR, 8, TIN>(p, grid_tiles, stream);
+    }
+  } else {
+    switch (nb) {
+      case 2: return launch_contract<KIND, DIR, 2, TIN>(p, grid_tiles, stream);
+      case 4: return launch_contract<KIND, DIR, 4, TIN>(p, grid_tiles, stream);
+      case 8: return launch_contract<KIND, DIR, 8, TIN>(p, grid_tiles, stream);
+      default: return launch_contract<KIND, DIR, 16, TIN>(p, grid_tiles, stream);
+    }
+  }
+}
+
+int run_job(const Job& j, cudaStream_t stream) {
+  if (j.kind < 0 || j.kind > 2) return fail(HOLYSHT_ERR_INVALID, "unknown kind %d", j.kind);
+  if (j.dir != HOLYSHT_DIR_FORWARD && j.dir != HOLYSHT_DIR_INVERSE)
+    return fail(HOLYSHT_ERR_INVALID, "unknown direction %d", j.dir);
+  if (j.flags & ~(HOLYSHT_FLAG_CONJ_W1 | HOLYSHT_FLAG_ROUND_BF16 | HOLYSHT_FLAG_IRFFT_PREP))
+    return fail(HOLYSHT_ERR_INVALID, "unknown flags 0x%x", j.flags);
+  if (j.B < 0 || j.K < 0 || j.L < 0 || j.M < 0)
+    return fail(HOLYSHT_ERR_INVALID, "negative extent (batch=%lld nlat=%lld lmax=%lld mmax=%lld)",
+                j.B, j.K, j.L, j.M);
+  if (!fits_int(j.B) || !fits_int(j.K) || !fits_int(j.L) || !fits_int(j.M) || !fits_int(j.out_cols))
+    return fail(HOLYSHT_ERR_INVALID, "extent exceeds the 32-bit tile range");
+  if (j.out_cols < j.M) return fail(HOLYSHT_ERR_INVALID, "out_cols (%lld) < mmax (%lld)", j.out_cols, j.M);
+  const long long R = j.dir == HOLYSHT_DIR_FORWARD ? j.L : j.K;
+  const long long S = j.dir == HOLYSHT_DIR_FORWARD ? j.K : j.L;
+  if (j.B == 0 || R == 0 || j.out_cols == 0) return ok();
+  if (!j.out) return fail(HOLYSHT_ERR_INVALID, "output pointer is null");
+  if (S > 0 && j.M > 0 && (!j.in || !j.w0)) return fail(HOLYSHT_ERR_INVALID, "input or table pointer is null");
+  if (j.kind == HOLYSHT_KIND_VECTOR && S > 0 && j.M > 0 && !j.w1)
+    return fail(HOLYSHT_ERR_INVALID, "vector contraction needs both tables");
+  if (j.kind == HOLYSHT_KIND_REAL) {
+    if (j.in_dtype != HOLYSHT_DTYPE_F32 && j.in_dtype != HOLYSHT_DTYPE_BF16)
+      return fail(HOLYSHT_ERR_INVALID, "input must be float32 or bfloat16");
+    if (j.flags & (HOLYSHT_FLAG_CONJ_W1 | HOLYSHT_FLAG_IRFFT_PREP))
+      return fail(HOLYSHT_ERR_INVALID, "flag not valid for a real contraction");
+  } else if (j.in_dtype != HOLYSHT_DTYPE_C64) {
+    return fail(HOLYSHT_ERR_INVALID, "input must be complex64");
+  }
+  if (j.ksplit != 0 && j.ksplit != 1 && j.ksplit != 2 && j.ksplit != 4 && j.ksplit != 8)
+    return fail(HOLYSHT_ERR_INVALID, "ksplit must be 0, 1, 2, 4 or 8");
+
+  hsb::ContractParams p = {};
+  p.in = j.in;
+  p.out = j.out;
+  p.w0 = j.w0;
+  p.w1 = j.w1;
+  p.in_bs = j.in_bs;
+  p.in_ps = j.in_ps;
+  p.in_rs = j.in_rs;
+  p.out_bs = j.out_bs;
+  p.out_ps = j.out_ps;
+  p.out_rs = j.out_rs;
+  p.w_ls = j.w_ls;
+  p.w_ks = j.w_ks;
+  p.B = (int)j.B;
+  p.K = (int)j.K;
+  p.L = (int)j.L;
+  p.M = (int)j.M;
+  p.out_cols = (int)j.out_cols;
+  p.R = (int)R;
+  p.S = (int)S;
+  p.scale = j.scale;
+  p.w1_sign = (j.flags & HOLYSHT_FLAG_CONJ_W1) ? -1.f : 1.f;
+  p.zero_imag_col0 = (j.flags & HOLYSHT_FLAG_IRFFT_PREP) ? 1 : 0;
+  p.nyquist = ((j.flags & HOLYSHT_FLAG_IRFFT_PREP) && j.nlon > 0 && j.nlon % 2 == 0) ? (int)(j.nlon / 2) : -1;
+  p.round_bf16 = (j.flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0;
+
+  p.n_rt = (int)((R + hsb::kRows - 1) / hsb::kRows);
+  p.n_mt = (int)((j.out_cols + hsb::kMTile - 1) / hsb::kMTile);
+  const long long act = (S > 0) ? (j.M < j.L ? j.M : j.L) : 0;
+  p.j_act = (int)((act + hsb::kMTile - 1) / hsb::kMTile);
+  if (p.j_act > p.n_mt) p.j_act = p.n_mt;
+  long long n_compute = 0, n_zero = 0;
+  for (int jt = 0; jt < p.n_mt; ++jt) {
+    if (jt < p.j_act) {
+      const int first = j.dir == HOLYSHT_DIR_FORWARD ? jt : 0;
+      n_compute += p.n_rt > first ? p.n_rt - first : 0;
+      n_zero += j.dir == HOLYSHT_DIR_FORWARD ? (jt < p.n_rt ? jt : p.n_rt) : 0;
+    } else {
+      n_zero += p.n_rt;
+    }
+  }
+  p.n_compute = (int)n_compute;
+  p.n_zero = (int)n_zero;
+
+  int nb;
+  if (j.kind == HOLYSHT_KIND_VECTOR)
+    nb = next_pow2_at_least(j.B, 1, 4);
+  else if (j.kind == HOLYSHT_KIND_SCALAR)
+    nb = next_pow2_at_least(j.B, 1, 8);
+  else
+    nb = next_pow2_at_least(j.B, 2, 16);
+
+  // reduction split: enough CTAs for about two resident waves, at least two
+  // staged chunks per cluster rank
+  int ks = j.ksplit ? j.ksplit : env_ksplit();
+  if (ks == 0) {
+    const long long n_bg = (j.B + nb - 1) / nb;
+    const long long tiles = n_compute * n_bg;
+    const long long want = 4LL * sm_count_of_current_device();
+    ks = 1;
+    while (ks < 8 && tiles * ks < want && S / (2LL * ks) >= 2LL * hsb::kChunk) ks *= 2;
+  }
+  p.ks = ks;
+
+  if (j.kind == HOLYSHT_KIND_SCALAR) {
+    return j.dir == HOLYSHT_DIR_FORWARD
+               ? dispatch_nb<hsb::KIND_SCALAR, hsb::DIR_FWD, float2>(p, nb, stream)
+               : dispatch_nb<hsb::KIND_SCALAR, hsb::DIR_INV, float2>(p, nb, stream);
+  }
+  if (j.kind == HOLYSHT_KIND_VECTOR) {
+    return j.dir == HOLYSHT_DIR_FORWARD
+               ? dispatch_nb<hsb::KIND_VECTOR, hsb::DIR_FWD, float2>(p, nb, stream)
+               : dispatch_nb<hsb::KIND_VECTOR, hsb::DIR_INV, float2>(p, nb, stream);
+  }
+  if (j.in_dtype == HOLYSHT_DTYPE_BF16) {
+    return j.dir == HOLYSHT_DIR_FORWARD
+               ? dispatch_nb<hsb::KIND_REAL, hsb::DIR_FWD, __nv_bfloat16>(p, nb, stream)
+               : dispatch_nb<hsb::KIND_REAL, hsb::DIR_INV, __nv_bfloat16>(p, nb, stream);
+  }
+  return j.dir == HOLYSHT_DIR_FORWARD
+             ? dispatch_nb<hsb::KIND_REAL, hsb::DIR_FWD, float>(p, nb, stream)
+             : dispatch_nb<hsb::KIND_REAL, hsb::DIR_INV, float>(p, nb, stream);
+}
+
+// Dense contiguous job in the reference layouts.
+Job dense_job(int kind, int dir, int in_dtype, const void* in, void* out, const float* w0,
+              const float* w1, long long B, long long K, long long L, long long M) {
+  Job j = {};
+  j.kind = kind;
+  j.dir = dir;
+  j.in_dtype = in_dtype;
+  j.flags = 0;
+  j.in = in;
+  j.out = out;
+  j.w0 = w0;
+  j.w1 = w1;
+  j.B = B;
+  j.K = K;
+  j.L = L;
+  j.M = M;
+  const long long P = kind == HOLYSHT_KIND_VECTOR ? 2 : 1;
+  const long long in_rows = dir == HOLYSHT_DIR_FORWARD ? K : L;
+  const long long out_rows = dir == HOLYSHT_DIR_FORWARD ? L : K;
+  j.in_rs = M;
+  j.in_ps = in_rows * M;
+  j.in_bs = P * in_rows * M;
+  j.out_rs = M;
+  j.out_ps = out_rows * M;
+  j.out_bs = P * out_rows * M;
+  j.out_cols = M;
+  j.w_ks = M;
+  j.w_ls = K * M;
+  j.nlon = 0;
+  j.scale = 1.f;
+  j.ksplit = 0;
+  return j;
+}
+
+}  // namespace
+
+extern "C" {
+
+int holysht_version(void) { return 100; }
+
+const char* holysht_last_error(void) { return g_last_error.c_str(); }
+
+int holysht_fused_legendre_forward(void* out, const void* in, const float* weight_t, int64_t batch,
+                                   int64_t nlat, int64_t lmax, int64_t mmax, void* stream) {
+  Job j = dense_job(HOLYSHT_KIND_SCALAR, HOLYSHT_DIR_FORWARD, HOLYSHT_DTYPE_C64, in, out, weight_t,
+                    nullptr, batch, nlat, lmax, mmax);
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_fused_legendre_inverse(void* out, const void* in, const float* weight_t, int64_t batch,
+                                   int64_t nlat, int64_t lmax, int64_t mmax, void* stream) {
+  Job j = dense_job(HOLYSHT_KIND_SCALAR, HOLYSHT_DIR_INVERSE, HOLYSHT_DTYPE_C64, in, out, weight_t,
+                    nullptr, batch, nlat, lmax, mmax);
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_fused_legendre_forward_real(float* out, const void* in, int in_dtype,
+                                        const float* weight_t, int64_t batch, int64_t nlat,
+                                        int64_t lmax, int64_t mmax, int backend_hint,
+                                        void* stream) {
+  if (backend_hint < HOLYSHT_BACKEND_AUTO || backend_hint > HOLYSHT_BACKEND_TC_BF16)
+    return fail(HOLYSHT_ERR_INVALID, "unknown backend_hint %d", backend_hint);
+  Job j = dense_job(HOLYSHT_KIND_REAL, HOLYSHT_DIR_FORWARD, in_dtype, in, out, weight_t, nullptr,
+                    batch, nlat, lmax, mmax);
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_fused_legendre_inverse_real(float* out, const float* in, const float* weight_t,
+                                        int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                        void* stream) {
+  Job j = dense_job(HOLYSHT_KIND_REAL, HOLYSHT_DIR_INVERSE, HOLYSHT_DTYPE_F32, in, out, weight_t,
+                    nullptr, batch, nlat, lmax, mmax);
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_fused_vector_legendre_forward(void* out, const void* in, const float* w0_t,
+                                          const float* w1_t, int64_t batch, int64_t nlat,
+                                          int64_t lmax, int64_t mmax, int backend_hint,
+                                          void* stream) {
+  if (backend_hint < HOLYSHT_BACKEND_AUTO || backend_hint > HOLYSHT_BACKEND_TC_BF16)
+    return fail(HOLYSHT_ERR_INVALID, "unknown backend_hint %d", backend_hint);
+  Job j = dense_job(HOLYSHT_KIND_VECTOR, HOLYSHT_DIR_FORWARD, HOLYSHT_DTYPE_C64, in, out, w0_t,
+                    w1_t, batch, nlat, lmax, mmax);
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_fused_vector_legendre_inverse(void* out, const void* in, const float* w0_t,
+                                          const float* w1_t, int64_t batch, int64_t nlat,
+                                          int64_t lmax, int64_t mmax, void* stream) {
+  Job j = dense_job(HOLYSHT_KIND_VECTOR, HOLYSHT_DIR_INVERSE, HOLYSHT_DTYPE_C64, in, out, w0_t,
+                    w1_t, batch, nlat, lmax, mmax);
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
+  if (!d) return fail(HOLYSHT_ERR_INVALID, "descriptor is null");
+  Job j = {};
+  j.kind = d->kind;
+  j.dir = d->direction;
+  j.in_dtype = d->in_dtype;
+  j.flags = d->flags;
+  j.in = d->in;
+  j.out = d->out;
+  j.w0 = d->w0;
+  j.w1 = d->w1;
+  j.B = d->batch;
+  j.K = d->nlat;
+  j.L = d->lmax;
+  j.M = d->mmax;
+  j.in_bs = d->in_batch_stride;
+  j.in_ps = d->in_comp_stride;
+  j.in_rs = d->in_row_stride;
+  j.out_bs = d->out_batch_stride;
+  j.out_ps = d->out_comp_stride;
+  j.out_rs = d->out_row_stride;
+  j.out_cols = d->out_cols;
+  j.w_ls = d->w_l_stride;
+  j.w_ks = d->w_k_stride;
+  j.nlon = d->nlon;
+  j.scale = d->scale;
+  j.ksplit = d->ksplit;
+  if ((j.flags & HOLYSHT_FLAG_IRFFT_PREP) && (j.nlon <= 0 || j.out_cols > j.nlon / 2 + 1))
+    return fail(HOLYSHT_ERR_INVALID, "irfft preparation needs nlon > 0 and out_cols <= nlon/2+1");
+  return run_job(j, static_cast<cudaStream_t>(stream));
+}
+
+int holysht_fused_vector_forward_pack_real(float* s0, float* s1, const void* in, int64_t batch,
+                                           int64_t nlat, int64_t mmax, void* stream) {
+  if (batch < 0 || nlat < 0 || mmax < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  const long long plane = (long long)nlat * mmax;
+  if (batch == 0 || plane == 0) return ok();
+  if (!s0 || !s1 || !in) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  const long long total = batch * plane;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  hsb::vector_pack_real_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      s0, s1, static_cast<const float2*>(in), (int)batch, plane);
+  return check_launch("fused_vector_forward_pack_real");
+}
+
+int holysht_fused_vector_forward_recompose_real(void* out, const float* o0, const float* o1,
+                                                int64_t batch, int64_t lmax, int64_t mmax,
+                                                void* stream) {
+  if (batch < 0 || lmax < 0 || mmax < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  const long long plane = (long long)lmax * mmax;
+  if (batch == 0 || plane == 0) return ok();
+  if (!out || !o0 || !o1) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  const long long total = batch * plane;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  hsb::vector_recompose_real_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<float2*>(out), o0, o1, (int)batch, plane);
+  return check_launch("fused_vector_forward_recompose_real");
+}
+
+int holysht_sht_prepare_irfft(void* data, int64_t rows, int64_t width, int64_t mmax, int64_t nlon,
+                              void* stream) {
+  if (rows < 0 || width < 0 || mmax < 0 || nlon <= 0)
+    return fail(HOLYSHT_ERR_INVALID, "invalid extents (rows=%lld width=%lld mmax=%lld nlon=%lld)",
+                (long long)rows, (long long)width, (long long)mmax, (long long)nlon);
+  if (width > INT_MAX) return fail(HOLYSHT_ERR_INVALID, "width too large");
+  const long long total = rows * width;
+  if (total == 0) return ok();
+  if (!data) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  const int nyq = (nlon % 2 == 0) ? (int)(nlon / 2) : -1;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  hsb::prepare_irfft_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<float2*>(data), rows, (int)width, (int)(mmax < width ? mmax : width), nyq);
+  return check_launch("sht_prepare_irfft");
+}
+
+}  // extern "C"

@@ -1,0 +1,460 @@
+// Per-order Legendre contraction for sm_100a.
+//
+// One kernel template covers every contraction on the HOLYSHT hot path:
+//
+//   forward  (DIR_FWD): out[b,p,l,m] = sum_k  W[l,k,m] * in[b,p,k,m]   (l >= m)
+//   inverse  (DIR_INV): out[b,p,k,m] = sum_l  W[l,k,m] * in[b,p,l,m]   (l >= m)
+//
+// for three element kinds:
+//   KIND_SCALAR  complex input/output, one table             (fused_legendre_*)
+//   KIND_VECTOR  complex, two tables W0/W1, two components   (fused_vector_legendre_*)
+//                sph = W0 c0 + i s W1 c1,  tor = i s W1 c0 - W0 c1,  s = w1_sign
+//   KIND_REAL    real input/output, one table                (fused_legendre_*_real)
+//
+// The tables stay in the reference operator layout W[l][k][m] (m contiguous,
+// torch-ext/torch_binding.cpp:12-24; zero above the diagonal m > l).  Lanes
+// of a warp own 32 consecutive orders m, so every table load is one coalesced
+// 128-byte row segment and each table element is read from HBM exactly once
+// per batch group; only the l >= m triangle is ever loaded.
+//
+// Work decomposition (see DESIGN.md for the roofline):
+//   * a CTA owns a 32-order m-tile x 32 output rows (8 warps x 4 rows) x a
+//     batch group of NB batches;
+//   * the reduction axis is split across a thread-block cluster of KS CTAs;
+//     each CTA streams its slice of the input spectrum through a cp.async
+//     double buffer in shared memory (all 8 warps reuse it) and its table
+//     rows straight into registers (a 4-deep register ring), and the partial
+//     sums are reduced through distributed shared memory at the end, in a
+//     fixed rank order (deterministic);
+//   * the inner product is FP32 FMA issued as packed f32x2 FMAs.
+#pragma once
+
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+namespace hsb {
+
+namespace cg = cooperative_groups;
+
+enum Kind : int { KIND_SCALAR = 0, KIND_VECTOR = 1, KIND_REAL = 2 };
+enum Dir : int { DIR_FWD = 0, DIR_INV = 1 };
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kRowsPerWarp = 4;
+constexpr int kRows = kWarps * kRowsPerWarp;  // output rows per CTA
+constexpr int kMTile = 32;                     // orders per CTA (one per lane)
+constexpr int kChunk = 8;                      // reduction steps per smem stage
+constexpr int kRing = 4;                       // register ring for table rows
+constexpr int kSmemBytes = 64 * 1024;
+
+struct ContractParams {
+  const void* in;
+  void* out;
+  const float* w0;
+  const float* w1;
+  long long in_bs, in_ps, in_rs;     // input strides (elements): batch, component, row
+  long long out_bs, out_ps, out_rs;  // output strides (elements)
+  long long w_ls, w_ks;              // table strides (floats) of l and k; m is contiguous
+  int B, K, L, M;                    // batch, nlat, lmax, mmax (table extents)
+  int out_cols;                      // output columns written (>= M; extra are zero)
+  int R, S;                          // output rows, reduction extent
+  float scale;                       // applied to every output
+  float w1_sign;                     // +1 (A) or -1 (conjugate transpose)
+  int zero_imag_col0;                // irfft preparation: Im(m=0) = 0
+  int nyquist;                       // irfft preparation: Im(m=nyquist) = 0, -1 = off
+  int round_bf16;                    // round inputs to bf16 before use
+  int n_rt, n_mt, j_act, n_bg;       // row tiles, m tiles, active m tiles, batch groups
+  int n_compute, n_zero;             // tiles per batch group
+  int ks;                            // cluster size (reduction split)
+};
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  return __ffma2_rn(a, b, c);
+}
+
+__device__ __forceinline__ void cp_async_bytes(void* smem_dst, const void* gsrc, int bytes_valid,
+                                               int size) {
+  unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  if (size == 8) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gsrc),
+                 "r"(bytes_valid));
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gsrc),
+                 "r"(bytes_valid));
+  }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;\n" ::); }
+
+// streaming table load: read once, no L1 allocation, evict-first in L2 so the
+// table stream does not push the (re-read) input spectrum out of L2
+__device__ __forceinline__ unsigned long long evict_first_policy() {
+  unsigned long long pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ float ld_stream(const float* p, unsigned long long pol) {
+  float v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;\n"
+               : "=f"(v)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+__device__ __forceinline__ float round_to_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Decode a tile index into (m tile j, row tile rt).  Compute tiles come first,
+// ordered by m tile (longest reductions first for the inverse direction),
+// then tiles that are entirely zero (rows above the diagonal, or orders with
+// no l >= m inside the table).
+template <int DIR>
+__device__ __forceinline__ bool decode_tile(const ContractParams& p, int t, int& j, int& rt) {
+  if (t < p.n_compute) {
+    int rem = t;
+    for (j = 0; j < p.j_act; ++j) {
+      const int first = (DIR == DIR_FWD) ? j : 0;
+      const int cnt = p.n_rt > first ? p.n_rt - first : 0;
+      if (rem < cnt) {
+        rt = first + rem;
+        return true;
+      }
+      rem -= cnt;
+    }
+    rt = 0;
+    return true;  // unreachable for consistent host parameters
+  }
+  int rem = t - p.n_compute;
+  for (j = 0; j < p.n_mt; ++j) {
+    int cnt;
+    if (j < p.j_act)
+      cnt = (DIR == DIR_FWD) ? (j < p.n_rt ? j : p.n_rt) : 0;
+    else
+      cnt = p.n_rt;
+    if (rem < cnt) {
+      rt = rem;
+      return false;
+    }
+    rem -= cnt;
+  }
+  rt = 0;
+  j = p.n_mt;  // out of range: nothing to write
+  return false;
+}
+
+template <int KIND>
+struct KindTraits;
+template <>
+struct KindTraits<KIND_SCALAR> {
+  static constexpr int P = 1;  // components per batch
+  using SE = float2;           // staged element
+};
+template <>
+struct KindTraits<KIND_VECTOR> {
+  static constexpr int P = 2;
+  using SE = float2;
+};
+template <>
+struct KindTraits<KIND_REAL> {
+  static constexpr int P = 1;
+  using SE = float;
+};
+
+template <int KIND, int NB>
+struct Acc {
+  // number of packed (float2) accumulators per output row
+  static constexpr int NA = KIND == KIND_VECTOR ? 2 * NB : (KIND == KIND_SCALAR ? NB : NB / 2);
+};
+
+template <int KIND, int DIR, int NB, typename TIN>
+__device__ __forceinline__ void write_zero_tile(const ContractParams& p, int j, int rt, int bg,
+                                                int rank) {
+  constexpr int P = KindTraits<KIND>::P;
+  constexpr int NA = Acc<KIND, NB>::NA;
+  const int rpr = kRows / p.ks;
+  const int total = rpr * NA * 32;
+  for (int e = threadIdx.x; e < total; e += kThreads) {
+    const int col = e & 31;
+    const int a = (e >> 5) % NA;
+    const int rl = e / (NA * 32);
+    const int row = rt * kRows + rank * rpr + rl;
+    const int mm = j * kMTile + col;
+    if (row >= p.R || mm >= p.out_cols) continue;
+    if (KIND == KIND_REAL) {
+      float* out = static_cast<float*>(p.out);
+      const int b = bg * NB + 2 * a;
+      const long long off = (long long)row * p.out_rs + mm;
+      if (b < p.B) out[(long long)b * p.out_bs + off] = 0.f;
+      if (b + 1 < p.B) out[(long long)(b + 1) * p.out_bs + off] = 0.f;
+    } else {
+      float2* out = static_cast<float2*>(p.out);
+      const int b = bg * NB + a / P;
+      const int pl = a % P;
+      if (b < p.B)
+        out[(long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs + mm] =
+            make_float2(0.f, 0.f);
+    }
+  }
+}
+
+template <int KIND, int DIR, int NB, typename TIN>
+__global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? 1 : 2)
+    contract_kernel(const ContractParams p) {
+  constexpr int P = KindTraits<KIND>::P;
+  constexpr int PB = NB * P;  // staged planes per reduction step
+  constexpr int NA = Acc<KIND, NB>::NA;
+  using SE = typename KindTraits<KIND>::SE;
+  constexpr bool kAsyncStage = !std::is_same<TIN, __nv_bfloat16>::value;
+  static_assert(kRows * NA * 32 * 8 <= kSmemBytes, "partial sums exceed shared memory");
+  static_assert(2 * kChunk * PB * 32 * sizeof(SE) <= kSmemBytes, "stage exceeds shared memory");
+  static_assert(KIND != KIND_REAL || NB % 2 == 0, "real kind pairs batches");
+  static_assert(kChunk % kRing == 0, "ring slots are compile-time within a chunk");
+
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  SE* stage = reinterpret_cast<SE*>(smem_raw);  // [2][kChunk][PB][32]
+  float2* part = reinterpret_cast<float2*>(smem_raw);  // [kRows][NA][32], after the loop
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int ks = p.ks;
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tile = blockIdx.x / ks;
+  const int bg = tile % p.n_bg;
+  const int t = tile / p.n_bg;
+  int j, rt;
+  const bool compute = decode_tile<DIR>(p, t, j, rt);
+  if (!compute) {
+    // uniform across the cluster: no cluster barrier is reached on this path
+    write_zero_tile<KIND, DIR, NB, TIN>(p, j, rt, bg, rank);
+    return;
+  }
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int m0 = j * kMTile;
+  const int m = m0 + lane;
+  const int row0 = rt * kRows;
+  const int b0 = bg * NB;
+
+  // reduction range of this cluster rank (chunk aligned)
+  const int s_begin = (DIR == DIR_FWD) ? 0 : m0;
+  const int s_end = p.S;
+  const int nsteps = s_end > s_begin ? s_end - s_begin : 0;
+  const int per = ((nsteps + ks * kChunk - 1) / (ks * kChunk)) * kChunk;
+  const int r_begin = min(s_end, s_begin + rank * per);
+  const int r_end = min(s_end, r_begin + per);
+  const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
+
+  // table offsets of this lane (32-bit: a table holds < 2^32 floats)
+  const unsigned sstride = (unsigned)((DIR == DIR_FWD) ? p.w_ks : p.w_ls);
+  const unsigned rstride = (unsigned)((DIR == DIR_FWD) ? p.w_ls : p.w_ks);
+  unsigned roff[kRowsPerWarp];
+  unsigned vmask = 0;
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int row = row0 + warp * kRowsPerWarp + i;
+    bool ok = row < p.R && m < p.M;
+    if (DIR == DIR_FWD) ok = ok && row >= m;  // l >= m
+    vmask |= ok ? (1u << i) : 0u;
+    roff[i] = ok ? (unsigned)row * rstride + (unsigned)m : 0u;
+  }
+  const float* __restrict__ w0 = p.w0;
+  const float* __restrict__ w1 = p.w1;
+
+  float2 acc[kRowsPerWarp][NA];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
+
+  // ---- staging of the input spectrum: [buf][step][plane][lane] ----
+  constexpr int kStageElems = kChunk * PB * 32;
+  auto stage_chunk = [&](int chunk, int buf) {
+    const int c0 = r_begin + chunk * kChunk;
+    SE* dst = stage + buf * kStageElems;
+    for (int e = threadIdx.x; e < kStageElems; e += kThreads) {
+      const int col = e & 31;
+      const int pb = (e >> 5) % PB;
+      const int ls = e / (PB * 32);
+      const int b = b0 + pb / P;
+      const int pl = pb % P;
+      const int s = c0 + ls;
+      const int mm = m0 + col;
+      const bool ok = s < r_end && b < p.B && mm < p.M;
+      const long long off = ok ? (long long)b * p.in_bs + (long long)pl * p.in_ps +
+                                     (long long)s * p.in_rs + mm
+                               : 0;
+      if constexpr (kAsyncStage) {
+        const SE* src = static_cast<const SE*>(p.in) + off;
+        cp_async_bytes(dst + e, src, ok ? (int)sizeof(SE) : 0, (int)sizeof(SE));
+      } else {
+        const TIN* src = static_cast<const TIN*>(p.in) + off;
+        dst[e] = ok ? static_cast<float>(*src) : 0.f;
+      }
+    }
+  };
+  auto round_own = [&](int buf) {
+    // each thread rounds the elements it staged itself (visible after its own wait)
+    if constexpr (KIND != KIND_REAL) {
+      float2* d = reinterpret_cast<float2*>(stage + buf * kStageElems);
+      for (int e = threadIdx.x; e < kStageElems; e += kThreads) {
+        float2 v = d[e];
+        d[e] = make_float2(round_to_bf16(v.x), round_to_bf16(v.y));
+      }
+    } else {
+      float* d = reinterpret_cast<float*>(stage + buf * kStageElems);
+      for (int e = threadIdx.x; e < kStageElems; e += kThreads) d[e] = round_to_bf16(d[e]);
+    }
+  };
+
+  // ---- table register ring ----
+  const unsigned long long pol = evict_first_policy();
+  float wr0[kRing][kRowsPerWarp];
+  float wr1[kRing][kRowsPerWarp];
+  auto load_step = [&](int slot_s, float (&d0)[kRowsPerWarp], float (&d1)[kRowsPerWarp]) {
+    const unsigned so = (unsigned)slot_s * sstride;
+    bool sok = slot_s < r_end;
+    if (DIR == DIR_INV) sok = sok && slot_s >= m;  // l >= m
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const bool ok = sok && ((vmask >> i) & 1u);
+      const unsigned off = roff[i] + so;
+      d0[i] = ok ? ld_stream(w0 + off, pol) : 0.f;
+      if (KIND == KIND_VECTOR) d1[i] = ok ? ld_stream(w1 + off, pol) * p.w1_sign : 0.f;
+    }
+  };
+
+  if (nchunks > 0) {
+    if constexpr (kAsyncStage) {
+      stage_chunk(0, 0);
+      cp_async_commit();
+    }
+#pragma unroll
+    for (int q = 0; q < kRing - 1; ++q) load_step(r_begin + q, wr0[q], wr1[q]);
+
+    for (int c = 0; c < nchunks; ++c) {
+      const int buf = c & 1;
+      if constexpr (kAsyncStage) {
+        if (c + 1 < nchunks) stage_chunk(c + 1, buf ^ 1);
+        cp_async_commit();
+        cp_async_wait_1();
+        if (p.round_bf16) round_own(buf);
+      } else {
+        stage_chunk(c, buf);
+      }
+      __syncthreads();
+      const SE* xs = stage + buf * kStageElems;
+      const int c0 = r_begin + c * kChunk;
+#pragma unroll 1
+      for (int sh = 0; sh < kChunk; sh += kRing) {
+#pragma unroll
+      for (int sq = 0; sq < kRing; ++sq) {
+        const int si = sh + sq;
+        const int cur = sq;
+        const int nxt = (sq + kRing - 1) % kRing;
+        load_step(c0 + si + kRing - 1, wr0[nxt], wr1[nxt]);
+        const SE* xrow = xs + si * PB * 32 + lane;
+        if constexpr (KIND == KIND_SCALAR) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const float2 x = xrow[b * 32];
+#pragma unroll
+            for (int i = 0; i < kRowsPerWarp; ++i) {
+              const float w = wr0[cur][i];
+              acc[i][b] = ffma2(make_float2(w, w), x, acc[i][b]);
+            }
+          }
+        } else if constexpr (KIND == KIND_VECTOR) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const float2 c0v = xrow[(2 * b) * 32];
+            const float2 c1v = xrow[(2 * b + 1) * 32];
+            const float2 c0s = make_float2(c0v.y, c0v.x);
+            const float2 c1s = make_float2(c1v.y, c1v.x);
+#pragma unroll
+            for (int i = 0; i < kRowsPerWarp; ++i) {
+              const float w0 = wr0[cur][i];
+              const float w1 = wr1[cur][i];
+              const float2 pw0 = make_float2(w0, w0);
+              const float2 pw1 = make_float2(-w1, w1);
+              const float2 nw0 = make_float2(-w0, -w0);
+              // sph += w0 c0 + i w1 c1
+              acc[i][2 * b] = ffma2(pw0, c0v, acc[i][2 * b]);
+              acc[i][2 * b] = ffma2(pw1, c1s, acc[i][2 * b]);
+              // tor += i w1 c0 - w0 c1
+              acc[i][2 * b + 1] = ffma2(pw1, c0s, acc[i][2 * b + 1]);
+              acc[i][2 * b + 1] = ffma2(nw0, c1v, acc[i][2 * b + 1]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int bp = 0; bp < NB / 2; ++bp) {
+            const float2 x = make_float2(xrow[(2 * bp) * 32], xrow[(2 * bp + 1) * 32]);
+#pragma unroll
+            for (int i = 0; i < kRowsPerWarp; ++i) {
+              const float w = wr0[cur][i];
+              acc[i][bp] = ffma2(make_float2(w, w), x, acc[i][bp]);
+            }
+          }
+        }
+      }
+      }
+      __syncthreads();
+    }
+    if constexpr (kAsyncStage) cp_async_wait_0();
+  }
+
+  // ---- cluster reduction of the partial sums through distributed smem ----
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int a = 0; a < NA; ++a) part[((warp * kRowsPerWarp + i) * NA + a) * 32 + lane] = acc[i][a];
+  cluster.sync();
+
+  const int rpr = kRows / ks;
+  const int total = rpr * NA * 32;
+  for (int e = threadIdx.x; e < total; e += kThreads) {
+    const int col = e & 31;
+    const int a = (e >> 5) % NA;
+    const int rl = e / (NA * 32);
+    const int rloc = rank * rpr + rl;
+    const int idx = (rloc * NA + a) * 32 + col;
+    float2 sum = make_float2(0.f, 0.f);
+    for (int q = 0; q < ks; ++q) {
+      const float2* pq = cluster.map_shared_rank(part, q);
+      const float2 v = pq[idx];
+      sum.x += v.x;
+      sum.y += v.y;
+    }
+    const int row = row0 + rloc;
+    const int mm = m0 + col;
+    if (row >= p.R || mm >= p.out_cols) continue;
+    sum.x *= p.scale;
+    sum.y *= p.scale;
+    if (KIND == KIND_REAL) {
+      float* out = static_cast<float*>(p.out);
+      const int b = b0 + 2 * a;
+      const long long off = (long long)row * p.out_rs + mm;
+      if (b < p.B) out[(long long)b * p.out_bs + off] = sum.x;
+      if (b + 1 < p.B) out[(long long)(b + 1) * p.out_bs + off] = sum.y;
+    } else {
+      if ((p.zero_imag_col0 && mm == 0) || mm == p.nyquist) sum.y = 0.f;
+      float2* out = static_cast<float2*>(p.out);
+      const int b = b0 + a / P;
+      const int pl = a % P;
+      if (b < p.B)
+        out[(long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs + mm] =
+            sum;
+    }
+  }
+  cluster.sync();  // keep this CTA's partials alive until every peer has read them
+}
+
+}  // namespace hsb

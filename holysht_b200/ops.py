@@ -1,0 +1,245 @@
+"""Reference-named operators over the C ABI.
+
+Each function here has the name, argument order and in-place semantics of
+one operator of the reference's torch binding (``torch-ext/torch_binding.cpp``
+:12-24): the caller allocates ``output``, the operator fills it on the
+current CUDA stream.  Argument checks raise ``RuntimeError`` for the same
+conditions the reference's ``TORCH_CHECK``s reject
+(``cuda/fused_legendre.cu:3157-3335``).
+
+``legendre_contract`` is the strided entry the modules use (no reference
+counterpart): it reads the rfft output in place, folds the 2*pi spectrum
+scale, writes irfft-ready buffers and runs the conjugate-transpose vector map.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "fused_legendre_forward",
+    "fused_legendre_inverse",
+    "fused_legendre_forward_real",
+    "fused_legendre_forward_real_ex",
+    "fused_legendre_inverse_real",
+    "fused_vector_legendre_forward",
+    "fused_vector_legendre_forward_ex",
+    "fused_vector_legendre_inverse",
+    "fused_vector_forward_pack_real",
+    "fused_vector_forward_recompose_real",
+    "sht_prepare_irfft",
+    "legendre_contract",
+]
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        _require(t.is_cuda, "holysht_b200 operators take CUDA tensors only")
+        _require(t.device == dev, "all tensors must be on the same CUDA device")
+    return dev
+
+
+def _contig(*ts: torch.Tensor) -> None:
+    for t in ts:
+        _require(t.is_contiguous(), "tensors must be contiguous")
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check_scalar(output, input, weight_t, inverse: bool, in_dtypes, out_dtype, what):
+    dev = _cuda(output, input, weight_t)
+    _contig(output, input, weight_t)
+    _require(input.dtype in in_dtypes, f"{what}: input has dtype {input.dtype}")
+    _require(output.dtype == out_dtype, f"{what}: output must be {out_dtype}")
+    _require(weight_t.dtype == torch.float32, f"{what}: weight must be float32")
+    _require(input.dim() == 3, f"{what}: input must be rank 3")
+    _require(output.dim() == 3, f"{what}: output must be rank 3")
+    _require(weight_t.dim() == 3, f"{what}: weight_t must be rank 3")
+    L, K, M = weight_t.shape
+    B = input.size(0)
+    if not inverse:
+        _require(input.size(1) == K, "weight dim 1 must match nlat")
+        _require(input.size(2) == M, "weight dim 2 must match mmax")
+        _require(tuple(output.shape) == (B, L, M), "output must be [batch, lmax, mmax]")
+    else:
+        _require(input.size(1) == L, "weight dim 0 must match lmax")
+        _require(input.size(2) == M, "weight dim 2 must match mmax")
+        _require(tuple(output.shape) == (B, K, M), "output must be [batch, nlat, mmax]")
+    return dev, B, K, L, M
+
+
+def _check_vector(output, input, w0, w1, inverse: bool, what):
+    dev = _cuda(output, input, w0, w1)
+    _contig(output, input, w0, w1)
+    _require(input.dtype == torch.complex64 and output.dtype == torch.complex64,
+             f"{what}: input and output must be complex64")
+    _require(w0.dtype == torch.float32 and w1.dtype == torch.float32, f"{what}: weights must be float32")
+    _require(input.dim() == 4 and output.dim() == 4, f"{what}: input and output must be rank 4")
+    _require(input.size(1) == 2 and output.size(1) == 2, f"{what}: component dimension must be 2")
+    _require(w0.dim() == 3 and w0.shape == w1.shape, f"{what}: weights must be matching rank-3 tensors")
+    L, K, M = w0.shape
+    B = input.size(0)
+    if not inverse:
+        _require(input.size(2) == K and input.size(3) == M, "input must be [batch, 2, nlat, mmax]")
+        _require(tuple(output.shape) == (B, 2, L, M), "output must be [batch, 2, lmax, mmax]")
+    else:
+        _require(input.size(2) == L and input.size(3) == M, "input must be [batch, 2, lmax, mmax]")
+        _require(tuple(output.shape) == (B, 2, K, M), "output must be [batch, 2, nlat, mmax]")
+    return dev, B, K, L, M
+
+
+def fused_legendre_forward(output: torch.Tensor, input: torch.Tensor, weight_t: torch.Tensor) -> None:
+    dev, B, K, L, M = _check_scalar(output, input, weight_t, False, (torch.complex64,),
+                                    torch.complex64, "fused_legendre_forward")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_legendre_forward(
+            _p(output), _p(input), _p(weight_t), B, K, L, M, _stream(dev)))
+
+
+def fused_legendre_inverse(output: torch.Tensor, input: torch.Tensor, weight_t: torch.Tensor) -> None:
+    dev, B, K, L, M = _check_scalar(output, input, weight_t, True, (torch.complex64,),
+                                    torch.complex64, "fused_legendre_inverse")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_legendre_inverse(
+            _p(output), _p(input), _p(weight_t), B, K, L, M, _stream(dev)))
+
+
+def fused_legendre_forward_real_ex(output: torch.Tensor, input: torch.Tensor, weight_t: torch.Tensor,
+                                   backend_hint: int) -> None:
+    dev, B, K, L, M = _check_scalar(output, input, weight_t, False, (torch.float32, torch.bfloat16),
+                                    torch.float32, "fused_legendre_forward_real")
+    dt = _lib.DTYPE_BF16 if input.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_legendre_forward_real(
+            _p(output), _p(input), dt, _p(weight_t), B, K, L, M, int(backend_hint), _stream(dev)))
+
+
+def fused_legendre_forward_real(output: torch.Tensor, input: torch.Tensor, weight_t: torch.Tensor) -> None:
+    fused_legendre_forward_real_ex(output, input, weight_t, 0)
+
+
+def fused_legendre_inverse_real(output: torch.Tensor, input: torch.Tensor, weight_t: torch.Tensor) -> None:
+    dev, B, K, L, M = _check_scalar(output, input, weight_t, True, (torch.float32,), torch.float32,
+                                    "fused_legendre_inverse_real")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_legendre_inverse_real(
+            _p(output), _p(input), _p(weight_t), B, K, L, M, _stream(dev)))
+
+
+def fused_vector_legendre_forward_ex(output: torch.Tensor, input: torch.Tensor, weight0_t: torch.Tensor,
+                                     weight1_t: torch.Tensor, backend_hint: int) -> None:
+    dev, B, K, L, M = _check_vector(output, input, weight0_t, weight1_t, False,
+                                    "fused_vector_legendre_forward")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_vector_legendre_forward(
+            _p(output), _p(input), _p(weight0_t), _p(weight1_t), B, K, L, M, int(backend_hint),
+            _stream(dev)))
+
+
+def fused_vector_legendre_forward(output: torch.Tensor, input: torch.Tensor, weight0_t: torch.Tensor,
+                                  weight1_t: torch.Tensor) -> None:
+    fused_vector_legendre_forward_ex(output, input, weight0_t, weight1_t, 0)
+
+
+def fused_vector_legendre_inverse(output: torch.Tensor, input: torch.Tensor, weight0_t: torch.Tensor,
+                                  weight1_t: torch.Tensor) -> None:
+    dev, B, K, L, M = _check_vector(output, input, weight0_t, weight1_t, True,
+                                    "fused_vector_legendre_inverse")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_vector_legendre_inverse(
+            _p(output), _p(input), _p(weight0_t), _p(weight1_t), B, K, L, M, _stream(dev)))
+
+
+def fused_vector_forward_pack_real(stacked_w0: torch.Tensor, stacked_w1: torch.Tensor,
+                                   input: torch.Tensor) -> None:
+    dev = _cuda(stacked_w0, stacked_w1, input)
+    _contig(stacked_w0, stacked_w1, input)
+    _require(input.dtype == torch.complex64, "input must be complex64")
+    _require(stacked_w0.dtype == torch.float32, "stacked_w0 must be float32")
+    _require(stacked_w1.dtype == torch.float32, "stacked_w1 must be float32")
+    _require(input.dim() == 4, "input must be rank 4")
+    _require(input.size(1) == 2, "input component dimension must be 2")
+    _require(stacked_w0.dim() == 3 and stacked_w1.dim() == 3, "stacked outputs must be rank 3")
+    B, _, K, M = input.shape
+    _require(stacked_w0.shape == stacked_w1.shape, "stacked outputs must match")
+    _require(tuple(stacked_w0.shape) == (4 * B, K, M), "stacked outputs must be [4*batch, nlat, mmax]")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_vector_forward_pack_real(
+            _p(stacked_w0), _p(stacked_w1), _p(input), B, K, M, _stream(dev)))
+
+
+def fused_vector_forward_recompose_real(output: torch.Tensor, out_w0: torch.Tensor,
+                                        out_w1: torch.Tensor) -> None:
+    dev = _cuda(output, out_w0, out_w1)
+    _contig(output, out_w0, out_w1)
+    _require(output.dtype == torch.complex64, "output must be complex64")
+    _require(out_w0.dtype == torch.float32 and out_w1.dtype == torch.float32, "real outputs must be float32")
+    _require(output.dim() == 4 and output.size(1) == 2, "output must be [batch, 2, lmax, mmax]")
+    _require(out_w0.dim() == 3 and out_w0.shape == out_w1.shape, "real outputs must match")
+    _require(out_w0.size(0) % 4 == 0, "real output batch dimension must be divisible by 4")
+    B, _, L, M = output.shape
+    _require(tuple(out_w0.shape) == (4 * B, L, M), "real outputs must be [4*batch, lmax, mmax]")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_fused_vector_forward_recompose_real(
+            _p(output), _p(out_w0), _p(out_w1), B, L, M, _stream(dev)))
+
+
+def sht_prepare_irfft(data: torch.Tensor, mmax: int, nlon: int) -> None:
+    dev = _cuda(data)
+    _contig(data)
+    _require(data.dtype == torch.complex64, "data must be complex64")
+    _require(data.dim() == 3, "data must be rank 3")
+    rows = data.size(0) * data.size(1)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_sht_prepare_irfft(
+            _p(data), rows, data.size(2), int(mmax), int(nlon), _stream(dev)))
+
+
+def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,
+                      w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
+                      lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
+                      scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0) -> None:
+    """Strided contraction; strides are (batch, component, row) in elements."""
+    dev = _cuda(output, input, w0)
+    if w1 is not None:
+        _cuda(output, w1)
+        _require(w1.stride() == w0.stride(), "W0 and W1 must share strides")
+    _require(w0.dtype == torch.float32 and w0.dim() == 3 and w0.stride(2) == 1,
+             "tables must be float32 [lmax, nlat, mmax] with contiguous mmax")
+    if input.dtype == torch.complex64:
+        dt = _lib.DTYPE_C64
+    elif input.dtype == torch.float32:
+        dt = _lib.DTYPE_F32
+    elif input.dtype == torch.bfloat16:
+        dt = _lib.DTYPE_BF16
+    else:
+        raise RuntimeError(f"unsupported input dtype {input.dtype}")
+    d = _lib.ContractDesc()
+    d.kind, d.direction, d.in_dtype, d.flags = kind, direction, dt, flags
+    d.in_, d.out, d.w0, d.w1 = _p(input), _p(output), _p(w0), _p(w1)
+    d.batch, d.nlat, d.lmax, d.mmax = batch, nlat, lmax, mmax
+    d.in_batch_stride, d.in_comp_stride, d.in_row_stride = in_strides
+    d.out_batch_stride, d.out_comp_stride, d.out_row_stride = out_strides
+    d.out_cols = out_cols
+    d.w_l_stride, d.w_k_stride = w0.stride(0), w0.stride(1)
+    d.nlon = nlon
+    d.scale = scale
+    d.ksplit = ksplit
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))

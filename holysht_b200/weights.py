@@ -1,0 +1,262 @@
+"""Host-side construction of the Legendre weight tables.
+
+The reference's modules obtain their tables from torch-harmonics at
+construction time (``torch-ext/holysht/__init__.py:1247-1273`` for RealSHT,
+:1406-1424 InverseRealSHT, :1452-1480 RealVectorSHT, :1710-1730
+InverseRealVectorSHT).  When torch-harmonics is importable this module does
+exactly that.  Otherwise it builds the same tables in float64 from the
+mathematics they are defined by:
+
+* equiangular grid: Clenshaw-Curtis weights from the closed-form cosine sum
+  w_j = c_j/(n-1) * (1 - sum_k b_k cos(2 k theta_j) / (4 k^2 - 1));
+* legendre-gauss grid: numpy's Gauss-Legendre rule;
+* lobatto grid: Gauss-Lobatto-Legendre rule (Newton on (1-x^2) P'_{n-1});
+* orthonormal associated Legendre functions P_l^m(cos theta) by the
+  three-term recurrence in l, all orders at once (vectorised over m);
+* vector tables: dP/dtheta and m P / sin(theta) from the ladder identities.
+
+Layout returned: ``[mmax, lmax, nlat]`` (``[2, mmax, lmax, nlat]`` for the
+vector tables), the torch-harmonics layout; nodes run north pole first.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+GRIDS = ("equiangular", "legendre-gauss", "lobatto")
+NORMS = ("ortho", "four-pi", "schmidt")
+
+
+def _check(grid: str, norm: str) -> None:
+    if grid not in GRIDS:
+        raise ValueError(f"Unknown quadrature mode {grid!r}; expected one of {GRIDS}")
+    if norm not in NORMS:
+        raise ValueError(f"Unknown normalization {norm!r}; expected one of {NORMS}")
+
+
+def default_lmax(nlat: int, grid: str) -> int:
+    return nlat - 1 if grid == "lobatto" else nlat
+
+
+def default_mmax(nlon: int) -> int:
+    return nlon // 2 + 1
+
+
+def clenshaw_curtis(n: int):
+    """Nodes x_j = -cos(pi j/(n-1)) (ascending) and Clenshaw-Curtis weights."""
+    if n < 2:
+        raise ValueError("equiangular grid needs nlat >= 2")
+    N = n - 1
+    theta = np.pi * np.arange(n) / N
+    x = -np.cos(theta)
+    if n == 2:
+        return x, np.ones(2)
+    w = np.ones(n)
+    half = N // 2
+    for k in range(1, half + 1):
+        b = 1.0 if 2 * k == N else 2.0
+        w -= b * np.cos(2.0 * k * theta) / (4.0 * k * k - 1.0)
+    c = np.full(n, 2.0)
+    c[0] = c[-1] = 1.0
+    return x, c * w / N
+
+
+def gauss_lobatto(n: int):
+    if n < 2:
+        raise ValueError("lobatto grid needs nlat >= 2")
+    N = n - 1
+    x = -np.cos(np.pi * np.arange(n) / N)
+    for _ in range(200):
+        p0, p1 = np.ones_like(x), x.copy()
+        for k in range(2, N + 1):
+            p0, p1 = p1, ((2.0 * k - 1.0) * x * p1 - (k - 1.0) * p0) / k
+        step = (x * p1 - p0) / (n * p1)
+        step[0] = step[-1] = 0.0
+        x = x - step
+        if np.max(np.abs(step)) < 1e-16:
+            break
+    p0, p1 = np.ones_like(x), x.copy()
+    for k in range(2, N + 1):
+        p0, p1 = p1, ((2.0 * k - 1.0) * x * p1 - (k - 1.0) * p0) / k
+    return x, 2.0 / (N * n * p1 * p1)
+
+
+def nodes_and_weights(nlat: int, grid: str):
+    """(colatitudes north-first, quadrature weights)."""
+    if grid == "equiangular":
+        x, w = clenshaw_curtis(nlat)
+    elif grid == "legendre-gauss":
+        x, w = np.polynomial.legendre.leggauss(nlat)
+    elif grid == "lobatto":
+        x, w = gauss_lobatto(nlat)
+    else:
+        raise ValueError(f"Unknown quadrature mode {grid!r}")
+    return np.flip(np.arccos(x)).copy(), np.asarray(w, np.float64)
+
+
+def _legendre_rows(n_m: int, n_l: int, x: np.ndarray, seed: float):
+    """Yield (l, row) with row[m, k] = P_l^m(x_k) (no Condon-Shortley phase,
+    zero for m > l), for l = 0 .. n_l-1 and all m < n_m at once.
+
+    The recurrence runs upwards in l for every order simultaneously, keeping
+    only the two previous rows, so memory stays O(n_m * nlat)."""
+    sin_t = np.sqrt((1.0 + x) * (1.0 - x))
+    K = x.size
+    mm = np.arange(n_m, dtype=np.float64)
+    sect = np.full(K, seed)  # P_l^l at the current l
+    prev2 = np.zeros((n_m, K))
+    prev1 = np.zeros((n_m, K))
+    for l in range(n_l):
+        row = np.zeros((n_m, K))
+        if l > 0:
+            sect = math.sqrt((2.0 * l + 1.0) / (2.0 * l)) * sin_t * sect
+        if l >= 2:
+            k = min(l - 1, n_m)
+            m = mm[:k]
+            a = np.sqrt((4.0 * l * l - 1.0) / (l * l - m * m))
+            b = np.sqrt(((l - 1.0) ** 2 - m * m) * (2.0 * l + 1.0) / ((2.0 * l - 3.0) * (l * l - m * m)))
+            row[:k] = a[:, None] * x[None, :] * prev1[:k] - b[:, None] * prev2[:k]
+        if l >= 1 and l - 1 < n_m:
+            row[l - 1] = math.sqrt(2.0 * l + 1.0) * x * prev1[l - 1]
+        if l < n_m:
+            row[l] = sect
+        yield l, row
+        prev2, prev1 = prev1, row
+
+
+def _norm_seed(norm: str, inverse: bool) -> float:
+    f = 1.0 if norm == "ortho" else math.sqrt(4.0 * math.pi)
+    f = 1.0 / f if inverse else f
+    return f / math.sqrt(4.0 * math.pi)
+
+
+def _schmidt(norm: str, inverse: bool, l: int) -> float:
+    if norm != "schmidt":
+        return 1.0
+    s = math.sqrt(2.0 * l + 1.0)
+    return s if inverse else 1.0 / s
+
+
+def legendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
+             inverse: bool = False, csphase: bool = True, kscale=None,
+             dtype=np.float64) -> np.ndarray:
+    """[mmax, lmax, nlat] normalised associated Legendre functions, each
+    latitude optionally multiplied by ``kscale`` (the quadrature weights)."""
+    x = np.cos(theta)
+    out = np.zeros((mmax, lmax, x.size), dtype=dtype)
+    sign = np.ones(mmax)
+    if csphase:
+        sign[1::2] = -1.0
+    ks = np.ones(x.size) if kscale is None else np.asarray(kscale, np.float64)
+    for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, inverse)):
+        out[:, l, :] = row * (sign * _schmidt(norm, inverse, l))[:, None] * ks[None, :]
+    return out
+
+
+def dlegendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
+              inverse: bool = False, csphase: bool = True, kscale=None, lscale=None,
+              dtype=np.float64) -> np.ndarray:
+    """[2, mmax, lmax, nlat]: dP/dtheta and m P / sin(theta), optionally
+    multiplied by ``kscale[k]`` and ``lscale[l]``."""
+    x = np.cos(theta)
+    K = x.size
+    out = np.zeros((2, mmax, lmax, K), dtype=dtype)
+    m = np.arange(mmax, dtype=np.float64)
+    sign = np.ones(mmax)
+    if csphase:
+        sign[1::2] = -1.0
+    ks = np.ones(K) if kscale is None else np.asarray(kscale, np.float64)
+    rows = _legendre_rows(mmax + 1, lmax + 1, x, _norm_seed(norm, inverse))
+    _, cur = next(rows)
+    for l in range(lmax):
+        _, nxt = next(rows)
+        cur = cur * _schmidt(norm, inverse, l)
+        nxt_s = nxt * _schmidt(norm, inverse, l + 1)
+        lower = np.zeros((mmax, K))
+        lower[1:] = cur[: mmax - 1]
+        upper = cur[1 : mmax + 1]
+        d0 = 0.5 * (np.sqrt(np.maximum((l + m) * (l - m + 1.0), 0.0))[:, None] * lower
+                    - np.sqrt(np.maximum((l - m) * (l + m + 1.0), 0.0))[:, None] * upper)
+        d0[0] = -math.sqrt(l * (l + 1.0)) * cur[1]
+        lower1 = np.zeros((mmax, K))
+        lower1[1:] = nxt_s[: mmax - 1]
+        upper1 = nxt_s[1 : mmax + 1]
+        d1 = 0.5 * math.sqrt((2.0 * l + 1.0) / (2.0 * l + 3.0)) * (
+            np.sqrt(np.maximum((l - m + 1.0) * (l - m + 2.0), 0.0))[:, None] * lower1
+            + np.sqrt((l + m + 1.0) * (l + m + 2.0))[:, None] * upper1)
+        d1[0] = 0.0
+        keep = (m <= l)[:, None]
+        f = (sign * (1.0 if lscale is None else lscale[l]))[:, None] * ks[None, :]
+        out[0, :, l, :] = np.where(keep, d0, 0.0) * f
+        out[1, :, l, :] = np.where(keep, d1, 0.0) * f
+        cur = nxt
+    return out
+
+
+def _try_torch_harmonics():
+    try:
+        import torch_harmonics  # noqa: F401
+        return torch_harmonics
+    except Exception:
+        return None
+
+
+def _resolve(nlat, nlon, lmax, mmax, grid, norm):
+    _check(grid, norm)
+    lmax = lmax or default_lmax(nlat, grid)
+    mmax = mmax or default_mmax(nlon)
+    return lmax, mmax
+
+
+def scalar_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
+                   dtype=np.float64):
+    """RealSHT ``weights`` [mmax, lmax, nlat] (float64) and (lmax, mmax)."""
+    th = _try_torch_harmonics()
+    if th is not None:
+        ref = th.RealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
+        return ref.weights.double().numpy().astype(dtype), ref.lmax, ref.mmax
+    lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
+    theta, w = nodes_and_weights(nlat, grid)
+    return legendre(mmax, lmax, theta, norm, False, csphase, kscale=w, dtype=dtype), lmax, mmax
+
+
+def scalar_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
+                   dtype=np.float64):
+    """InverseRealSHT ``pct`` [mmax, lmax, nlat]."""
+    th = _try_torch_harmonics()
+    if th is not None:
+        ref = th.InverseRealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
+        return ref.pct.double().numpy().astype(dtype), ref.lmax, ref.mmax
+    lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
+    theta, _ = nodes_and_weights(nlat, grid)
+    return legendre(mmax, lmax, theta, norm, True, csphase, dtype=dtype), lmax, mmax
+
+
+def vector_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
+                   dtype=np.float64):
+    """RealVectorSHT ``weights`` [2, mmax, lmax, nlat]."""
+    th = _try_torch_harmonics()
+    if th is not None:
+        ref = th.RealVectorSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
+        return ref.weights.double().numpy().astype(dtype), ref.lmax, ref.mmax
+    lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
+    theta, w = nodes_and_weights(nlat, grid)
+    ll = np.arange(lmax, dtype=np.float64)
+    lscale = np.ones(lmax)
+    lscale[1:] = 1.0 / (ll[1:] * (ll[1:] + 1.0))
+    d = dlegendre(mmax, lmax, theta, norm, False, csphase, kscale=w, lscale=lscale, dtype=dtype)
+    d[1] = -d[1]
+    return d, lmax, mmax
+
+
+def vector_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
+                   dtype=np.float64):
+    """InverseRealVectorSHT ``dpct`` [2, mmax, lmax, nlat]."""
+    th = _try_torch_harmonics()
+    if th is not None:
+        ref = th.InverseRealVectorSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
+        return ref.dpct.double().numpy().astype(dtype), ref.lmax, ref.mmax
+    lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
+    theta, _ = nodes_and_weights(nlat, grid)
+    return dlegendre(mmax, lmax, theta, norm, True, csphase, dtype=dtype), lmax, mmax

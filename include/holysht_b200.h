@@ -1,0 +1,167 @@
+/*
+ * holysht_b200 -- C ABI of the B200 (sm_100a) Legendre kernels.
+ *
+ * Drop-in boundary for the HOLYSHT hot path.  Each reference-named entry point
+ * below replaces one operator of the reference's torch binding
+ * (chrisvoncsefalvay/holysht, torch-ext/torch_binding.cpp:12-24, implemented
+ * in cuda/fused_legendre.cu:3354-3545 and cuda/fused_sht.cu:74-98) with the
+ * same argument meaning, expressed as plain device pointers and sizes:
+ *
+ *   - every pointer is a device pointer on the CURRENT CUDA device;
+ *   - complex tensors are interleaved float pairs (complex64);
+ *   - all tensors are dense and contiguous in the reference's layouts
+ *     (input [B,K,M], output [B,L,M], tables weight_t [L,K,M] float32,
+ *     vector tensors [B,2,.,M]); tables hold zeros above the diagonal (m > l)
+ *     and those entries are never read;
+ *   - the caller allocates every output (as the reference's Python does);
+ *     forward entry points write the exact zeros for m > l themselves;
+ *   - work is enqueued on `stream` (cudaStream_t; NULL = legacy default
+ *     stream) and is asynchronous; no entry point synchronises or allocates.
+ *
+ * Every function returns HOLYSHT_OK (0) or an error code; the matching
+ * message is available from holysht_last_error() on the calling thread
+ * (the reference raises the same conditions as c10::Error via TORCH_CHECK,
+ * cuda/fused_legendre.cu:3157-3335).
+ */
+#ifndef HOLYSHT_B200_H_
+#define HOLYSHT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HOLYSHT_OK 0
+#define HOLYSHT_ERR_INVALID 1     /* bad pointer, shape, stride or flag */
+#define HOLYSHT_ERR_CUDA 2        /* CUDA runtime error at launch */
+#define HOLYSHT_ERR_UNSUPPORTED 3 /* no kernel for this device / configuration */
+
+/* backend hints of the reference's *_ex operators (cuda/fused_legendre.cu:59-80).
+ * Accepted for compatibility; every hint runs the FP32 sm_100a kernel. */
+#define HOLYSHT_BACKEND_AUTO 0
+#define HOLYSHT_BACKEND_FMA 1
+#define HOLYSHT_BACKEND_TMA 2
+#define HOLYSHT_BACKEND_TC_TF32 3
+#define HOLYSHT_BACKEND_TC_BF16 4
+
+#define HOLYSHT_DTYPE_C64 0  /* complex64 */
+#define HOLYSHT_DTYPE_F32 1  /* float32 */
+#define HOLYSHT_DTYPE_BF16 2 /* bfloat16 */
+
+#define HOLYSHT_KIND_SCALAR 0 /* complex input, one table */
+#define HOLYSHT_KIND_VECTOR 1 /* complex input [.,2,.,.], tables W0 and W1 */
+#define HOLYSHT_KIND_REAL 2   /* real input, one table */
+
+#define HOLYSHT_DIR_FORWARD 0 /* out rows are l, reduce over k */
+#define HOLYSHT_DIR_INVERSE 1 /* out rows are k, reduce over l >= m */
+
+#define HOLYSHT_FLAG_CONJ_W1 1    /* vector: use -W1 (conjugate-transpose map for autograd) */
+#define HOLYSHT_FLAG_ROUND_BF16 2 /* round the input to bfloat16 before the contraction */
+#define HOLYSHT_FLAG_IRFFT_PREP 4 /* complex output: Im(m=0)=0 and, even nlon, Im(m=nlon/2)=0 */
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+int holysht_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* holysht_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Reference operator mirrors
+ * ------------------------------------------------------------------------- */
+
+/* fused_legendre_forward (torch_binding.cpp:12; fused_legendre.cu:3354-3370):
+ * out[b,l,m] = sum_k weight_t[l,k,m] * in[b,k,m] for l >= m, 0 for m > l.
+ * out [B,L,M] c64, in [B,K,M] c64, weight_t [L,K,M] f32. */
+int holysht_fused_legendre_forward(void* out, const void* in, const float* weight_t, int64_t batch,
+                                   int64_t nlat, int64_t lmax, int64_t mmax, void* stream);
+
+/* fused_legendre_inverse (torch_binding.cpp:13; fused_legendre.cu:3372-3388):
+ * out[b,k,m] = sum_{l>=m} weight_t[l,k,m] * in[b,l,m].
+ * out [B,K,M] c64, in [B,L,M] c64, weight_t [L,K,M] f32. */
+int holysht_fused_legendre_inverse(void* out, const void* in, const float* weight_t, int64_t batch,
+                                   int64_t nlat, int64_t lmax, int64_t mmax, void* stream);
+
+/* fused_legendre_forward_real and fused_legendre_forward_real_ex
+ * (torch_binding.cpp:14,16; fused_legendre.cu:3390-3424): real input
+ * (in_dtype HOLYSHT_DTYPE_F32 or HOLYSHT_DTYPE_BF16), FP32 accumulation.
+ * out [B,L,M] f32, in [B,K,M], weight_t [L,K,M] f32. */
+int holysht_fused_legendre_forward_real(float* out, const void* in, int in_dtype,
+                                        const float* weight_t, int64_t batch, int64_t nlat,
+                                        int64_t lmax, int64_t mmax, int backend_hint,
+                                        void* stream);
+
+/* fused_legendre_inverse_real (torch_binding.cpp:15; fused_legendre.cu:3426-3450):
+ * out [B,K,M] f32, in [B,L,M] f32, weight_t [L,K,M] f32. */
+int holysht_fused_legendre_inverse_real(float* out, const float* in, const float* weight_t,
+                                        int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                        void* stream);
+
+/* fused_vector_legendre_forward and _ex (torch_binding.cpp:17-18;
+ * fused_legendre.cu:3452-3480):
+ *   sph = sum_k (W0 c0 + i W1 c1),  tor = sum_k (i W1 c0 - W0 c1).
+ * out [B,2,L,M] c64, in [B,2,K,M] c64, w0_t / w1_t [L,K,M] f32. */
+int holysht_fused_vector_legendre_forward(void* out, const void* in, const float* w0_t,
+                                          const float* w1_t, int64_t batch, int64_t nlat,
+                                          int64_t lmax, int64_t mmax, int backend_hint,
+                                          void* stream);
+
+/* fused_vector_legendre_inverse (torch_binding.cpp:19; fused_legendre.cu:3482-3499):
+ *   c0 = sum_{l>=m} (W0 sph + i W1 tor),  c1 = sum_{l>=m} (i W1 sph - W0 tor).
+ * out [B,2,K,M] c64, in [B,2,L,M] c64. */
+int holysht_fused_vector_legendre_inverse(void* out, const void* in, const float* w0_t,
+                                          const float* w1_t, int64_t batch, int64_t nlat,
+                                          int64_t lmax, int64_t mmax, void* stream);
+
+/* fused_vector_forward_pack_real (torch_binding.cpp:20; fused_legendre.cu:3501-3522):
+ * in [B,2,K,M] c64 -> stacked_w0, stacked_w1 [4B,K,M] f32. */
+int holysht_fused_vector_forward_pack_real(float* stacked_w0, float* stacked_w1, const void* in,
+                                           int64_t batch, int64_t nlat, int64_t mmax,
+                                           void* stream);
+
+/* fused_vector_forward_recompose_real (torch_binding.cpp:21; fused_legendre.cu:3524-3545):
+ * out_w0, out_w1 [4B,L,M] f32 -> out [B,2,L,M] c64. */
+int holysht_fused_vector_forward_recompose_real(void* out, const float* out_w0,
+                                                const float* out_w1, int64_t batch, int64_t lmax,
+                                                int64_t mmax, void* stream);
+
+/* sht_prepare_irfft (torch_binding.cpp:24; fused_sht.cu:74-98): in place on
+ * data [rows, width] c64 with width = nlon/2+1: zero columns >= mmax, zero
+ * Im at m = 0 and, for even nlon, at m = nlon/2. */
+int holysht_sht_prepare_irfft(void* data, int64_t rows, int64_t width, int64_t mmax,
+                              int64_t nlon, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Strided contraction (no counterpart operator in the reference; it is what
+ * the module fast paths use to read the rfft output in place, fold the 2*pi
+ * spectrum scale, write straight into an irfft-ready buffer, and run the
+ * conjugate-transpose vector map for autograd).  Strides are in elements of
+ * the input/output type; the table is [L,K,M]-shaped with its own strides
+ * and contiguous m.
+ * ------------------------------------------------------------------------- */
+typedef struct holysht_contract_desc {
+  int kind;      /* HOLYSHT_KIND_* */
+  int direction; /* HOLYSHT_DIR_* */
+  int in_dtype;  /* HOLYSHT_DTYPE_*: C64 for SCALAR/VECTOR; F32 or BF16 for REAL */
+  int flags;     /* HOLYSHT_FLAG_* */
+  const void* in;
+  void* out;
+  const float* w0;
+  const float* w1; /* VECTOR only */
+  int64_t batch, nlat, lmax, mmax;
+  int64_t in_batch_stride, in_comp_stride, in_row_stride;
+  int64_t out_batch_stride, out_comp_stride, out_row_stride;
+  int64_t out_cols; /* columns written, >= mmax; columns >= mmax are written as 0 */
+  int64_t w_l_stride, w_k_stride;
+  int64_t nlon;  /* used with HOLYSHT_FLAG_IRFFT_PREP */
+  float scale;   /* multiplies every output */
+  int ksplit;    /* reduction split across a CTA cluster: 0 = auto, else 1,2,4,8 */
+} holysht_contract_desc;
+
+int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HOLYSHT_B200_H_ */

@@ -1,0 +1,130 @@
+"""CPU tests of the host side: the C ABI library loads and exports every
+declared symbol, the package's weight generator agrees with the oracle, the
+modules construct with the reference's buffers, and the product path refuses
+CPU tensors (there is no CPU fallback)."""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import holysht_b200 as hs
+from holysht_b200 import _lib, weights
+from oracle import sht_oracle as orc
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = h.read_text()
+        names |= set(re.findall(r"^\s*(?:int|const char\*)\s+(holysht_\w+)\s*\(", text, re.M))
+    return names
+
+
+def test_header_declares_the_exports():
+    assert _declared_symbols() == set(_lib.EXPORTS)
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = _lib.load()
+    for name in _declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.holysht_version() >= 100
+    assert lib.holysht_last_error() == b""
+
+
+def test_invalid_arguments_are_rejected_without_gpu():
+    lib = _lib.load()
+    # negative extents and null pointers are caught before any CUDA call
+    st = lib.holysht_fused_legendre_forward(None, None, None, -1, 4, 4, 4, None)
+    assert st == _lib.HOLYSHT_ERR_INVALID
+    assert b"negative" in lib.holysht_last_error()
+    st = lib.holysht_fused_legendre_forward(None, None, None, 2, 4, 4, 4, None)
+    assert st == _lib.HOLYSHT_ERR_INVALID
+    st = lib.holysht_fused_legendre_forward_real(None, None, 0, None, 1, 1, 1, 1, 9, None)
+    assert st == _lib.HOLYSHT_ERR_INVALID and b"backend_hint" in lib.holysht_last_error()
+    d = _lib.ContractDesc()
+    d.kind, d.direction, d.in_dtype, d.batch, d.nlat, d.lmax, d.mmax, d.out_cols = 1, 0, 0, 1, 4, 4, 4, 2
+    assert lib.holysht_legendre_contract(ctypes.byref(d), None) == _lib.HOLYSHT_ERR_INVALID
+    assert b"out_cols" in lib.holysht_last_error()
+    d.out_cols, d.kind = 4, 7
+    assert lib.holysht_legendre_contract(ctypes.byref(d), None) == _lib.HOLYSHT_ERR_INVALID
+    # empty problems are a no-op success
+    assert lib.holysht_fused_legendre_forward(None, None, None, 0, 4, 4, 4, None) == _lib.HOLYSHT_OK
+    with pytest.raises(RuntimeError, match="invalid extents"):
+        _lib.check(lib.holysht_sht_prepare_irfft(None, -1, 4, 4, 6, None))
+
+
+@pytest.mark.parametrize("grid", ["equiangular", "legendre-gauss", "lobatto"])
+@pytest.mark.parametrize("norm", ["ortho", "schmidt", "four-pi"])
+def test_package_tables_match_oracle(grid, norm):
+    nlat, nlon = 11, 20
+    for cs in (True, False):
+        a, L, M = weights.scalar_forward(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+        np.testing.assert_allclose(a, orc.scalar_forward_table(nlat, nlon, grid=grid, norm=norm, csphase=cs), atol=1e-13)
+        b, _, _ = weights.scalar_inverse(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+        np.testing.assert_allclose(b, orc.scalar_inverse_table(nlat, nlon, grid=grid, norm=norm, csphase=cs), atol=1e-13)
+        c, _, _ = weights.vector_forward(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+        np.testing.assert_allclose(c, orc.vector_forward_tables(nlat, nlon, grid=grid, norm=norm, csphase=cs), atol=1e-13)
+        d, _, _ = weights.vector_inverse(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+        np.testing.assert_allclose(d, orc.vector_inverse_tables(nlat, nlon, grid=grid, norm=norm, csphase=cs), atol=1e-13)
+        assert (L, M) == (orc.default_lmax(nlat, grid), orc.default_mmax(nlon))
+
+
+def test_package_tables_custom_lmax_mmax():
+    a, L, M = weights.vector_forward(10, 20, lmax=6, mmax=4)
+    assert a.shape == (2, 4, 6, 10) and (L, M) == (6, 4)
+    np.testing.assert_allclose(a, orc.vector_forward_tables(10, 20, lmax=6, mmax=4), atol=1e-13)
+
+
+def test_bad_grid_and_norm():
+    with pytest.raises(ValueError):
+        weights.scalar_forward(8, 16, grid="healpix")
+    with pytest.raises(ValueError):
+        weights.scalar_forward(8, 16, norm="bogus")
+
+
+def test_module_buffers_and_shapes():
+    m = hs.RealSHT(12, 24)
+    assert (m.lmax, m.mmax) == (12, 13)
+    assert m.weights.shape == (13, 12, 12) and m.weight_t.shape == (12, 12, 13)
+    assert set(m.state_dict()) == {"weights", "weight_t"}
+    v = hs.RealVectorSHT(12, 24, dtype="bf16")
+    assert v.w0.dtype == torch.bfloat16 and v.w0_t.dtype == torch.float32
+    assert set(v.state_dict()) == {"w0", "w1", "w0_t", "w1_t"}
+    i = hs.InverseRealSHT(12, 24, lmax=8, mmax=6)
+    assert i.pct.shape == (6, 8, 12) and i.pct_t.shape == (8, 12, 6)
+    iv = hs.InverseRealVectorSHT(12, 24)
+    assert set(iv.state_dict()) == {"d0", "d1", "d0_t", "d1_t"}
+    torch.testing.assert_close(m.weight_t, m.weights.permute(1, 2, 0))
+
+
+def test_aliases():
+    assert hs.FusedRealSHT is hs.RealSHT
+    assert hs.FusedInverseRealSHT is hs.InverseRealSHT
+    assert hs.FusedRealVectorSHT is hs.RealVectorSHT
+    assert hs.FusedInverseRealVectorSHT is hs.InverseRealVectorSHT
+    assert hs.legendre_forward is hs.fused_legendre_forward
+    assert hs.sht_inverse is hs.fused_sht_inverse
+
+
+def test_cpu_tensors_fail_loudly():
+    m = hs.RealSHT(8, 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.randn(2, 8, 16))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        hs.fused_legendre_forward(torch.zeros(1, 8, 9, dtype=torch.complex64), m.weights)
+    out = torch.empty(1, 8, 9, dtype=torch.complex64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        hs.ops.fused_legendre_forward(out, out, m.weight_t)
+
+
+def test_graphed_module_passthrough_on_cpu():
+    inner = torch.nn.Identity()
+    g = hs.GraphedModule(inner)
+    x = torch.randn(3)
+    assert g(x) is x
