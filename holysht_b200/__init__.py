@@ -30,7 +30,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib, ops, weights as _weights
-from .ops import legendre_contract as _contract
+from .ops import legendre_contract as _contract, tile_table as _tile_table
 
 __all__ = [
     "RealSHT",
@@ -64,6 +64,16 @@ def _need_cuda(x: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what}: holysht_b200 runs on CUDA tensors only (no CPU fallback)")
 
 
+def _require_table(w: torch.Tensor, L: int, K: int, M: int) -> None:
+    """A dense [L, K, M] or m-tiled [L, ceil(M/32), K, 32] table of these extents."""
+    if w.dim() == 4:
+        ok = tuple(w.shape) == (L, (M + 31) // 32, K, 32)
+    else:
+        ok = tuple(w.shape) == (L, K, M)
+    if not ok:
+        raise RuntimeError(f"table of shape {tuple(w.shape)} does not match lmax={L} nlat={K} mmax={M}")
+
+
 def _strides3(t: torch.Tensor, vector: bool):
     """(batch, component, row) element strides of a [B,(2),R,C] tensor."""
     if vector:
@@ -85,6 +95,7 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         vector = w1 is not None
         B, K, W = spec.size(0), spec.size(-2), spec.size(-1)
         L = w0.size(0)
+        _require_table(w0, L, K, mmax)
         shape = (B, 2, L, mmax) if vector else (B, L, mmax)
         out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
         _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_FORWARD,
@@ -117,7 +128,8 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
     def forward(ctx, coef, w0, w1, nlon: int):
         vector = w1 is not None
         B, L, M = coef.size(0), coef.size(-2), coef.size(-1)
-        K = w0.size(1)
+        K = w0.size(2) if w0.dim() == 4 else w0.size(1)
+        _require_table(w0, L, K, M)
         W = nlon // 2 + 1
         c = coef.contiguous()
         shape = (B, 2, K, W) if vector else (B, K, W)
@@ -396,6 +408,7 @@ class RealSHT(nn.Module):
         wt = torch.from_numpy(w)
         self.register_buffer("weights", wt.to(w_dtype))
         self.register_buffer("weight_t", wt.permute(1, 2, 0).contiguous())
+        self.register_buffer("weight_t_tiled", _tile_table(self.weight_t), persistent=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealSHT")
@@ -403,7 +416,7 @@ class RealSHT(nn.Module):
         spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
         lead = spec.shape[:-2]
         spec = spec.reshape(-1, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self.weight_t, None, self.mmax,
+        out = _SpectrumLegendreForward.apply(spec, self.weight_t_tiled, None, self.mmax,
                                              self._use_bf16 or self._use_fp16)
         return out.reshape(lead + (self.lmax, self.mmax))
 
@@ -421,11 +434,18 @@ class InverseRealSHT(nn.Module):
         pt = torch.from_numpy(p)
         self.register_buffer("pct", pt)
         self.register_buffer("pct_t", pt.permute(1, 2, 0).contiguous())
+        self.register_buffer("pct_t_tiled", _tile_table(self.pct_t), persistent=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "InverseRealSHT")
         assert x.shape[-2] == self.lmax and x.shape[-1] == self.mmax
-        return fused_sht_inverse(x, self.pct, self.nlon, self.pct_t)
+        lead = x.shape[:-2]
+        c = x.reshape(-1, self.lmax, self.mmax)
+        if c.dtype != torch.complex64:
+            c = c.to(torch.complex64)
+        spec = _SpectrumLegendreInverse.apply(c, self.pct_t_tiled, None, self.nlon)
+        y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
+        return y.reshape(lead + (self.nlat, self.nlon))
 
 
 class RealVectorSHT(nn.Module):
@@ -448,6 +468,8 @@ class RealVectorSHT(nn.Module):
         self.register_buffer("w1", wt[1].to(w_dtype))
         self.register_buffer("w0_t", wt[0].permute(1, 2, 0).contiguous())
         self.register_buffer("w1_t", wt[1].permute(1, 2, 0).contiguous())
+        self.register_buffer("w0_t_tiled", _tile_table(self.w0_t), persistent=False)
+        self.register_buffer("w1_t_tiled", _tile_table(self.w1_t), persistent=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealVectorSHT")
@@ -455,7 +477,7 @@ class RealVectorSHT(nn.Module):
         spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
         lead = spec.shape[:-3]
         spec = spec.reshape(-1, 2, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self.w0_t, self.w1_t, self.mmax,
+        out = _SpectrumLegendreForward.apply(spec, self.w0_t_tiled, self.w1_t_tiled, self.mmax,
                                              self._use_bf16 or self._use_fp16)
         return out.reshape(lead + (2, self.lmax, self.mmax))
 
@@ -475,6 +497,8 @@ class InverseRealVectorSHT(nn.Module):
         self.register_buffer("d1", dt[1].contiguous())
         self.register_buffer("d0_t", dt[0].permute(1, 2, 0).contiguous())
         self.register_buffer("d1_t", dt[1].permute(1, 2, 0).contiguous())
+        self.register_buffer("d0_t_tiled", _tile_table(self.d0_t), persistent=False)
+        self.register_buffer("d1_t_tiled", _tile_table(self.d1_t), persistent=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "InverseRealVectorSHT")
@@ -483,7 +507,7 @@ class InverseRealVectorSHT(nn.Module):
         c = x.reshape(-1, 2, self.lmax, self.mmax)
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
-        spec = _SpectrumLegendreInverse.apply(c, self.d0_t, self.d1_t, self.nlon)
+        spec = _SpectrumLegendreInverse.apply(c, self.d0_t_tiled, self.d1_t_tiled, self.nlon)
         y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
         return y.reshape(lead + (2, self.nlat, self.nlon))
 

@@ -66,6 +66,7 @@ class ContractDesc(ctypes.Structure):
         ("nlon", ctypes.c_int64),
         ("scale", ctypes.c_float),
         ("ksplit", ctypes.c_int),
+        ("w_m_tile_stride", ctypes.c_int64),
     ]
 
 

@@ -118,7 +118,7 @@ struct Job {
   const float* w0;
   const float* w1;
   long long B, K, L, M;
-  long long in_bs, in_ps, in_rs, out_bs, out_ps, out_rs, out_cols, w_ls, w_ks, nlon;
+  long long in_bs, in_ps, in_rs, out_bs, out_ps, out_rs, out_cols, w_ls, w_ks, w_mt, nlon;
   float scale;
   int ksplit;
 };
@@ -181,6 +181,14 @@ int run_job(const Job& j, cudaStream_t stream) {
   } else if (j.in_dtype != HOLYSHT_DTYPE_C64) {
     return fail(HOLYSHT_ERR_INVALID, "input must be complex64");
   }
+  {
+    // the kernel addresses a table with 32-bit float offsets
+    const long long n_mt_tab = (j.M + hsb::kMTile - 1) / hsb::kMTile;
+    const long long span = (j.L > 0 ? (j.L - 1) * j.w_ls : 0) + (j.K > 0 ? (j.K - 1) * j.w_ks : 0) +
+                           (n_mt_tab > 0 ? (n_mt_tab - 1) * j.w_mt : 0) + hsb::kMTile;
+    if (j.w_ls < 0 || j.w_ks < 0 || j.w_mt < 0 || span >= (1LL << 32))
+      return fail(HOLYSHT_ERR_INVALID, "table strides must be non-negative and span < 2^32 floats");
+  }
   if (j.ksplit != 0 && j.ksplit != 1 && j.ksplit != 2 && j.ksplit != 4 && j.ksplit != 8)
     return fail(HOLYSHT_ERR_INVALID, "ksplit must be 0, 1, 2, 4 or 8");
 
@@ -197,6 +205,7 @@ int run_job(const Job& j, cudaStream_t stream) {
   p.out_rs = j.out_rs;
   p.w_ls = j.w_ls;
   p.w_ks = j.w_ks;
+  p.w_mt = j.w_mt;
   p.B = (int)j.B;
   p.K = (int)j.K;
   p.L = (int)j.L;
@@ -296,6 +305,7 @@ Job dense_job(int kind, int dir, int in_dtype, const void* in, void* out, const 
   j.out_cols = M;
   j.w_ks = M;
   j.w_ls = K * M;
+  j.w_mt = hsb::kMTile;
   j.nlon = 0;
   j.scale = 1.f;
   j.ksplit = 0;
@@ -386,6 +396,7 @@ int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
   j.out_cols = d->out_cols;
   j.w_ls = d->w_l_stride;
   j.w_ks = d->w_k_stride;
+  j.w_mt = d->w_m_tile_stride ? d->w_m_tile_stride : hsb::kMTile;
   j.nlon = d->nlon;
   j.scale = d->scale;
   j.ksplit = d->ksplit;

@@ -50,6 +50,7 @@ constexpr int kRows = kWarps * kRowsPerWarp;  // output rows per CTA
 constexpr int kMTile = 32;                     // orders per CTA (one per lane)
 constexpr int kChunk = 8;                      // reduction steps per smem stage
 constexpr int kRing = 4;                       // register ring for table rows
+constexpr int kPrefetchChunks = 2;            // L2 prefetch distance of the table
 constexpr int kSmemBytes = 64 * 1024;
 
 struct ContractParams {
@@ -59,7 +60,8 @@ struct ContractParams {
   const float* w1;
   long long in_bs, in_ps, in_rs;     // input strides (elements): batch, component, row
   long long out_bs, out_ps, out_rs;  // output strides (elements)
-  long long w_ls, w_ks;              // table strides (floats) of l and k; m is contiguous
+  long long w_ls, w_ks;              // table strides (floats) of l and k
+  long long w_mt;                    // table stride (floats) of a 32-order m tile (32 = dense m)
   int B, K, L, M;                    // batch, nlat, lmax, mmax (table extents)
   int out_cols;                      // output columns written (>= M; extra are zero)
   int R, S;                          // output rows, reduction extent
@@ -99,12 +101,24 @@ __device__ __forceinline__ unsigned long long evict_first_policy() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
   return pol;
 }
-__device__ __forceinline__ float ld_stream(const float* p, unsigned long long pol) {
+// Predicated streaming load: the destination is zeroed and the load issued
+// under a predicate inside one asm block, so no instruction consumes the
+// result until the FMA that needs it several steps later (a select or a
+// multiply right after the load would stall the warp for the full latency).
+__device__ __forceinline__ float ld_stream(const float* p, bool ok, unsigned long long pol) {
   float v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;\n"
-               : "=f"(v)
-               : "l"(p), "l"(pol));
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "setp.ne.b32 q, %2, 0;\n\t"
+      "mov.b32 %0, 0;\n\t"
+      "@q ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %3;\n\t}"
+      : "=f"(v)
+      : "l"(p), "r"((int)ok), "l"(pol));
   return v;
+}
+
+__device__ __forceinline__ void prefetch_l2(const float* p) {
+  asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
 }
 
 __device__ __forceinline__ float round_to_bf16(float x) {
@@ -262,10 +276,22 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? 1 : 2)
     bool ok = row < p.R && m < p.M;
     if (DIR == DIR_FWD) ok = ok && row >= m;  // l >= m
     vmask |= ok ? (1u << i) : 0u;
-    roff[i] = ok ? (unsigned)row * rstride + (unsigned)m : 0u;
+    roff[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) + (unsigned)lane : 0u;
   }
+  // warp-uniform row validity and lane-0 offsets for the L2 prefetch
+  unsigned pf_off[kRowsPerWarp];
+  unsigned pf_mask = 0;
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int row = row0 + warp * kRowsPerWarp + i;
+    const bool ok = row < p.R && m0 < p.M && (DIR == DIR_INV || row >= m0);
+    pf_mask |= ok ? (1u << i) : 0u;
+    pf_off[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) : 0u;
+  }
+  const int m_last = min(kMTile, p.M - m0) - 1;  // last valid lane of this tile
   const float* __restrict__ w0 = p.w0;
   const float* __restrict__ w1 = p.w1;
+  const float w1s = p.w1_sign;
 
   float2 acc[kRowsPerWarp][NA];
 #pragma unroll
@@ -325,12 +351,37 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? 1 : 2)
     for (int i = 0; i < kRowsPerWarp; ++i) {
       const bool ok = sok && ((vmask >> i) & 1u);
       const unsigned off = roff[i] + so;
-      d0[i] = ok ? ld_stream(w0 + off, pol) : 0.f;
-      if (KIND == KIND_VECTOR) d1[i] = ok ? ld_stream(w1 + off, pol) * p.w1_sign : 0.f;
+      d0[i] = ld_stream(w0 + off, ok, pol);
+      if (KIND == KIND_VECTOR) d1[i] = ld_stream(w1 + off, ok, pol);
+    }
+  };
+
+  // L2 prefetch of the table lines of one future chunk: lane q < kChunk takes
+  // step q, every valid row and table, first and last line of the 32 orders
+  auto prefetch_chunk = [&](int chunk) {
+    if (lane >= kChunk) return;
+    const int s = r_begin + chunk * kChunk + lane;
+    if (s >= r_end) return;
+    const unsigned so = (unsigned)s * sstride;
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      if (!((pf_mask >> i) & 1u)) continue;
+      const float* a0 = w0 + pf_off[i] + so;
+      prefetch_l2(a0);
+      const bool two = ((reinterpret_cast<uintptr_t>(a0) >> 7) !=
+                        (reinterpret_cast<uintptr_t>(a0 + m_last) >> 7));
+      if (two) prefetch_l2(a0 + m_last);
+      if (KIND == KIND_VECTOR) {
+        const float* a1 = w1 + pf_off[i] + so;
+        prefetch_l2(a1);
+        if (two) prefetch_l2(a1 + m_last);
+      }
     }
   };
 
   if (nchunks > 0) {
+#pragma unroll
+    for (int q = 0; q < kPrefetchChunks; ++q) prefetch_chunk(q);
     if constexpr (kAsyncStage) {
       stage_chunk(0, 0);
       cp_async_commit();
@@ -340,6 +391,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? 1 : 2)
 
     for (int c = 0; c < nchunks; ++c) {
       const int buf = c & 1;
+      if (c + kPrefetchChunks < nchunks) prefetch_chunk(c + kPrefetchChunks);
       if constexpr (kAsyncStage) {
         if (c + 1 < nchunks) stage_chunk(c + 1, buf ^ 1);
         cp_async_commit();
@@ -380,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? 1 : 2)
 #pragma unroll
             for (int i = 0; i < kRowsPerWarp; ++i) {
               const float w0 = wr0[cur][i];
-              const float w1 = wr1[cur][i];
+              const float w1 = wr1[cur][i] * w1s;
               const float2 pw0 = make_float2(w0, w0);
               const float2 pw1 = make_float2(-w1, w1);
               const float2 nw0 = make_float2(-w0, -w0);

@@ -33,6 +33,7 @@ __all__ = [
     "fused_vector_forward_recompose_real",
     "sht_prepare_irfft",
     "legendre_contract",
+    "tile_table",
 ]
 
 
@@ -211,17 +212,40 @@ def sht_prepare_irfft(data: torch.Tensor, mmax: int, nlon: int) -> None:
             _p(data), rows, data.size(2), int(mmax), int(nlon), _stream(dev)))
 
 
+def tile_table(weight_t: torch.Tensor) -> torch.Tensor:
+    """[lmax, nlat, mmax] -> m-tiled [lmax, ceil(mmax/32), nlat, 32] (orders
+    padded with zeros): every 32-order row segment starts a 128-byte line, so
+    each warp-wide table load is exactly one aligned line."""
+    L, K, M = weight_t.shape
+    mt = (M + 31) // 32
+    padded = torch.zeros((L, K, mt * 32), dtype=torch.float32, device=weight_t.device)
+    padded[..., :M] = weight_t
+    return padded.view(L, K, mt, 32).permute(0, 2, 1, 3).contiguous()
+
+
 def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,
                       w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
-                      scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0) -> None:
-    """Strided contraction; strides are (batch, component, row) in elements."""
+                      scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0,
+                      w_strides=None) -> None:
+    """Strided contraction; strides are (batch, component, row) in elements.
+
+    ``w0``/``w1`` are either dense [lmax, nlat, mmax] tables (m contiguous) or
+    m-tiled tables from :func:`tile_table` ([lmax, ceil(mmax/32), nlat, 32]);
+    ``w_strides`` = (l, k, m-tile) strides in floats overrides the inference."""
     dev = _cuda(output, input, w0)
     if w1 is not None:
         _cuda(output, w1)
         _require(w1.stride() == w0.stride(), "W0 and W1 must share strides")
-    _require(w0.dtype == torch.float32 and w0.dim() == 3 and w0.stride(2) == 1,
-             "tables must be float32 [lmax, nlat, mmax] with contiguous mmax")
+    _require(w0.dtype == torch.float32, "tables must be float32")
+    if w_strides is None:
+        if w0.dim() == 4:
+            _require(w0.is_contiguous() and w0.size(3) == 32, "m-tiled tables must be contiguous [L, Mt, K, 32]")
+            w_strides = (w0.stride(0), w0.stride(2), w0.stride(1))
+        else:
+            _require(w0.dim() == 3 and w0.stride(2) == 1,
+                     "tables must be [lmax, nlat, mmax] with contiguous mmax")
+            w_strides = (w0.stride(0), w0.stride(1), 32)
     if input.dtype == torch.complex64:
         dt = _lib.DTYPE_C64
     elif input.dtype == torch.float32:
@@ -237,7 +261,7 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
     d.in_batch_stride, d.in_comp_stride, d.in_row_stride = in_strides
     d.out_batch_stride, d.out_comp_stride, d.out_row_stride = out_strides
     d.out_cols = out_cols
-    d.w_l_stride, d.w_k_stride = w0.stride(0), w0.stride(1)
+    d.w_l_stride, d.w_k_stride, d.w_m_tile_stride = w_strides
     d.nlon = nlon
     d.scale = scale
     d.ksplit = ksplit

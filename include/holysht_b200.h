@@ -156,6 +156,9 @@ typedef struct holysht_contract_desc {
   int64_t nlon;  /* used with HOLYSHT_FLAG_IRFFT_PREP */
   float scale;   /* multiplies every output */
   int ksplit;    /* reduction split across a CTA cluster: 0 = auto, else 1,2,4,8 */
+  int64_t w_m_tile_stride; /* table stride of one 32-order m tile; 0 = 32 (dense, m contiguous).
+                              The m-tiled layout [L][ceil(M/32)][K][32] (k stride 32) keeps
+                              every 32-order row segment on one 128-byte line. */
 } holysht_contract_desc;
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);

@@ -362,8 +362,8 @@ def test_training_roundtrip_gradients_match_float64_autograd():
     coef = sht(torch.tanh(isht(ct)))
     (coef.real.square().sum() + coef.imag.square().sum()).backward()
 
-    P = torch.from_numpy(isht.pct.double().numpy() if not isht.pct.is_cuda else isht.pct.double().cpu().numpy())
-    W = sht.weight_t.permute(2, 0, 1).double().cpu()
+    P = isht.pct.double().cpu().to(torch.complex128)
+    W = sht.weight_t.permute(2, 0, 1).double().cpu().to(torch.complex128)
     c64 = torch.from_numpy(c.astype(np.complex128)).requires_grad_(True)
     y = torch.einsum("blm,mlk->bkm", c64, P)
     full = torch.zeros(B, nlat, nlon // 2 + 1, dtype=torch.complex128)

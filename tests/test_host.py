@@ -128,3 +128,15 @@ def test_graphed_module_passthrough_on_cpu():
     g = hs.GraphedModule(inner)
     x = torch.randn(3)
     assert g(x) is x
+
+
+def test_tile_table_layout():
+    L, K, M = 3, 5, 37
+    w = torch.arange(L * K * M, dtype=torch.float32).reshape(L, K, M)
+    t = hs.ops.tile_table(w)
+    assert t.shape == (L, 2, K, 32) and t.is_contiguous()
+    for l in range(L):
+        for k in range(K):
+            for m in range(M):
+                assert t[l, m // 32, k, m % 32] == w[l, k, m]
+    assert torch.all(t[:, 1, :, M - 32:] == 0)
