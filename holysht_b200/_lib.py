@@ -9,7 +9,9 @@ import ctypes
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libholysht_b200.so"
+import os
+
+LIB_PATH = Path(os.environ.get("HOLYSHT_B200_LIBRARY") or Path(__file__).resolve().parent / "libholysht_b200.so")
 
 HOLYSHT_OK = 0
 HOLYSHT_ERR_INVALID = 1

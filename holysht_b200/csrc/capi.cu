@@ -82,6 +82,25 @@ int launch_contract(const hsb::ContractParams& p_in, int grid_tiles, cudaStream_
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   hsb::ContractParams p = p_in;
+  if (p.ks == 0) {
+    // one resident wave: the largest split whose CTAs all fit on the GPU at
+    // once (zero tiles are short-lived and not counted), each cluster rank
+    // keeping at least two staged chunks of the reduction
+    static std::atomic<int> occ_cache[kMaxDevices];
+    int occ = (dev >= 0 && dev < kMaxDevices) ? occ_cache[dev].load(std::memory_order_relaxed) : 0;
+    if (occ <= 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, hsb::kThreads, hsb::kSmemBytes) !=
+              cudaSuccess ||
+          occ <= 0)
+        occ = 1;
+      if (dev >= 0 && dev < kMaxDevices) occ_cache[dev].store(occ, std::memory_order_relaxed);
+    }
+    const long long slots = (long long)occ * sm_count_of_current_device();
+    const long long tiles = (long long)p.n_compute * p.n_bg;
+    int ks = 1;
+    while (ks < 8 && tiles * ks * 2 <= slots && p.S / (2LL * ks) >= 2LL * hsb::kChunk) ks *= 2;
+    p.ks = ks;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid_tiles) * static_cast<unsigned>(p.ks), 1, 1);
   cfg.blockDim = dim3(hsb::kThreads, 1, 1);
@@ -129,7 +148,7 @@ int dispatch_nb(const hsb::ContractParams& p0, int nb, cudaStream_t stream) {
   p.n_bg = (p.B + nb - 1) / nb;
   const long long tiles = (long long)(p.n_compute + p.n_zero) * p.n_bg;
   if (tiles == 0) return ok();
-  if (tiles * p.ks > INT_MAX / 2) return fail(HOLYSHT_ERR_INVALID, "problem too large for one launch");
+  if (tiles * 8 > INT_MAX / 2) return fail(HOLYSHT_ERR_INVALID, "problem too large for one launch");
   const int grid_tiles = static_cast<int>(tiles);
   if constexpr (KIND == hsb::KIND_VECTOR) {
     switch (nb) {
@@ -245,16 +264,8 @@ int run_job(const Job& j, cudaStream_t stream) {
   else
     nb = next_pow2_at_least(j.B, 2, 16);
 
-  // reduction split: enough CTAs for about two resident waves, at least two
-  // staged chunks per cluster rank
+  // reduction split (cluster size): 0 = choose at launch from the occupancy
   int ks = j.ksplit ? j.ksplit : env_ksplit();
-  if (ks == 0) {
-    const long long n_bg = (j.B + nb - 1) / nb;
-    const long long tiles = n_compute * n_bg;
-    const long long want = 4LL * sm_count_of_current_device();
-    ks = 1;
-    while (ks < 8 && tiles * ks < want && S / (2LL * ks) >= 2LL * hsb::kChunk) ks *= 2;
-  }
   p.ks = ks;
 
   if (j.kind == HOLYSHT_KIND_SCALAR) {

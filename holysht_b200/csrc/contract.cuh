@@ -48,9 +48,21 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kRowsPerWarp = 4;
 constexpr int kRows = kWarps * kRowsPerWarp;  // output rows per CTA
 constexpr int kMTile = 32;                     // orders per CTA (one per lane)
-constexpr int kChunk = 8;                      // reduction steps per smem stage
-constexpr int kRing = 4;                       // register ring for table rows
-constexpr int kPrefetchChunks = 2;            // L2 prefetch distance of the table
+#ifndef HSB_CHUNK
+#define HSB_CHUNK 8
+#endif
+constexpr int kChunk = HSB_CHUNK;              // reduction steps per smem stage
+#ifndef HSB_RING
+#define HSB_RING 8
+#endif
+#ifndef HSB_VECTOR_MIN_BLOCKS
+#define HSB_VECTOR_MIN_BLOCKS 1
+#endif
+constexpr int kRing = HSB_RING;                // register ring for table rows (steps in flight + 1)
+#ifndef HSB_PREFETCH_CHUNKS
+#define HSB_PREFETCH_CHUNKS 2
+#endif
+constexpr int kPrefetchChunks = HSB_PREFETCH_CHUNKS;  // L2 prefetch distance of the table (chunks)
 constexpr int kSmemBytes = 64 * 1024;
 
 struct ContractParams {
@@ -219,7 +231,7 @@ __device__ __forceinline__ void write_zero_tile(const ContractParams& p, int j, 
 }
 
 template <int KIND, int DIR, int NB, typename TIN>
-__global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? 1 : 2)
+__global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN_BLOCKS : 2)
     contract_kernel(const ContractParams p) {
   constexpr int P = KindTraits<KIND>::P;
   constexpr int PB = NB * P;  // staged planes per reduction step
