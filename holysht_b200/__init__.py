@@ -30,7 +30,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib, ops, weights as _weights
-from .ops import legendre_contract as _contract, tile_table as _tile_table
+from .ops import legendre_contract as _contract
 
 __all__ = [
     "RealSHT",
@@ -64,21 +64,64 @@ def _need_cuda(x: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what}: holysht_b200 runs on CUDA tensors only (no CPU fallback)")
 
 
-def _require_table(w: torch.Tensor, L: int, K: int, M: int) -> None:
-    """A dense [L, K, M] or m-tiled [L, ceil(M/32), K, 32] table of these extents."""
-    if w.dim() == 4:
-        ok = tuple(w.shape) == (L, (M + 31) // 32, K, 32)
-    else:
-        ok = tuple(w.shape) == (L, K, M)
-    if not ok:
-        raise RuntimeError(f"table of shape {tuple(w.shape)} does not match lmax={L} nlat={K} mmax={M}")
-
-
 def _strides3(t: torch.Tensor, vector: bool):
     """(batch, component, row) element strides of a [B,(2),R,C] tensor."""
     if vector:
         return t.stride(0), t.stride(1), t.stride(2)
     return t.stride(0), 0, t.stride(1)
+
+
+# ---------------------------------------------------------------------------
+# table sources: where a transform's Legendre tables live
+# ---------------------------------------------------------------------------
+
+class _DenseTables:
+    """Tables in the reference operator layout [lmax, nlat, mmax] (strided path)."""
+
+    def __init__(self, w0: torch.Tensor, w1: Optional[torch.Tensor] = None):
+        self.w0, self.w1 = w0, w1
+        self.vector = w1 is not None
+        self.lmax, self.nlat, self.mmax = w0.shape
+
+    def table(self, direction: int):
+        return self.w0, self.w1, False
+
+
+class _GroupedTablesMixin:
+    """Module mixin: dense buffers plus cached row-grouped copies per direction
+    (``ops.group_table``), built for the transform's own direction at
+    construction and for the other direction on first backward.  The copies
+    are non-persistent buffers (they follow ``.to()``) and are dropped when a
+    state dict is loaded into the dense buffers."""
+
+    def _init_tables(self, names, hot_direction: int) -> None:
+        self._table_names = tuple(names)
+        self.vector = len(self._table_names) == 2
+        self.register_buffer("_grouped_fwd", None, persistent=False)
+        self.register_buffer("_grouped_inv", None, persistent=False)
+        self.table(hot_direction)
+        self.register_load_state_dict_post_hook(lambda module, _keys: module._drop_grouped())
+
+    def _drop_grouped(self) -> None:
+        self._grouped_fwd = None
+        self._grouped_inv = None
+
+    def table(self, direction: int):
+        name = "_grouped_fwd" if direction == _lib.DIR_FORWARD else "_grouped_inv"
+        t = getattr(self, name)
+        dense = tuple(getattr(self, n) for n in self._table_names)
+        if t is None or t.device != dense[0].device:
+            t = ops.group_table(dense, direction)
+            setattr(self, name, t)
+        return t, None, True
+
+
+def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_cols, scale, flags, nlon=0):
+    w0, w1, grouped = src.table(direction)
+    _contract(kind=_lib.KIND_VECTOR if src.vector else _lib.KIND_SCALAR, direction=direction,
+              input=inp, output=out, w0=w0, w1=w1, batch=B, nlat=src.nlat, lmax=src.lmax, mmax=M,
+              in_strides=in_vec_strides, out_strides=out_vec_strides, out_cols=out_cols, scale=scale,
+              flags=flags, nlon=nlon, grouped=grouped)
 
 
 # ---------------------------------------------------------------------------
@@ -91,33 +134,31 @@ class _SpectrumLegendreForward(torch.autograd.Function):
     vector map) contraction written straight into a [B,(2),K,W] gradient."""
 
     @staticmethod
-    def forward(ctx, spec, w0, w1, mmax: int, round_bf16: bool):
-        vector = w1 is not None
+    def forward(ctx, spec, src, round_bf16: bool):
+        vector = src.vector
         B, K, W = spec.size(0), spec.size(-2), spec.size(-1)
-        L = w0.size(0)
-        _require_table(w0, L, K, mmax)
-        shape = (B, 2, L, mmax) if vector else (B, L, mmax)
+        if K != src.nlat:
+            raise RuntimeError(f"spectrum has {K} latitudes, tables {src.nlat}")
+        L, M = src.lmax, src.mmax
+        shape = (B, 2, L, M) if vector else (B, L, M)
         out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
-        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_FORWARD,
-                  input=spec, output=out, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=mmax,
-                  in_strides=_strides3(spec, vector), out_strides=_strides3(out, vector),
-                  out_cols=mmax, scale=TWO_PI, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
-        ctx.save_for_backward(w0, w1)
-        ctx.dims = (B, K, W, L, mmax, vector)
+        _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
+             M, TWO_PI, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+        ctx.src = src
+        ctx.dims = (B, K, W)
         return out
 
     @staticmethod
     def backward(ctx, grad):
-        w0, w1 = ctx.saved_tensors
-        B, K, W, L, mmax, vector = ctx.dims
+        src = ctx.src
+        B, K, W = ctx.dims
+        vector = src.vector
         g = grad.contiguous()
         shape = (B, 2, K, W) if vector else (B, K, W)
         gspec = torch.empty(shape, device=g.device, dtype=torch.complex64)
-        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_INVERSE,
-                  input=g, output=gspec, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=mmax,
-                  in_strides=_strides3(g, vector), out_strides=_strides3(gspec, vector),
-                  out_cols=W, scale=TWO_PI, flags=_lib.FLAG_CONJ_W1 if vector else 0)
-        return gspec, None, None, None, None
+        _run(src, _lib.DIR_INVERSE, g, gspec, B, src.mmax, _strides3(g, vector), _strides3(gspec, vector),
+             W, TWO_PI, _lib.FLAG_CONJ_W1 if vector else 0)
+        return gspec, None, None
 
 
 class _SpectrumLegendreInverse(torch.autograd.Function):
@@ -125,28 +166,28 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
     m >= M are zero and Im at m = 0 (and m = nlon/2 for even nlon) dropped."""
 
     @staticmethod
-    def forward(ctx, coef, w0, w1, nlon: int):
-        vector = w1 is not None
+    def forward(ctx, coef, src, nlon: int):
+        vector = src.vector
         B, L, M = coef.size(0), coef.size(-2), coef.size(-1)
-        K = w0.size(2) if w0.dim() == 4 else w0.size(1)
-        _require_table(w0, L, K, M)
+        if (L, M) != (src.lmax, src.mmax):
+            raise RuntimeError(f"coefficients are {L}x{M}, tables {src.lmax}x{src.mmax}")
+        K = src.nlat
         W = nlon // 2 + 1
         c = coef.contiguous()
         shape = (B, 2, K, W) if vector else (B, K, W)
         spec = torch.empty(shape, device=c.device, dtype=torch.complex64)
-        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_INVERSE,
-                  input=c, output=spec, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=M,
-                  in_strides=_strides3(c, vector), out_strides=_strides3(spec, vector),
-                  out_cols=W, scale=1.0, flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
-        ctx.save_for_backward(w0, w1)
-        ctx.dims = (B, K, W, L, M, vector)
+        _run(src, _lib.DIR_INVERSE, c, spec, B, M, _strides3(c, vector), _strides3(spec, vector),
+             W, 1.0, _lib.FLAG_IRFFT_PREP, nlon)
+        ctx.src = src
+        ctx.dims = (B, K, W, L, M)
         ctx.nyq = nlon // 2 if nlon % 2 == 0 else None
         return spec
 
     @staticmethod
     def backward(ctx, grad):
-        w0, w1 = ctx.saved_tensors
-        B, K, W, L, M, vector = ctx.dims
+        src = ctx.src
+        B, K, W, L, M = ctx.dims
+        vector = src.vector
         g = grad.clone(memory_format=torch.contiguous_format)
         # adjoint of dropping Im at m = 0 / m = nlon/2: drop it from the gradient
         g[..., 0] = g[..., 0].real.to(g.dtype)
@@ -154,11 +195,9 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
             g[..., ctx.nyq] = g[..., ctx.nyq].real.to(g.dtype)
         shape = (B, 2, L, M) if vector else (B, L, M)
         gc = torch.empty(shape, device=g.device, dtype=torch.complex64)
-        _contract(kind=_lib.KIND_VECTOR if vector else _lib.KIND_SCALAR, direction=_lib.DIR_FORWARD,
-                  input=g, output=gc, w0=w0, w1=w1, batch=B, nlat=K, lmax=L, mmax=M,
-                  in_strides=_strides3(g, vector), out_strides=_strides3(gc, vector),
-                  out_cols=M, scale=1.0, flags=_lib.FLAG_CONJ_W1 if vector else 0)
-        return gc, None, None, None
+        _run(src, _lib.DIR_FORWARD, g, gc, B, M, _strides3(g, vector), _strides3(gc, vector),
+             M, 1.0, _lib.FLAG_CONJ_W1 if vector else 0)
+        return gc, None, None
 
 
 # ---------------------------------------------------------------------------
@@ -316,7 +355,10 @@ def fused_sht_forward(x: torch.Tensor, weights: torch.Tensor, mmax: int,
     spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
     lead = spec.shape[:-2]
     spec = spec.reshape(-1, spec.size(-2), spec.size(-1))
-    out = _SpectrumLegendreForward.apply(spec, _as_weight_t(weights, weight_t), None, int(mmax), False)
+    wt = _as_weight_t(weights, weight_t)
+    if wt.size(2) != int(mmax):
+        raise RuntimeError(f"weight_t has mmax={wt.size(2)}, expected {int(mmax)}")
+    out = _SpectrumLegendreForward.apply(spec, _DenseTables(wt), False)
     return out.reshape(lead + out.shape[-2:])
 
 
@@ -328,7 +370,7 @@ def fused_sht_inverse(coeffs: torch.Tensor, pct: torch.Tensor, nlon: int,
     c = coeffs.reshape(-1, coeffs.size(-2), coeffs.size(-1))
     if c.dtype != torch.complex64:
         c = c.to(torch.complex64)
-    spec = _SpectrumLegendreInverse.apply(c, _as_weight_t(pct, pct_t), None, int(nlon))
+    spec = _SpectrumLegendreInverse.apply(c, _DenseTables(_as_weight_t(pct, pct_t)), int(nlon))
     y = torch.fft.irfft(spec, n=int(nlon), dim=-1, norm="forward")
     return y.reshape(lead + y.shape[-2:])
 
@@ -387,7 +429,7 @@ def _check_mmax(mmax: int, nlon: int) -> None:
         raise ValueError(f"mmax={mmax} exceeds nlon//2+1={nlon // 2 + 1}")
 
 
-class RealSHT(nn.Module):
+class RealSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``RealSHT``: ``x`` [..., nlat, nlon] real -> [..., lmax, mmax] complex64.
 
     ``dtype="bf16"`` rounds the post-FFT spectrum to bfloat16 and contracts it
@@ -408,7 +450,7 @@ class RealSHT(nn.Module):
         wt = torch.from_numpy(w)
         self.register_buffer("weights", wt.to(w_dtype))
         self.register_buffer("weight_t", wt.permute(1, 2, 0).contiguous())
-        self.register_buffer("weight_t_tiled", _tile_table(self.weight_t), persistent=False)
+        self._init_tables(("weight_t",), _lib.DIR_FORWARD)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealSHT")
@@ -416,12 +458,11 @@ class RealSHT(nn.Module):
         spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
         lead = spec.shape[:-2]
         spec = spec.reshape(-1, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self.weight_t_tiled, None, self.mmax,
-                                             self._use_bf16 or self._use_fp16)
+        out = _SpectrumLegendreForward.apply(spec, self, self._use_bf16 or self._use_fp16)
         return out.reshape(lead + (self.lmax, self.mmax))
 
 
-class InverseRealSHT(nn.Module):
+class InverseRealSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``InverseRealSHT``: [..., lmax, mmax] complex -> [..., nlat, nlon] real."""
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
@@ -434,7 +475,7 @@ class InverseRealSHT(nn.Module):
         pt = torch.from_numpy(p)
         self.register_buffer("pct", pt)
         self.register_buffer("pct_t", pt.permute(1, 2, 0).contiguous())
-        self.register_buffer("pct_t_tiled", _tile_table(self.pct_t), persistent=False)
+        self._init_tables(("pct_t",), _lib.DIR_INVERSE)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "InverseRealSHT")
@@ -443,12 +484,12 @@ class InverseRealSHT(nn.Module):
         c = x.reshape(-1, self.lmax, self.mmax)
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
-        spec = _SpectrumLegendreInverse.apply(c, self.pct_t_tiled, None, self.nlon)
+        spec = _SpectrumLegendreInverse.apply(c, self, self.nlon)
         y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
         return y.reshape(lead + (self.nlat, self.nlon))
 
 
-class RealVectorSHT(nn.Module):
+class RealVectorSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``RealVectorSHT``: [..., 2, nlat, nlon] -> [..., 2, lmax, mmax] complex64
     (spheroidal, toroidal), both tables fused in one pass."""
 
@@ -468,8 +509,7 @@ class RealVectorSHT(nn.Module):
         self.register_buffer("w1", wt[1].to(w_dtype))
         self.register_buffer("w0_t", wt[0].permute(1, 2, 0).contiguous())
         self.register_buffer("w1_t", wt[1].permute(1, 2, 0).contiguous())
-        self.register_buffer("w0_t_tiled", _tile_table(self.w0_t), persistent=False)
-        self.register_buffer("w1_t_tiled", _tile_table(self.w1_t), persistent=False)
+        self._init_tables(("w0_t", "w1_t"), _lib.DIR_FORWARD)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealVectorSHT")
@@ -477,12 +517,11 @@ class RealVectorSHT(nn.Module):
         spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
         lead = spec.shape[:-3]
         spec = spec.reshape(-1, 2, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self.w0_t_tiled, self.w1_t_tiled, self.mmax,
-                                             self._use_bf16 or self._use_fp16)
+        out = _SpectrumLegendreForward.apply(spec, self, self._use_bf16 or self._use_fp16)
         return out.reshape(lead + (2, self.lmax, self.mmax))
 
 
-class InverseRealVectorSHT(nn.Module):
+class InverseRealVectorSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``InverseRealVectorSHT``: [..., 2, lmax, mmax] -> [..., 2, nlat, nlon]."""
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
@@ -497,8 +536,7 @@ class InverseRealVectorSHT(nn.Module):
         self.register_buffer("d1", dt[1].contiguous())
         self.register_buffer("d0_t", dt[0].permute(1, 2, 0).contiguous())
         self.register_buffer("d1_t", dt[1].permute(1, 2, 0).contiguous())
-        self.register_buffer("d0_t_tiled", _tile_table(self.d0_t), persistent=False)
-        self.register_buffer("d1_t_tiled", _tile_table(self.d1_t), persistent=False)
+        self._init_tables(("d0_t", "d1_t"), _lib.DIR_INVERSE)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "InverseRealVectorSHT")
@@ -507,7 +545,7 @@ class InverseRealVectorSHT(nn.Module):
         c = x.reshape(-1, 2, self.lmax, self.mmax)
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
-        spec = _SpectrumLegendreInverse.apply(c, self.d0_t_tiled, self.d1_t_tiled, self.nlon)
+        spec = _SpectrumLegendreInverse.apply(c, self, self.nlon)
         y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
         return y.reshape(lead + (2, self.nlat, self.nlon))
 

@@ -22,6 +22,7 @@ DTYPE_C64, DTYPE_F32, DTYPE_BF16 = 0, 1, 2
 KIND_SCALAR, KIND_VECTOR, KIND_REAL = 0, 1, 2
 DIR_FORWARD, DIR_INVERSE = 0, 1
 FLAG_CONJ_W1, FLAG_ROUND_BF16, FLAG_IRFFT_PREP = 1, 2, 4
+TABLE_STRIDED, TABLE_GROUPED = 0, 1
 
 # every symbol include/holysht_b200.h declares
 EXPORTS = (
@@ -69,6 +70,7 @@ class ContractDesc(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("ksplit", ctypes.c_int),
         ("w_m_tile_stride", ctypes.c_int64),
+        ("table_layout", ctypes.c_int),
     ]
 
 

@@ -66,10 +66,10 @@ int env_ksplit() {
   return v;
 }
 
-template <int KIND, int DIR, int NB, typename TIN>
+template <int KIND, int DIR, int NB, typename TIN, bool GROUPED>
 int launch_contract(const hsb::ContractParams& p_in, int grid_tiles, cudaStream_t stream) {
   static std::atomic<unsigned long long> configured{0};
-  auto kernel = hsb::contract_kernel<KIND, DIR, NB, TIN>;
+  auto kernel = hsb::contract_kernel<KIND, DIR, NB, TIN, GROUPED>;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
@@ -140,9 +140,10 @@ struct Job {
   long long in_bs, in_ps, in_rs, out_bs, out_ps, out_rs, out_cols, w_ls, w_ks, w_mt, nlon;
   float scale;
   int ksplit;
+  int grouped;
 };
 
-template <int KIND, int DIR, typename TIN>
+template <int KIND, int DIR, typename TIN, bool GROUPED>
 int dispatch_nb(const hsb::ContractParams& p0, int nb, cudaStream_t stream) {
   hsb::ContractParams p = p0;
   p.n_bg = (p.B + nb - 1) / nb;
@@ -152,26 +153,34 @@ int dispatch_nb(const hsb::ContractParams& p0, int nb, cudaStream_t stream) {
   const int grid_tiles = static_cast<int>(tiles);
   if constexpr (KIND == hsb::KIND_VECTOR) {
     switch (nb) {
-      case 1: return launch_contract<KIND, DIR, 1, TIN>(p, grid_tiles, stream);
-      case 2: return launch_contract<KIND, DIR, 2, TIN>(p, grid_tiles, stream);
-      default: return launch_contract<KIND, DIR, 4, TIN>(p, grid_tiles, stream);
+      case 1: return launch_contract<KIND, DIR, 1, TIN, GROUPED>(p, grid_tiles, stream);
+      case 2: return launch_contract<KIND, DIR, 2, TIN, GROUPED>(p, grid_tiles, stream);
+      default: return launch_contract<KIND, DIR, 4, TIN, GROUPED>(p, grid_tiles, stream);
     }
   } else if constexpr (KIND == hsb::KIND_SCALAR) {
     switch (nb) {
-      case 1: return launch_contract<KIND, DIR, 1, TIN>(p, grid_tiles, stream);
-      case 2: return launch_contract<KIND, DIR, 2, TIN>(p, grid_tiles, stream);
-      case 4: return launch_contract<KIND, DIR, 4, TIN>(p, grid_tiles, stream);
-      default: return launch_contract<KIND, DIR, 8, TIN>(p, grid_tiles, stream);
+      case 1: return launch_contract<KIND, DIR, 1, TIN, GROUPED>(p, grid_tiles, stream);
+      case 2: return launch_contract<KIND, DIR, 2, TIN, GROUPED>(p, grid_tiles, stream);
+      case 4: return launch_contract<KIND, DIR, 4, TIN, GROUPED>(p, grid_tiles, stream);
+      default: return launch_contract<KIND, DIR, 8, TIN, GROUPED>(p, grid_tiles, stream);
     }
   } else {
     switch (nb) {
-      case 2: return launch_contract<KIND, DIR, 2, TIN>(p, grid_tiles, stream);
-      case 4: return launch_contract<KIND, DIR, 4, TIN>(p, grid_tiles, stream);
-      case 8: return launch_contract<KIND, DIR, 8, TIN>(p, grid_tiles, stream);
-      default: return launch_contract<KIND, DIR, 16, TIN>(p, grid_tiles, stream);
+      case 2: return launch_contract<KIND, DIR, 2, TIN, false>(p, grid_tiles, stream);
+      case 4: return launch_contract<KIND, DIR, 4, TIN, false>(p, grid_tiles, stream);
+      case 8: return launch_contract<KIND, DIR, 8, TIN, false>(p, grid_tiles, stream);
+      default: return launch_contract<KIND, DIR, 16, TIN, false>(p, grid_tiles, stream);
     }
   }
 }
+
+template <int KIND, typename TIN, bool GROUPED>
+int dispatch_dir(const hsb::ContractParams& p, int dir, int nb, cudaStream_t stream) {
+  return dir == HOLYSHT_DIR_FORWARD ? dispatch_nb<KIND, hsb::DIR_FWD, TIN, GROUPED>(p, nb, stream)
+                                    : dispatch_nb<KIND, hsb::DIR_INV, TIN, GROUPED>(p, nb, stream);
+}
+
+int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream);
 
 int run_job(const Job& j, cudaStream_t stream) {
   if (j.kind < 0 || j.kind > 2) return fail(HOLYSHT_ERR_INVALID, "unknown kind %d", j.kind);
@@ -190,7 +199,7 @@ int run_job(const Job& j, cudaStream_t stream) {
   if (j.B == 0 || R == 0 || j.out_cols == 0) return ok();
   if (!j.out) return fail(HOLYSHT_ERR_INVALID, "output pointer is null");
   if (S > 0 && j.M > 0 && (!j.in || !j.w0)) return fail(HOLYSHT_ERR_INVALID, "input or table pointer is null");
-  if (j.kind == HOLYSHT_KIND_VECTOR && S > 0 && j.M > 0 && !j.w1)
+  if (j.kind == HOLYSHT_KIND_VECTOR && !j.grouped && S > 0 && j.M > 0 && !j.w1)
     return fail(HOLYSHT_ERR_INVALID, "vector contraction needs both tables");
   if (j.kind == HOLYSHT_KIND_REAL) {
     if (j.in_dtype != HOLYSHT_DTYPE_F32 && j.in_dtype != HOLYSHT_DTYPE_BF16)
@@ -200,7 +209,25 @@ int run_job(const Job& j, cudaStream_t stream) {
   } else if (j.in_dtype != HOLYSHT_DTYPE_C64) {
     return fail(HOLYSHT_ERR_INVALID, "input must be complex64");
   }
-  {
+  if (j.grouped && j.kind == HOLYSHT_KIND_REAL)
+    return fail(HOLYSHT_ERR_INVALID, "the row-grouped table layout is for complex contractions");
+  Job jj = j;
+  if (j.grouped) {
+    // row-grouped layout: [R/4 groups][ceil(M/32) tiles][S steps][32 lanes][4 rows][tables]
+    const long long G = (long long)hsb::kRowsPerWarp * (j.kind == HOLYSHT_KIND_VECTOR ? 2 : 1);
+    const long long mt = (j.M + hsb::kMTile - 1) / hsb::kMTile;
+    const long long groups = (R + hsb::kRowsPerWarp - 1) / hsb::kRowsPerWarp;
+    jj.w_ks = 32 * G;
+    jj.w_mt = S * 32 * G;
+    jj.w_ls = mt * S * 32 * G;
+    if (groups * jj.w_ls >= (1LL << 32))
+      return fail(HOLYSHT_ERR_INVALID, "grouped table exceeds 2^32 floats");
+  }
+  return run_job_resolved(jj, R, S, stream);
+}
+
+int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream) {
+  if (!j.grouped) {
     // the kernel addresses a table with 32-bit float offsets
     const long long n_mt_tab = (j.M + hsb::kMTile - 1) / hsb::kMTile;
     const long long span = (j.L > 0 ? (j.L - 1) * j.w_ls : 0) + (j.K > 0 ? (j.K - 1) * j.w_ks : 0) +
@@ -268,24 +295,15 @@ int run_job(const Job& j, cudaStream_t stream) {
   int ks = j.ksplit ? j.ksplit : env_ksplit();
   p.ks = ks;
 
-  if (j.kind == HOLYSHT_KIND_SCALAR) {
-    return j.dir == HOLYSHT_DIR_FORWARD
-               ? dispatch_nb<hsb::KIND_SCALAR, hsb::DIR_FWD, float2>(p, nb, stream)
-               : dispatch_nb<hsb::KIND_SCALAR, hsb::DIR_INV, float2>(p, nb, stream);
-  }
-  if (j.kind == HOLYSHT_KIND_VECTOR) {
-    return j.dir == HOLYSHT_DIR_FORWARD
-               ? dispatch_nb<hsb::KIND_VECTOR, hsb::DIR_FWD, float2>(p, nb, stream)
-               : dispatch_nb<hsb::KIND_VECTOR, hsb::DIR_INV, float2>(p, nb, stream);
-  }
-  if (j.in_dtype == HOLYSHT_DTYPE_BF16) {
-    return j.dir == HOLYSHT_DIR_FORWARD
-               ? dispatch_nb<hsb::KIND_REAL, hsb::DIR_FWD, __nv_bfloat16>(p, nb, stream)
-               : dispatch_nb<hsb::KIND_REAL, hsb::DIR_INV, __nv_bfloat16>(p, nb, stream);
-  }
-  return j.dir == HOLYSHT_DIR_FORWARD
-             ? dispatch_nb<hsb::KIND_REAL, hsb::DIR_FWD, float>(p, nb, stream)
-             : dispatch_nb<hsb::KIND_REAL, hsb::DIR_INV, float>(p, nb, stream);
+  if (j.kind == HOLYSHT_KIND_SCALAR)
+    return j.grouped ? dispatch_dir<hsb::KIND_SCALAR, float2, true>(p, j.dir, nb, stream)
+                     : dispatch_dir<hsb::KIND_SCALAR, float2, false>(p, j.dir, nb, stream);
+  if (j.kind == HOLYSHT_KIND_VECTOR)
+    return j.grouped ? dispatch_dir<hsb::KIND_VECTOR, float2, true>(p, j.dir, nb, stream)
+                     : dispatch_dir<hsb::KIND_VECTOR, float2, false>(p, j.dir, nb, stream);
+  if (j.in_dtype == HOLYSHT_DTYPE_BF16)
+    return dispatch_dir<hsb::KIND_REAL, __nv_bfloat16, false>(p, j.dir, nb, stream);
+  return dispatch_dir<hsb::KIND_REAL, float, false>(p, j.dir, nb, stream);
 }
 
 // Dense contiguous job in the reference layouts.
@@ -320,6 +338,7 @@ Job dense_job(int kind, int dir, int in_dtype, const void* in, void* out, const 
   j.nlon = 0;
   j.scale = 1.f;
   j.ksplit = 0;
+  j.grouped = 0;
   return j;
 }
 
@@ -408,6 +427,9 @@ int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
   j.w_ls = d->w_l_stride;
   j.w_ks = d->w_k_stride;
   j.w_mt = d->w_m_tile_stride ? d->w_m_tile_stride : hsb::kMTile;
+  j.grouped = d->table_layout == HOLYSHT_TABLE_GROUPED;
+  if (d->table_layout != HOLYSHT_TABLE_STRIDED && d->table_layout != HOLYSHT_TABLE_GROUPED)
+    return fail(HOLYSHT_ERR_INVALID, "unknown table_layout %d", d->table_layout);
   j.nlon = d->nlon;
   j.scale = d->scale;
   j.ksplit = d->ksplit;

@@ -129,6 +129,23 @@ __device__ __forceinline__ float ld_stream(const float* p, bool ok, unsigned lon
   return v;
 }
 
+__device__ __forceinline__ float4 ld_stream4(const float* p, bool ok, unsigned long long pol) {
+  float4 v;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "setp.ne.b32 q, %4, 0;\n\t"
+      "mov.b32 %0, 0;\n\tmov.b32 %1, 0;\n\tmov.b32 %2, 0;\n\tmov.b32 %3, 0;\n\t"
+      "@q ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%5], %6;\n\t}"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"((int)ok), "l"(p), "l"(pol));
+  return v;
+}
+
+// bulk L2 prefetch of a contiguous range (16-byte aligned, multiple of 16 bytes)
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_l2(const float* p) {
   asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
 }
@@ -230,7 +247,14 @@ __device__ __forceinline__ void write_zero_tile(const ContractParams& p, int j, 
   }
 }
 
-template <int KIND, int DIR, int NB, typename TIN>
+// GROUPED: the table is in the row-grouped layout built by the host
+// (holysht_b200.ops.group_table): for every group of kRowsPerWarp output
+// rows, every 32-order m tile and every reduction step, the 32 lanes' values
+// of all rows and tables are contiguous ([rows][tables] per lane), so a lane
+// fetches its whole step with one or two 16-byte loads and a warp's step is
+// one contiguous 512-byte / 1-KB block.  Strides: w_ls = group, w_mt = m tile,
+// w_ks = step (floats).  Otherwise the table is strided [l][k][m-tile][32].
+template <int KIND, int DIR, int NB, typename TIN, bool GROUPED>
 __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN_BLOCKS : 2)
     contract_kernel(const ContractParams p) {
   constexpr int P = KindTraits<KIND>::P;
@@ -278,19 +302,34 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
   const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
 
   // table offsets of this lane (32-bit: a table holds < 2^32 floats)
-  const unsigned sstride = (unsigned)((DIR == DIR_FWD) ? p.w_ks : p.w_ls);
+  constexpr int NT = (KIND == KIND_VECTOR) ? 2 : 1;        // tables
+  constexpr int GF = kRowsPerWarp * NT;                     // grouped floats per lane-step
+  const unsigned sstride = GROUPED ? (unsigned)p.w_ks : (unsigned)((DIR == DIR_FWD) ? p.w_ks : p.w_ls);
   const unsigned rstride = (unsigned)((DIR == DIR_FWD) ? p.w_ls : p.w_ks);
   unsigned roff[kRowsPerWarp];
   unsigned vmask = 0;
+  unsigned gbase = 0;  // grouped: this lane's offset at step 0
+  unsigned gwarp = 0;  // grouped: lane 0's offset at step 0 (prefetch)
+  bool gvalid = false;
+  if constexpr (GROUPED) {
+    const int rg = (row0 / kRowsPerWarp) + warp;
+    const int r_first = rg * kRowsPerWarp;
+    gvalid = r_first < p.R && m < p.M && (DIR == DIR_INV || r_first + kRowsPerWarp - 1 >= m);
+    gwarp = (unsigned)rg * (unsigned)p.w_ls + (unsigned)j * (unsigned)p.w_mt;
+    gbase = gwarp + (unsigned)lane * GF;
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int row = row0 + warp * kRowsPerWarp + i;
-    bool ok = row < p.R && m < p.M;
-    if (DIR == DIR_FWD) ok = ok && row >= m;  // l >= m
-    vmask |= ok ? (1u << i) : 0u;
-    roff[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) + (unsigned)lane : 0u;
+    for (int i = 0; i < kRowsPerWarp; ++i) roff[i] = 0u;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      const int row = row0 + warp * kRowsPerWarp + i;
+      bool ok = row < p.R && m < p.M;
+      if (DIR == DIR_FWD) ok = ok && row >= m;  // l >= m
+      vmask |= ok ? (1u << i) : 0u;
+      roff[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) + (unsigned)lane : 0u;
+    }
   }
-  // warp-uniform row validity and lane-0 offsets for the L2 prefetch
+  // warp-uniform row validity and lane-0 offsets for the L2 prefetch (strided layout)
   unsigned pf_off[kRowsPerWarp];
   unsigned pf_mask = 0;
 #pragma unroll
@@ -300,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
     pf_mask |= ok ? (1u << i) : 0u;
     pf_off[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) : 0u;
   }
+  const bool pf_any = pf_mask != 0;
   const int m_last = min(kMTile, p.M - m0) - 1;  // last valid lane of this tile
   const float* __restrict__ w0 = p.w0;
   const float* __restrict__ w1 = p.w1;
@@ -359,18 +399,40 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
     const unsigned so = (unsigned)slot_s * sstride;
     bool sok = slot_s < r_end;
     if (DIR == DIR_INV) sok = sok && slot_s >= m;  // l >= m
+    if constexpr (GROUPED) {
+      const bool ok = sok && gvalid;
+      const float* a = w0 + gbase + so;
+      if constexpr (KIND == KIND_VECTOR) {
+        const float4 u = ld_stream4(a, ok, pol);      // rows 0,1 x (W0, W1)
+        const float4 v = ld_stream4(a + 4, ok, pol);  // rows 2,3 x (W0, W1)
+        d0[0] = u.x; d1[0] = u.y; d0[1] = u.z; d1[1] = u.w;
+        d0[2] = v.x; d1[2] = v.y; d0[3] = v.z; d1[3] = v.w;
+      } else {
+        const float4 u = ld_stream4(a, ok, pol);
+        d0[0] = u.x; d0[1] = u.y; d0[2] = u.z; d0[3] = u.w;
+      }
+    } else {
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-      const bool ok = sok && ((vmask >> i) & 1u);
-      const unsigned off = roff[i] + so;
-      d0[i] = ld_stream(w0 + off, ok, pol);
-      if (KIND == KIND_VECTOR) d1[i] = ld_stream(w1 + off, ok, pol);
+      for (int i = 0; i < kRowsPerWarp; ++i) {
+        const bool ok = sok && ((vmask >> i) & 1u);
+        const unsigned off = roff[i] + so;
+        d0[i] = ld_stream(w0 + off, ok, pol);
+        if (KIND == KIND_VECTOR) d1[i] = ld_stream(w1 + off, ok, pol);
+      }
     }
   };
 
   // L2 prefetch of the table lines of one future chunk: lane q < kChunk takes
   // step q, every valid row and table, first and last line of the 32 orders
   auto prefetch_chunk = [&](int chunk) {
+    if constexpr (GROUPED) {
+      // the warp's chunk is one contiguous block: one bulk prefetch by lane 0
+      const int s0 = r_begin + chunk * kChunk;
+      if (lane != 0 || s0 >= r_end || !pf_any) return;
+      const int n = min(kChunk, r_end - s0);
+      prefetch_l2_bulk(w0 + gwarp + (unsigned)s0 * sstride, (unsigned)(n * 32 * GF * 4));
+      return;
+    }
     if (lane >= kChunk) return;
     const int s = r_begin + chunk * kChunk + lane;
     if (s >= r_end) return;

@@ -34,6 +34,7 @@ __all__ = [
     "sht_prepare_irfft",
     "legendre_contract",
     "tile_table",
+    "group_table",
 ]
 
 
@@ -223,22 +224,55 @@ def tile_table(weight_t: torch.Tensor) -> torch.Tensor:
     return padded.view(L, K, mt, 32).permute(0, 2, 1, 3).contiguous()
 
 
+def group_table(tables, direction: int) -> torch.Tensor:
+    """Row-grouped table for the contraction kernel (``HOLYSHT_TABLE_GROUPED``).
+
+    ``tables``: one dense [lmax, nlat, mmax] table, or a (W0, W1) pair for the
+    vector kind.  ``direction``: ``DIR_FORWARD`` (rows = l, steps = k) or
+    ``DIR_INVERSE`` (rows = k, steps = l).  Result [R/4, ceil(M/32), S, 32, 4, T]:
+    per 4-row group, m tile and step, the 32 lanes' rows x tables are
+    contiguous, zero outside the tables."""
+    if torch.is_tensor(tables):
+        tables = (tables,)
+    L, K, M = tables[0].shape
+    mt = (M + 31) // 32
+    fwd = direction == _lib.DIR_FORWARD
+    R, S = (L, K) if fwd else (K, L)
+    rg = (R + 3) // 4
+    dev = tables[0].device
+    out = torch.zeros((rg, mt, S, 32, 4, len(tables)), dtype=torch.float32, device=dev)
+    for t, w in enumerate(tables):
+        _require(tuple(w.shape) == (L, K, M) and w.dtype == torch.float32, "tables must match, float32")
+        pad = torch.zeros((rg * 4 if fwd else L, K if fwd else rg * 4, mt * 32), dtype=torch.float32, device=dev)
+        pad[:L, :K, :M] = w
+        if fwd:   # [l, k, m] -> [g, r, k, mt, lane] -> [g, mt, k, lane, r]
+            v = pad.view(rg, 4, K, mt, 32).permute(0, 3, 2, 4, 1)
+        else:     # [l, k, m] -> [l, g, r, mt, lane] -> [g, mt, l, lane, r]
+            v = pad.view(L, rg, 4, mt, 32).permute(1, 3, 0, 4, 2)
+        out[..., t] = v
+    return out
+
+
 def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,
                       w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
                       scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0,
-                      w_strides=None) -> None:
+                      w_strides=None, grouped: bool = False) -> None:
     """Strided contraction; strides are (batch, component, row) in elements.
 
     ``w0``/``w1`` are either dense [lmax, nlat, mmax] tables (m contiguous) or
     m-tiled tables from :func:`tile_table` ([lmax, ceil(mmax/32), nlat, 32]);
-    ``w_strides`` = (l, k, m-tile) strides in floats overrides the inference."""
+    ``w_strides`` = (l, k, m-tile) strides in floats overrides the inference.
+    ``grouped``: ``w0`` is a :func:`group_table` table (``w1`` unused)."""
     dev = _cuda(output, input, w0)
     if w1 is not None:
         _cuda(output, w1)
         _require(w1.stride() == w0.stride(), "W0 and W1 must share strides")
     _require(w0.dtype == torch.float32, "tables must be float32")
-    if w_strides is None:
+    if grouped:
+        _require(w0.dim() == 6 and w0.is_contiguous(), "grouped tables come from group_table()")
+        w_strides = (0, 0, 0)
+    elif w_strides is None:
         if w0.dim() == 4:
             _require(w0.is_contiguous() and w0.size(3) == 32, "m-tiled tables must be contiguous [L, Mt, K, 32]")
             w_strides = (w0.stride(0), w0.stride(2), w0.stride(1))
@@ -265,5 +299,6 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
     d.nlon = nlon
     d.scale = scale
     d.ksplit = ksplit
+    d.table_layout = _lib.TABLE_GROUPED if grouped else _lib.TABLE_STRIDED
     with torch.cuda.device(dev):
         _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))

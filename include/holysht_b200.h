@@ -159,7 +159,19 @@ typedef struct holysht_contract_desc {
   int64_t w_m_tile_stride; /* table stride of one 32-order m tile; 0 = 32 (dense, m contiguous).
                               The m-tiled layout [L][ceil(M/32)][K][32] (k stride 32) keeps
                               every 32-order row segment on one 128-byte line. */
+  int table_layout;         /* HOLYSHT_TABLE_STRIDED (the strides above) or
+                               HOLYSHT_TABLE_GROUPED (see below; strides ignored) */
 } holysht_contract_desc;
+
+/* Table layouts of holysht_contract_desc.table_layout.
+ * GROUPED (SCALAR and VECTOR kinds): output rows in groups of 4 (rows = l for
+ * HOLYSHT_DIR_FORWARD, k for HOLYSHT_DIR_INVERSE), reduction steps s (k resp. l):
+ *   T[g][mt][s][lane][r][t] = W_t(row = 4g + r, step = s, m = 32 mt + lane), table t
+ * with g < ceil(R/4), mt < ceil(M/32), lane < 32, r < 4, t < (VECTOR ? 2 : 1);
+ * entries outside the tables (and above the diagonal) are zero.  w0 points at
+ * the start; w1 is ignored (both tables are interleaved). */
+#define HOLYSHT_TABLE_STRIDED 0
+#define HOLYSHT_TABLE_GROUPED 1
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
