@@ -102,6 +102,19 @@ class _GroupedTablesMixin:
         self.table(hot_direction)
         self.register_load_state_dict_post_hook(lambda module, _keys: module._drop_grouped())
 
+    def _spectrum(self, x: torch.Tensor):
+        """(rfft spectrum, kernel scale, round-to-bf16 flag) of a real field.
+
+        FP32: the unnormalised rfft, with the 2*pi/nlon of the reference's
+        ``2*pi*rfft(x, norm="forward")`` folded into the Legendre kernel (no
+        separate scaling pass).  BF16/FP16 modules round the scaled spectrum,
+        as the reference does (``__init__.py:1291-1295``), so it is scaled
+        before the kernel rounds it."""
+        low = bool(getattr(self, "_use_bf16", False) or getattr(self, "_use_fp16", False))
+        if low:
+            return TWO_PI * torch.fft.rfft(x.float(), dim=-1, norm="forward"), 1.0, True
+        return torch.fft.rfft(x.float(), dim=-1), TWO_PI / self.nlon, False
+
     def _drop_grouped(self) -> None:
         self._grouped_fwd = None
         self._grouped_inv = None
@@ -134,7 +147,7 @@ class _SpectrumLegendreForward(torch.autograd.Function):
     vector map) contraction written straight into a [B,(2),K,W] gradient."""
 
     @staticmethod
-    def forward(ctx, spec, src, round_bf16: bool):
+    def forward(ctx, spec, src, round_bf16: bool, scale: float):
         vector = src.vector
         B, K, W = spec.size(0), spec.size(-2), spec.size(-1)
         if K != src.nlat:
@@ -143,9 +156,10 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         shape = (B, 2, L, M) if vector else (B, L, M)
         out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
         _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
-             M, TWO_PI, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+             M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
         ctx.src = src
         ctx.dims = (B, K, W)
+        ctx.scale = scale
         return out
 
     @staticmethod
@@ -157,8 +171,8 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         shape = (B, 2, K, W) if vector else (B, K, W)
         gspec = torch.empty(shape, device=g.device, dtype=torch.complex64)
         _run(src, _lib.DIR_INVERSE, g, gspec, B, src.mmax, _strides3(g, vector), _strides3(gspec, vector),
-             W, TWO_PI, _lib.FLAG_CONJ_W1 if vector else 0)
-        return gspec, None, None
+             W, ctx.scale, _lib.FLAG_CONJ_W1 if vector else 0)
+        return gspec, None, None, None
 
 
 class _SpectrumLegendreInverse(torch.autograd.Function):
@@ -352,13 +366,13 @@ def fused_sht_forward(x: torch.Tensor, weights: torch.Tensor, mmax: int,
                       weight_t: Optional[torch.Tensor] = None) -> torch.Tensor:
     """rfft -> Legendre: [B, nlat, nlon] float32 -> [B, lmax, mmax] complex64."""
     _need_cuda(x, "fused_sht_forward")
-    spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
+    spec = torch.fft.rfft(x.float(), dim=-1)
     lead = spec.shape[:-2]
     spec = spec.reshape(-1, spec.size(-2), spec.size(-1))
     wt = _as_weight_t(weights, weight_t)
     if wt.size(2) != int(mmax):
         raise RuntimeError(f"weight_t has mmax={wt.size(2)}, expected {int(mmax)}")
-    out = _SpectrumLegendreForward.apply(spec, _DenseTables(wt), False)
+    out = _SpectrumLegendreForward.apply(spec, _DenseTables(wt), False, TWO_PI / x.size(-1))
     return out.reshape(lead + out.shape[-2:])
 
 
@@ -455,10 +469,10 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealSHT")
         assert x.shape[-2] == self.nlat and x.shape[-1] == self.nlon
-        spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
+        spec, scale, low = self._spectrum(x)
         lead = spec.shape[:-2]
         spec = spec.reshape(-1, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self, self._use_bf16 or self._use_fp16)
+        out = _SpectrumLegendreForward.apply(spec, self, low, scale)
         return out.reshape(lead + (self.lmax, self.mmax))
 
 
@@ -514,10 +528,10 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealVectorSHT")
         assert x.shape[-2] == self.nlat and x.shape[-1] == self.nlon and x.shape[-3] == 2
-        spec = torch.fft.rfft(x.float(), dim=-1, norm="forward")
+        spec, scale, low = self._spectrum(x)
         lead = spec.shape[:-3]
         spec = spec.reshape(-1, 2, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self, self._use_bf16 or self._use_fp16)
+        out = _SpectrumLegendreForward.apply(spec, self, low, scale)
         return out.reshape(lead + (2, self.lmax, self.mmax))
 
 

@@ -350,6 +350,13 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
   for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
     for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
+  // vector kind: the four products per (row, batch), see the inner loop
+  constexpr int NQ = (KIND == KIND_VECTOR) ? 4 * NB : 1;
+  float2 vq[kRowsPerWarp][NQ];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int a = 0; a < NQ; ++a) vq[i][a] = make_float2(0.f, 0.f);
 
   // ---- staging of the input spectrum: [buf][step][plane][lane] ----
   constexpr int kStageElems = kChunk * PB * 32;
@@ -497,25 +504,20 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
             }
           }
         } else if constexpr (KIND == KIND_VECTOR) {
+          // four real-table products per batch, composed once after the loop:
+          // q0 = W0 c0, q1 = W1 c1, q2 = W1 c0, q3 = W0 c1
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
             const float2 c0v = xrow[(2 * b) * 32];
             const float2 c1v = xrow[(2 * b + 1) * 32];
-            const float2 c0s = make_float2(c0v.y, c0v.x);
-            const float2 c1s = make_float2(c1v.y, c1v.x);
 #pragma unroll
             for (int i = 0; i < kRowsPerWarp; ++i) {
-              const float w0 = wr0[cur][i];
-              const float w1 = wr1[cur][i] * w1s;
-              const float2 pw0 = make_float2(w0, w0);
-              const float2 pw1 = make_float2(-w1, w1);
-              const float2 nw0 = make_float2(-w0, -w0);
-              // sph += w0 c0 + i w1 c1
-              acc[i][2 * b] = ffma2(pw0, c0v, acc[i][2 * b]);
-              acc[i][2 * b] = ffma2(pw1, c1s, acc[i][2 * b]);
-              // tor += i w1 c0 - w0 c1
-              acc[i][2 * b + 1] = ffma2(pw1, c0s, acc[i][2 * b + 1]);
-              acc[i][2 * b + 1] = ffma2(nw0, c1v, acc[i][2 * b + 1]);
+              const float2 pw0 = make_float2(wr0[cur][i], wr0[cur][i]);
+              const float2 pw1 = make_float2(wr1[cur][i], wr1[cur][i]);
+              vq[i][4 * b + 0] = ffma2(pw0, c0v, vq[i][4 * b + 0]);
+              vq[i][4 * b + 1] = ffma2(pw1, c1v, vq[i][4 * b + 1]);
+              vq[i][4 * b + 2] = ffma2(pw1, c0v, vq[i][4 * b + 2]);
+              vq[i][4 * b + 3] = ffma2(pw0, c1v, vq[i][4 * b + 3]);
             }
           }
         } else {
@@ -536,6 +538,17 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
     if constexpr (kAsyncStage) cp_async_wait_0();
   }
 
+  if constexpr (KIND == KIND_VECTOR) {
+    // sph = q0 + i s q1,  tor = i s q2 - q3   (s = w1_sign)
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const float2 q0 = vq[i][4 * b], q1 = vq[i][4 * b + 1], q2 = vq[i][4 * b + 2], q3 = vq[i][4 * b + 3];
+        acc[i][2 * b] = make_float2(q0.x - w1s * q1.y, q0.y + w1s * q1.x);
+        acc[i][2 * b + 1] = make_float2(-w1s * q2.y - q3.x, w1s * q2.x - q3.y);
+      }
+  }
   // ---- cluster reduction of the partial sums through distributed smem ----
   __syncthreads();
 #pragma unroll

@@ -311,10 +311,11 @@ def test_bf16_module_paths():
     o32, o16 = m32(x), m16(x)
     assert rel_l2(o16.cpu(), o32.cpu()) < 1e-2
     # the bf16 path is FP32 on the bf16-rounded spectrum
-    spec = torch.fft.rfft(x, dim=-1, norm="forward")
+    # the reference rounds the 2*pi-scaled spectrum (torch-ext/holysht/__init__.py:1291-1295)
+    spec = 2 * torch.pi * torch.fft.rfft(x, dim=-1, norm="forward")
     spec = torch.complex(spec.real.bfloat16().float(), spec.imag.bfloat16().float())
     w = m32.weight_t.permute(2, 0, 1).double().cpu().numpy()
-    ref = 2 * np.pi * np.einsum("...km,mlk->...lm", spec.cpu().numpy()[..., : m32.mmax].astype(np.complex128), w)
+    ref = np.einsum("...km,mlk->...lm", spec.cpu().numpy()[..., : m32.mmax].astype(np.complex128), w)
     assert_fp32_close(o16, ref)
 
 
