@@ -71,6 +71,7 @@ class ContractDesc(ctypes.Structure):
         ("ksplit", ctypes.c_int),
         ("w_m_tile_stride", ctypes.c_int64),
         ("table_layout", ctypes.c_int),
+        ("m_offset", ctypes.c_int64),
     ]
 
 

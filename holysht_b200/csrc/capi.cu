@@ -141,6 +141,7 @@ struct Job {
   float scale;
   int ksplit;
   int grouped;
+  long long m_off;
 };
 
 template <int KIND, int DIR, typename TIN, bool GROUPED>
@@ -267,15 +268,20 @@ int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream
 
   p.n_rt = (int)((R + hsb::kRows - 1) / hsb::kRows);
   p.n_mt = (int)((j.out_cols + hsb::kMTile - 1) / hsb::kMTile);
-  const long long act = (S > 0) ? (j.M < j.L ? j.M : j.L) : 0;
+  // active m tiles: inside the table columns and with some l >= m below L
+  const long long act_cols = (S > 0) ? j.M : 0;
+  const long long act_l = (S > 0 && j.L > j.m_off) ? j.L - j.m_off : 0;
+  const long long act = act_cols < act_l ? act_cols : act_l;
   p.j_act = (int)((act + hsb::kMTile - 1) / hsb::kMTile);
+  p.m_off = (int)j.m_off;
+  p.mt_off = (int)(j.m_off / hsb::kMTile);
   if (p.j_act > p.n_mt) p.j_act = p.n_mt;
   long long n_compute = 0, n_zero = 0;
   for (int jt = 0; jt < p.n_mt; ++jt) {
     if (jt < p.j_act) {
-      const int first = j.dir == HOLYSHT_DIR_FORWARD ? jt : 0;
+      const int first = j.dir == HOLYSHT_DIR_FORWARD ? jt + p.mt_off : 0;
       n_compute += p.n_rt > first ? p.n_rt - first : 0;
-      n_zero += j.dir == HOLYSHT_DIR_FORWARD ? (jt < p.n_rt ? jt : p.n_rt) : 0;
+      n_zero += j.dir == HOLYSHT_DIR_FORWARD ? (first < p.n_rt ? first : p.n_rt) : 0;
     } else {
       n_zero += p.n_rt;
     }
@@ -339,6 +345,7 @@ Job dense_job(int kind, int dir, int in_dtype, const void* in, void* out, const 
   j.scale = 1.f;
   j.ksplit = 0;
   j.grouped = 0;
+  j.m_off = 0;
   return j;
 }
 
@@ -428,6 +435,9 @@ int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
   j.w_ks = d->w_k_stride;
   j.w_mt = d->w_m_tile_stride ? d->w_m_tile_stride : hsb::kMTile;
   j.grouped = d->table_layout == HOLYSHT_TABLE_GROUPED;
+  j.m_off = d->m_offset;
+  if (j.m_off < 0 || j.m_off % hsb::kMTile != 0 || !fits_int(j.m_off))
+    return fail(HOLYSHT_ERR_INVALID, "m_offset must be a non-negative multiple of 32");
   if (d->table_layout != HOLYSHT_TABLE_STRIDED && d->table_layout != HOLYSHT_TABLE_GROUPED)
     return fail(HOLYSHT_ERR_INVALID, "unknown table_layout %d", d->table_layout);
   j.nlon = d->nlon;

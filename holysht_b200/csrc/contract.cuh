@@ -85,6 +85,7 @@ struct ContractParams {
   int n_rt, n_mt, j_act, n_bg;       // row tiles, m tiles, active m tiles, batch groups
   int n_compute, n_zero;             // tiles per batch group
   int ks;                            // cluster size (reduction split)
+  int m_off, mt_off;                 // global order of local column 0 (multiple of 32), /32
 };
 
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
@@ -163,7 +164,7 @@ __device__ __forceinline__ bool decode_tile(const ContractParams& p, int t, int&
   if (t < p.n_compute) {
     int rem = t;
     for (j = 0; j < p.j_act; ++j) {
-      const int first = (DIR == DIR_FWD) ? j : 0;
+      const int first = (DIR == DIR_FWD) ? j + p.mt_off : 0;
       const int cnt = p.n_rt > first ? p.n_rt - first : 0;
       if (rem < cnt) {
         rt = first + rem;
@@ -178,7 +179,7 @@ __device__ __forceinline__ bool decode_tile(const ContractParams& p, int t, int&
   for (j = 0; j < p.n_mt; ++j) {
     int cnt;
     if (j < p.j_act)
-      cnt = (DIR == DIR_FWD) ? (j < p.n_rt ? j : p.n_rt) : 0;
+      cnt = (DIR == DIR_FWD) ? (j + p.mt_off < p.n_rt ? j + p.mt_off : p.n_rt) : 0;
     else
       cnt = p.n_rt;
     if (rem < cnt) {
@@ -289,11 +290,13 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
   const int warp = threadIdx.x >> 5;
   const int m0 = j * kMTile;
   const int m = m0 + lane;
+  const int mg = m + p.m_off;    // global order (triangle l >= m)
+  const int m0g = m0 + p.m_off;
   const int row0 = rt * kRows;
   const int b0 = bg * NB;
 
   // reduction range of this cluster rank (chunk aligned)
-  const int s_begin = (DIR == DIR_FWD) ? 0 : m0;
+  const int s_begin = (DIR == DIR_FWD) ? 0 : m0g;
   const int s_end = p.S;
   const int nsteps = s_end > s_begin ? s_end - s_begin : 0;
   const int per = ((nsteps + ks * kChunk - 1) / (ks * kChunk)) * kChunk;
@@ -314,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
   if constexpr (GROUPED) {
     const int rg = (row0 / kRowsPerWarp) + warp;
     const int r_first = rg * kRowsPerWarp;
-    gvalid = r_first < p.R && m < p.M && (DIR == DIR_INV || r_first + kRowsPerWarp - 1 >= m);
+    gvalid = r_first < p.R && m < p.M && (DIR == DIR_INV || r_first + kRowsPerWarp - 1 >= mg);
     gwarp = (unsigned)rg * (unsigned)p.w_ls + (unsigned)j * (unsigned)p.w_mt;
     gbase = gwarp + (unsigned)lane * GF;
 #pragma unroll
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
     for (int i = 0; i < kRowsPerWarp; ++i) {
       const int row = row0 + warp * kRowsPerWarp + i;
       bool ok = row < p.R && m < p.M;
-      if (DIR == DIR_FWD) ok = ok && row >= m;  // l >= m
+      if (DIR == DIR_FWD) ok = ok && row >= mg;  // l >= m
       vmask |= ok ? (1u << i) : 0u;
       roff[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) + (unsigned)lane : 0u;
     }
@@ -335,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i) {
     const int row = row0 + warp * kRowsPerWarp + i;
-    const bool ok = row < p.R && m0 < p.M && (DIR == DIR_INV || row >= m0);
+    const bool ok = row < p.R && m0 < p.M && (DIR == DIR_INV || row >= m0g);
     pf_mask |= ok ? (1u << i) : 0u;
     pf_off[i] = ok ? (unsigned)row * rstride + (unsigned)(j * p.w_mt) : 0u;
   }
@@ -405,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
   auto load_step = [&](int slot_s, float (&d0)[kRowsPerWarp], float (&d1)[kRowsPerWarp]) {
     const unsigned so = (unsigned)slot_s * sstride;
     bool sok = slot_s < r_end;
-    if (DIR == DIR_INV) sok = sok && slot_s >= m;  // l >= m
+    if (DIR == DIR_INV) sok = sok && slot_s >= mg;  // l >= m
     if constexpr (GROUPED) {
       const bool ok = sok && gvalid;
       const float* a = w0 + gbase + so;

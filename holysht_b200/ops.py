@@ -257,7 +257,7 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
                       w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
                       scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0,
-                      w_strides=None, grouped: bool = False) -> None:
+                      w_strides=None, grouped: bool = False, m_offset: int = 0) -> None:
     """Strided contraction; strides are (batch, component, row) in elements.
 
     ``w0``/``w1`` are either dense [lmax, nlat, mmax] tables (m contiguous) or
@@ -300,5 +300,6 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
     d.scale = scale
     d.ksplit = ksplit
     d.table_layout = _lib.TABLE_GROUPED if grouped else _lib.TABLE_STRIDED
+    d.m_offset = m_offset
     with torch.cuda.device(dev):
         _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))

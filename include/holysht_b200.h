@@ -161,6 +161,10 @@ typedef struct holysht_contract_desc {
                               every 32-order row segment on one 128-byte line. */
   int table_layout;         /* HOLYSHT_TABLE_STRIDED (the strides above) or
                                HOLYSHT_TABLE_GROUPED (see below; strides ignored) */
+  int64_t m_offset;         /* global order of column 0 of the input, output and tables
+                               (a multiple of 32; 0 for whole transforms).  Lets one GPU
+                               contract a slice of the orders with the global l >= m
+                               triangle, for the order-partitioned multi-GPU transform. */
 } holysht_contract_desc;
 
 /* Table layouts of holysht_contract_desc.table_layout.
