@@ -97,6 +97,7 @@ class _GroupedTablesMixin:
     def _init_tables(self, names, hot_direction: int) -> None:
         self._table_names = tuple(names)
         self.vector = len(self._table_names) == 2
+        self._hot_direction = hot_direction
         self.register_buffer("_grouped_fwd", None, persistent=False)
         self.register_buffer("_grouped_inv", None, persistent=False)
         self.table(hot_direction)
@@ -124,13 +125,20 @@ class _GroupedTablesMixin:
         t = getattr(self, name)
         dense = tuple(getattr(self, n) for n in self._table_names)
         if t is None or t.device != dense[0].device:
-            t = ops.group_table(dense, direction)
+            # the non-hot direction serves autograd: for the vector map it is the
+            # conjugate transpose, whose grouped table carries the sign of W1
+            conj = self.vector and direction != self._hot_direction
+            t = ops.group_table(dense, direction, conj=conj)
             setattr(self, name, t)
         return t, None, True
 
 
 def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_cols, scale, flags, nlon=0):
     w0, w1, grouped = src.table(direction)
+    if grouped and src.vector:
+        # grouped vector tables already encode the conjugate map (see table())
+        assert bool(flags & _lib.FLAG_CONJ_W1) == (direction != src._hot_direction)
+        flags &= ~_lib.FLAG_CONJ_W1
     _contract(kind=_lib.KIND_VECTOR if src.vector else _lib.KIND_SCALAR, direction=direction,
               input=inp, output=out, w0=w0, w1=w1, batch=B, nlat=src.nlat, lmax=src.lmax, mmax=M,
               in_strides=in_vec_strides, out_strides=out_vec_strides, out_cols=out_cols, scale=scale,

@@ -212,6 +212,10 @@ int run_job(const Job& j, cudaStream_t stream) {
   }
   if (j.grouped && j.kind == HOLYSHT_KIND_REAL)
     return fail(HOLYSHT_ERR_INVALID, "the row-grouped table layout is for complex contractions");
+  if (j.grouped && j.kind == HOLYSHT_KIND_VECTOR && (j.flags & HOLYSHT_FLAG_CONJ_W1))
+    return fail(HOLYSHT_ERR_INVALID,
+                "grouped vector tables carry the sign of W1 (W0 + W1, W0 - W1); build the "
+                "conjugate map's table from (W0, -W1) instead of passing HOLYSHT_FLAG_CONJ_W1");
   Job jj = j;
   if (j.grouped) {
     // row-grouped layout: [R/4 groups][ceil(M/32) tiles][S steps][32 lanes][4 rows][tables]

@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
 #pragma unroll
     for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
   // vector kind: the four products per (row, batch), see the inner loop
-  constexpr int NQ = (KIND == KIND_VECTOR) ? 4 * NB : 1;
+  constexpr int NQ = (KIND == KIND_VECTOR) ? 2 * NB : 1;
   float2 vq[kRowsPerWarp][NQ];
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i)
@@ -363,41 +363,71 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
 
   // ---- staging of the input spectrum: [buf][step][plane][lane] ----
   constexpr int kStageElems = kChunk * PB * 32;
+  auto stage_one = [&](SE* dst, int e, int ls, int bl, int pl, int col, int c0) {
+    const int b = b0 + bl;
+    const int s = c0 + ls;
+    const int mm = m0 + col;
+    const bool ok = s < r_end && b < p.B && mm < p.M;
+    const long long off = ok ? (long long)b * p.in_bs + (long long)pl * p.in_ps + (long long)s * p.in_rs + mm : 0;
+    if constexpr (kAsyncStage) {
+      const SE* src = static_cast<const SE*>(p.in) + off;
+      cp_async_bytes(dst + e, src, ok ? (int)sizeof(SE) : 0, (int)sizeof(SE));
+    } else {
+      const TIN* src = static_cast<const TIN*>(p.in) + off;
+      dst[e] = ok ? static_cast<float>(*src) : 0.f;
+    }
+  };
+  // vector kind: one thread stages both components of a (step, batch, order)
+  // so it can combine them into u = c0 + i c1, v = c0 - i c1 without a barrier
+  constexpr int kStageUnits = (KIND == KIND_VECTOR) ? kStageElems / 2 : kStageElems;
   auto stage_chunk = [&](int chunk, int buf) {
     const int c0 = r_begin + chunk * kChunk;
     SE* dst = stage + buf * kStageElems;
-    for (int e = threadIdx.x; e < kStageElems; e += kThreads) {
+    for (int e = threadIdx.x; e < kStageUnits; e += kThreads) {
       const int col = e & 31;
-      const int pb = (e >> 5) % PB;
-      const int ls = e / (PB * 32);
-      const int b = b0 + pb / P;
-      const int pl = pb % P;
-      const int s = c0 + ls;
-      const int mm = m0 + col;
-      const bool ok = s < r_end && b < p.B && mm < p.M;
-      const long long off = ok ? (long long)b * p.in_bs + (long long)pl * p.in_ps +
-                                     (long long)s * p.in_rs + mm
-                               : 0;
-      if constexpr (kAsyncStage) {
-        const SE* src = static_cast<const SE*>(p.in) + off;
-        cp_async_bytes(dst + e, src, ok ? (int)sizeof(SE) : 0, (int)sizeof(SE));
+      if constexpr (KIND == KIND_VECTOR) {
+        const int bl = (e >> 5) % NB;
+        const int ls = e / (NB * 32);
+        const int i0 = (ls * PB + 2 * bl) * 32 + col;
+        stage_one(dst, i0, ls, bl, 0, col, c0);
+        stage_one(dst, i0 + 32, ls, bl, 1, col, c0);
       } else {
-        const TIN* src = static_cast<const TIN*>(p.in) + off;
-        dst[e] = ok ? static_cast<float>(*src) : 0.f;
+        const int pb = (e >> 5) % PB;
+        const int ls = e / (PB * 32);
+        stage_one(dst, e, ls, pb / P, pb % P, col, c0);
       }
     }
   };
   auto round_own = [&](int buf) {
     // each thread rounds the elements it staged itself (visible after its own wait)
-    if constexpr (KIND != KIND_REAL) {
+    if constexpr (KIND == KIND_SCALAR) {
       float2* d = reinterpret_cast<float2*>(stage + buf * kStageElems);
       for (int e = threadIdx.x; e < kStageElems; e += kThreads) {
         float2 v = d[e];
         d[e] = make_float2(round_to_bf16(v.x), round_to_bf16(v.y));
       }
-    } else {
+    } else if constexpr (KIND == KIND_REAL) {
       float* d = reinterpret_cast<float*>(stage + buf * kStageElems);
       for (int e = threadIdx.x; e < kStageElems; e += kThreads) d[e] = round_to_bf16(d[e]);
+    }
+  };
+  auto combine_own = [&](int buf, bool round) {
+    // vector kind: (c0, c1) -> (u, v) in place, on this thread's own pairs
+    if constexpr (KIND == KIND_VECTOR) {
+      float2* d = reinterpret_cast<float2*>(stage + buf * kStageElems);
+      for (int e = threadIdx.x; e < kStageUnits; e += kThreads) {
+        const int col = e & 31;
+        const int bl = (e >> 5) % NB;
+        const int ls = e / (NB * 32);
+        const int i0 = (ls * PB + 2 * bl) * 32 + col;
+        float2 a = d[i0], b = d[i0 + 32];
+        if (round) {
+          a = make_float2(round_to_bf16(a.x), round_to_bf16(a.y));
+          b = make_float2(round_to_bf16(b.x), round_to_bf16(b.y));
+        }
+        d[i0] = make_float2(a.x - b.y, a.y + b.x);
+        d[i0 + 32] = make_float2(a.x + b.y, a.y - b.x);
+      }
     }
   };
 
@@ -480,7 +510,10 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
         if (c + 1 < nchunks) stage_chunk(c + 1, buf ^ 1);
         cp_async_commit();
         cp_async_wait_1();
-        if (p.round_bf16) round_own(buf);
+        if (KIND == KIND_VECTOR)
+          combine_own(buf, p.round_bf16 != 0);
+        else if (p.round_bf16)
+          round_own(buf);
       } else {
         stage_chunk(c, buf);
       }
@@ -507,20 +540,25 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
             }
           }
         } else if constexpr (KIND == KIND_VECTOR) {
-          // four real-table products per batch, composed once after the loop:
-          // q0 = W0 c0, q1 = W1 c1, q2 = W1 c0, q3 = W0 c1
+          // sph - i tor = Wp u and sph + i tor = Wm v with Wp = W0 + s W1,
+          // Wm = W0 - s W1, u = c0 + i c1, v = c0 - i c1: two complex products
+          // per (row, batch) instead of four real-table products
 #pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const float2 c0v = xrow[(2 * b) * 32];
-            const float2 c1v = xrow[(2 * b + 1) * 32];
+          for (int i = 0; i < kRowsPerWarp; ++i) {
+            float wp, wm;
+            if constexpr (GROUPED) {
+              wp = wr0[cur][i];  // the grouped table already holds Wp, Wm
+              wm = wr1[cur][i];
+            } else {
+              wp = fmaf(w1s, wr1[cur][i], wr0[cur][i]);
+              wm = fmaf(-w1s, wr1[cur][i], wr0[cur][i]);
+            }
+            const float2 pwp = make_float2(wp, wp);
+            const float2 pwm = make_float2(wm, wm);
 #pragma unroll
-            for (int i = 0; i < kRowsPerWarp; ++i) {
-              const float2 pw0 = make_float2(wr0[cur][i], wr0[cur][i]);
-              const float2 pw1 = make_float2(wr1[cur][i], wr1[cur][i]);
-              vq[i][4 * b + 0] = ffma2(pw0, c0v, vq[i][4 * b + 0]);
-              vq[i][4 * b + 1] = ffma2(pw1, c1v, vq[i][4 * b + 1]);
-              vq[i][4 * b + 2] = ffma2(pw1, c0v, vq[i][4 * b + 2]);
-              vq[i][4 * b + 3] = ffma2(pw0, c1v, vq[i][4 * b + 3]);
+            for (int b = 0; b < NB; ++b) {
+              vq[i][2 * b] = ffma2(pwp, xrow[(2 * b) * 32], vq[i][2 * b]);
+              vq[i][2 * b + 1] = ffma2(pwm, xrow[(2 * b + 1) * 32], vq[i][2 * b + 1]);
             }
           }
         } else {
@@ -542,14 +580,14 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
   }
 
   if constexpr (KIND == KIND_VECTOR) {
-    // sph = q0 + i s q1,  tor = i s q2 - q3   (s = w1_sign)
+    // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
 #pragma unroll
     for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
-        const float2 q0 = vq[i][4 * b], q1 = vq[i][4 * b + 1], q2 = vq[i][4 * b + 2], q3 = vq[i][4 * b + 3];
-        acc[i][2 * b] = make_float2(q0.x - w1s * q1.y, q0.y + w1s * q1.x);
-        acc[i][2 * b + 1] = make_float2(-w1s * q2.y - q3.x, w1s * q2.x - q3.y);
+        const float2 pu = vq[i][2 * b], mv = vq[i][2 * b + 1];
+        acc[i][2 * b] = make_float2(0.5f * (mv.x + pu.x), 0.5f * (mv.y + pu.y));
+        acc[i][2 * b + 1] = make_float2(0.5f * (mv.y - pu.y), -0.5f * (mv.x - pu.x));
       }
   }
   // ---- cluster reduction of the partial sums through distributed smem ----

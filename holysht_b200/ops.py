@@ -224,16 +224,22 @@ def tile_table(weight_t: torch.Tensor) -> torch.Tensor:
     return padded.view(L, K, mt, 32).permute(0, 2, 1, 3).contiguous()
 
 
-def group_table(tables, direction: int) -> torch.Tensor:
+def group_table(tables, direction: int, conj: bool = False) -> torch.Tensor:
     """Row-grouped table for the contraction kernel (``HOLYSHT_TABLE_GROUPED``).
 
     ``tables``: one dense [lmax, nlat, mmax] table, or a (W0, W1) pair for the
     vector kind.  ``direction``: ``DIR_FORWARD`` (rows = l, steps = k) or
     ``DIR_INVERSE`` (rows = k, steps = l).  Result [R/4, ceil(M/32), S, 32, 4, T]:
     per 4-row group, m tile and step, the 32 lanes' rows x tables are
-    contiguous, zero outside the tables."""
+    contiguous, zero outside the tables.  A vector pair is stored as
+    (W0 + s W1, W0 - s W1), s = -1 when ``conj`` (the conjugate-transpose map
+    autograd needs), which is the form the kernel contracts."""
     if torch.is_tensor(tables):
         tables = (tables,)
+    if len(tables) == 2:
+        w0, w1 = tables
+        s1 = -1.0 if conj else 1.0
+        tables = (w0 + s1 * w1, w0 - s1 * w1)
     L, K, M = tables[0].shape
     mt = (M + 31) // 32
     fwd = direction == _lib.DIR_FORWARD

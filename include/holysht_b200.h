@@ -173,7 +173,11 @@ typedef struct holysht_contract_desc {
  *   T[g][mt][s][lane][r][t] = W_t(row = 4g + r, step = s, m = 32 mt + lane), table t
  * with g < ceil(R/4), mt < ceil(M/32), lane < 32, r < 4, t < (VECTOR ? 2 : 1);
  * entries outside the tables (and above the diagonal) are zero.  w0 points at
- * the start; w1 is ignored (both tables are interleaved). */
+ * the start; w1 is ignored (both tables are interleaved).  For VECTOR the two
+ * interleaved tables are t = 0: W0 + W1 and t = 1: W0 - W1 (the kernel applies
+ * sph - i tor = (W0 + W1)(c0 + i c1) and sph + i tor = (W0 - W1)(c0 - i c1),
+ * half the multiplies of the direct form); the conjugate map is a table built
+ * from (W0, -W1), and HOLYSHT_FLAG_CONJ_W1 is rejected with this layout. */
 #define HOLYSHT_TABLE_STRIDED 0
 #define HOLYSHT_TABLE_GROUPED 1
 

@@ -146,13 +146,16 @@ def test_group_table_layout():
     L, K, M = 6, 5, 37
     w0, w1 = torch.randn(L, K, M), torch.randn(L, K, M)
     g = hs.ops.group_table((w0, w1), _lib.DIR_FORWARD)
+    gc = hs.ops.group_table((w0, w1), _lib.DIR_FORWARD, conj=True)
     assert g.shape == (2, 2, K, 32, 4, 2)
     gi = hs.ops.group_table(w0, _lib.DIR_INVERSE)
     assert gi.shape == (2, 2, L, 32, 4, 1)
     for l in range(L):
         for k in range(K):
             for m in range(M):
-                assert g[l // 4, m // 32, k, m % 32, l % 4, 0] == w0[l, k, m]
-                assert g[l // 4, m // 32, k, m % 32, l % 4, 1] == w1[l, k, m]
+                # vector pairs are stored as (W0 + W1, W0 - W1), the form the kernel contracts
+                assert g[l // 4, m // 32, k, m % 32, l % 4, 0] == w0[l, k, m] + w1[l, k, m]
+                assert g[l // 4, m // 32, k, m % 32, l % 4, 1] == w0[l, k, m] - w1[l, k, m]
+                assert gc[l // 4, m // 32, k, m % 32, l % 4, 0] == w0[l, k, m] - w1[l, k, m]
                 assert gi[k // 4, m // 32, l, m % 32, k % 4, 0] == w0[l, k, m]
     assert torch.all(g[1, :, :, :, 2:, :] == 0)  # rows beyond lmax are zero
