@@ -49,16 +49,28 @@ constexpr int kRowsPerWarp = 4;
 constexpr int kRows = kWarps * kRowsPerWarp;  // output rows per CTA
 constexpr int kMTile = 32;                     // orders per CTA (one per lane)
 #ifndef HSB_CHUNK
-#define HSB_CHUNK 8
+#define HSB_CHUNK 16
 #endif
-constexpr int kChunk = HSB_CHUNK;              // reduction steps per smem stage
+#ifndef HSB_CHUNK_SMALL
+#define HSB_CHUNK_SMALL 8
+#endif
+// reduction steps per shared-memory stage (vector kind / the others)
+constexpr int kChunkVector = HSB_CHUNK;
+constexpr int kChunkSmall = HSB_CHUNK_SMALL;
+constexpr int kChunk = kChunkSmall;  // host-side minimum granularity
 #ifndef HSB_RING
-#define HSB_RING 8
+#define HSB_RING 16
+#endif
+#ifndef HSB_RING_SMALL
+#define HSB_RING_SMALL 8
 #endif
 #ifndef HSB_VECTOR_MIN_BLOCKS
 #define HSB_VECTOR_MIN_BLOCKS 1
 #endif
-constexpr int kRing = HSB_RING;                // register ring for table rows (steps in flight + 1)
+// register ring for table rows (steps in flight + 1): deep for the vector kind
+// (one CTA per SM, registers to spare), shallower for the two-CTA kinds
+constexpr int kRingVector = HSB_RING;
+constexpr int kRingSmall = HSB_RING_SMALL;
 #ifndef HSB_PREFETCH_CHUNKS
 #define HSB_PREFETCH_CHUNKS 2
 #endif
@@ -260,6 +272,8 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
     contract_kernel(const ContractParams p) {
   constexpr int P = KindTraits<KIND>::P;
   constexpr int PB = NB * P;  // staged planes per reduction step
+  constexpr int kRing = (KIND == KIND_VECTOR) ? kRingVector : kRingSmall;
+  constexpr int kChunk = (KIND == KIND_VECTOR) ? kChunkVector : kChunkSmall;
   constexpr int NA = Acc<KIND, NB>::NA;
   using SE = typename KindTraits<KIND>::SE;
   constexpr bool kAsyncStage = !std::is_same<TIN, __nv_bfloat16>::value;
