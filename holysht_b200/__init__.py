@@ -133,6 +133,23 @@ class _GroupedTablesMixin:
         return t, None, True
 
 
+DENSE_TC_MIN_BATCH = 128  # flattened batch from which the scalar forward runs on tcgen05
+
+
+def _dense_tc_eligible(src, B: int) -> bool:
+    """Scalar forward of a module with fp32 ``weights`` [M, L, K], nlat % 4 == 0
+    and a large flattened batch (N = 2B GEMM columns); ``HOLYSHT_DENSE_TC`` =
+    0 / 1 forces it off / on (when the layout allows)."""
+    import os
+
+    if src.vector or not hasattr(src, "weights") or src.weights.dtype != torch.float32 or src.nlat % 4:
+        return False
+    force = os.environ.get("HOLYSHT_DENSE_TC", "")
+    if force in ("0", "1"):
+        return force == "1"
+    return B >= DENSE_TC_MIN_BATCH
+
+
 def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_cols, scale, flags, nlon=0):
     w0, w1, grouped = src.table(direction)
     if grouped and src.vector:
@@ -163,8 +180,12 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         L, M = src.lmax, src.mmax
         shape = (B, 2, L, M) if vector else (B, L, M)
         out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
-        _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
-             M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+        if not round_bf16 and _dense_tc_eligible(src, B):
+            # large batch: the per-order contraction is a dense GEMM -> tcgen05
+            ops.legendre_forward_tc(out, spec, src.weights, M, scale)
+        else:
+            _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
+                 M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
         ctx.src = src
         ctx.dims = (B, K, W)
         ctx.scale = scale

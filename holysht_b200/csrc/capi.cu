@@ -10,11 +10,13 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <string>
 
 #include "../../include/holysht_b200.h"
 #include "contract.cuh"
 #include "elementwise.cuh"
+#include "tc_dense.cuh"
 
 namespace {
 
@@ -353,9 +355,134 @@ Job dense_job(int kind, int dir, int in_dtype, const void* in, void* out, const 
   return j;
 }
 
+// ---- tcgen05 dense path: host side ----
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// 3-D fp32 tensor map (inner dim contiguous), 128-byte swizzle, zero OOB fill
+bool make_map_3d(CUtensorMap* map, const void* base, unsigned long long d0, unsigned long long d1,
+                 unsigned long long d2, unsigned box0, unsigned box1) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * 4, d0 * d1 * 4};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+long long align256(long long v) { return (v + 255) & ~255LL; }
+
+long long tc_workspace(long long B, long long K, long long L, long long M) {
+  return align256(M * 2 * B * K * 4) + align256(M * L * 2 * B * 4);
+}
+
 }  // namespace
 
 extern "C" {
+
+int holysht_legendre_forward_tc_workspace(int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax, int64_t* bytes) {
+  if (!bytes) return fail(HOLYSHT_ERR_INVALID, "bytes pointer is null");
+  if (batch < 0 || nlat < 0 || lmax < 0 || mmax < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  *bytes = tc_workspace(batch, nlat, lmax, mmax);
+  return ok();
+}
+
+int holysht_legendre_forward_tc(void* out, const void* spec, int64_t spec_batch_stride, int64_t spec_row_stride,
+                                const float* table_mlk, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                float scale, void* workspace, int64_t workspace_bytes, void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  const long long B = batch, K = nlat, L = lmax, M = mmax;
+  if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  if (B == 0 || L == 0 || M == 0) return ok();
+  if (!out || !spec || !table_mlk || !workspace) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  if (K % 4 != 0 || K == 0) return fail(HOLYSHT_ERR_UNSUPPORTED, "tensor-core path needs nlat to be a multiple of 4");
+  if ((reinterpret_cast<uintptr_t>(table_mlk) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(HOLYSHT_ERR_INVALID, "table must be 16-byte and workspace 256-byte aligned");
+  if (2 * B > (1LL << 30) || !fits_int(K) || !fits_int(L) || !fits_int(M) || L > 65535)
+    return fail(HOLYSHT_ERR_INVALID, "extent out of range for the tensor-core path");
+  if (workspace_bytes < tc_workspace(B, K, L, M)) return fail(HOLYSHT_ERR_INVALID, "workspace too small");
+  if (spec_row_stride < M || spec_batch_stride < K * spec_row_stride)
+    return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
+  const long long N = 2 * B;
+  float* xt = static_cast<float*>(workspace);
+  float* D = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(M * N * K * 4));
+  const int Mrows = (int)(M < L ? M : L);
+
+  {  // spectrum -> Xt [M][2B][K]
+    dim3 grid((unsigned)((M + 31) / 32), (unsigned)((K + 31) / 32), (unsigned)B), block(32, 8);
+    if (B > 65535) return fail(HOLYSHT_ERR_INVALID, "batch too large for one launch");
+    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(spec), xt, (int)B, (int)K,
+                                                             (int)M, spec_batch_stride, spec_row_stride, scale);
+    if (int st = check_launch("transpose_in")) return st;
+  }
+  CUtensorMap map_a, map_b;
+  if (!make_map_3d(&map_a, table_mlk, K, L, M, hsb::tc::kBK, hsb::tc::kBM) ||
+      !make_map_3d(&map_b, xt, K, N, M, hsb::tc::kBK, hsb::tc::kBN))
+    return fail(HOLYSHT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable or rejected the tensors");
+  hsb::tc::DenseParams p;
+  p.K = (int)K;
+  p.L = (int)L;
+  p.M = Mrows;
+  p.N = (int)N;
+  p.n_nt = (int)((N + hsb::tc::kBN - 1) / hsb::tc::kBN);
+  p.n_bands = (int)((L + hsb::tc::kBM - 1) / hsb::tc::kBM);
+  p.D = D;
+  long long tiles = 0;
+  for (int q = 0; q < p.n_bands; ++q) {
+    const long long m_hi = std::min<long long>(Mrows, L - (long long)hsb::tc::kBM * q);
+    const long long m_lo = std::max<long long>(0, L - (long long)hsb::tc::kBM * (q + 1));
+    if (m_hi > m_lo) tiles += (m_hi - m_lo) * (q + 1) * p.n_nt;
+  }
+  if (tiles > INT_MAX) return fail(HOLYSHT_ERR_INVALID, "too many tiles");
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    if (cudaFuncSetAttribute(hsb::tc::dense_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             hsb::tc::kSmemBytes) != cudaSuccess)
+      return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the tensor-core kernel");
+    configured.fetch_or(bit);
+  }
+  if (tiles > 0) {
+    hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(map_a, map_b, p);
+    if (int st = check_launch("dense tcgen05 kernel")) return st;
+  }
+  {  // D [M][L][2B] -> out [B][L][M]
+    dim3 grid((unsigned)((M + 31) / 32), (unsigned)((B + 31) / 32), (unsigned)L), block(32, 8);
+    hsb::tc::transpose_out_kernel<<<grid, block, 0, stream>>>(D, static_cast<float2*>(out), (int)B, (int)L, (int)M,
+                                                              Mrows);
+    if (int st = check_launch("transpose_out")) return st;
+  }
+  return ok();
+}
+
+int holysht_tc_error_word(unsigned* value) {
+  if (!value) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  unsigned zero = 0;
+  if (cudaMemcpyFromSymbol(value, hsb::tc::g_tc_error, sizeof(unsigned)) != cudaSuccess ||
+      cudaMemcpyToSymbol(hsb::tc::g_tc_error, &zero, sizeof(unsigned)) != cudaSuccess)
+    return fail(HOLYSHT_ERR_CUDA, "cannot read the tensor-core error word");
+  return ok();
+}
+
 
 int holysht_version(void) { return 100; }
 

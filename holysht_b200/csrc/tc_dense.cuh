@@ -1,0 +1,370 @@
+// Dense per-order Legendre GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// For large batches (the 1024x2048, 16x64-slice configuration) the per-order
+// contraction is a real GEMM:  D_m[l, n] = sum_k A_m[l, k] X_m[k, n]  with
+// A_m = the order-m slice of the table in the torch-harmonics layout
+// W[m][l][k] (k contiguous, the module's `weights` buffer) and X_m the
+// spectrum of order m transposed to Xt[m][n][k] (n = 2*batch + re/im).
+//
+// FP32 accuracy from TF32 tensor cores: each operand is split in shared
+// memory into hi = rna_tf32(x) and lo = x - hi; the products hi*hi go to a
+// TMEM accumulator that is restarted every 32-wide k block and drained into
+// fp32 registers with round-to-nearest adds (the tensor core's own
+// accumulation truncates, an error that grows with the chain length), while
+// the small corrections hi*lo + lo*hi accumulate in a second TMEM block over
+// the whole k range (the lo*lo term is below fp32 resolution).
+//
+// CTA: one order m, 128 output rows l (TMEM lanes), 256 columns n (TMEM
+// columns), the full k range in 32-wide blocks.  Pipeline per k block:
+// TMA (cp.async.bulk.tensor, SWIZZLE_128B, K-major) -> all threads split the
+// stage in place -> one thread issues 4 k-steps x 3 tcgen05.mma (kind::tf32,
+// cta_group::1) -> tcgen05.commit frees the stage.  Two stages in flight.
+// Epilogue: tcgen05.ld 32x32b -> coalesced row stores of D[m][l][n].
+// Every mbarrier wait is bounded; a timeout sets a device error word and the
+// CTA drains and releases its TMEM instead of hanging.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hsb {
+namespace tc {
+
+constexpr int kBM = 128;       // rows (l) per CTA = TMEM lanes
+constexpr int kBN = 256;       // columns (n) per CTA = TMEM columns
+constexpr int kBK = 32;        // k per stage (one 128-byte swizzle row of fp32)
+constexpr int kTmemCols = 2 * kBN;  // D1 (per-block hi*hi) and D2 (corrections)
+constexpr int kStages = 2;
+constexpr int kThreads = 256;
+constexpr int kABytes = kBM * kBK * 4;   // 16 KiB
+constexpr int kBBytes = kBN * kBK * 4;   // 32 KiB
+constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;  // hi and lo of A and B
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr unsigned kWaitLimit = 1u << 26;
+
+// device error word: bit 0 = an mbarrier wait timed out
+__device__ unsigned g_tc_error = 0;
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// bounded wait: returns false (and records the timeout) instead of hanging
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  for (unsigned it = 0; it < kWaitLimit; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (it > 64) __nanosleep(64);
+  }
+  atomicOr(&g_tc_error, 1u);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];\n" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, SWIZZLE_128B (8-row groups of
+// 128-byte rows, 1024 bytes apart), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(unsigned smem_addr) {
+  const uint64_t start = (smem_addr & 0x3FFFFu) >> 4;
+  const uint64_t lbo = 1;             // unused for swizzled K-major layouts
+  const uint64_t sbo = 1024u >> 4;    // 8 rows x 128 bytes
+  return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = 256
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4)                      // D format f32
+         | (2u << 7) | (2u << 10)       // A, B format tf32
+         | ((uint32_t)(n >> 3) << 17)   // N / 8
+         | ((uint32_t)(m >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ void mma_tf32(unsigned tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         unsigned accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ float rna_tf32(float x) {
+  unsigned r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+struct DenseParams {
+  int K, L, M, N;  // nlat, lmax, orders with rows (< lmax), columns = 2 * batch
+  int n_nt;        // column tiles
+  int n_bands;     // ceil(L / 128)
+  float* D;        // [M][L][N]
+};
+
+// tile index -> (m, l-tile, n-tile); orders grouped in bands of equal row-tile
+// count, the bands with most row tiles first (longest work first)
+__device__ __forceinline__ bool decode(const DenseParams& p, int t, int& m, int& lt, int& nt) {
+  for (int q = p.n_bands - 1; q >= 0; --q) {
+    const int m_hi = min(p.M, p.L - kBM * q);
+    const int m_lo = max(0, p.L - kBM * (q + 1));
+    if (m_hi <= m_lo) continue;
+    const int per_m = (q + 1) * p.n_nt;
+    const int cnt = (m_hi - m_lo) * per_m;
+    if (t < cnt) {
+      m = m_lo + t / per_m;
+      const int r = t % per_m;
+      lt = r / p.n_nt;
+      nt = r % p.n_nt;
+      return true;
+    }
+    t -= cnt;
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    dense_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const DenseParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* d1_bar = empty + kStages;
+  unsigned* tmem_slot = reinterpret_cast<unsigned*>(d1_bar + 1);
+
+  int m, lt, nt;
+  if (!decode(p, blockIdx.x, m, lt, nt)) return;  // uniform per CTA
+  const int l0 = m + lt * kBM;
+  const int n0 = nt * kBN;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nk = (p.K + kBK - 1) / kBK;
+
+  auto a_hi = [&](int s) { return smem + s * kStageBytes; };
+  auto a_lo = [&](int s) { return smem + s * kStageBytes + kABytes; };
+  auto b_hi = [&](int s) { return smem + s * kStageBytes + 2 * kABytes; };
+  auto b_lo = [&](int s) { return smem + s * kStageBytes + 2 * kABytes + kBBytes; };
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(d1_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  const unsigned tmem = *tmem_slot;
+  constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
+
+  auto issue_loads = [&](int kb, int s) {
+    mbar_expect_tx(&full[s], kABytes + kBBytes);
+    tma_load_3d(a_hi(s), &map_a, &full[s], kb * kBK, l0, m);
+    tma_load_3d(b_hi(s), &map_b, &full[s], kb * kBK, n0, m);
+  };
+  if (tid == 0) issue_loads(0, 0);
+
+  // TMEM: columns [0, 256) = D1 (hi*hi of one k block, drained every block),
+  //       columns [256, 512) = D2 (hi*lo + lo*hi over all blocks)
+  const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31 (the rows this warp may read)
+  const int col_half = warp >> 2;   // warps 4-7 take the upper 128 columns
+  const unsigned trow = tmem + ((unsigned)(quarter * 32) << 16) + (unsigned)(col_half * (kBN / 2));
+  float acc[kBN / 2];
+#pragma unroll
+  for (int c = 0; c < kBN / 2; ++c) acc[c] = 0.f;
+
+  auto tmem_ld32 = [&](unsigned taddr, unsigned (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+  };
+  // add TMEM columns [base, base + 128) of this thread's row into acc (round to nearest)
+  auto drain_into_acc = [&](unsigned base) {
+#pragma unroll
+    for (int cc = 0; cc < kBN / 2; cc += 32) {
+      unsigned r[32];
+      tmem_ld32(base + (unsigned)cc, r);
+      asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+      for (int q = 0; q < 32; ++q) acc[cc + q] += __uint_as_float(r[q]);
+    }
+  };
+
+  for (int kb = 0; kb < nk; ++kb) {
+    const int s = kb & 1;
+    const unsigned ph = (kb >> 1) & 1;
+    if (tid == 0 && kb + 1 < nk) {
+      const int s2 = s ^ 1;
+      if (kb + 1 >= kStages) mbar_wait(&empty[s2], ((kb + 1) / kStages - 1) & 1);  // MMAs of kb-1 done
+      issue_loads(kb + 1, s2);
+    }
+    mbar_wait(&full[s], ph);
+    // split the stage in place: hi = rna_tf32(x) where x was, lo = x - hi alongside
+    {
+      float4* ah = reinterpret_cast<float4*>(a_hi(s));
+      float4* al = reinterpret_cast<float4*>(a_lo(s));
+      for (int i = tid; i < kABytes / 16; i += kThreads) {
+        const float4 v = ah[i];
+        const float4 h = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
+        ah[i] = h;
+        al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+      }
+      float4* bh = reinterpret_cast<float4*>(b_hi(s));
+      float4* bl = reinterpret_cast<float4*>(b_lo(s));
+      for (int i = tid; i < kBBytes / 16; i += kThreads) {
+        const float4 v = bh[i];
+        const float4 h = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
+        bh[i] = h;
+        bl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    // drain the previous block's D1 before this block's MMAs overwrite it
+    if (kb > 0) {
+      mbar_wait(d1_bar, (kb - 1) & 1);
+      asm volatile("tcgen05.fence::after_thread_sync;\n");
+      drain_into_acc(trow);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n");
+    __syncthreads();
+    if (warp == 1 && lane == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;\n");
+      const unsigned ahi = smem_u32(a_hi(s)), alo = smem_u32(a_lo(s));
+      const unsigned bhi = smem_u32(b_hi(s)), blo = smem_u32(b_lo(s));
+#pragma unroll
+      for (int j = 0; j < kBK / 8; ++j) {  // 8 tf32 = 32 bytes per k-step
+        const unsigned off = j * 32;
+        mma_tf32(tmem, sw128_desc(ahi + off), sw128_desc(bhi + off), idesc, j > 0 ? 1u : 0u);
+        const unsigned acc2 = (kb > 0 || j > 0) ? 1u : 0u;
+        mma_tf32(tmem + kBN, sw128_desc(ahi + off), sw128_desc(blo + off), idesc, acc2);
+        mma_tf32(tmem + kBN, sw128_desc(alo + off), sw128_desc(bhi + off), idesc, 1u);
+      }
+      mma_commit(&empty[s]);
+      mma_commit(d1_bar);
+    }
+  }
+
+  // ---- epilogue: last D1 block and the corrections D2 -> D[m][l][n] ----
+  mbar_wait(d1_bar, (nk - 1) & 1);
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  drain_into_acc(trow);
+  drain_into_acc(trow + kBN);
+  {
+    const int row = l0 + quarter * 32 + lane;
+    const int nb = n0 + col_half * (kBN / 2);
+    if (row < p.L) {
+      float* dst = p.D + ((size_t)m * p.L + row) * p.N + nb;
+      if (nb + kBN / 2 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < kBN / 8; ++q)
+          reinterpret_cast<float4*>(dst)[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kBN / 2; ++q)
+          if (nb + q < p.N) dst[q] = acc[q];
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// spec [B][K][W] complex (rfft layout, orders < M used) -> Xt [M][2B][K] fp32 * scale
+__global__ void transpose_in_kernel(const float2* __restrict__ spec, float* __restrict__ xt, int B, int K, int M,
+                                    long long spec_bs, long long spec_rs, float scale) {
+  __shared__ float2 tile[32][33];
+  const int b = blockIdx.z;
+  const int m0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int i = ty; i < 32; i += 8) {
+    const int k = k0 + i, m = m0 + tx;
+    tile[i][tx] = (k < K && m < M) ? spec[(long long)b * spec_bs + (long long)k * spec_rs + m] : make_float2(0.f, 0.f);
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int m = m0 + i, k = k0 + tx;
+    if (m < M && k < K) {
+      const float2 v = tile[tx][i];
+      float* row = xt + ((long long)m * (2LL * B) + 2LL * b) * K;
+      row[k] = v.x * scale;
+      row[K + k] = v.y * scale;
+    }
+  }
+}
+
+// D [M][L][2B] -> out [B][L][M] complex, exact zeros for m > l and for m >= Mrows
+__global__ void transpose_out_kernel(const float* __restrict__ D, float2* __restrict__ out, int B, int L, int M,
+                                     int Mrows) {
+  __shared__ float2 tile[32][33];
+  const int l = blockIdx.z;
+  const int m0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int i = ty; i < 32; i += 8) {
+    const int m = m0 + i, b = b0 + tx;
+    float2 v = make_float2(0.f, 0.f);
+    if (m < Mrows && m <= l && b < B) {
+      const float* src = D + ((long long)m * L + l) * (2LL * B) + 2LL * b;
+      v = make_float2(src[0], src[1]);
+    }
+    tile[i][tx] = v;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int b = b0 + i, m = m0 + tx;
+    if (b < B && m < M) out[((long long)b * L + l) * M + m] = tile[tx][i];
+  }
+}
+
+}  // namespace tc
+}  // namespace hsb

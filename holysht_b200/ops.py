@@ -35,6 +35,8 @@ __all__ = [
     "legendre_contract",
     "tile_table",
     "group_table",
+    "legendre_forward_tc",
+    "tc_error_word",
 ]
 
 
@@ -309,3 +311,36 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
     d.m_offset = m_offset
     with torch.cuda.device(dev):
         _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))
+
+
+def legendre_forward_tc(output: torch.Tensor, spec: torch.Tensor, table_mlk: torch.Tensor, mmax: int,
+                        scale: float = 1.0) -> None:
+    """Dense tensor-core forward: output [B, L, M] complex64 =
+    scale * sum_k table_mlk[m, l, k] * spec[b, k, m] (l >= m), with ``spec`` an
+    rfft-layout complex64 [B, K, W >= M] tensor (contiguous rows) and
+    ``table_mlk`` float32 [M, L, K] (the torch-harmonics ``weights`` layout).
+    The GEMM workspace comes from torch's caching allocator."""
+    dev = _cuda(output, spec, table_mlk)
+    _require(spec.dtype == torch.complex64 and output.dtype == torch.complex64, "spectrum and output are complex64")
+    _require(table_mlk.dtype == torch.float32 and table_mlk.is_contiguous(), "table must be contiguous float32")
+    _require(spec.dim() == 3 and spec.stride(2) == 1, "spectrum must be [B, K, W] with contiguous orders")
+    M, L, K = table_mlk.shape
+    _require(int(mmax) == M, "mmax must match the table")
+    B = spec.size(0)
+    _require(spec.size(1) == K and spec.size(2) >= M, "spectrum must be [B, nlat, >= mmax]")
+    _require(output.is_contiguous() and tuple(output.shape) == (B, L, M), "output must be [B, lmax, mmax]")
+    lib = _lib.load()
+    nbytes = ctypes.c_int64(0)
+    _lib.check(lib.holysht_legendre_forward_tc_workspace(B, K, L, M, ctypes.byref(nbytes)))
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=dev)
+        _lib.check(lib.holysht_legendre_forward_tc(
+            _p(output), _p(spec), spec.stride(0), spec.stride(1), _p(table_mlk), B, K, L, M, float(scale),
+            _p(ws), nbytes.value, _stream(dev)))
+
+
+def tc_error_word() -> int:
+    """Read and clear the tensor-core kernel's device error word (synchronous)."""
+    v = ctypes.c_uint(0)
+    _lib.check(_lib.load().holysht_tc_error_word(ctypes.byref(v)))
+    return int(v.value)

@@ -183,6 +183,31 @@ typedef struct holysht_contract_desc {
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Dense tensor-core forward (no counterpart operator in the reference; the
+ * reference's TF32 wmma path, cuda/fused_legendre.cu:635-714, is its
+ * approximate analogue).  For large batches the per-order contraction is a
+ * GEMM; this entry runs it on tcgen05 tensor cores with a three-product
+ * split-TF32 scheme (fp32-level accuracy):
+ *   out[b,l,m] = scale * sum_k table_mlk[m,l,k] * spec[b,k,m]    (l >= m; 0 otherwise)
+ * spec: complex64, element (b,k,m) at spec + b*spec_batch_stride + k*spec_row_stride + m
+ * (the rfft output can be passed as is, with spec_row_stride = nlon/2+1);
+ * table_mlk: float32 [mmax][lmax][nlat] (the torch-harmonics `weights` layout),
+ * nlat a multiple of 4; out: complex64 [B][lmax][mmax].
+ * workspace: caller-allocated device memory of at least the size reported by
+ * holysht_legendre_forward_tc_workspace (256-byte aligned); it holds the
+ * transposed spectrum and the GEMM output between the three launches. */
+int holysht_legendre_forward_tc_workspace(int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                          int64_t* bytes);
+int holysht_legendre_forward_tc(void* out, const void* spec, int64_t spec_batch_stride,
+                                int64_t spec_row_stride, const float* table_mlk, int64_t batch,
+                                int64_t nlat, int64_t lmax, int64_t mmax, float scale, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* Diagnostics: reads and clears the tensor-core kernel's device error word
+ * (bit 0: a pipeline wait gave up instead of hanging).  Synchronous. */
+int holysht_tc_error_word(unsigned* value);
+
 #ifdef __cplusplus
 }
 #endif

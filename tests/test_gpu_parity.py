@@ -387,3 +387,40 @@ def test_graphed_module_matches_eager():
     torch.testing.assert_close(g(x), ref, rtol=0, atol=0)
     x2 = torch.randn_like(x)
     torch.testing.assert_close(g(x2), m(x2), rtol=0, atol=0)
+
+
+# ------------------------------------------------------------- tensor-core dense path
+
+TC_SHAPES = [  # (B, K, L, M, W)
+    (4, 32, 128, 129, 129),
+    (128, 64, 200, 201, 260),
+    (100, 36, 130, 65, 65),
+    (200, 512, 300, 301, 301),
+]
+
+
+@pytest.mark.parametrize("B,K,L,M,W", TC_SHAPES)
+def test_dense_tensor_core_forward_matches_oracle(B, K, L, M, W):
+    rng = np.random.default_rng(B + K)
+    w = tri_table(rng, L, K, M)
+    spec = cplx(rng, (B, K, W))
+    tab = torch.from_numpy(np.ascontiguousarray(w.transpose(2, 0, 1))).to(DEV)  # [M, L, K]
+    out = torch.full((B, L, M), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    ops.legendre_forward_tc(out, torch.from_numpy(spec).to(DEV), tab, M, scale=1.5)
+    ref = 1.5 * orc.legendre_forward(spec[..., :M].astype(np.complex128), w.astype(np.float64))
+    assert_fp32_close(out, ref)
+    upper = np.arange(M)[None, :] > np.arange(L)[:, None]
+    assert np.all(out.cpu().numpy()[:, upper] == 0)
+    assert ops.tc_error_word() == 0
+
+
+def test_scalar_module_uses_tensor_cores_for_large_batches(monkeypatch):
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((2, 80, 64, 128)).astype(np.float32)  # 160 slices >= 128
+    m = hs.RealSHT(64, 128).to(DEV)
+    xt = torch.from_numpy(x).to(DEV)
+    got = m(xt)
+    assert_fp32_close(got, _module_oracle_scalar(m, x.astype(np.float64)))
+    monkeypatch.setenv("HOLYSHT_DENSE_TC", "0")
+    simt = m(xt)
+    assert_fp32_close(got, simt.cpu().numpy().astype(np.complex128), rel=5e-7, maxabs=5e-6)
