@@ -312,6 +312,7 @@ def cpu_baseline(vsht, x):
 
     from oracle import sht_oracle as orc
 
+    _use_all_cores()
     w = np.stack([vsht.w0.float().cpu().numpy(), vsht.w1.float().cpu().numpy()])
     fn = orc.CpuForwardBaseline(w, vector=True)
     xh = x.cpu().numpy()
@@ -324,6 +325,16 @@ def cpu_baseline(vsht, x):
         times.append((time.perf_counter() - t) * 1e3)
     return {"value": round(statistics.median(times), 3), "unit": UNIT, "cores": _blas_threads(), "kind": "port",
             "sample": f"full workload (4,2,512,1024), median of {len(times)} runs"}
+
+
+def _use_all_cores():
+    """Give the CPU baseline every host core (torchrun sets OMP_NUM_THREADS=1)."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(os.cpu_count())
+    except Exception:
+        pass
 
 
 def _blas_threads():
@@ -344,6 +355,7 @@ def run_reference(args, rank, world):
 
     from oracle import sht_oracle as orc
 
+    _use_all_cores()
     w = orc.vector_forward_tables(NLAT, NLON).astype(np.float32)
     fn = orc.CpuForwardBaseline(w, vector=True)
     rng = np.random.default_rng(1)
