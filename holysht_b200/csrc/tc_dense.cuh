@@ -7,12 +7,12 @@
 // spectrum of order m transposed to Xt[m][n][k] (n = 2*batch + re/im).
 //
 // FP32 accuracy from TF32 tensor cores: each operand is split in shared
-// memory into hi = rna_tf32(x) and lo = x - hi; the products hi*hi go to a
-// TMEM accumulator that is restarted every 32-wide k block and drained into
-// fp32 registers with round-to-nearest adds (the tensor core's own
-// accumulation truncates, an error that grows with the chain length), while
-// the small corrections hi*lo + lo*hi accumulate in a second TMEM block over
-// the whole k range (the lo*lo term is below fp32 resolution).
+// memory into hi = rna_tf32(x) and lo = x - hi; the products hi*hi + hi*lo +
+// lo*hi of one 32-wide k block go to a TMEM accumulator that starts from zero,
+// and the block sums are added into fp32 registers with round-to-nearest
+// (the tensor core's own accumulation truncates, an error that grows with the
+// chain length; the lo*lo term is below fp32 resolution).  Two TMEM slots
+// alternate so the warps drain one block while the tensor core runs the next.
 //
 // CTA: one order m, 128 output rows l (TMEM lanes), 256 columns n (TMEM
 // columns), the full k range in 32-wide blocks.  Pipeline per k block:
@@ -34,7 +34,7 @@ namespace tc {
 constexpr int kBM = 128;       // rows (l) per CTA = TMEM lanes
 constexpr int kBN = 256;       // columns (n) per CTA = TMEM columns
 constexpr int kBK = 32;        // k per stage (one 128-byte swizzle row of fp32)
-constexpr int kTmemCols = 2 * kBN;  // D1 (per-block hi*hi) and D2 (corrections)
+constexpr int kTmemCols = 2 * kBN;  // two accumulator slots (k blocks alternate)
 constexpr int kStages = 2;
 constexpr int kThreads = 256;
 constexpr int kABytes = kBM * kBK * 4;   // 16 KiB
@@ -57,6 +57,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
@@ -164,8 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   uint64_t* empty = full + kStages;
-  uint64_t* d1_bar = empty + kStages;
-  unsigned* tmem_slot = reinterpret_cast<unsigned*>(d1_bar + 1);
+  uint64_t* d1_full = empty + kStages;
+  uint64_t* d1_free = d1_full + 2;
+  unsigned* tmem_slot = reinterpret_cast<unsigned*>(d1_free + 2);
 
   int m, lt, nt;
   if (!decode(p, blockIdx.x, m, lt, nt)) return;  // uniform per CTA
@@ -186,7 +191,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(d1_bar, 1);
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&d1_full[q], 1);
+      mbar_init(&d1_free[q], kThreads / 32);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) {
@@ -207,8 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   if (tid == 0) issue_loads(0, 0);
 
-  // TMEM: columns [0, 256) = D1 (hi*hi of one k block, drained every block),
-  //       columns [256, 512) = D2 (hi*lo + lo*hi over all blocks)
+  // TMEM: two accumulator slots of 256 columns; k block kb accumulates all its
+  // products (hi*hi + hi*lo + lo*hi) into slot kb & 1 from zero, and the warps
+  // drain it into fp32 registers (round to nearest) while the tensor core works
+  // on the next block in the other slot.
   const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31 (the rows this warp may read)
   const int col_half = warp >> 2;   // warps 4-7 take the upper 128 columns
   const unsigned trow = tmem + ((unsigned)(quarter * 32) << 16) + (unsigned)(col_half * (kBN / 2));
@@ -236,6 +246,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q = 0; q < 32; ++q) acc[cc + q] += __uint_as_float(r[q]);
     }
+  };
+  auto drain_block = [&](int kb) {
+    const int slot = kb & 1;
+    mbar_wait(&d1_full[slot], (kb >> 1) & 1);
+    __syncwarp();  // tcgen05.ld is warp-aligned: reconverge after the per-lane wait
+    asm volatile("tcgen05.fence::after_thread_sync;\n");
+    drain_into_acc(trow + (unsigned)(slot * kBN));
+    asm volatile("tcgen05.fence::before_thread_sync;\n");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&d1_free[slot]);
   };
 
   for (int kb = 0; kb < nk; ++kb) {
@@ -267,36 +287,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-    // drain the previous block's D1 before this block's MMAs overwrite it
-    if (kb > 0) {
-      mbar_wait(d1_bar, (kb - 1) & 1);
-      asm volatile("tcgen05.fence::after_thread_sync;\n");
-      drain_into_acc(trow);
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;\n");
     __syncthreads();
     if (warp == 1 && lane == 0) {
+      const int slot = kb & 1;
+      if (kb >= 2) mbar_wait(&d1_free[slot], ((kb >> 1) - 1) & 1);  // block kb-2 drained
       asm volatile("tcgen05.fence::after_thread_sync;\n");
+      const unsigned d = tmem + (unsigned)(slot * kBN);
       const unsigned ahi = smem_u32(a_hi(s)), alo = smem_u32(a_lo(s));
       const unsigned bhi = smem_u32(b_hi(s)), blo = smem_u32(b_lo(s));
 #pragma unroll
       for (int j = 0; j < kBK / 8; ++j) {  // 8 tf32 = 32 bytes per k-step
         const unsigned off = j * 32;
-        mma_tf32(tmem, sw128_desc(ahi + off), sw128_desc(bhi + off), idesc, j > 0 ? 1u : 0u);
-        const unsigned acc2 = (kb > 0 || j > 0) ? 1u : 0u;
-        mma_tf32(tmem + kBN, sw128_desc(ahi + off), sw128_desc(blo + off), idesc, acc2);
-        mma_tf32(tmem + kBN, sw128_desc(alo + off), sw128_desc(bhi + off), idesc, 1u);
+        mma_tf32(d, sw128_desc(ahi + off), sw128_desc(bhi + off), idesc, j > 0 ? 1u : 0u);
+        mma_tf32(d, sw128_desc(ahi + off), sw128_desc(blo + off), idesc, 1u);
+        mma_tf32(d, sw128_desc(alo + off), sw128_desc(bhi + off), idesc, 1u);
       }
       mma_commit(&empty[s]);
-      mma_commit(d1_bar);
+      mma_commit(&d1_full[slot]);
     }
+    __syncwarp();
+    if (kb > 0) drain_block(kb - 1);
   }
 
-  // ---- epilogue: last D1 block and the corrections D2 -> D[m][l][n] ----
-  mbar_wait(d1_bar, (nk - 1) & 1);
-  asm volatile("tcgen05.fence::after_thread_sync;\n");
-  drain_into_acc(trow);
-  drain_into_acc(trow + kBN);
+  // ---- epilogue: the last block, then D[m][l][n] from the registers ----
+  drain_block(nk - 1);
   {
     const int row = l0 + quarter * 32 + lane;
     const int nb = n0 + col_half * (kBN / 2);
