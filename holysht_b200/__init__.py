@@ -119,6 +119,26 @@ class _GroupedTablesMixin:
     def _drop_grouped(self) -> None:
         self._grouped_fwd = None
         self._grouped_inv = None
+        if hasattr(self, "_dense_inv"):
+            self._dense_inv = None
+
+    def dense_table(self, direction: int) -> torch.Tensor:
+        """Per-order fp32 table for the tensor-core path: forward [mmax, lmax, nlat]
+        (the reference's ``weights`` / ``pct`` layout), inverse [mmax, nlat, lmax]
+        (built on first use, non-persistent buffer)."""
+        mlk = getattr(self, self._mlk_name)
+        if mlk.dtype != torch.float32:
+            mlk = getattr(self, self._table_names[0]).permute(2, 0, 1)
+        if direction == _lib.DIR_FORWARD:
+            return mlk.contiguous()
+        t = getattr(self, "_dense_inv", None)
+        if t is None or t.device != mlk.device:
+            t = mlk.transpose(1, 2).contiguous()
+            if "_dense_inv" not in self._buffers:
+                self.register_buffer("_dense_inv", t, persistent=False)
+            else:
+                self._dense_inv = t
+        return t
 
     def table(self, direction: int):
         name = "_grouped_fwd" if direction == _lib.DIR_FORWARD else "_grouped_inv"
@@ -136,13 +156,17 @@ class _GroupedTablesMixin:
 DENSE_TC_MIN_BATCH = 128  # flattened batch from which the scalar forward runs on tcgen05
 
 
-def _dense_tc_eligible(src, B: int) -> bool:
-    """Scalar forward of a module with fp32 ``weights`` [M, L, K], nlat % 4 == 0
-    and a large flattened batch (N = 2B GEMM columns); ``HOLYSHT_DENSE_TC`` =
-    0 / 1 forces it off / on (when the layout allows)."""
+def _dense_tc_eligible(src, B: int, direction: int) -> bool:
+    """Scalar modules with fp32 per-order tables, a reduction extent that is a
+    multiple of 4 (nlat forward, lmax inverse) and a large flattened batch
+    (N = 2B GEMM columns).  ``HOLYSHT_DENSE_TC`` = 0 / 1 forces it off / on
+    (when the layout allows)."""
     import os
 
-    if src.vector or not hasattr(src, "weights") or src.weights.dtype != torch.float32 or src.nlat % 4:
+    if src.vector or not hasattr(src, "dense_table"):
+        return False
+    red = src.nlat if direction == _lib.DIR_FORWARD else src.lmax
+    if red % 4:
         return False
     force = os.environ.get("HOLYSHT_DENSE_TC", "")
     if force in ("0", "1"):
@@ -180,9 +204,10 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         L, M = src.lmax, src.mmax
         shape = (B, 2, L, M) if vector else (B, L, M)
         out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
-        if not round_bf16 and _dense_tc_eligible(src, B):
+        if _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
             # large batch: the per-order contraction is a dense GEMM -> tcgen05
-            ops.legendre_forward_tc(out, spec, src.weights, M, scale)
+            ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
+                                  lmax=L, mmax=M, scale=scale, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
         else:
             _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
                  M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
@@ -199,8 +224,12 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         g = grad.contiguous()
         shape = (B, 2, K, W) if vector else (B, K, W)
         gspec = torch.empty(shape, device=g.device, dtype=torch.complex64)
-        _run(src, _lib.DIR_INVERSE, g, gspec, B, src.mmax, _strides3(g, vector), _strides3(gspec, vector),
-             W, ctx.scale, _lib.FLAG_CONJ_W1 if vector else 0)
+        if _dense_tc_eligible(src, B, _lib.DIR_INVERSE):
+            ops.legendre_dense_tc(_lib.DIR_INVERSE, gspec, g, src.dense_table(_lib.DIR_INVERSE), nlat=K,
+                                  lmax=src.lmax, mmax=src.mmax, scale=ctx.scale)
+        else:
+            _run(src, _lib.DIR_INVERSE, g, gspec, B, src.mmax, _strides3(g, vector), _strides3(gspec, vector),
+                 W, ctx.scale, _lib.FLAG_CONJ_W1 if vector else 0)
         return gspec, None, None, None
 
 
@@ -219,8 +248,12 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
         c = coef.contiguous()
         shape = (B, 2, K, W) if vector else (B, K, W)
         spec = torch.empty(shape, device=c.device, dtype=torch.complex64)
-        _run(src, _lib.DIR_INVERSE, c, spec, B, M, _strides3(c, vector), _strides3(spec, vector),
-             W, 1.0, _lib.FLAG_IRFFT_PREP, nlon)
+        if _dense_tc_eligible(src, B, _lib.DIR_INVERSE):
+            ops.legendre_dense_tc(_lib.DIR_INVERSE, spec, c, src.dense_table(_lib.DIR_INVERSE), nlat=K, lmax=L,
+                                  mmax=M, scale=1.0, flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
+        else:
+            _run(src, _lib.DIR_INVERSE, c, spec, B, M, _strides3(c, vector), _strides3(spec, vector),
+                 W, 1.0, _lib.FLAG_IRFFT_PREP, nlon)
         ctx.src = src
         ctx.dims = (B, K, W, L, M)
         ctx.nyq = nlon // 2 if nlon % 2 == 0 else None
@@ -238,8 +271,12 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
             g[..., ctx.nyq] = g[..., ctx.nyq].real.to(g.dtype)
         shape = (B, 2, L, M) if vector else (B, L, M)
         gc = torch.empty(shape, device=g.device, dtype=torch.complex64)
-        _run(src, _lib.DIR_FORWARD, g, gc, B, M, _strides3(g, vector), _strides3(gc, vector),
-             M, 1.0, _lib.FLAG_CONJ_W1 if vector else 0)
+        if _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
+            ops.legendre_dense_tc(_lib.DIR_FORWARD, gc, g, src.dense_table(_lib.DIR_FORWARD), nlat=K, lmax=L,
+                                  mmax=M, scale=1.0)
+        else:
+            _run(src, _lib.DIR_FORWARD, g, gc, B, M, _strides3(g, vector), _strides3(gc, vector),
+                 M, 1.0, _lib.FLAG_CONJ_W1 if vector else 0)
         return gc, None, None
 
 
@@ -493,6 +530,7 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
         wt = torch.from_numpy(w)
         self.register_buffer("weights", wt.to(w_dtype))
         self.register_buffer("weight_t", wt.permute(1, 2, 0).contiguous())
+        self._mlk_name = "weights"
         self._init_tables(("weight_t",), _lib.DIR_FORWARD)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -518,6 +556,7 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
         pt = torch.from_numpy(p)
         self.register_buffer("pct", pt)
         self.register_buffer("pct_t", pt.permute(1, 2, 0).contiguous())
+        self._mlk_name = "pct"
         self._init_tables(("pct_t",), _lib.DIR_INVERSE)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -552,6 +591,7 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
         self.register_buffer("w1", wt[1].to(w_dtype))
         self.register_buffer("w0_t", wt[0].permute(1, 2, 0).contiguous())
         self.register_buffer("w1_t", wt[1].permute(1, 2, 0).contiguous())
+        self._mlk_name = "w0"
         self._init_tables(("w0_t", "w1_t"), _lib.DIR_FORWARD)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -579,6 +619,7 @@ class InverseRealVectorSHT(_GroupedTablesMixin, nn.Module):
         self.register_buffer("d1", dt[1].contiguous())
         self.register_buffer("d0_t", dt[0].permute(1, 2, 0).contiguous())
         self.register_buffer("d1_t", dt[1].permute(1, 2, 0).contiguous())
+        self._mlk_name = "d0"
         self._init_tables(("d0_t", "d1_t"), _lib.DIR_INVERSE)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:

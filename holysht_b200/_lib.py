@@ -38,8 +38,8 @@ EXPORTS = (
     "holysht_fused_vector_forward_recompose_real",
     "holysht_sht_prepare_irfft",
     "holysht_legendre_contract",
-    "holysht_legendre_forward_tc_workspace",
-    "holysht_legendre_forward_tc",
+    "holysht_legendre_dense_tc_workspace",
+    "holysht_legendre_dense_tc",
     "holysht_tc_error_word",
 )
 
@@ -109,9 +109,9 @@ def load() -> ctypes.CDLL:
             "holysht_fused_vector_forward_recompose_real": ([vp, vp, vp, i64, i64, i64, vp], i32),
             "holysht_sht_prepare_irfft": ([vp, i64, i64, i64, i64, vp], i32),
             "holysht_legendre_contract": ([ctypes.POINTER(ContractDesc), vp], i32),
-            "holysht_legendre_forward_tc_workspace": ([i64, i64, i64, i64, ctypes.POINTER(ctypes.c_int64)], i32),
-            "holysht_legendre_forward_tc": ([vp, vp, i64, i64, vp, i64, i64, i64, i64, ctypes.c_float, vp, i64, vp],
-                                            i32),
+            "holysht_legendre_dense_tc_workspace": ([i32, i64, i64, i64, i64, ctypes.POINTER(ctypes.c_int64)], i32),
+            "holysht_legendre_dense_tc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,
+                                           ctypes.c_float, i32, i64, vp, i64, vp], i32),
             "holysht_tc_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
         }
         for name, (args, res) in sig.items():

@@ -389,86 +389,115 @@ bool make_map_3d(CUtensorMap* map, const void* base, unsigned long long d0, unsi
 
 long long align256(long long v) { return (v + 255) & ~255LL; }
 
-long long tc_workspace(long long B, long long K, long long L, long long M) {
-  return align256(M * 2 * B * K * 4) + align256(M * L * 2 * B * 4);
+long long tc_workspace(long long B, long long R, long long S, long long M) {
+  return align256(M * 2 * B * S * 4) + align256(M * R * 2 * B * 4);
 }
 
 }  // namespace
 
 extern "C" {
 
-int holysht_legendre_forward_tc_workspace(int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax, int64_t* bytes) {
+int holysht_legendre_dense_tc_workspace(int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                        int64_t* bytes) {
   if (!bytes) return fail(HOLYSHT_ERR_INVALID, "bytes pointer is null");
+  if (direction != HOLYSHT_DIR_FORWARD && direction != HOLYSHT_DIR_INVERSE)
+    return fail(HOLYSHT_ERR_INVALID, "unknown direction %d", direction);
   if (batch < 0 || nlat < 0 || lmax < 0 || mmax < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
-  *bytes = tc_workspace(batch, nlat, lmax, mmax);
+  const bool fwd = direction == HOLYSHT_DIR_FORWARD;
+  const long long Mrows = mmax < lmax ? mmax : lmax;
+  *bytes = tc_workspace(batch, fwd ? lmax : nlat, fwd ? nlat : lmax, Mrows);
   return ok();
 }
 
-int holysht_legendre_forward_tc(void* out, const void* spec, int64_t spec_batch_stride, int64_t spec_row_stride,
-                                const float* table_mlk, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
-                                float scale, void* workspace, int64_t workspace_bytes, void* stream_v) {
+int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride, int64_t out_row_stride,
+                              int64_t out_cols, const void* in, int64_t in_batch_stride, int64_t in_row_stride,
+                              const float* table, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                              float scale, int flags, int64_t nlon, void* workspace, int64_t workspace_bytes,
+                              void* stream_v) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (direction != HOLYSHT_DIR_FORWARD && direction != HOLYSHT_DIR_INVERSE)
+    return fail(HOLYSHT_ERR_INVALID, "unknown direction %d", direction);
+  if (flags & ~(HOLYSHT_FLAG_ROUND_BF16 | HOLYSHT_FLAG_IRFFT_PREP))
+    return fail(HOLYSHT_ERR_INVALID, "unsupported flags 0x%x", flags);
+  const bool fwd = direction == HOLYSHT_DIR_FORWARD;
   const long long B = batch, K = nlat, L = lmax, M = mmax;
   if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
-  if (B == 0 || L == 0 || M == 0) return ok();
-  if (!out || !spec || !table_mlk || !workspace) return fail(HOLYSHT_ERR_INVALID, "null pointer");
-  if (K % 4 != 0 || K == 0) return fail(HOLYSHT_ERR_UNSUPPORTED, "tensor-core path needs nlat to be a multiple of 4");
-  if ((reinterpret_cast<uintptr_t>(table_mlk) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+  if (out_cols < M) return fail(HOLYSHT_ERR_INVALID, "out_cols (%lld) < mmax (%lld)", (long long)out_cols, M);
+  const long long R = fwd ? L : K, S = fwd ? K : L;
+  if (B == 0 || R == 0 || out_cols == 0) return ok();
+  if (!out || !in || !table || !workspace) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  if (S % 4 != 0 || S == 0)
+    return fail(HOLYSHT_ERR_UNSUPPORTED, "tensor-core path needs the reduction extent to be a multiple of 4");
+  if ((reinterpret_cast<uintptr_t>(table) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(HOLYSHT_ERR_INVALID, "table must be 16-byte and workspace 256-byte aligned");
-  if (2 * B > (1LL << 30) || !fits_int(K) || !fits_int(L) || !fits_int(M) || L > 65535)
+  if (2 * B > (1LL << 30) || B > 65535 || !fits_int(K) || !fits_int(L) || !fits_int(M) || R > 65535 ||
+      !fits_int(out_cols))
     return fail(HOLYSHT_ERR_INVALID, "extent out of range for the tensor-core path");
-  if (workspace_bytes < tc_workspace(B, K, L, M)) return fail(HOLYSHT_ERR_INVALID, "workspace too small");
-  if (spec_row_stride < M || spec_batch_stride < K * spec_row_stride)
-    return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
+  if ((flags & HOLYSHT_FLAG_IRFFT_PREP) && (fwd || nlon <= 0 || out_cols > nlon / 2 + 1))
+    return fail(HOLYSHT_ERR_INVALID, "irfft preparation is for the inverse with out_cols <= nlon/2+1");
+  const long long Mrows = M < L ? M : L;
+  if (workspace_bytes < tc_workspace(B, R, S, Mrows)) return fail(HOLYSHT_ERR_INVALID, "workspace too small");
+  if (in_row_stride < M || in_batch_stride < S * in_row_stride || out_row_stride < out_cols ||
+      out_batch_stride < R * out_row_stride)
+    return fail(HOLYSHT_ERR_INVALID, "input or output strides too small");
   const long long N = 2 * B;
   float* xt = static_cast<float*>(workspace);
-  float* D = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(M * N * K * 4));
-  const int Mrows = (int)(M < L ? M : L);
+  float* D = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(Mrows * N * S * 4));
 
-  {  // spectrum -> Xt [M][2B][K]
-    dim3 grid((unsigned)((M + 31) / 32), (unsigned)((K + 31) / 32), (unsigned)B), block(32, 8);
-    if (B > 65535) return fail(HOLYSHT_ERR_INVALID, "batch too large for one launch");
-    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(spec), xt, (int)B, (int)K,
-                                                             (int)M, spec_batch_stride, spec_row_stride, scale);
+  if (Mrows > 0) {  // input -> Xt [Mrows][2B][S]
+    dim3 grid((unsigned)((Mrows + 31) / 32), (unsigned)((S + 31) / 32), (unsigned)B), block(32, 8);
+    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(in), xt, (int)B, (int)S,
+                                                             (int)Mrows, in_batch_stride, in_row_stride, scale,
+                                                             (flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0);
     if (int st = check_launch("transpose_in")) return st;
+    // table: forward [M][L][K] (rows l, reduce k); inverse [M][K][L] (rows k, reduce l)
+    CUtensorMap map_a, map_b;
+    if (!make_map_3d(&map_a, table, S, R, Mrows, hsb::tc::kBK, hsb::tc::kBM) ||
+        !make_map_3d(&map_b, xt, S, N, Mrows, hsb::tc::kBK, hsb::tc::kBN))
+      return fail(HOLYSHT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable or rejected the tensors");
+    hsb::tc::DenseParams p;
+    p.R = (int)R;
+    p.S = (int)S;
+    p.M = (int)Mrows;
+    p.N = (int)N;
+    p.inverse = fwd ? 0 : 1;
+    p.n_nt = (int)((N + hsb::tc::kBN - 1) / hsb::tc::kBN);
+    p.n_bands = (int)((R + hsb::tc::kBM - 1) / hsb::tc::kBM);
+    p.D = D;
+    long long tiles = 0;
+    if (fwd) {
+      for (int q = 0; q < p.n_bands; ++q) {
+        const long long m_hi = std::min<long long>(Mrows, R - (long long)hsb::tc::kBM * q);
+        const long long m_lo = std::max<long long>(0, R - (long long)hsb::tc::kBM * (q + 1));
+        if (m_hi > m_lo) tiles += (m_hi - m_lo) * (q + 1) * p.n_nt;
+      }
+    } else {
+      tiles = Mrows * p.n_bands * p.n_nt;
+    }
+    if (tiles > INT_MAX) return fail(HOLYSHT_ERR_INVALID, "too many tiles");
+    static std::atomic<unsigned long long> configured{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
+      if (cudaFuncSetAttribute(hsb::tc::dense_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               hsb::tc::kSmemBytes) != cudaSuccess)
+        return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the tensor-core kernel");
+      configured.fetch_or(bit);
+    }
+    if (tiles > 0) {
+      hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(map_a, map_b,
+                                                                                                        p);
+      if (int st = check_launch("dense tcgen05 kernel")) return st;
+    }
   }
-  CUtensorMap map_a, map_b;
-  if (!make_map_3d(&map_a, table_mlk, K, L, M, hsb::tc::kBK, hsb::tc::kBM) ||
-      !make_map_3d(&map_b, xt, K, N, M, hsb::tc::kBK, hsb::tc::kBN))
-    return fail(HOLYSHT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable or rejected the tensors");
-  hsb::tc::DenseParams p;
-  p.K = (int)K;
-  p.L = (int)L;
-  p.M = Mrows;
-  p.N = (int)N;
-  p.n_nt = (int)((N + hsb::tc::kBN - 1) / hsb::tc::kBN);
-  p.n_bands = (int)((L + hsb::tc::kBM - 1) / hsb::tc::kBM);
-  p.D = D;
-  long long tiles = 0;
-  for (int q = 0; q < p.n_bands; ++q) {
-    const long long m_hi = std::min<long long>(Mrows, L - (long long)hsb::tc::kBM * q);
-    const long long m_lo = std::max<long long>(0, L - (long long)hsb::tc::kBM * (q + 1));
-    if (m_hi > m_lo) tiles += (m_hi - m_lo) * (q + 1) * p.n_nt;
-  }
-  if (tiles > INT_MAX) return fail(HOLYSHT_ERR_INVALID, "too many tiles");
-  static std::atomic<unsigned long long> configured{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(configured.load() & bit)) {
-    if (cudaFuncSetAttribute(hsb::tc::dense_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             hsb::tc::kSmemBytes) != cudaSuccess)
-      return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the tensor-core kernel");
-    configured.fetch_or(bit);
-  }
-  if (tiles > 0) {
-    hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(map_a, map_b, p);
-    if (int st = check_launch("dense tcgen05 kernel")) return st;
-  }
-  {  // D [M][L][2B] -> out [B][L][M]
-    dim3 grid((unsigned)((M + 31) / 32), (unsigned)((B + 31) / 32), (unsigned)L), block(32, 8);
-    hsb::tc::transpose_out_kernel<<<grid, block, 0, stream>>>(D, static_cast<float2*>(out), (int)B, (int)L, (int)M,
-                                                              Mrows);
+  {  // D [Mrows][R][2B] -> out [B][R][out_cols]
+    dim3 grid((unsigned)((out_cols + 31) / 32), (unsigned)((B + 31) / 32), (unsigned)R), block(32, 8);
+    const int prep = (flags & HOLYSHT_FLAG_IRFFT_PREP) ? 1 : 0;
+    const int nyq = (prep && nlon % 2 == 0) ? (int)(nlon / 2) : -1;
+    hsb::tc::transpose_out_kernel<<<grid, block, 0, stream>>>(D, static_cast<float2*>(out), (int)B, (int)R,
+                                                              (int)out_cols, (int)Mrows, out_batch_stride,
+                                                              out_row_stride, fwd ? 1 : 0, prep, nyq);
     if (int st = check_launch("transpose_out")) return st;
   }
   return ok();

@@ -25,6 +25,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -133,18 +134,28 @@ __device__ __forceinline__ float rna_tf32(float x) {
 }
 
 struct DenseParams {
-  int K, L, M, N;  // nlat, lmax, orders with rows (< lmax), columns = 2 * batch
+  int R, S;        // output rows and reduction length (forward: lmax, nlat; inverse: nlat, lmax)
+  int M, N;        // orders with work (< lmax), columns = 2 * batch
+  int inverse;     // 0: rows l >= m, all k; 1: all rows k, reduction l >= m
   int n_nt;        // column tiles
-  int n_bands;     // ceil(L / 128)
-  float* D;        // [M][L][N]
+  int n_bands;     // forward: ceil(lmax / 128); inverse: row tiles ceil(nlat / 128)
+  float* D;        // [M][R][N]
 };
 
 // tile index -> (m, l-tile, n-tile); orders grouped in bands of equal row-tile
 // count, the bands with most row tiles first (longest work first)
 __device__ __forceinline__ bool decode(const DenseParams& p, int t, int& m, int& lt, int& nt) {
+  if (p.inverse) {  // every order has all row tiles; low orders (longest reductions) first
+    const int per_m = p.n_bands * p.n_nt;
+    if (t >= p.M * per_m) return false;
+    m = t / per_m;
+    lt = (t % per_m) / p.n_nt;
+    nt = t % p.n_nt;
+    return true;
+  }
   for (int q = p.n_bands - 1; q >= 0; --q) {
-    const int m_hi = min(p.M, p.L - kBM * q);
-    const int m_lo = max(0, p.L - kBM * (q + 1));
+    const int m_hi = min(p.M, p.R - kBM * q);
+    const int m_lo = max(0, p.R - kBM * (q + 1));
     if (m_hi <= m_lo) continue;
     const int per_m = (q + 1) * p.n_nt;
     const int cnt = (m_hi - m_lo) * per_m;
@@ -174,12 +185,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int m, lt, nt;
   if (!decode(p, blockIdx.x, m, lt, nt)) return;  // uniform per CTA
-  const int l0 = m + lt * kBM;
+  const int l0 = (p.inverse ? 0 : m) + lt * kBM;  // first output row of the tile
   const int n0 = nt * kBN;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int nk = (p.K + kBK - 1) / kBK;
+  const int kb0 = p.inverse ? m / kBK : 0;  // inverse: the table is zero for l < m
+  const int nk = (p.S + kBK - 1) / kBK - kb0;
 
   auto a_hi = [&](int s) { return smem + s * kStageBytes; };
   auto a_lo = [&](int s) { return smem + s * kStageBytes + kABytes; };
@@ -210,8 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   auto issue_loads = [&](int kb, int s) {
     mbar_expect_tx(&full[s], kABytes + kBBytes);
-    tma_load_3d(a_hi(s), &map_a, &full[s], kb * kBK, l0, m);
-    tma_load_3d(b_hi(s), &map_b, &full[s], kb * kBK, n0, m);
+    tma_load_3d(a_hi(s), &map_a, &full[s], (kb0 + kb) * kBK, l0, m);
+    tma_load_3d(b_hi(s), &map_b, &full[s], (kb0 + kb) * kBK, n0, m);
   };
   if (tid == 0) issue_loads(0, 0);
 
@@ -314,8 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   {
     const int row = l0 + quarter * 32 + lane;
     const int nb = n0 + col_half * (kBN / 2);
-    if (row < p.L) {
-      float* dst = p.D + ((size_t)m * p.L + row) * p.N + nb;
+    if (row < p.R) {
+      float* dst = p.D + ((size_t)m * p.R + row) * p.N + nb;
       if (nb + kBN / 2 <= p.N && (p.N & 3) == 0) {
 #pragma unroll
         for (int q = 0; q < kBN / 8; ++q)
@@ -334,41 +346,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// spec [B][K][W] complex (rfft layout, orders < M used) -> Xt [M][2B][K] fp32 * scale
-__global__ void transpose_in_kernel(const float2* __restrict__ spec, float* __restrict__ xt, int B, int K, int M,
-                                    long long spec_bs, long long spec_rs, float scale) {
+// input [B][S][W] complex (orders < M used) -> Xt [M][2B][S] fp32 * scale,
+// optionally rounded to bf16 (after scaling)
+__global__ void transpose_in_kernel(const float2* __restrict__ in, float* __restrict__ xt, int B, int S, int M,
+                                    long long in_bs, long long in_rs, float scale, int round_bf16) {
   __shared__ float2 tile[32][33];
   const int b = blockIdx.z;
-  const int m0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int m0 = blockIdx.x * 32, s0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
   for (int i = ty; i < 32; i += 8) {
-    const int k = k0 + i, m = m0 + tx;
-    tile[i][tx] = (k < K && m < M) ? spec[(long long)b * spec_bs + (long long)k * spec_rs + m] : make_float2(0.f, 0.f);
+    const int sidx = s0 + i, m = m0 + tx;
+    tile[i][tx] = (sidx < S && m < M) ? in[(long long)b * in_bs + (long long)sidx * in_rs + m] : make_float2(0.f, 0.f);
   }
   __syncthreads();
   for (int i = ty; i < 32; i += 8) {
-    const int m = m0 + i, k = k0 + tx;
-    if (m < M && k < K) {
+    const int m = m0 + i, sidx = s0 + tx;
+    if (m < M && sidx < S) {
       const float2 v = tile[tx][i];
-      float* row = xt + ((long long)m * (2LL * B) + 2LL * b) * K;
-      row[k] = v.x * scale;
-      row[K + k] = v.y * scale;
+      float re = v.x * scale, im = v.y * scale;
+      if (round_bf16) {
+        re = __bfloat162float(__float2bfloat16_rn(re));
+        im = __bfloat162float(__float2bfloat16_rn(im));
+      }
+      float* row = xt + ((long long)m * (2LL * B) + 2LL * b) * S;
+      row[sidx] = re;
+      row[S + sidx] = im;
     }
   }
 }
 
-// D [M][L][2B] -> out [B][L][M] complex, exact zeros for m > l and for m >= Mrows
-__global__ void transpose_out_kernel(const float* __restrict__ D, float2* __restrict__ out, int B, int L, int M,
-                                     int Mrows) {
+// D [Mrows][R][2B] -> out [B][R][cols] complex.  Forward: exact zeros for m > r
+// (r = l).  Columns m >= Mrows are zero.  irfft preparation: Im = 0 at m = 0
+// and m = nyquist (-1: none).
+__global__ void transpose_out_kernel(const float* __restrict__ D, float2* __restrict__ out, int B, int R, int cols,
+                                     int Mrows, long long out_bs, long long out_rs, int forward, int zero_im0,
+                                     int nyquist) {
   __shared__ float2 tile[32][33];
-  const int l = blockIdx.z;
+  const int r = blockIdx.z;
   const int m0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
   for (int i = ty; i < 32; i += 8) {
     const int m = m0 + i, b = b0 + tx;
     float2 v = make_float2(0.f, 0.f);
-    if (m < Mrows && m <= l && b < B) {
-      const float* src = D + ((long long)m * L + l) * (2LL * B) + 2LL * b;
+    if (m < Mrows && (!forward || m <= r) && b < B) {
+      const float* src = D + ((long long)m * R + r) * (2LL * B) + 2LL * b;
       v = make_float2(src[0], src[1]);
     }
     tile[i][tx] = v;
@@ -376,7 +397,11 @@ __global__ void transpose_out_kernel(const float* __restrict__ D, float2* __rest
   __syncthreads();
   for (int i = ty; i < 32; i += 8) {
     const int b = b0 + i, m = m0 + tx;
-    if (b < B && m < M) out[((long long)b * L + l) * M + m] = tile[tx][i];
+    if (b < B && m < cols) {
+      float2 v = tile[tx][i];
+      if ((zero_im0 && m == 0) || m == nyquist) v.y = 0.f;
+      out[(long long)b * out_bs + (long long)r * out_rs + m] = v;
+    }
   }
 }
 

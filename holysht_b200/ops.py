@@ -35,7 +35,7 @@ __all__ = [
     "legendre_contract",
     "tile_table",
     "group_table",
-    "legendre_forward_tc",
+    "legendre_dense_tc",
     "tc_error_word",
 ]
 
@@ -313,29 +313,32 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
         _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))
 
 
-def legendre_forward_tc(output: torch.Tensor, spec: torch.Tensor, table_mlk: torch.Tensor, mmax: int,
-                        scale: float = 1.0) -> None:
-    """Dense tensor-core forward: output [B, L, M] complex64 =
-    scale * sum_k table_mlk[m, l, k] * spec[b, k, m] (l >= m), with ``spec`` an
-    rfft-layout complex64 [B, K, W >= M] tensor (contiguous rows) and
-    ``table_mlk`` float32 [M, L, K] (the torch-harmonics ``weights`` layout).
-    The GEMM workspace comes from torch's caching allocator."""
-    dev = _cuda(output, spec, table_mlk)
-    _require(spec.dtype == torch.complex64 and output.dtype == torch.complex64, "spectrum and output are complex64")
-    _require(table_mlk.dtype == torch.float32 and table_mlk.is_contiguous(), "table must be contiguous float32")
-    _require(spec.dim() == 3 and spec.stride(2) == 1, "spectrum must be [B, K, W] with contiguous orders")
-    M, L, K = table_mlk.shape
-    _require(int(mmax) == M, "mmax must match the table")
-    B = spec.size(0)
-    _require(spec.size(1) == K and spec.size(2) >= M, "spectrum must be [B, nlat, >= mmax]")
-    _require(output.is_contiguous() and tuple(output.shape) == (B, L, M), "output must be [B, lmax, mmax]")
+def legendre_dense_tc(direction: int, output: torch.Tensor, input: torch.Tensor, table: torch.Tensor,
+                      *, nlat: int, lmax: int, mmax: int, scale: float = 1.0, flags: int = 0,
+                      nlon: int = 0) -> None:
+    """Dense tensor-core contraction (SCALAR kind, ``holysht_legendre_dense_tc``).
+
+    forward: output [B, lmax, >= mmax] <- input [B, nlat, >= mmax], table [mmax, lmax, nlat];
+    inverse: output [B, nlat, >= mmax] <- input [B, lmax, >= mmax], table [mmax, nlat, lmax].
+    Rows of input and output may be strided (rfft / irfft buffers); orders are
+    contiguous.  The GEMM workspace comes from torch's caching allocator."""
+    dev = _cuda(output, input, table)
+    _require(input.dtype == torch.complex64 and output.dtype == torch.complex64, "input and output are complex64")
+    _require(table.dtype == torch.float32 and table.is_contiguous(), "table must be contiguous float32")
+    _require(input.dim() == 3 and output.dim() == 3 and input.stride(2) == 1 and output.stride(2) == 1,
+             "input and output must be [B, rows, cols] with contiguous orders")
+    fwd = direction == _lib.DIR_FORWARD
+    want = (mmax, lmax, nlat) if fwd else (mmax, nlat, lmax)
+    _require(tuple(table.shape) == want, f"table must be {want}")
+    B = input.size(0)
     lib = _lib.load()
     nbytes = ctypes.c_int64(0)
-    _lib.check(lib.holysht_legendre_forward_tc_workspace(B, K, L, M, ctypes.byref(nbytes)))
+    _lib.check(lib.holysht_legendre_dense_tc_workspace(direction, B, nlat, lmax, mmax, ctypes.byref(nbytes)))
     with torch.cuda.device(dev):
         ws = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=dev)
-        _lib.check(lib.holysht_legendre_forward_tc(
-            _p(output), _p(spec), spec.stride(0), spec.stride(1), _p(table_mlk), B, K, L, M, float(scale),
+        _lib.check(lib.holysht_legendre_dense_tc(
+            direction, _p(output), output.stride(0), output.stride(1), output.size(2), _p(input),
+            input.stride(0), input.stride(1), _p(table), B, nlat, lmax, mmax, float(scale), int(flags), int(nlon),
             _p(ws), nbytes.value, _stream(dev)))
 
 

@@ -184,25 +184,32 @@ typedef struct holysht_contract_desc {
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
 /* ---------------------------------------------------------------------------
- * Dense tensor-core forward (no counterpart operator in the reference; the
- * reference's TF32 wmma path, cuda/fused_legendre.cu:635-714, is its
+ * Dense tensor-core contraction (no counterpart operator in the reference; the
+ * reference's TF32 wmma forward, cuda/fused_legendre.cu:635-714, is its
  * approximate analogue).  For large batches the per-order contraction is a
  * GEMM; this entry runs it on tcgen05 tensor cores with a three-product
- * split-TF32 scheme (fp32-level accuracy):
- *   out[b,l,m] = scale * sum_k table_mlk[m,l,k] * spec[b,k,m]    (l >= m; 0 otherwise)
- * spec: complex64, element (b,k,m) at spec + b*spec_batch_stride + k*spec_row_stride + m
- * (the rfft output can be passed as is, with spec_row_stride = nlon/2+1);
- * table_mlk: float32 [mmax][lmax][nlat] (the torch-harmonics `weights` layout),
- * nlat a multiple of 4; out: complex64 [B][lmax][mmax].
- * workspace: caller-allocated device memory of at least the size reported by
- * holysht_legendre_forward_tc_workspace (256-byte aligned); it holds the
- * transposed spectrum and the GEMM output between the three launches. */
-int holysht_legendre_forward_tc_workspace(int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
-                                          int64_t* bytes);
-int holysht_legendre_forward_tc(void* out, const void* spec, int64_t spec_batch_stride,
-                                int64_t spec_row_stride, const float* table_mlk, int64_t batch,
-                                int64_t nlat, int64_t lmax, int64_t mmax, float scale, void* workspace,
-                                int64_t workspace_bytes, void* stream);
+ * split-TF32 scheme (fp32-level accuracy), for the SCALAR kind:
+ *   forward: out[b,l,m] = scale * sum_k W[m,l,k] in[b,k,m]        (l >= m; 0 otherwise)
+ *   inverse: out[b,k,m] = scale * sum_{l>=m} W[m,l,k] in[b,l,m]
+ * in / out: complex64, element (b,row,m) at ptr + b*batch_stride + row*row_stride + m
+ * (the rfft output and the irfft input buffers can be passed as they are);
+ * columns out_cols > mmax of out are written as zeros; HOLYSHT_FLAG_IRFFT_PREP
+ * (inverse) also zeroes Im at m = 0 and, for even nlon, m = nlon/2;
+ * HOLYSHT_FLAG_ROUND_BF16 rounds the scaled input to bfloat16 first.
+ * table: float32, forward [mmax][lmax][nlat] (the torch-harmonics `weights`
+ * layout), inverse [mmax][nlat][lmax] (the same table transposed per order);
+ * the reduction extent (nlat forward, lmax inverse) must be a multiple of 4.
+ * workspace: caller-allocated device memory (256-byte aligned) of at least
+ * the size holysht_legendre_dense_tc_workspace reports; it holds the
+ * transposed input and the GEMM output between the three launches. */
+int holysht_legendre_dense_tc_workspace(int direction, int64_t batch, int64_t nlat, int64_t lmax,
+                                        int64_t mmax, int64_t* bytes);
+int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride,
+                              int64_t out_row_stride, int64_t out_cols, const void* in,
+                              int64_t in_batch_stride, int64_t in_row_stride, const float* table,
+                              int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax, float scale,
+                              int flags, int64_t nlon, void* workspace, int64_t workspace_bytes,
+                              void* stream);
 
 /* Diagnostics: reads and clears the tensor-core kernel's device error word
  * (bit 0: a pipeline wait gave up instead of hanging).  Synchronous. */

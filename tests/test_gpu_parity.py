@@ -406,7 +406,8 @@ def test_dense_tensor_core_forward_matches_oracle(B, K, L, M, W):
     spec = cplx(rng, (B, K, W))
     tab = torch.from_numpy(np.ascontiguousarray(w.transpose(2, 0, 1))).to(DEV)  # [M, L, K]
     out = torch.full((B, L, M), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
-    ops.legendre_forward_tc(out, torch.from_numpy(spec).to(DEV), tab, M, scale=1.5)
+    ops.legendre_dense_tc(_lib.DIR_FORWARD, out, torch.from_numpy(spec).to(DEV), tab, nlat=K, lmax=L, mmax=M,
+                          scale=1.5)
     ref = 1.5 * orc.legendre_forward(spec[..., :M].astype(np.complex128), w.astype(np.float64))
     assert_fp32_close(out, ref)
     upper = np.arange(M)[None, :] > np.arange(L)[:, None]
@@ -414,13 +415,42 @@ def test_dense_tensor_core_forward_matches_oracle(B, K, L, M, W):
     assert ops.tc_error_word() == 0
 
 
-def test_scalar_module_uses_tensor_cores_for_large_batches(monkeypatch):
+@pytest.mark.parametrize("B,K,L,M,nlon", [(4, 30, 128, 129, 256), (130, 64, 200, 101, 220), (200, 300, 512, 257, 512)])
+def test_dense_tensor_core_inverse_matches_oracle(B, K, L, M, nlon):
+    rng = np.random.default_rng(B + L)
+    w = tri_table(rng, L, K, M)
+    c = cplx(rng, (B, L, M)) * (np.arange(M)[None, None, :] <= np.arange(L)[None, :, None])
+    W = nlon // 2 + 1
+    tab = torch.from_numpy(np.ascontiguousarray(w.transpose(2, 1, 0))).to(DEV)  # [M, K, L]
+    out = torch.full((B, K, W), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    ops.legendre_dense_tc(_lib.DIR_INVERSE, out, torch.from_numpy(c.astype(np.complex64)).to(DEV), tab, nlat=K,
+                          lmax=L, mmax=M, flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
+    y = orc.legendre_inverse(c.astype(np.complex128), w.astype(np.float64))
+    ref = orc.prepare_irfft(y, nlon)
+    assert_fp32_close(out, ref)
+    assert ops.tc_error_word() == 0
+
+
+def test_scalar_modules_use_tensor_cores_for_large_batches(monkeypatch):
     rng = np.random.default_rng(9)
     x = rng.standard_normal((2, 80, 64, 128)).astype(np.float32)  # 160 slices >= 128
     m = hs.RealSHT(64, 128).to(DEV)
     xt = torch.from_numpy(x).to(DEV)
     got = m(xt)
     assert_fp32_close(got, _module_oracle_scalar(m, x.astype(np.float64)))
+    # inverse + training round trip on tensor cores vs the SIMT kernels
+    inv = hs.InverseRealSHT(64, 128).to(DEV)
+
+    def roundtrip():
+        c = got.detach().clone().requires_grad_(True)
+        coef = m(torch.tanh(inv(c)))
+        (coef.real.square().sum() + coef.imag.square().sum()).backward()
+        return coef.detach(), c.grad
+
+    coef_tc, grad_tc = roundtrip()
     monkeypatch.setenv("HOLYSHT_DENSE_TC", "0")
     simt = m(xt)
-    assert_fp32_close(got, simt.cpu().numpy().astype(np.complex128), rel=5e-7, maxabs=5e-6)
+    coef_simt, grad_simt = roundtrip()
+    assert_fp32_close(got, simt.cpu().numpy().astype(np.complex128), rel=1e-6, maxabs=1e-5)
+    assert_fp32_close(coef_tc, coef_simt.cpu().numpy().astype(np.complex128), rel=2e-6, maxabs=2e-5)
+    assert_fp32_close(grad_tc, grad_simt.cpu().numpy().astype(np.complex128), rel=2e-6, maxabs=2e-5)
