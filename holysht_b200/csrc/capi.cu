@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "../../include/holysht_b200.h"
@@ -649,6 +650,66 @@ int holysht_sht_prepare_irfft(void* data, int64_t rows, int64_t width, int64_t m
   hsb::prepare_irfft_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<float2*>(data), rows, (int)width, (int)(mmax < width ? mmax : width), nyq);
   return check_launch("sht_prepare_irfft");
+}
+
+// ---------------------------------------------------------------------------
+// Dense tensor-core contraction without any allocation.
+//
+// Some callers cannot allocate device memory themselves: code embedded in a
+// host whose allocator owns all GPU memory (a raw cudaMalloc there would bypass
+// its memory budget), or a latency-critical loop that must not pay for an
+// allocation on every call, or a plugin loaded through a bare C ABI that was
+// given no allocator.  For them the scratch the dense path needs (the
+// transposed input and the GEMM output) lives in the static device array below.
+// It has a fixed size of kNoAllocScratchBytes and occupies that much memory on
+// every GPU that loads this library, until the process exits.
+// ---------------------------------------------------------------------------
+
+constexpr long long kNoAllocScratchBytes = 64LL << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device; looked up once per
+// device (the host-side name of the array is not a device address).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(HOLYSHT_ERR_CUDA, "no current CUDA device for the built-in scratch");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      return fail(HOLYSHT_ERR_CUDA, "cannot get the address of the built-in scratch: %s", cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return HOLYSHT_OK;
+}
+}  // namespace
+
+int holysht_legendre_dense_tc_noalloc(int direction, void* out, int64_t out_batch_stride, int64_t out_row_stride,
+                                      int64_t out_cols, const void* in, int64_t in_batch_stride,
+                                      int64_t in_row_stride, const float* table, int64_t batch, int64_t nlat,
+                                      int64_t lmax, int64_t mmax, float scale, int flags, int64_t nlon,
+                                      void* stream) {
+  int64_t need = 0;
+  if (int st = holysht_legendre_dense_tc_workspace(direction, batch, nlat, lmax, mmax, &need)) return st;
+  if (need > kNoAllocScratchBytes)
+    return fail(HOLYSHT_ERR_INVALID,
+                "problem needs %lld bytes of scratch but the built-in scratch holds %lld bytes (64 MiB); "
+                "call holysht_legendre_dense_tc with a workspace instead",
+                (long long)need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  return holysht_legendre_dense_tc(direction, out, out_batch_stride, out_row_stride, out_cols, in, in_batch_stride,
+                                   in_row_stride, table, batch, nlat, lmax, mmax, scale, flags, nlon, scratch,
+                                   kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"

@@ -211,6 +211,25 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
                               int flags, int64_t nlon, void* workspace, int64_t workspace_bytes,
                               void* stream);
 
+/* Same contraction as holysht_legendre_dense_tc, for callers that cannot
+ * allocate device memory (a host whose own allocator owns the GPU memory, a
+ * loop that must not allocate per call, a plugin handed no allocator).  No
+ * counterpart in the reference.  The scratch is a 64 MiB array built into the
+ * library (held on every GPU that loads it until the process exits); problems
+ * whose holysht_legendre_dense_tc_workspace size exceeds 64 MiB are rejected
+ * with HOLYSHT_ERR_INVALID.  The first call on a device looks the array's
+ * device address up (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (other streams, other host threads) race on it and must be serialised
+ * by the caller.  Nothing in the array carries over between calls: every
+ * scratch element a call reads was written earlier in the same call.  No
+ * cudaMalloc, cudaFree or other allocating routine is called. */
+int holysht_legendre_dense_tc_noalloc(int direction, void* out, int64_t out_batch_stride,
+                                      int64_t out_row_stride, int64_t out_cols, const void* in,
+                                      int64_t in_batch_stride, int64_t in_row_stride,
+                                      const float* table, int64_t batch, int64_t nlat, int64_t lmax,
+                                      int64_t mmax, float scale, int flags, int64_t nlon, void* stream);
+
 /* Diagnostics: reads and clears the tensor-core kernel's device error word
  * (bit 0: a pipeline wait gave up instead of hanging).  Synchronous. */
 int holysht_tc_error_word(unsigned* value);
