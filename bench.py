@@ -237,6 +237,20 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     scalar_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(ss, se)))
     del ssht
+    # the on-the-fly (recurrence) variant of the same scalar forward
+    rsht = hs.RealSHT(NLAT, NLON, variant="recurrence").to(dev)
+    for _ in range(3):
+        rsht(xs)
+    rs = [torch.cuda.Event(enable_timing=True) for _ in range(sn)]
+    re_ = [torch.cuda.Event(enable_timing=True) for _ in range(sn)]
+    for i in range(sn):
+        flush.zero_()
+        rs[i].record(stream)
+        rsht(xs)
+        re_[i].record(stream)
+    torch.cuda.synchronize(dev)
+    rec_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(rs, re_)))
+    del rsht
 
     # ---- end to end through the public API with host buffers ----
     xh = torch.empty((BATCH, 2, NLAT, NLON), dtype=torch.float32).pin_memory()
@@ -291,7 +305,8 @@ def run_ours(args, rank, world, local_rank):
                    "global_batch": BATCH * world, "parallelism": f"batch-partition x{world}, no collective",
                    "l2": "flushed (256 MiB write) before every timed step; tables 2x538 MB exceed L2"},
         "transforms_per_s": round(BATCH * world / (ms * 1e-3), 2),
-        "secondary": {"RealSHT.forward_ms": round(scalar_ms, 5)},
+        "secondary": {"RealSHT.forward_ms": round(scalar_ms, 5),
+                      "RealSHT.forward_recurrence_variant_ms": round(rec_ms, 5)},
         "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * K,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -204,7 +204,11 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         L, M = src.lmax, src.mmax
         shape = (B, 2, L, M) if vector else (B, L, M)
         out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
-        if _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
+        if getattr(src, "variant", "table") == "recurrence" and not round_bf16:
+            # on-the-fly Legendre functions: no table stream
+            seeds, coef, ct = src.recurrence_tables()
+            ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
+        elif _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
             # large batch: the per-order contraction is a dense GEMM -> tcgen05
             ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
                                   lmax=L, mmax=M, scale=scale, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
@@ -514,12 +518,18 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
 
     ``dtype="bf16"`` rounds the post-FFT spectrum to bfloat16 and contracts it
     with the FP32 table in FP32 (the reference's BF16 path, ``__init__.py:1289-1337``).
+    ``variant="recurrence"`` (an addition) computes the Legendre functions on the
+    fly in the forward pass instead of streaming the table (the backward pass
+    uses the table).
     """
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
                  grid: str = "equiangular", norm: str = "ortho", csphase: bool = True,
-                 dtype: str = "fp32"):
+                 dtype: str = "fp32", variant: str = "table"):
         super().__init__()
+        if variant not in ("table", "recurrence"):
+            raise ValueError(f"variant must be 'table' or 'recurrence', got {variant!r}")
+        self.variant = variant
         w_dtype = _w_dtype(dtype)
         w, L, M = _weights.scalar_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
         _check_mmax(M, nlon)
@@ -532,6 +542,14 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
         self.register_buffer("weight_t", wt.permute(1, 2, 0).contiguous())
         self._mlk_name = "weights"
         self._init_tables(("weight_t",), _lib.DIR_FORWARD)
+        if variant == "recurrence":
+            seeds, coef, ct = _weights.scalar_recurrence_tables(nlat, nlon, lmax, mmax, grid, norm, csphase)
+            self.register_buffer("rec_seeds", torch.from_numpy(seeds), persistent=False)
+            self.register_buffer("rec_coef", torch.from_numpy(coef), persistent=False)
+            self.register_buffer("rec_cos_theta", torch.from_numpy(ct), persistent=False)
+
+    def recurrence_tables(self):
+        return self.rec_seeds, self.rec_coef, self.rec_cos_theta
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "RealSHT")

@@ -1,0 +1,177 @@
+// Scalar forward Legendre transform with on-the-fly associated Legendre
+// functions (the "recurrence" variant): no table stream.
+//
+//   out[b, l, m] = scale * sum_k X[b, k, m] * w_k P_l^m(x_k)        (l >= m)
+//
+// P is generated in registers by the three-term recurrence in l
+//   P_l = a_lm x P_{l-1} - b_lm P_{l-2}
+// in fp32, re-seeded every kSeg degrees from checkpoints (P_{l0}, P_{l0+1})
+// computed in float64 on the host (quadrature weight folded in; values below
+// fp32 range are exact zeros, which is what they contribute).  Re-seeding
+// bounds the fp32 drift of the recurrence: with 16-degree segments the
+// coefficients stay within ~5e-7 relative L2 of the float64 transform at
+// lmax = 512.
+//
+// CTA: one order m, 4 checkpoint segments (64 degrees), a group of 4 batches,
+// threads over latitude (kKpt latitudes per thread, in registers with the
+// kKpt x 4 complex spectrum values they multiply).  Per degree each thread forms 8 partial sums (4 batches x re/im);
+// every 4 degrees a warp transposes-and-reduces its 32 values with shuffles
+// (lane j ends with value j summed over the warp's latitudes) and the warps'
+// results are summed through shared memory.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace hsb {
+namespace rec {
+
+constexpr int kSeg = 16;      // degrees per checkpoint segment
+#ifndef HSB_REC_KPT
+#define HSB_REC_KPT 4
+#endif
+constexpr int kKpt = HSB_REC_KPT;  // latitudes per thread
+constexpr int kNB = 4;        // batches per CTA
+constexpr int kMaxWarps = 8;  // nlat <= 8 * 32 * 8 = 2048
+
+struct RecParams {
+  const float2* spec;  // [B][K][W] complex, element (b, k, m) at b*sbs + k*srs + m
+  long long sbs, srs;
+  const float* seeds;  // [M][nseg][K][2]
+  const float* coef;   // [M][L][2]: a_lm, b_lm
+  const float* x;      // [K] cos(theta_k)
+  float2* out;         // [B][L][M]
+  int B, K, L, M, nseg;
+  float scale;
+};
+
+#ifndef HSB_REC_SEGS_PER_CTA
+#define HSB_REC_SEGS_PER_CTA 4
+#endif
+constexpr int kSegPerCta = HSB_REC_SEGS_PER_CTA;  // checkpoint segments per CTA
+
+// grid: x = order m, y = block of kSegPerCta segments, z = batch group
+__global__ void __launch_bounds__(kMaxWarps * 32) recurrence_forward_kernel(const RecParams p) {
+  __shared__ float red[kMaxWarps][32];
+  const int m = blockIdx.x;
+  const int b0 = blockIdx.z * kNB;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int lm = p.L - m;  // degrees l = m .. L-1
+  const int nseg = lm > 0 ? (lm + kSeg - 1) / kSeg : 0;
+  const int c_begin = blockIdx.y * kSegPerCta;
+
+  if (blockIdx.y == 0) {
+    // rows l < m (and every row of an order without degrees) are exact zeros
+    const int zrows = lm > 0 ? m : p.L;
+    for (int e = tid; e < zrows * kNB; e += blockDim.x) {
+      const int l = e / kNB, b = b0 + e % kNB;
+      if (b < p.B) p.out[((long long)b * p.L + l) * p.M + m] = make_float2(0.f, 0.f);
+    }
+  }
+  if (c_begin >= nseg) return;  // uniform per CTA
+  const int c_end = min(nseg, c_begin + kSegPerCta);
+
+  // this thread's latitudes, their cos(theta) and scaled spectrum values
+  const int k0 = tid * kKpt;
+  float xk[kKpt];
+  float2 X[kKpt][kNB];
+#pragma unroll
+  for (int i = 0; i < kKpt; ++i) {
+    const int k = k0 + i;
+    xk[i] = k < p.K ? p.x[k] : 0.f;
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      float2 v = make_float2(0.f, 0.f);
+      if (k < p.K && b0 + b < p.B) v = p.spec[(long long)(b0 + b) * p.sbs + (long long)k * p.srs + m];
+      X[i][b] = make_float2(v.x * p.scale, v.y * p.scale);
+    }
+  }
+
+  const float* coef_m = p.coef + (long long)m * p.L * 2;
+  for (int c = c_begin; c < c_end; ++c) {
+    const int lseg = m + c * kSeg;
+    // the segment's seeds and recurrence coefficients, loaded up front
+    const float* sd = p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 2;
+    float p1[kKpt], p2[kKpt];
+    float ca[kSeg], cb[kSeg];
+#pragma unroll
+    for (int q = 2; q < kSeg; ++q) {
+      const int l = lseg + q;
+      ca[q] = l < p.L ? coef_m[2 * l] : 0.f;
+      cb[q] = l < p.L ? coef_m[2 * l + 1] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kKpt; ++i) {
+      const bool ok = k0 + i < p.K;
+      p2[i] = ok ? sd[2 * i] : 0.f;      // P at lseg
+      p1[i] = ok ? sd[2 * i + 1] : 0.f;  // P at lseg + 1
+    }
+#pragma unroll
+    for (int qb = 0; qb < kSeg; qb += 4) {
+      float v[32];  // 4 degrees x (4 batches x re/im)
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int q = qb + q4;
+        float pl[kKpt];
+        if (q == 0) {
+#pragma unroll
+          for (int i = 0; i < kKpt; ++i) pl[i] = p2[i];
+        } else if (q == 1) {
+#pragma unroll
+          for (int i = 0; i < kKpt; ++i) pl[i] = p1[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < kKpt; ++i) {
+            pl[i] = fmaf(ca[q] * xk[i], p1[i], -cb[q] * p2[i]);
+            p2[i] = p1[i];
+            p1[i] = pl[i];
+          }
+        }
+        float2 acc[kNB];
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) acc[b] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < kKpt; ++i)
+#pragma unroll
+          for (int b = 0; b < kNB; ++b) acc[b] = __ffma2_rn(make_float2(pl[i], pl[i]), X[i][b], acc[b]);
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) {
+          v[q4 * 8 + 2 * b] = acc[b].x;
+          v[q4 * 8 + 2 * b + 1] = acc[b].y;
+        }
+      }
+      // warp transpose-reduce: lane j ends with value j summed over the warp
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < d; ++i) {
+          const float send = upper ? v[i] : v[i + d];
+          const float keep = upper ? v[i + d] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+      if (nwarps == 1) {
+        const int q4 = lane >> 3, b = (lane >> 1) & 3, ri = lane & 1;
+        const int l = lseg + qb + q4;
+        if (l < p.L && b0 + b < p.B)
+          reinterpret_cast<float*>(p.out)[(((long long)(b0 + b) * p.L + l) * p.M + m) * 2 + ri] = v[0];
+      } else {
+        red[warp][lane] = v[0];
+        __syncthreads();
+        if (warp == 0) {
+          float sum = 0.f;
+          for (int w = 0; w < nwarps; ++w) sum += red[w][lane];
+          const int q4 = lane >> 3, b = (lane >> 1) & 3, ri = lane & 1;
+          const int l = lseg + qb + q4;
+          if (l < p.L && b0 + b < p.B)
+            reinterpret_cast<float*>(p.out)[(((long long)(b0 + b) * p.L + l) * p.M + m) * 2 + ri] = sum;
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
+}  // namespace rec
+}  // namespace hsb

@@ -37,6 +37,7 @@ __all__ = [
     "group_table",
     "legendre_dense_tc",
     "tc_error_word",
+    "legendre_forward_recurrence",
 ]
 
 
@@ -347,3 +348,24 @@ def tc_error_word() -> int:
     v = ctypes.c_uint(0)
     _lib.check(_lib.load().holysht_tc_error_word(ctypes.byref(v)))
     return int(v.value)
+
+
+def legendre_forward_recurrence(output: torch.Tensor, spec: torch.Tensor, seeds: torch.Tensor, coef: torch.Tensor,
+                                cos_theta: torch.Tensor, scale: float = 1.0) -> None:
+    """Scalar forward with on-the-fly Legendre functions (``holysht_legendre_forward_recurrence``):
+    output [B, L, M] complex64 from an rfft-layout spectrum [B, K, W >= M]; ``seeds``,
+    ``coef`` and ``cos_theta`` from :func:`holysht_b200.weights.scalar_recurrence_tables`."""
+    dev = _cuda(output, spec, seeds, coef, cos_theta)
+    _require(spec.dtype == torch.complex64 and output.dtype == torch.complex64, "spectrum and output are complex64")
+    _require(spec.dim() == 3 and spec.stride(2) == 1, "spectrum must be [B, K, W] with contiguous orders")
+    _contig(output, seeds, coef, cos_theta)
+    M, nseg, K, two = seeds.shape
+    L = coef.size(1)
+    B = spec.size(0)
+    _require(two == 2 and tuple(coef.shape) == (M, L, 2) and cos_theta.numel() == K, "inconsistent tables")
+    _require(spec.size(1) == K and spec.size(2) >= M, "spectrum must be [B, nlat, >= mmax]")
+    _require(tuple(output.shape) == (B, L, M), "output must be [B, lmax, mmax]")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_legendre_forward_recurrence(
+            _p(output), _p(spec), spec.stride(0), spec.stride(1), _p(seeds), _p(coef), _p(cos_theta),
+            B, K, L, M, float(scale), _stream(dev)))

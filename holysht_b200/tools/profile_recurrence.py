@@ -1,0 +1,33 @@
+"""Run the recurrence-variant RealSHT forward (512x1024, batch 4) for profilers.
+
+    python -m holysht_b200.tools.profile_recurrence [reps]
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+import holysht_b200 as hs
+
+
+def main(argv):
+    reps = int(argv[1]) if len(argv) > 1 else 3
+    dev = torch.device("cuda")
+    m = hs.RealSHT(512, 1024, variant="recurrence").to(dev)
+    x = torch.randn(4, 512, 1024, device=dev)
+    with torch.no_grad():
+        for _ in range(reps):
+            m(x)
+        torch.cuda.synchronize()
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e[0].record()
+        for _ in range(10):
+            m(x)
+        e[1].record()
+        torch.cuda.synchronize()
+    print("recurrence RealSHT 512x1024 b4 ms", round(e[0].elapsed_time(e[1]) / 10, 4))
+
+
+if __name__ == "__main__":
+    main(sys.argv)

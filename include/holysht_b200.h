@@ -211,6 +211,25 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
                               int flags, int64_t nlon, void* workspace, int64_t workspace_bytes,
                               void* stream);
 
+/* Scalar forward with on-the-fly Legendre functions (the recurrence variant;
+ * no counterpart operator in the reference, whose kernels all stream a table):
+ *   out[b,l,m] = scale * sum_k spec[b,k,m] * w_k P_l^m(cos theta_k)   (l >= m; 0 otherwise)
+ * P comes from the three-term recurrence in fp32 registers, re-seeded every
+ * 16 degrees from float64 checkpoints:
+ *   seeds     float32 [mmax][ceil(lmax/16)][nlat][2]: w_k P_l^m at l = m + 16c and
+ *             m + 16c + 1 (normalisation, Condon-Shortley phase and quadrature
+ *             weight included);
+ *   coef      float32 [mmax][lmax][2]: the recurrence coefficients (a_lm, b_lm);
+ *   cos_theta float32 [nlat].
+ * spec: complex64, element (b,k,m) at spec + b*spec_batch_stride + k*spec_row_stride + m;
+ * out: complex64 [B][lmax][mmax].  nlat <= 2048.  (holysht_b200.weights builds
+ * the three inputs.) */
+int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spec_batch_stride,
+                                        int64_t spec_row_stride, const float* seeds,
+                                        const float* coef, const float* cos_theta, int64_t batch,
+                                        int64_t nlat, int64_t lmax, int64_t mmax, float scale,
+                                        void* stream);
+
 /* Same contraction as holysht_legendre_dense_tc, for callers that cannot
  * allocate device memory (a host whose own allocator owns the GPU memory, a
  * loop that must not allocate per call, a plugin handed no allocator).  No

@@ -454,3 +454,21 @@ def test_scalar_modules_use_tensor_cores_for_large_batches(monkeypatch):
     assert_fp32_close(got, simt.cpu().numpy().astype(np.complex128), rel=1e-6, maxabs=1e-5)
     assert_fp32_close(coef_tc, coef_simt.cpu().numpy().astype(np.complex128), rel=2e-6, maxabs=2e-5)
     assert_fp32_close(grad_tc, grad_simt.cpu().numpy().astype(np.complex128), rel=2e-6, maxabs=2e-5)
+
+
+# ------------------------------------------------------------- recurrence variant
+
+@pytest.mark.parametrize("nlat,nlon,grid,norm,cs", [
+    (512, 1024, "equiangular", "ortho", True),
+    (96, 192, "legendre-gauss", "schmidt", False),
+    (33, 64, "lobatto", "four-pi", True),
+    (256, 512, "equiangular", "ortho", True),
+])
+def test_recurrence_variant_matches_oracle(nlat, nlon, grid, norm, cs):
+    rng = np.random.default_rng(nlat)
+    x = rng.standard_normal((5, nlat, nlon)).astype(np.float32)  # 5 batches: two batch groups
+    m = hs.RealSHT(nlat, nlon, grid=grid, norm=norm, csphase=cs, variant="recurrence").to(DEV)
+    out = m(torch.from_numpy(x).to(DEV))
+    assert_fp32_close(out, _module_oracle_scalar(m, x.astype(np.float64)))
+    upper = np.arange(m.mmax)[None, :] > np.arange(m.lmax)[:, None]
+    assert np.all(out.cpu().numpy()[:, upper] == 0)
