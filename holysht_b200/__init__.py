@@ -83,8 +83,8 @@ class _DenseTables:
         self.vector = w1 is not None
         self.lmax, self.nlat, self.mmax = w0.shape
 
-    def table(self, direction: int):
-        return self.w0, self.w1, False
+    def table(self, direction: int, layout=None):
+        return self.w0, self.w1, "strided"
 
 
 class _GroupedTablesMixin:
@@ -100,6 +100,7 @@ class _GroupedTablesMixin:
         self._hot_direction = hot_direction
         self.register_buffer("_grouped_fwd", None, persistent=False)
         self.register_buffer("_grouped_inv", None, persistent=False)
+        self.register_buffer("_grouped8_fwd", None, persistent=False)
         self.table(hot_direction)
         self.register_load_state_dict_post_hook(lambda module, _keys: module._drop_grouped())
 
@@ -117,8 +118,10 @@ class _GroupedTablesMixin:
         return torch.fft.rfft(x.float(), dim=-1), TWO_PI / self.nlon, False
 
     def _drop_grouped(self) -> None:
+        self.__dict__.pop("_contract_plans", None)
         self._grouped_fwd = None
         self._grouped_inv = None
+        self._grouped8_fwd = None
         if hasattr(self, "_dense_inv"):
             self._dense_inv = None
 
@@ -140,17 +143,38 @@ class _GroupedTablesMixin:
                 self._dense_inv = t
         return t
 
-    def table(self, direction: int):
-        name = "_grouped_fwd" if direction == _lib.DIR_FORWARD else "_grouped_inv"
+    def table(self, direction: int, layout=None):
+        """(table, None, layout) for one contraction direction.
+
+        ``layout`` "grouped8" (``ops.group_table8``, the streaming kernel) is
+        the default for the FP32 forward direction; "grouped"
+        (``ops.group_table``, 4-row groups) serves the inverse direction and
+        the BF16/FP16 modules, whose forward rounds the spectrum in the kernel.
+        ``HOLYSHT_FORWARD_LAYOUT=grouped`` selects the 4-row kernel for the
+        forward direction too."""
+        if layout is None:
+            import os
+
+            low = bool(getattr(self, "_use_bf16", False) or getattr(self, "_use_fp16", False))
+            stream = os.environ.get("HOLYSHT_FORWARD_LAYOUT", "grouped8") != "grouped"
+            layout = "grouped8" if direction == _lib.DIR_FORWARD and not low and stream else "grouped"
+        if layout == "grouped8":
+            if direction != _lib.DIR_FORWARD:
+                raise RuntimeError("module tables in the GROUPED8 layout are built for the forward direction")
+            name = "_grouped8_fwd"
+        else:
+            name = "_grouped_fwd" if direction == _lib.DIR_FORWARD else "_grouped_inv"
         t = getattr(self, name)
         dense = tuple(getattr(self, n) for n in self._table_names)
         if t is None or t.device != dense[0].device:
             # the non-hot direction serves autograd: for the vector map it is the
             # conjugate transpose, whose grouped table carries the sign of W1
             conj = self.vector and direction != self._hot_direction
-            t = ops.group_table(dense, direction, conj=conj)
+            build = ops.group_table8 if layout == "grouped8" else ops.group_table
+            t = build(dense, direction, conj=conj)
             setattr(self, name, t)
-        return t, None, True
+            self.__dict__.pop("_contract_plans", None)  # prepared calls point at the old table
+        return t, None, layout
 
 
 DENSE_TC_MIN_BATCH = 128  # flattened batch from which the scalar forward runs on tcgen05
@@ -174,21 +198,65 @@ def _dense_tc_eligible(src, B: int, direction: int) -> bool:
     return B >= DENSE_TC_MIN_BATCH
 
 
+_MAX_PLANS = 32  # prepared contraction calls cached per table source
+
+
 def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_cols, scale, flags, nlon=0):
-    w0, w1, grouped = src.table(direction)
-    if grouped and src.vector:
+    w0, w1, layout = src.table(direction)
+    if layout != "strided" and src.vector:
         # grouped vector tables already encode the conjugate map (see table())
         assert bool(flags & _lib.FLAG_CONJ_W1) == (direction != src._hot_direction)
         flags &= ~_lib.FLAG_CONJ_W1
-    _contract(kind=_lib.KIND_VECTOR if src.vector else _lib.KIND_SCALAR, direction=direction,
-              input=inp, output=out, w0=w0, w1=w1, batch=B, nlat=src.nlat, lmax=src.lmax, mmax=M,
-              in_strides=in_vec_strides, out_strides=out_vec_strides, out_cols=out_cols, scale=scale,
-              flags=flags, nlon=nlon, grouped=grouped)
+    # the descriptor of a repeated call is built and checked once (ops.ContractPlan)
+    key = (direction, B, M, tuple(in_vec_strides), tuple(out_vec_strides), out_cols, scale, flags, nlon, layout,
+           w0.data_ptr(), None if w1 is None else w1.data_ptr(), inp.dtype, out.dtype, inp.device.index)
+    plans = src.__dict__.setdefault("_contract_plans", {})
+    plan = plans.get(key)
+    if plan is None:
+        if len(plans) >= _MAX_PLANS:
+            plans.clear()
+        plan = ops.ContractPlan(input_like=inp, output_like=out, kind=_lib.KIND_VECTOR if src.vector else _lib.KIND_SCALAR,
+                                direction=direction, w0=w0, w1=w1, batch=B, nlat=src.nlat, lmax=src.lmax, mmax=M,
+                                in_strides=in_vec_strides, out_strides=out_vec_strides, out_cols=out_cols,
+                                scale=scale, flags=flags, nlon=nlon, grouped=layout == "grouped",
+                                grouped8=layout == "grouped8")
+        plans[key] = plan
+    plan.launch(inp, out)
 
 
 # ---------------------------------------------------------------------------
 # module-level autograd functions (spectrum in rfft layout)
 # ---------------------------------------------------------------------------
+
+def _legendre_forward(spec, src, round_bf16: bool, scale: float):
+    """coef = scale * Legendre(spec[..., :mmax]) (the body of the module forward)."""
+    vector = src.vector
+    B, K = spec.size(0), spec.size(-2)
+    if K != src.nlat:
+        raise RuntimeError(f"spectrum has {K} latitudes, tables {src.nlat}")
+    L, M = src.lmax, src.mmax
+    shape = (B, 2, L, M) if vector else (B, L, M)
+    out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
+    if getattr(src, "variant", "table") == "recurrence" and not round_bf16:
+        # on-the-fly Legendre functions: no table stream
+        seeds, coef, ct = src.recurrence_tables()
+        ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
+    elif _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
+        # large batch: the per-order contraction is a dense GEMM -> tcgen05
+        ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
+                              lmax=L, mmax=M, scale=scale, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+    else:
+        _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
+             M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+    return out
+
+
+def _forward_coefficients(spec, src, round_bf16: bool, scale: float):
+    """Module forward: through autograd only when a gradient is wanted."""
+    if torch.is_grad_enabled() and spec.requires_grad:
+        return _SpectrumLegendreForward.apply(spec, src, round_bf16, scale)
+    return _legendre_forward(spec, src, round_bf16, scale)
+
 
 class _SpectrumLegendreForward(torch.autograd.Function):
     """coef = 2*pi * Legendre(spec[..., :mmax]) for an rfft spectrum
@@ -197,26 +265,9 @@ class _SpectrumLegendreForward(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, spec, src, round_bf16: bool, scale: float):
-        vector = src.vector
-        B, K, W = spec.size(0), spec.size(-2), spec.size(-1)
-        if K != src.nlat:
-            raise RuntimeError(f"spectrum has {K} latitudes, tables {src.nlat}")
-        L, M = src.lmax, src.mmax
-        shape = (B, 2, L, M) if vector else (B, L, M)
-        out = torch.empty(shape, device=spec.device, dtype=torch.complex64)
-        if getattr(src, "variant", "table") == "recurrence" and not round_bf16:
-            # on-the-fly Legendre functions: no table stream
-            seeds, coef, ct = src.recurrence_tables()
-            ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
-        elif _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
-            # large batch: the per-order contraction is a dense GEMM -> tcgen05
-            ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
-                                  lmax=L, mmax=M, scale=scale, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
-        else:
-            _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
-                 M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+        out = _legendre_forward(spec, src, round_bf16, scale)
         ctx.src = src
-        ctx.dims = (B, K, W)
+        ctx.dims = (spec.size(0), spec.size(-2), spec.size(-1))
         ctx.scale = scale
         return out
 
@@ -557,7 +608,7 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
         spec, scale, low = self._spectrum(x)
         lead = spec.shape[:-2]
         spec = spec.reshape(-1, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self, low, scale)
+        out = _forward_coefficients(spec, self, low, scale)
         return out.reshape(lead + (self.lmax, self.mmax))
 
 
@@ -618,7 +669,7 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
         spec, scale, low = self._spectrum(x)
         lead = spec.shape[:-3]
         spec = spec.reshape(-1, 2, self.nlat, spec.size(-1))
-        out = _SpectrumLegendreForward.apply(spec, self, low, scale)
+        out = _forward_coefficients(spec, self, low, scale)
         return out.reshape(lead + (2, self.lmax, self.mmax))
 
 

@@ -22,7 +22,7 @@ DTYPE_C64, DTYPE_F32, DTYPE_BF16 = 0, 1, 2
 KIND_SCALAR, KIND_VECTOR, KIND_REAL = 0, 1, 2
 DIR_FORWARD, DIR_INVERSE = 0, 1
 FLAG_CONJ_W1, FLAG_ROUND_BF16, FLAG_IRFFT_PREP = 1, 2, 4
-TABLE_STRIDED, TABLE_GROUPED = 0, 1
+TABLE_STRIDED, TABLE_GROUPED, TABLE_GROUPED8 = 0, 1, 2
 
 # every symbol include/holysht_b200.h declares
 EXPORTS = (
@@ -41,6 +41,7 @@ EXPORTS = (
     "holysht_legendre_dense_tc_workspace",
     "holysht_legendre_dense_tc",
     "holysht_tc_error_word",
+    "holysht_stream_error_word",
     "holysht_legendre_dense_tc_noalloc",
     "holysht_legendre_forward_recurrence",
 )
@@ -115,6 +116,7 @@ def load() -> ctypes.CDLL:
             "holysht_legendre_dense_tc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,
                                            ctypes.c_float, i32, i64, vp, i64, vp], i32),
             "holysht_tc_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
+            "holysht_stream_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
             "holysht_legendre_forward_recurrence": ([vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64,
                                                      ctypes.c_float, vp], i32),
             "holysht_legendre_dense_tc_noalloc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,

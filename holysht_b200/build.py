@@ -16,9 +16,9 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 SOURCES = [PKG / "csrc" / "capi.cu"]
-HEADERS = [PKG / "csrc" / "contract.cuh", PKG / "csrc" / "elementwise.cuh", ROOT / "include" / "holysht_b200.h"]
+HEADERS = [*(PKG / "csrc").glob("*.cuh"), ROOT / "include" / "holysht_b200.h"]
 LIB = PKG / "libholysht_b200.so"
-PROBE_SRC = PKG / "csrc" / "fp32_probe.cu"
+PROBE_SRCS = [PKG / "csrc" / "fp32_probe.cu", PKG / "csrc" / "bulk_probe.cu"]
 PROBE_LIB = PKG / "libholysht_b200_probe.so"
 
 
@@ -47,7 +47,7 @@ def command(verbose: bool = False) -> list[str]:
 
 def probe_command() -> list[str]:
     return [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-            "-shared", "-Xcompiler", "-fPIC", "-o", str(PROBE_LIB), str(PROBE_SRC), "-lcudart"]
+            "-shared", "-Xcompiler", "-fPIC", "-o", str(PROBE_LIB), *map(str, PROBE_SRCS), "-lcudart"]
 
 
 def up_to_date() -> bool:
@@ -64,7 +64,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             raise RuntimeError(f"nvcc failed:\n{res.stdout}\n{res.stderr}")
         if verbose:
             sys.stderr.write(res.stderr)
-    if force or not PROBE_LIB.exists() or PROBE_SRC.stat().st_mtime > PROBE_LIB.stat().st_mtime:
+    if force or not PROBE_LIB.exists() or any(p.stat().st_mtime > PROBE_LIB.stat().st_mtime for p in PROBE_SRCS):
         res = subprocess.run(probe_command(), capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"nvcc failed on the FP32 probe:\n{res.stdout}\n{res.stderr}")

@@ -19,6 +19,7 @@
 #include "elementwise.cuh"
 #include "tc_dense.cuh"
 #include "recurrence.cuh"
+#include "stream.cuh"
 
 namespace {
 
@@ -144,7 +145,8 @@ struct Job {
   long long in_bs, in_ps, in_rs, out_bs, out_ps, out_rs, out_cols, w_ls, w_ks, w_mt, nlon;
   float scale;
   int ksplit;
-  int grouped;
+  int grouped;   // HOLYSHT_TABLE_GROUPED
+  int grouped8;  // HOLYSHT_TABLE_GROUPED8 (streaming kernel)
   long long m_off;
 };
 
@@ -186,6 +188,7 @@ int dispatch_dir(const hsb::ContractParams& p, int dir, int nb, cudaStream_t str
 }
 
 int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream);
+int run_stream_job(const Job& j, long long R, long long S, cudaStream_t stream);
 
 int run_job(const Job& j, cudaStream_t stream) {
   if (j.kind < 0 || j.kind > 2) return fail(HOLYSHT_ERR_INVALID, "unknown kind %d", j.kind);
@@ -204,7 +207,7 @@ int run_job(const Job& j, cudaStream_t stream) {
   if (j.B == 0 || R == 0 || j.out_cols == 0) return ok();
   if (!j.out) return fail(HOLYSHT_ERR_INVALID, "output pointer is null");
   if (S > 0 && j.M > 0 && (!j.in || !j.w0)) return fail(HOLYSHT_ERR_INVALID, "input or table pointer is null");
-  if (j.kind == HOLYSHT_KIND_VECTOR && !j.grouped && S > 0 && j.M > 0 && !j.w1)
+  if (j.kind == HOLYSHT_KIND_VECTOR && !j.grouped && !j.grouped8 && S > 0 && j.M > 0 && !j.w1)
     return fail(HOLYSHT_ERR_INVALID, "vector contraction needs both tables");
   if (j.kind == HOLYSHT_KIND_REAL) {
     if (j.in_dtype != HOLYSHT_DTYPE_F32 && j.in_dtype != HOLYSHT_DTYPE_BF16)
@@ -220,6 +223,15 @@ int run_job(const Job& j, cudaStream_t stream) {
     return fail(HOLYSHT_ERR_INVALID,
                 "grouped vector tables carry the sign of W1 (W0 + W1, W0 - W1); build the "
                 "conjugate map's table from (W0, -W1) instead of passing HOLYSHT_FLAG_CONJ_W1");
+  if (j.grouped8) {
+    if (j.kind == HOLYSHT_KIND_REAL)
+      return fail(HOLYSHT_ERR_INVALID, "the GROUPED8 table layout is for complex contractions");
+    if (j.flags & (HOLYSHT_FLAG_CONJ_W1 | HOLYSHT_FLAG_ROUND_BF16))
+      return fail(HOLYSHT_ERR_INVALID,
+                  "the GROUPED8 layout takes neither HOLYSHT_FLAG_CONJ_W1 (build the table from "
+                  "(W0, -W1)) nor HOLYSHT_FLAG_ROUND_BF16");
+    return run_stream_job(j, R, S, stream);
+  }
   Job jj = j;
   if (j.grouped) {
     // row-grouped layout: [R/4 groups][ceil(M/32) tiles][S steps][32 lanes][4 rows][tables]
@@ -318,6 +330,123 @@ int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream
   if (j.in_dtype == HOLYSHT_DTYPE_BF16)
     return dispatch_dir<hsb::KIND_REAL, __nv_bfloat16, false>(p, j.dir, nb, stream);
   return dispatch_dir<hsb::KIND_REAL, float, false>(p, j.dir, nb, stream);
+}
+
+// ---- streaming kernel (GROUPED8 tables) ----
+
+template <int KIND, int DIR, int NB>
+int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStream_t stream) {
+  using Sm = hsb::stream::Smem<KIND, NB>;
+  static std::atomic<unsigned long long> configured{0};
+  auto kernel = hsb::stream::stream_kernel<KIND, DIR, NB>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Sm::kBytes);
+    if (e != cudaSuccess)
+      return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the streaming Legendre kernel: %s",
+                  cudaGetErrorString(e));
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  hsb::stream::Params p = p_in;
+  if (p.n_compute == 0) p.ks = 1;  // a grid of zero writers only
+  if (p.ks == 0) {
+    // one CTA per SM: the largest split whose compute CTAs all fit in one wave,
+    // each cluster rank keeping at least two spectrum chunks of the reduction
+    const long long slots = sm_count_of_current_device();
+    const long long tiles = (long long)p.n_compute * p.n_bg;
+    int ks = 1;
+    while (ks < 8 && tiles * ks * 2 <= slots && p.S / (2LL * ks) >= 2LL * hsb::stream::kMaxChunk) ks *= 2;
+    p.ks = ks;
+  }
+  if (grid_tiles * p.ks > INT_MAX / 2) return fail(HOLYSHT_ERR_INVALID, "problem too large for one launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_tiles * p.ks), 1, 1);
+  cfg.blockDim = dim3(hsb::stream::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Sm::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(HOLYSHT_ERR_CUDA, "streaming Legendre kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  return ok();
+}
+
+template <int KIND, int DIR>
+int stream_nb(const hsb::stream::Params& p, int nb, long long grid_tiles, cudaStream_t stream) {
+  switch (nb) {
+    case 1: return launch_stream<KIND, DIR, 1>(p, grid_tiles, stream);
+    case 2: return launch_stream<KIND, DIR, 2>(p, grid_tiles, stream);
+    case 4: return launch_stream<KIND, DIR, 4>(p, grid_tiles, stream);
+    default:
+      if constexpr (KIND == hsb::KIND_SCALAR) return launch_stream<KIND, DIR, 8>(p, grid_tiles, stream);
+      return launch_stream<KIND, DIR, 4>(p, grid_tiles, stream);
+  }
+}
+
+int run_stream_job(const Job& j, long long R, long long S, cudaStream_t stream) {
+  namespace st = hsb::stream;
+  if (j.ksplit != 0 && j.ksplit != 1 && j.ksplit != 2 && j.ksplit != 4 && j.ksplit != 8)
+    return fail(HOLYSHT_ERR_INVALID, "ksplit must be 0, 1, 2, 4 or 8");
+  const long long T = j.kind == HOLYSHT_KIND_VECTOR ? 2 : 1;
+  const long long step = 32LL * st::kRowsPerWarp * T;  // floats per (group, m tile, step)
+  const long long mt_tab = (j.M + st::kMTile - 1) / st::kMTile;
+  st::Params p = {};
+  p.in = static_cast<const float2*>(j.in);
+  p.out = j.out;
+  p.table = j.w0;
+  p.in_bs = j.in_bs;
+  p.in_ps = j.in_ps;
+  p.in_rs = j.in_rs;
+  p.out_bs = j.out_bs;
+  p.out_ps = j.out_ps;
+  p.out_rs = j.out_rs;
+  p.t_mt = S * step;
+  p.t_group = mt_tab * S * step;
+  p.B = (int)j.B;
+  p.M = (int)j.M;
+  p.R = (int)R;
+  p.S = (int)S;
+  p.out_cols = (int)j.out_cols;
+  p.scale = j.scale;
+  p.zero_imag_col0 = (j.flags & HOLYSHT_FLAG_IRFFT_PREP) ? 1 : 0;
+  p.nyquist = ((j.flags & HOLYSHT_FLAG_IRFFT_PREP) && j.nlon > 0 && j.nlon % 2 == 0) ? (int)(j.nlon / 2) : -1;
+  p.n_mt = (int)((j.out_cols + st::kMTile - 1) / st::kMTile);
+  const long long act_cols = (S > 0) ? j.M : 0;
+  const long long act_l = (S > 0 && j.L > j.m_off) ? j.L - j.m_off : 0;
+  const long long act = act_cols < act_l ? act_cols : act_l;
+  p.j_act = (int)std::min<long long>((act + st::kMTile - 1) / st::kMTile, p.n_mt);
+  p.m_off = (int)j.m_off;
+  p.mt_off = (int)(j.m_off / st::kMTile);
+  long long n_compute = 0, n_zero = 0;
+  for (int jt = 0; jt < p.n_mt; ++jt) {
+    const long long first =
+        jt < p.j_act ? (j.dir == HOLYSHT_DIR_FORWARD ? std::min<long long>(32LL * (jt + p.mt_off), R) : 0) : R;
+    if (jt < p.j_act) n_compute += (R - first + st::kRows - 1) / st::kRows;
+    n_zero += (first + st::kRows - 1) / st::kRows;
+  }
+  p.n_compute = (int)n_compute;
+  p.n_zero = (int)n_zero;
+  const int nb = next_pow2_at_least(j.B, 1, j.kind == HOLYSHT_KIND_VECTOR ? 4 : 8);
+  p.n_bg = (int)((j.B + nb - 1) / nb);
+  p.ks = j.ksplit ? j.ksplit : env_ksplit();
+  // the grid holds the compute tiles; their CTAs also write the zero tiles
+  if (n_compute + n_zero == 0) return ok();
+  const long long grid_tiles = n_compute > 0 ? n_compute * p.n_bg : std::min<long long>(n_zero * p.n_bg, 148);
+  if (j.kind == HOLYSHT_KIND_VECTOR)
+    return j.dir == HOLYSHT_DIR_FORWARD ? stream_nb<hsb::KIND_VECTOR, 0>(p, nb, grid_tiles, stream)
+                                        : stream_nb<hsb::KIND_VECTOR, 1>(p, nb, grid_tiles, stream);
+  return j.dir == HOLYSHT_DIR_FORWARD ? stream_nb<hsb::KIND_SCALAR, 0>(p, nb, grid_tiles, stream)
+                                      : stream_nb<hsb::KIND_SCALAR, 1>(p, nb, grid_tiles, stream);
 }
 
 // Dense contiguous job in the reference layouts.
@@ -551,6 +680,15 @@ int holysht_tc_error_word(unsigned* value) {
 }
 
 
+int holysht_stream_error_word(unsigned* value) {
+  if (!value) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  unsigned zero = 0;
+  if (cudaMemcpyFromSymbol(value, hsb::stream::g_stream_error, sizeof(unsigned)) != cudaSuccess ||
+      cudaMemcpyToSymbol(hsb::stream::g_stream_error, &zero, sizeof(unsigned)) != cudaSuccess)
+    return fail(HOLYSHT_ERR_CUDA, "cannot read the streaming kernel's error word");
+  return ok();
+}
+
 int holysht_version(void) { return 100; }
 
 const char* holysht_last_error(void) { return g_last_error.c_str(); }
@@ -633,10 +771,12 @@ int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
   j.w_ks = d->w_k_stride;
   j.w_mt = d->w_m_tile_stride ? d->w_m_tile_stride : hsb::kMTile;
   j.grouped = d->table_layout == HOLYSHT_TABLE_GROUPED;
+  j.grouped8 = d->table_layout == HOLYSHT_TABLE_GROUPED8;
   j.m_off = d->m_offset;
   if (j.m_off < 0 || j.m_off % hsb::kMTile != 0 || !fits_int(j.m_off))
     return fail(HOLYSHT_ERR_INVALID, "m_offset must be a non-negative multiple of 32");
-  if (d->table_layout != HOLYSHT_TABLE_STRIDED && d->table_layout != HOLYSHT_TABLE_GROUPED)
+  if (d->table_layout != HOLYSHT_TABLE_STRIDED && d->table_layout != HOLYSHT_TABLE_GROUPED &&
+      d->table_layout != HOLYSHT_TABLE_GROUPED8)
     return fail(HOLYSHT_ERR_INVALID, "unknown table_layout %d", d->table_layout);
   j.nlon = d->nlon;
   j.scale = d->scale;

@@ -1,0 +1,523 @@
+// Warp-specialised streaming Legendre contraction for sm_100a (row groups of 8).
+//
+// Same contraction as contract.cuh (KIND_SCALAR / KIND_VECTOR, both
+// directions), for the table layout HOLYSHT_TABLE_GROUPED8:
+//
+//   T[g][mt][s][q][lane][4]   g = row / 8, mt = m / 32, s = reduction step,
+//                             lane = m % 32, q = quad of the lane's 8 rows x T tables
+//   vector (T = 2): quad q holds (row 2q: T0, T1, row 2q+1: T0, T1), T0 = W0 + W1, T1 = W0 - W1
+//   scalar (T = 1): quad q holds rows 4q .. 4q+3
+//
+// so one warp's step is one contiguous 1 KB (scalar) / 2 KB (vector) block in
+// which every 16-byte read of the 32 lanes is a conflict-free 512-byte row.
+//
+// CTA = 8 warps x 8 rows (64 output rows) x 32 orders x NB batches; the
+// reduction is split over a thread-block cluster of ks CTAs whose partial sums
+// meet in distributed shared memory (fixed rank order: deterministic).
+//   * every warp streams its own table block into a private ring of
+//     shared-memory stages with cp.async.bulk (one elected lane, mbarrier
+//     transaction counts), so the table never occupies registers and HBM
+//     requests stay in flight without any per-load instruction;
+//   * the input spectrum (shared by the 8 warps) goes through a 3-deep ring
+//     staged by all threads with cp.async; each thread's copies arrive on the
+//     chunk's full mbarrier when they land (cp.async.mbarrier.arrive.noinc),
+//     and an empty mbarrier per stage keeps a stage from being refilled before
+//     every warp has read it: no __syncthreads in the main loop;
+//   * 8 rows per warp halve the spectrum reads per FMA relative to 4 rows; the
+//     vector kind forms u = c0 + i c1, v = c0 - i c1 in registers; the FMAs
+//     are packed f32x2 (FFMA2).
+// Every mbarrier wait is bounded; a wait that gives up sets bit 0 of
+// g_stream_error and the CTA skips the rest of its reduction (its output is
+// then garbage, and the host reads the error word).
+#pragma once
+
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hsb {
+namespace stream {
+
+namespace cg = cooperative_groups;
+
+constexpr int kCons = 8;  // warps
+constexpr int kThreads = kCons * 32;
+constexpr int kRowsPerWarp = 8;
+constexpr int kRows = kCons * kRowsPerWarp;  // 64 output rows per CTA
+constexpr int kMTile = 32;
+#ifndef HSB_STREAM_CHUNK_V
+#define HSB_STREAM_CHUNK_V 4
+#endif
+#ifndef HSB_STREAM_CHUNK_S
+#define HSB_STREAM_CHUNK_S 8
+#endif
+#ifndef HSB_STREAM_TAB_STAGES_V
+#define HSB_STREAM_TAB_STAGES_V 3
+#endif
+#ifndef HSB_STREAM_TAB_STAGES_S
+#define HSB_STREAM_TAB_STAGES_S 3
+#endif
+// a chunk = the reduction steps of one spectrum stage and of one table stage
+// per warp: 4 steps (8 KB of table per warp) for the vector kind, 8 steps
+// (8 KB) for the scalar kind
+constexpr int kMaxChunk = HSB_STREAM_CHUNK_V > HSB_STREAM_CHUNK_S ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S;
+#ifndef HSB_STREAM_SPEC_STAGES
+#define HSB_STREAM_SPEC_STAGES 4
+#endif
+#ifndef HSB_STREAM_SPEC_AHEAD
+#define HSB_STREAM_SPEC_AHEAD 3
+#endif
+constexpr int kSpecStages = HSB_STREAM_SPEC_STAGES;  // spectrum ring depth
+constexpr int kSpecAhead = HSB_STREAM_SPEC_AHEAD;    // chunks staged ahead of the one being read
+static_assert(kSpecStages >= kSpecAhead + 1 && kSpecAhead >= 1, "spectrum ring too shallow");
+constexpr int kSmemLimit = 227 * 1024 - 2048;  // dynamic shared memory per CTA, minus static and reserve
+constexpr unsigned kWaitLimit = 1u << 22;
+
+__device__ unsigned g_stream_error = 0;
+
+struct Params {
+  const float2* in;
+  void* out;
+  const float* table;
+  long long in_bs, in_ps, in_rs;
+  long long out_bs, out_ps, out_rs;
+  long long t_group, t_mt;  // table strides (floats): row group of 8, m tile; a step is 256*T floats
+  int B, M, R, S;           // batch, table orders, output rows, reduction extent
+  int out_cols;
+  float scale;
+  int zero_imag_col0, nyquist;
+  int n_mt, j_act, n_compute, n_zero, n_bg, ks;
+  int m_off, mt_off;
+};
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait: false (and the error bit) instead of hanging
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  for (unsigned it = 0; it < kWaitLimit; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (it > 32) __nanosleep(32);
+  }
+  atomicOr(&g_stream_error, 1u);
+  return false;
+}
+// one elected lane: expect `bytes` on `bar`, then bulk-copy them global -> shared
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async8(void* dst, const void* src, bool ok) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(ok ? 8 : 0));
+}
+
+template <int KIND>
+struct Shape {
+  static constexpr int P = KIND == 1 ? 2 : 1;  // components (KIND_VECTOR = 1)
+  static constexpr int T = KIND == 1 ? 2 : 1;  // interleaved tables
+  static constexpr int kStepFloats = 32 * kRowsPerWarp * T;  // one warp's step
+  static constexpr int kQuads = kRowsPerWarp * T / 4;
+  static constexpr int kChunk = KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S;
+};
+
+template <int KIND, int NB>
+struct Smem {
+  static constexpr int P = Shape<KIND>::P;
+  static constexpr int PB = NB * P;
+  static constexpr int NA = NB * P;  // complex accumulators per row
+  static constexpr int kSpecBytes = kSpecStages * Shape<KIND>::kChunk * PB * 32 * 8;
+  static constexpr int kStageBytes = kCons * Shape<KIND>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
+  // table ring depth: the configured one, or as many as fit next to the spectrum ring
+  static constexpr int kWant = KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S;
+  static constexpr int kFit = (kSmemLimit - kSpecBytes) / kStageBytes;
+  static constexpr int kTabStages = kWant < kFit ? kWant : kFit;
+  static_assert(kTabStages >= 2, "table ring needs two stages");
+  static constexpr int kTabBytes = kTabStages * kStageBytes;
+  static constexpr int kPartBytes = kRows * NA * 32 * 8;
+  static constexpr int kLoop = kSpecBytes + kTabBytes;
+  static constexpr int kBytes = kLoop > kPartBytes ? kLoop : kPartBytes;
+};
+
+// Tile t -> m tile j and output rows [r0, r1); compute tiles first (by m
+// tile), then tiles of exact zeros (rows above the diagonal, and m tiles
+// with no l >= m inside the table).
+template <int DIR>
+__device__ __forceinline__ bool decode(const Params& p, int t, int& j, int& r0, int& r1) {
+  if (t < p.n_compute) {
+    int rem = t;
+    for (j = 0; j < p.j_act; ++j) {
+      const int first = DIR == 0 ? min(kMTile * (j + p.mt_off), p.R) : 0;
+      const int cnt = (p.R - first + kRows - 1) / kRows;
+      if (rem < cnt) {
+        r0 = first + rem * kRows;
+        r1 = min(r0 + kRows, p.R);
+        return true;
+      }
+      rem -= cnt;
+    }
+  } else {
+    int rem = t - p.n_compute;
+    for (j = 0; j < p.n_mt; ++j) {
+      const int zr = j < p.j_act ? (DIR == 0 ? min(kMTile * (j + p.mt_off), p.R) : 0) : p.R;
+      const int cnt = (zr + kRows - 1) / kRows;
+      if (rem < cnt) {
+        r0 = rem * kRows;
+        r1 = min(r0 + kRows, zr);
+        return false;
+      }
+      rem -= cnt;
+    }
+  }
+  j = p.n_mt;
+  r0 = r1 = 0;
+  return false;
+}
+
+// Exact zeros of the output outside the compute tiles (rows above the
+// diagonal, and m tiles with no l >= m inside the table), spread over the
+// grid's CTAs before their own tiles: the grid holds compute tiles only, so no
+// SM is taken by a CTA that only writes zeros.
+template <int DIR, int NB, int P>
+__device__ __forceinline__ void write_zero_units(const Params& p) {
+  const int nz = p.n_zero * p.n_bg;
+  for (int z = blockIdx.x; z < nz; z += gridDim.x) {
+    int j, r0, r1;
+    decode<DIR>(p, p.n_compute + z / p.n_bg, j, r0, r1);
+    const int b0 = (z % p.n_bg) * NB, m0 = j * kMTile;
+    const int total = (r1 - r0) * NB * P * 32;
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int col = e & 31;
+      const int a = (e >> 5) % (NB * P);
+      const int row = r0 + e / (NB * P * 32);
+      const int mm = m0 + col, b = b0 + a / P, pl = a % P;
+      if (mm < p.out_cols && b < p.B)
+        static_cast<float2*>(p.out)[(long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs +
+                                    mm] = make_float2(0.f, 0.f);
+    }
+  }
+}
+
+template <int KIND, int DIR, int NB>
+__global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
+  using S = Smem<KIND, NB>;
+  constexpr int P = S::P, PB = S::PB, NA = S::NA;
+  constexpr int T = Shape<KIND>::T;
+  constexpr int kStepFloats = Shape<KIND>::kStepFloats;
+  constexpr int kTabStages = S::kTabStages;
+  constexpr int kChunk = Shape<KIND>::kChunk;
+  constexpr int kStageFloats = kChunk * kStepFloats;  // one warp's table stage
+  constexpr int kSpecStageElems = kChunk * PB * 32;  // float2 per spectrum stage
+
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  float2* spec = reinterpret_cast<float2*>(smem_raw);                    // [stage][step][plane][lane]
+  float* tab = reinterpret_cast<float*>(smem_raw + S::kSpecBytes);       // [warp][stage][step floats]
+  float2* part = reinterpret_cast<float2*>(smem_raw);  // [source rank][owned row][NA][lane], after the loop
+  __shared__ __align__(8) uint64_t full_bar[kSpecStages], empty_bar[kSpecStages];
+  __shared__ __align__(8) uint64_t tab_bar[kCons][Smem<KIND, NB>::kTabStages];
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int ks = p.ks;
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tile = blockIdx.x / ks;
+  const int bg = tile % p.n_bg;
+  int j, r0, r1;
+  const bool compute = decode<DIR>(p, tile / p.n_bg, j, r0, r1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b0 = bg * NB;
+  const int m0 = j * kMTile;
+
+  // zeros first: fire-and-forget stores that drain while the table stream ramps up
+  write_zero_units<DIR, NB, P>(p);
+  if (!compute) return;  // the grid holds no compute tile (launched with clusters of one)
+
+  const int m0g = m0 + p.m_off;
+  const int s_begin = DIR == 0 ? 0 : min(m0g, p.S);
+  const int nsteps = p.S - s_begin;
+  const int per = ((nsteps + ks * kChunk - 1) / (ks * kChunk)) * kChunk;
+  const int r_begin = min(p.S, s_begin + rank * per);
+  const int r_end = min(p.S, r_begin + per);
+  const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
+  const int n_valid = min(kCons, (r1 - r0 + kRowsPerWarp - 1) / kRowsPerWarp);  // warps with rows
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSpecStages; ++i) {
+      mbar_init(&full_bar[i], kThreads);
+      mbar_init(&empty_bar[i], kThreads);
+    }
+    for (int w = 0; w < kCons; ++w)
+      for (int i = 0; i < kTabStages; ++i) mbar_init(&tab_bar[w][i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+
+  float2 acc[kRowsPerWarp][NA];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+    for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
+
+  // ---- spectrum ring, staged by all threads ----
+  // thread -> (batch, order) column and steps st_ls0, st_ls0 + kLsStep, ... of
+  // each chunk; it copies every component of those entries.  Scalar: the
+  // copies arrive on the chunk's full barrier when they land (no thread waits
+  // for them).  Vector: the thread waits for its own copies one chunk later,
+  // forms u = c0 + i c1, v = c0 - i c1 in place (once per CTA, not per warp)
+  // and then arrives.
+  constexpr int kLsStep = kThreads / (NB * 32);
+  constexpr int kStageIters = (kChunk + kLsStep - 1) / kLsStep;
+  static_assert(kThreads % (NB * 32) == 0, "spectrum staging map");
+  const int st_b = (threadIdx.x >> 5) % NB;
+  const int st_ls0 = threadIdx.x / (NB * 32);
+  const bool st_ok = m0 + lane < p.M && b0 + st_b < p.B;
+  const float2* st_src = p.in + (st_ok ? (long long)(b0 + st_b) * p.in_bs + m0 + lane : 0);
+  float2* const st_dst = spec + (st_ls0 * PB + st_b * P) * 32 + lane;  // + slot * kSpecStageElems
+  auto stage = [&](int c, int slot) {
+    float2* dst = st_dst + slot * kSpecStageElems;
+    const int s0 = r_begin + c * kChunk + st_ls0;
+#pragma unroll
+    for (int it = 0; it < kStageIters; ++it) {
+      if (kChunk % kLsStep == 0 || st_ls0 + it * kLsStep < kChunk) {
+        const int s = s0 + it * kLsStep;
+        const bool ok = st_ok && s < r_end;
+        const float2* src = ok ? st_src + (long long)s * p.in_rs : p.in;
+#pragma unroll
+        for (int pl = 0; pl < P; ++pl)
+          cp_async8(dst + (it * kLsStep * PB + pl) * 32, ok ? src + pl * p.in_ps : p.in, ok);
+      }
+    }
+  };
+  auto combine = [&](int slot) {
+    float2* d = st_dst + slot * kSpecStageElems;
+#pragma unroll
+    for (int it = 0; it < kStageIters; ++it) {
+      if (kChunk % kLsStep == 0 || st_ls0 + it * kLsStep < kChunk) {
+        float2* e = d + it * kLsStep * PB * 32;
+        const float2 c0 = e[0], c1 = e[32];
+        e[0] = make_float2(c0.x - c1.y, c0.y + c1.x);   // u = c0 + i c1
+        e[32] = make_float2(c0.x + c1.y, c0.y - c1.x);  // v = c0 - i c1
+      }
+    }
+  };
+  auto publish_async = [&](int slot) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(&full_bar[slot]))
+                 : "memory");
+  };
+
+  // ---- this warp's table ring (one stage per chunk) ----
+  const bool has_rows = warp < n_valid;
+  const int g = (r0 >> 3) + warp;  // row group of 8 (r0 is a multiple of 8)
+  const float* tsrc = p.table + (long long)(has_rows ? g : 0) * p.t_group + (long long)j * p.t_mt +
+                      (long long)r_begin * kStepFloats;
+  float* my = tab + warp * kTabStages * kStageFloats;
+  const int nst = has_rows ? nchunks : 0;
+  auto issue_tab = [&](int q, int slot) {
+    const int n = min(kChunk, r_end - (r_begin + q * kChunk));
+    bulk_load(my + slot * kStageFloats, tsrc + (long long)q * kChunk * kStepFloats,
+              (unsigned)(n * kStepFloats * 4), &tab_bar[warp][slot]);
+  };
+  if (lane == 0)
+    for (int q = 0; q < kTabStages && q < nst; ++q) issue_tab(q, q);
+  int issued = min(kTabStages, nst);
+
+  auto step = [&](const float* ts, const float2* xs) {
+    // ts: this step's table block; xs: this step's staged spectrum planes
+    // (vector: planes 2b, 2b+1 hold u, v of batch b)
+    float w[kRowsPerWarp * T];
+#pragma unroll
+    for (int q = 0; q < Shape<KIND>::kQuads; ++q) {
+      const float4 v = reinterpret_cast<const float4*>(ts)[q * 32 + lane];
+      w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+    }
+    float2 x[PB];
+#pragma unroll
+    for (int a = 0; a < PB; ++a) x[a] = xs[a * 32 + lane];
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+      if constexpr (KIND == 1) {
+        const float wp = w[2 * i], wm = w[2 * i + 1];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          acc[i][2 * b] = __ffma2_rn(make_float2(wp, wp), x[2 * b], acc[i][2 * b]);
+          acc[i][2 * b + 1] = __ffma2_rn(make_float2(wm, wm), x[2 * b + 1], acc[i][2 * b + 1]);
+        }
+      } else {
+        const float wv = w[i];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[i][b] = __ffma2_rn(make_float2(wv, wv), x[b], acc[i][b]);
+      }
+    }
+  };
+
+  bool alive = true;
+  // running ring positions: chunk c's spectrum slot/phase; the slot chunk
+  // c + kSpecAhead is staged into and the phase of the empty barrier it waits
+  // on; this warp's table slot/phase
+  int cs = 0, cph = 0, ps = kSpecAhead % kSpecStages, pph = (kSpecAhead / kSpecStages) & 1, ts_ = 0, tph = 0;
+#pragma unroll
+  for (int q = 0; q < kSpecAhead; ++q) {
+    if (q < nchunks) {
+      stage(q, q);
+      if constexpr (KIND != 1) publish_async(q);
+    }
+    if constexpr (KIND == 1) cp_async_commit();
+  }
+  if constexpr (KIND == 1) {
+    if (nchunks > 0) {
+      cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk 0 have landed
+      combine(0);
+      mbar_arrive(&full_bar[0]);
+    }
+  }
+  for (int c = 0; c < nchunks; ++c) {
+    const int cn = c + kSpecAhead;
+    if (cn < nchunks) {
+      // the slot chunk cn reuses was last read by chunk cn - kSpecStages
+      if (cn >= kSpecStages && !mbar_wait(&empty_bar[ps], pph ^ 1)) {
+        alive = false;
+        break;
+      }
+      stage(cn, ps);
+      if constexpr (KIND != 1) publish_async(ps);
+    }
+    if (++ps == kSpecStages) {
+      ps = 0;
+      pph ^= 1;
+    }
+    if constexpr (KIND == 1) {
+      cp_async_commit();
+      if (c + 1 < nchunks) {
+        cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk c + 1 have landed
+        const int s1 = cs + 1 == kSpecStages ? 0 : cs + 1;
+        combine(s1);
+        mbar_arrive(&full_bar[s1]);
+      }
+    }
+    if (!mbar_wait(&full_bar[cs], cph)) {
+      alive = false;
+      break;
+    }
+    if (has_rows) {
+      if (!mbar_wait(&tab_bar[warp][ts_], tph)) {
+        alive = false;
+        break;
+      }
+      const float2* xs = spec + cs * kSpecStageElems;
+      const float* tsb = my + ts_ * kStageFloats;
+      const int s0 = r_begin + c * kChunk;
+      if (s0 + kChunk <= r_end) {
+#pragma unroll
+        for (int ls = 0; ls < kChunk; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
+      } else {
+#pragma unroll 1
+        for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
+      }
+      // stage consumed by every lane: refill it with chunk c + kTabStages
+      __syncwarp();
+      if (lane == 0 && issued < nst) {
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        issue_tab(issued, ts_);
+      }
+      ++issued;
+      if (++ts_ == kTabStages) {
+        ts_ = 0;
+        tph ^= 1;
+      }
+    }
+    mbar_arrive(&empty_bar[cs]);
+    if (++cs == kSpecStages) {
+      cs = 0;
+      cph ^= 1;
+    }
+  }
+  // nothing may still be writing into the rings when they become the partial-sum buffer
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  if (!alive && lane == 0 && has_rows) {
+    // a wait gave up: let this warp's table copies still in flight land first
+    const int done = min(issued, nst);
+    for (int q = max(0, done - kTabStages); q < done; ++q)
+      mbar_wait(&tab_bar[warp][q % kTabStages], (q / kTabStages) & 1);
+  }
+  __syncwarp();
+
+  if constexpr (KIND == 1) {
+    // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const float2 pu = acc[i][2 * b], mv = acc[i][2 * b + 1];
+        acc[i][2 * b] = make_float2(0.5f * (mv.x + pu.x), 0.5f * (mv.y + pu.y));
+        acc[i][2 * b + 1] = make_float2(0.5f * (mv.y - pu.y), -0.5f * (mv.x - pu.x));
+      }
+  }
+
+  // ---- cluster reduction: every warp stores its rows' partial sums straight
+  // into the shared memory of the cluster rank that owns those rows (remote
+  // stores do not stall the warp), one cluster barrier, then each owner adds
+  // its ks slices in rank order (deterministic) from local shared memory.
+  const int rpr = kRows / ks;  // rows per owner rank, a multiple of 8
+  cluster.sync();              // every CTA of the cluster is done with its rings
+  {
+    const int owner = (warp * kRowsPerWarp) / rpr;
+    const int rl0 = warp * kRowsPerWarp - owner * rpr;
+    float2* dst = cluster.map_shared_rank(part, owner) + ((rank * rpr + rl0) * NA) * 32 + lane;
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+      for (int a = 0; a < NA; ++a) dst[(i * NA + a) * 32] = acc[i][a];
+  }
+  cluster.sync();
+
+  const int total = rpr * NA * 32;
+  for (int e = threadIdx.x; e < total; e += kThreads) {
+    const int col = e & 31;
+    const int a = (e >> 5) % NA;
+    const int rl = e / (NA * 32);
+    const int row = r0 + rank * rpr + rl;
+    const int mm = m0 + col;
+    if (row >= r1 || mm >= p.out_cols) continue;
+    float2 sum = make_float2(0.f, 0.f);
+    for (int q = 0; q < ks; ++q) {
+      const float2 v = part[((q * rpr + rl) * NA + a) * 32 + col];
+      sum.x += v.x;
+      sum.y += v.y;
+    }
+    sum.x *= p.scale;
+    sum.y *= p.scale;
+    if ((p.zero_imag_col0 && mm == 0) || mm == p.nyquist) sum.y = 0.f;
+    const int b = b0 + a / P, pl = a % P;
+    if (b < p.B)
+      static_cast<float2*>(p.out)[(long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs +
+                                  mm] = sum;
+  }
+}
+
+}  // namespace stream
+}  // namespace hsb

@@ -105,7 +105,7 @@ class _OrderSharded(nn.Module):
         self.width_pad = max(b - a for a, b in self.ranges) or 1
         local = [t[:, :, lo:hi].contiguous() for t in dense_tables]  # [L, K, width]
         if hi > lo:
-            grouped = ops.group_table(tuple(local), _lib.DIR_FORWARD)  # (W0+W1, W0-W1) for vector
+            grouped = ops.group_table(tuple(local), _lib.DIR_FORWARD, m_offset=lo)  # (W0+W1, W0-W1) for vector
         else:
             grouped = torch.zeros((1, 1, 1, 32, 4, len(local)), dtype=torch.float32)
         self.register_buffer("table_local", grouped, persistent=False)

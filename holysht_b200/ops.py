@@ -33,8 +33,11 @@ __all__ = [
     "fused_vector_forward_recompose_real",
     "sht_prepare_irfft",
     "legendre_contract",
+    "ContractPlan",
     "tile_table",
     "group_table",
+    "group_table8",
+    "stream_error_word",
     "legendre_dense_tc",
     "tc_error_word",
     "legendre_forward_recurrence",
@@ -227,16 +230,19 @@ def tile_table(weight_t: torch.Tensor) -> torch.Tensor:
     return padded.view(L, K, mt, 32).permute(0, 2, 1, 3).contiguous()
 
 
-def group_table(tables, direction: int, conj: bool = False) -> torch.Tensor:
+def group_table(tables, direction: int, conj: bool = False, m_offset: int = 0) -> torch.Tensor:
     """Row-grouped table for the contraction kernel (``HOLYSHT_TABLE_GROUPED``).
 
     ``tables``: one dense [lmax, nlat, mmax] table, or a (W0, W1) pair for the
     vector kind.  ``direction``: ``DIR_FORWARD`` (rows = l, steps = k) or
     ``DIR_INVERSE`` (rows = k, steps = l).  Result [R/4, ceil(M/32), S, 32, 4, T]:
     per 4-row group, m tile and step, the 32 lanes' rows x tables are
-    contiguous, zero outside the tables.  A vector pair is stored as
-    (W0 + s W1, W0 - s W1), s = -1 when ``conj`` (the conjugate-transpose map
-    autograd needs), which is the form the kernel contracts."""
+    contiguous, zero outside the tables and above the diagonal (l < m, with m
+    the global order ``m_offset + column``: the kernel streams whole blocks
+    without per-entry predicates, so the zeros are part of the layout).  A
+    vector pair is stored as (W0 + s W1, W0 - s W1), s = -1 when ``conj`` (the
+    conjugate-transpose map autograd needs), which is the form the kernel
+    contracts."""
     if torch.is_tensor(tables):
         tables = (tables,)
     if len(tables) == 2:
@@ -250,10 +256,11 @@ def group_table(tables, direction: int, conj: bool = False) -> torch.Tensor:
     rg = (R + 3) // 4
     dev = tables[0].device
     out = torch.zeros((rg, mt, S, 32, 4, len(tables)), dtype=torch.float32, device=dev)
+    tri = (torch.arange(M, device=dev)[None, :] + m_offset <= torch.arange(L, device=dev)[:, None])
     for t, w in enumerate(tables):
         _require(tuple(w.shape) == (L, K, M) and w.dtype == torch.float32, "tables must match, float32")
         pad = torch.zeros((rg * 4 if fwd else L, K if fwd else rg * 4, mt * 32), dtype=torch.float32, device=dev)
-        pad[:L, :K, :M] = w
+        pad[:L, :K, :M] = w * tri[:, None, :]
         if fwd:   # [l, k, m] -> [g, r, k, mt, lane] -> [g, mt, k, lane, r]
             v = pad.view(rg, 4, K, mt, 32).permute(0, 3, 2, 4, 1)
         else:     # [l, k, m] -> [l, g, r, mt, lane] -> [g, mt, l, lane, r]
@@ -262,23 +269,116 @@ def group_table(tables, direction: int, conj: bool = False) -> torch.Tensor:
     return out
 
 
+def group_table8(tables, direction: int, conj: bool = False, m_offset: int = 0) -> torch.Tensor:
+    """Table in the ``HOLYSHT_TABLE_GROUPED8`` layout of the streaming kernel.
+
+    Rows (l for ``DIR_FORWARD``, k for ``DIR_INVERSE``) in groups of 8; per
+    group, 32-order m tile and reduction step, each lane's 8 rows x T tables
+    are stored as 2T quads of 4 floats, quad-major across the lanes:
+    result [ceil(R/8), ceil(M/32), S, 2T, 32, 4].  Vector quads hold
+    (row 2q: W0 + s W1, W0 - s W1, row 2q+1: the same), s = -1 when ``conj``;
+    scalar quads hold rows 4q .. 4q+3.  Zero outside the tables and above the
+    diagonal (l < m_offset + column)."""
+    if torch.is_tensor(tables):
+        tables = (tables,)
+    if len(tables) == 2:
+        w0, w1 = tables
+        s1 = -1.0 if conj else 1.0
+        tables = (w0 + s1 * w1, w0 - s1 * w1)
+    L, K, M = tables[0].shape
+    T = len(tables)
+    mt = (M + 31) // 32
+    fwd = direction == _lib.DIR_FORWARD
+    R, S = (L, K) if fwd else (K, L)
+    rg = (R + 7) // 8
+    dev = tables[0].device
+    x = torch.zeros((rg, mt, S, 32, 8, T), dtype=torch.float32, device=dev)
+    tri = (torch.arange(M, device=dev)[None, :] + m_offset <= torch.arange(L, device=dev)[:, None])
+    for t, w in enumerate(tables):
+        _require(tuple(w.shape) == (L, K, M) and w.dtype == torch.float32, "tables must match, float32")
+        pad = torch.zeros((rg * 8 if fwd else L, K if fwd else rg * 8, mt * 32), dtype=torch.float32, device=dev)
+        pad[:L, :K, :M] = w * tri[:, None, :]
+        if fwd:   # [l, k, m] -> [g, r, k, mt, lane] -> [g, mt, k, lane, r]
+            v = pad.view(rg, 8, K, mt, 32).permute(0, 3, 2, 4, 1)
+        else:     # [l, k, m] -> [l, g, r, mt, lane] -> [g, mt, l, lane, r]
+            v = pad.view(L, rg, 8, mt, 32).permute(1, 3, 0, 4, 2)
+        x[..., t] = v
+        del pad, v
+    return x.view(rg, mt, S, 32, 2 * T, 4).permute(0, 1, 2, 4, 3, 5).contiguous()
+
+
+def _current_stream_handle(dev_index: int) -> int:
+    getter = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if getter is not None:
+        return getter(dev_index)
+    return torch.cuda.current_stream(dev_index).cuda_stream
+
+
+class ContractPlan:
+    """A prepared :func:`legendre_contract` call: the descriptor is built and
+    checked once, :meth:`launch` only fills in the input and output pointers
+    (for callers that launch the same contraction repeatedly, such as the
+    modules' forward).  ``input_like`` / ``output_like`` fix the dtypes and the
+    device; later tensors must match them and the strides given here."""
+
+    __slots__ = ("_desc", "_dev", "_in_dtype", "_out_dtype", "_keep")
+
+    def __init__(self, *, input_like: torch.Tensor, output_like: torch.Tensor, **kw):
+        self._desc = _contract_desc(input=input_like, output=output_like, **kw)
+        self._dev = input_like.device.index
+        self._in_dtype, self._out_dtype = input_like.dtype, output_like.dtype
+        self._keep = (kw.get("w0"), kw.get("w1"))  # the tables stay alive with the plan
+
+    def launch(self, input: torch.Tensor, output: torch.Tensor) -> None:
+        _require(input.is_cuda and input.device.index == self._dev and output.device == input.device
+                 and input.dtype == self._in_dtype and output.dtype == self._out_dtype,
+                 "tensors do not match the contraction plan")
+        d = self._desc
+        d.in_, d.out = input.data_ptr(), output.data_ptr()
+        lib = _lib.load()
+        if torch.cuda.current_device() == self._dev:
+            _lib.check(lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev)))
+        else:
+            with torch.cuda.device(self._dev):
+                _lib.check(lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev)))
+
+
 def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,
                       w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
                       scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0,
-                      w_strides=None, grouped: bool = False, m_offset: int = 0) -> None:
+                      w_strides=None, grouped: bool = False, m_offset: int = 0,
+                      grouped8: bool = False) -> None:
     """Strided contraction; strides are (batch, component, row) in elements.
 
     ``w0``/``w1`` are either dense [lmax, nlat, mmax] tables (m contiguous) or
     m-tiled tables from :func:`tile_table` ([lmax, ceil(mmax/32), nlat, 32]);
     ``w_strides`` = (l, k, m-tile) strides in floats overrides the inference.
-    ``grouped``: ``w0`` is a :func:`group_table` table (``w1`` unused)."""
-    dev = _cuda(output, input, w0)
+    ``grouped``: ``w0`` is a :func:`group_table` table (``w1`` unused);
+    ``grouped8``: ``w0`` is a :func:`group_table8` table (streaming kernel)."""
+    d = _contract_desc(kind=kind, direction=direction, input=input, output=output, w0=w0, w1=w1, batch=batch,
+                       nlat=nlat, lmax=lmax, mmax=mmax, in_strides=in_strides, out_strides=out_strides,
+                       out_cols=out_cols, scale=scale, flags=flags, nlon=nlon, ksplit=ksplit, w_strides=w_strides,
+                       grouped=grouped, m_offset=m_offset, grouped8=grouped8)
+    dev = input.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))
+
+
+def _contract_desc(*, kind, direction, input, output, w0, w1=None, batch, nlat, lmax, mmax, in_strides,
+                   out_strides, out_cols, scale=1.0, flags=0, nlon=0, ksplit=0, w_strides=None, grouped=False,
+                   m_offset=0, grouped8=False):
+    """Checked ``holysht_contract_desc`` for :func:`legendre_contract` / :class:`ContractPlan`."""
+    _cuda(output, input, w0)
     if w1 is not None:
         _cuda(output, w1)
         _require(w1.stride() == w0.stride(), "W0 and W1 must share strides")
     _require(w0.dtype == torch.float32, "tables must be float32")
-    if grouped:
+    if grouped8:
+        _require(w0.dim() == 6 and w0.is_contiguous() and w0.size(-1) == 4 and w0.size(-2) == 32,
+                 "GROUPED8 tables come from group_table8()")
+        w_strides = (0, 0, 0)
+    elif grouped:
         _require(w0.dim() == 6 and w0.is_contiguous(), "grouped tables come from group_table()")
         w_strides = (0, 0, 0)
     elif w_strides is None:
@@ -308,10 +408,10 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
     d.nlon = nlon
     d.scale = scale
     d.ksplit = ksplit
-    d.table_layout = _lib.TABLE_GROUPED if grouped else _lib.TABLE_STRIDED
+    d.table_layout = (_lib.TABLE_GROUPED8 if grouped8 else
+                      _lib.TABLE_GROUPED if grouped else _lib.TABLE_STRIDED)
     d.m_offset = m_offset
-    with torch.cuda.device(dev):
-        _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))
+    return d
 
 
 def legendre_dense_tc(direction: int, output: torch.Tensor, input: torch.Tensor, table: torch.Tensor,
@@ -347,6 +447,13 @@ def tc_error_word() -> int:
     """Read and clear the tensor-core kernel's device error word (synchronous)."""
     v = ctypes.c_uint(0)
     _lib.check(_lib.load().holysht_tc_error_word(ctypes.byref(v)))
+    return int(v.value)
+
+
+def stream_error_word() -> int:
+    """Read and clear the streaming kernel's device error word (synchronous)."""
+    v = ctypes.c_uint(0)
+    _lib.check(_lib.load().holysht_stream_error_word(ctypes.byref(v)))
     return int(v.value)
 
 

@@ -160,7 +160,8 @@ typedef struct holysht_contract_desc {
                               The m-tiled layout [L][ceil(M/32)][K][32] (k stride 32) keeps
                               every 32-order row segment on one 128-byte line. */
   int table_layout;         /* HOLYSHT_TABLE_STRIDED (the strides above) or
-                               HOLYSHT_TABLE_GROUPED (see below; strides ignored) */
+                               HOLYSHT_TABLE_GROUPED / HOLYSHT_TABLE_GROUPED8 (see below;
+                               strides ignored) */
   int64_t m_offset;         /* global order of column 0 of the input, output and tables
                                (a multiple of 32; 0 for whole transforms).  Lets one GPU
                                contract a slice of the orders with the global l >= m
@@ -178,8 +179,19 @@ typedef struct holysht_contract_desc {
  * sph - i tor = (W0 + W1)(c0 + i c1) and sph + i tor = (W0 - W1)(c0 - i c1),
  * half the multiplies of the direct form); the conjugate map is a table built
  * from (W0, -W1), and HOLYSHT_FLAG_CONJ_W1 is rejected with this layout. */
+/* GROUPED8 (SCALAR and VECTOR kinds, complex64 input, no CONJ_W1 / ROUND_BF16
+ * flags): rows in groups of 8, each lane's 8 rows x T tables as quads of 4 floats:
+ *   T8[g][mt][s][q][lane][4], g < ceil(R/8), q < 2T,
+ *   VECTOR: quad q = (row 2q: t0, t1, row 2q+1: t0, t1), t0 = W0 + W1, t1 = W0 - W1
+ *   SCALAR: quad q = rows 4q .. 4q+3
+ * zero outside the tables and above the diagonal.  A warp's step is one
+ * contiguous 1 KB (SCALAR) / 2 KB (VECTOR) block, which the streaming kernel
+ * moves into shared memory with bulk asynchronous copies (cp.async.bulk),
+ * 64 output rows per CTA.  Bit 0 of holysht_stream_error_word reports a
+ * pipeline wait that gave up. */
 #define HOLYSHT_TABLE_STRIDED 0
 #define HOLYSHT_TABLE_GROUPED 1
+#define HOLYSHT_TABLE_GROUPED8 2
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
@@ -252,6 +264,11 @@ int holysht_legendre_dense_tc_noalloc(int direction, void* out, int64_t out_batc
 /* Diagnostics: reads and clears the tensor-core kernel's device error word
  * (bit 0: a pipeline wait gave up instead of hanging).  Synchronous. */
 int holysht_tc_error_word(unsigned* value);
+
+/* Diagnostics: reads and clears the streaming kernel's device error word
+ * (HOLYSHT_TABLE_GROUPED8; bit 0: a pipeline wait gave up instead of hanging).
+ * Synchronous. */
+int holysht_stream_error_word(unsigned* value);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,186 @@
+"""GPU parity of the streaming kernel (table layout HOLYSHT_TABLE_GROUPED8)
+against the float64 oracle, through the C ABI.
+
+Tolerance (FP32): relative L2 <= 1e-6 and max-abs <= 1e-5 * max|ref| on the
+same float32 tables; exact zeros above the diagonal and in padding columns;
+bit-identical repeat launches; the device error word stays clear.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from holysht_b200 import _lib, ops
+from oracle import sht_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+FP32_REL = 1e-6
+FP32_MAXABS = 1e-5
+
+
+def assert_fp32_close(got, ref):
+    got = got.detach().cpu().numpy().astype(np.complex128)
+    ref = np.asarray(ref, np.complex128)
+    nr = np.linalg.norm(ref)
+    rel = np.linalg.norm(got - ref) / nr if nr > 0 else np.linalg.norm(got)
+    assert rel <= FP32_REL, f"relative L2 {rel:.3e}"
+    assert np.abs(got - ref).max() <= FP32_MAXABS * max(np.abs(ref).max(), 1e-30)
+
+
+def tri_table(rng, L, K, M, m_offset=0):
+    w = rng.standard_normal((L, K, M)).astype(np.float32)
+    w *= (np.arange(M)[None, None, :] + m_offset <= np.arange(L)[:, None, None])
+    return w
+
+
+def cplx(rng, shape):
+    return (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)).astype(np.complex64)
+
+
+def run(kind, direction, x, out, table, B, K, L, M, W_in, W_out, ks=0, scale=1.0, flags=0, nlon=0, m_offset=0):
+    P = 2 if kind == _lib.KIND_VECTOR else 1
+    Rin = K if direction == _lib.DIR_FORWARD else L
+    Rout = L if direction == _lib.DIR_FORWARD else K
+    ops.legendre_contract(kind=kind, direction=direction, input=x, output=out, w0=table, batch=B, nlat=K,
+                          lmax=L, mmax=M, in_strides=(P * Rin * W_in, Rin * W_in, W_in),
+                          out_strides=(P * Rout * W_out, Rout * W_out, W_out), out_cols=W_out, scale=scale,
+                          flags=flags, nlon=nlon, ksplit=ks, grouped8=True, m_offset=m_offset)
+
+
+SHAPES = [  # (B, K, L, M)
+    (1, 1, 1, 1),
+    (3, 7, 5, 5),
+    (2, 16, 16, 17),
+    (5, 33, 40, 37),
+    (9, 64, 48, 65),
+    (4, 70, 96, 33),
+    (17, 20, 12, 70),
+    (4, 130, 129, 129),
+]
+
+
+@pytest.mark.parametrize("B,K,L,M", SHAPES)
+@pytest.mark.parametrize("ks", [0, 1, 2])
+def test_stream_scalar_forward_inverse(B, K, L, M, ks):
+    rng = np.random.default_rng(B * 131 + K + ks)
+    w = tri_table(rng, L, K, M)
+    wt = torch.from_numpy(w).to(DEV)
+    W = M + 3  # spectrum rows wider than the table (an rfft with more columns)
+    x = cplx(rng, (B, K, W))
+    out = torch.full((B, L, M), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    run(_lib.KIND_SCALAR, _lib.DIR_FORWARD, torch.from_numpy(x).to(DEV), out,
+        ops.group_table8(wt, _lib.DIR_FORWARD), B, K, L, M, W, M, ks=ks, scale=0.5)
+    ref = 0.5 * orc.legendre_forward(x[..., :M].astype(np.complex128), w.astype(np.float64))
+    assert_fp32_close(out, ref)
+    upper = np.arange(M)[None, :] > np.arange(L)[:, None]
+    assert np.all(out.cpu().numpy()[:, upper] == 0)
+
+    c = cplx(rng, (B, L, M))
+    inv = torch.full((B, K, M), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    run(_lib.KIND_SCALAR, _lib.DIR_INVERSE, torch.from_numpy(c).to(DEV), inv,
+        ops.group_table8(wt, _lib.DIR_INVERSE), B, K, L, M, M, M, ks=ks)
+    assert_fp32_close(inv, orc.legendre_inverse(c.astype(np.complex128), w.astype(np.float64)))
+    assert ops.stream_error_word() == 0
+
+
+@pytest.mark.parametrize("B,K,L,M", SHAPES)
+@pytest.mark.parametrize("ks", [0, 2, 4])
+def test_stream_vector_forward_inverse(B, K, L, M, ks):
+    rng = np.random.default_rng(B * 17 + M + ks)
+    w0, w1 = tri_table(rng, L, K, M), tri_table(rng, L, K, M)
+    t0, t1 = torch.from_numpy(w0).to(DEV), torch.from_numpy(w1).to(DEV)
+    W0, W1 = w0.astype(np.float64), w1.astype(np.float64)
+    x = cplx(rng, (B, 2, K, M))
+    out = torch.full((B, 2, L, M), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, torch.from_numpy(x).to(DEV), out,
+        ops.group_table8((t0, t1), _lib.DIR_FORWARD), B, K, L, M, M, M, ks=ks)
+    assert_fp32_close(out, orc.vector_legendre_forward(x.astype(np.complex128), W0, W1))
+
+    # inverse with the conjugate map (table built from (W0, -W1)) and irfft preparation
+    c = cplx(rng, (B, 2, L, M))
+    nlon = 2 * M + 2
+    Wout = nlon // 2 + 1
+    inv = torch.full((B, 2, K, Wout), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    run(_lib.KIND_VECTOR, _lib.DIR_INVERSE, torch.from_numpy(c).to(DEV), inv,
+        ops.group_table8((t0, t1), _lib.DIR_INVERSE, conj=True), B, K, L, M, M, Wout, ks=ks,
+        flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
+    ref = np.zeros((B, 2, K, Wout), np.complex128)
+    ref[..., :M] = orc.vector_legendre_inverse(c.astype(np.complex128), W0, W1, conj_w1=True)
+    ref[..., 0] = ref[..., 0].real
+    got = inv.cpu().numpy()
+    assert np.all(got[..., M:] == 0) and np.all(got[..., 0].imag == 0)
+    assert_fp32_close(inv, ref)
+    assert ops.stream_error_word() == 0
+
+
+def test_stream_order_slice_keeps_the_global_triangle():
+    rng = np.random.default_rng(5)
+    B, K, L, M, off = 3, 40, 100, 96, 32
+    w = tri_table(rng, L, K, M)              # full table
+    ws = np.ascontiguousarray(w[:, :, off:off + 48])  # orders 32 .. 79
+    x = cplx(rng, (B, K, 48))
+    out = torch.full((B, L, 48), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+    run(_lib.KIND_SCALAR, _lib.DIR_FORWARD, torch.from_numpy(x).to(DEV), out,
+        ops.group_table8(torch.from_numpy(ws).to(DEV), _lib.DIR_FORWARD, m_offset=off), B, K, L, 48, 48, 48,
+        m_offset=off)
+    assert_fp32_close(out, orc.legendre_forward(x.astype(np.complex128), ws.astype(np.float64)))
+    got = out.cpu().numpy()
+    upper = (np.arange(48)[None, :] + off) > np.arange(L)[:, None]
+    assert np.all(got[:, upper] == 0)
+
+
+@pytest.mark.parametrize("ks", [1, 2, 4, 8])
+def test_stream_split_is_deterministic_and_matches(ks):
+    rng = np.random.default_rng(ks + 40)
+    B, K, L, M = 4, 256, 160, 161
+    w0, w1 = tri_table(rng, L, K, M), tri_table(rng, L, K, M)
+    t0, t1 = torch.from_numpy(w0).to(DEV), torch.from_numpy(w1).to(DEV)
+    tab = ops.group_table8((t0, t1), _lib.DIR_FORWARD)
+    x = torch.from_numpy(cplx(rng, (B, 2, K, M))).to(DEV)
+    outs = []
+    for _ in range(2):
+        o = torch.empty((B, 2, L, M), dtype=torch.complex64, device=DEV)
+        run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, x, o, tab, B, K, L, M, M, M, ks=ks)
+        outs.append(o)
+    assert torch.equal(outs[0], outs[1])
+    ref = orc.vector_legendre_forward(x.cpu().numpy().astype(np.complex128), w0.astype(np.float64),
+                                      w1.astype(np.float64))
+    assert_fp32_close(outs[0], ref)
+
+
+def test_stream_metric_size_matches_grouped_kernel():
+    """512 x 1024 vector forward, batch 4: the streaming kernel against the
+    4-row kernel on the same (W0 + W1, W0 - W1) tables (both FP32, different
+    summation orders)."""
+    import holysht_b200 as hs
+
+    m = hs.RealVectorSHT(512, 1024).to(DEV)
+    B = 4
+    x = torch.randn((B, 2, 512, 1024), device=DEV, generator=torch.Generator(DEV).manual_seed(3))
+    spec = torch.fft.rfft(x, dim=-1)
+    L, M, W = m.lmax, m.mmax, spec.size(-1)
+    out4 = torch.empty((B, 2, L, M), dtype=torch.complex64, device=DEV)
+    ops.legendre_contract(kind=_lib.KIND_VECTOR, direction=_lib.DIR_FORWARD, input=spec, output=out4,
+                          w0=m.table(_lib.DIR_FORWARD, "grouped")[0], batch=B, nlat=512, lmax=L, mmax=M,
+                          in_strides=(2 * 512 * W, 512 * W, W), out_strides=(2 * L * M, L * M, M), out_cols=M,
+                          scale=2 * math.pi / 1024, grouped=True)
+    tab8 = ops.group_table8((m.w0_t, m.w1_t), _lib.DIR_FORWARD)
+    out8 = torch.empty_like(out4)
+    run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, spec, out8, tab8, B, 512, L, M, W, M, scale=2 * math.pi / 1024)
+    a = out8.cpu().numpy().astype(np.complex128)
+    b = out4.cpu().numpy().astype(np.complex128)
+    assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-6
+    assert ops.stream_error_word() == 0
+
+
+def test_stream_rejects_flags_it_does_not_take():
+    B, K, L, M = 1, 8, 8, 8
+    t = torch.zeros((L, K, M), device=DEV)
+    x = torch.zeros((B, 2, K, M), dtype=torch.complex64, device=DEV)
+    out = torch.zeros((B, 2, L, M), dtype=torch.complex64, device=DEV)
+    with pytest.raises(RuntimeError, match="GROUPED8"):
+        run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, x, out, ops.group_table8((t, t), _lib.DIR_FORWARD), B, K, L, M,
+            M, M, flags=_lib.FLAG_CONJ_W1)

@@ -150,12 +150,41 @@ def test_group_table_layout():
     assert g.shape == (2, 2, K, 32, 4, 2)
     gi = hs.ops.group_table(w0, _lib.DIR_INVERSE)
     assert gi.shape == (2, 2, L, 32, 4, 1)
+    go = hs.ops.group_table(w0, _lib.DIR_FORWARD, m_offset=2)
     for l in range(L):
         for k in range(K):
             for m in range(M):
-                # vector pairs are stored as (W0 + W1, W0 - W1), the form the kernel contracts
-                assert g[l // 4, m // 32, k, m % 32, l % 4, 0] == w0[l, k, m] + w1[l, k, m]
-                assert g[l // 4, m // 32, k, m % 32, l % 4, 1] == w0[l, k, m] - w1[l, k, m]
-                assert gc[l // 4, m // 32, k, m % 32, l % 4, 0] == w0[l, k, m] - w1[l, k, m]
-                assert gi[k // 4, m // 32, l, m % 32, k % 4, 0] == w0[l, k, m]
+                # vector pairs are stored as (W0 + W1, W0 - W1), the form the kernel
+                # contracts; entries above the diagonal (l < m) are zero whatever
+                # the input holds there
+                t = float(m <= l)
+                assert g[l // 4, m // 32, k, m % 32, l % 4, 0] == t * (w0[l, k, m] + w1[l, k, m])
+                assert g[l // 4, m // 32, k, m % 32, l % 4, 1] == t * (w0[l, k, m] - w1[l, k, m])
+                assert gc[l // 4, m // 32, k, m % 32, l % 4, 0] == t * (w0[l, k, m] - w1[l, k, m])
+                assert gi[k // 4, m // 32, l, m % 32, k % 4, 0] == t * w0[l, k, m]
+                # an order slice starting at global order 2: column m is order m + 2
+                assert go[l // 4, m // 32, k, m % 32, l % 4, 0] == float(m + 2 <= l) * w0[l, k, m]
     assert torch.all(g[1, :, :, :, 2:, :] == 0)  # rows beyond lmax are zero
+
+
+def test_group_table8_layout():
+    L, K, M = 11, 5, 37
+    w0, w1 = torch.randn(L, K, M), torch.randn(L, K, M)
+    g = hs.ops.group_table8((w0, w1), _lib.DIR_FORWARD)
+    assert g.shape == (2, 2, K, 4, 32, 4)
+    gi = hs.ops.group_table8(w0, _lib.DIR_INVERSE)
+    assert gi.shape == (1, 2, L, 2, 32, 4)
+    for l in range(L):
+        for k in range(K):
+            for m in range(M):
+                t = float(m <= l)
+                r = l % 8
+                # vector: quad r // 2 holds (row 2q: W0+W1, W0-W1, row 2q+1: W0+W1, W0-W1)
+                q, e = r // 2, 2 * (r % 2)
+                assert g[l // 8, m // 32, k, q, m % 32, e] == t * (w0[l, k, m] + w1[l, k, m])
+                assert g[l // 8, m // 32, k, q, m % 32, e + 1] == t * (w0[l, k, m] - w1[l, k, m])
+                # scalar inverse: rows are k, quad k // 4 of the group holds rows 4q .. 4q+3
+                rk = k % 8
+                assert gi[k // 8, m // 32, l, rk // 4, m % 32, rk % 4] == t * w0[l, k, m]
+    # rows 11 .. 15 of the last group are zero: row 11 in quad 1, rows 12 .. 15 in quads 2, 3
+    assert torch.all(g[1, :, :, 1, :, 2:] == 0) and torch.all(g[1, :, :, 2:, :, :] == 0)
