@@ -101,6 +101,7 @@ class _GroupedTablesMixin:
         self.register_buffer("_grouped_fwd", None, persistent=False)
         self.register_buffer("_grouped_inv", None, persistent=False)
         self.register_buffer("_grouped8_fwd", None, persistent=False)
+        self.register_buffer("_grouped8_inv", None, persistent=False)
         self.table(hot_direction)
         self.register_load_state_dict_post_hook(lambda module, _keys: module._drop_grouped())
 
@@ -122,6 +123,7 @@ class _GroupedTablesMixin:
         self._grouped_fwd = None
         self._grouped_inv = None
         self._grouped8_fwd = None
+        self._grouped8_inv = None
         if hasattr(self, "_dense_inv"):
             self._dense_inv = None
 
@@ -147,21 +149,19 @@ class _GroupedTablesMixin:
         """(table, None, layout) for one contraction direction.
 
         ``layout`` "grouped8" (``ops.group_table8``, the streaming kernel) is
-        the default for the FP32 forward direction; "grouped"
-        (``ops.group_table``, 4-row groups) serves the inverse direction and
-        the BF16/FP16 modules, whose forward rounds the spectrum in the kernel.
-        ``HOLYSHT_FORWARD_LAYOUT=grouped`` selects the 4-row kernel for the
-        forward direction too."""
+        the default for both directions; "grouped" (``ops.group_table``, 4-row
+        groups) serves the forward of the BF16/FP16 modules, whose forward
+        rounds the spectrum in the kernel.  ``HOLYSHT_TABLE_LAYOUT=grouped``
+        selects the 4-row kernel everywhere."""
         if layout is None:
             import os
 
             low = bool(getattr(self, "_use_bf16", False) or getattr(self, "_use_fp16", False))
-            stream = os.environ.get("HOLYSHT_FORWARD_LAYOUT", "grouped8") != "grouped"
-            layout = "grouped8" if direction == _lib.DIR_FORWARD and not low and stream else "grouped"
+            rounds = direction == _lib.DIR_FORWARD and low  # the forward rounds the spectrum in the kernel
+            stream = os.environ.get("HOLYSHT_TABLE_LAYOUT", "grouped8") != "grouped"
+            layout = "grouped8" if stream and not rounds else "grouped"
         if layout == "grouped8":
-            if direction != _lib.DIR_FORWARD:
-                raise RuntimeError("module tables in the GROUPED8 layout are built for the forward direction")
-            name = "_grouped8_fwd"
+            name = "_grouped8_fwd" if direction == _lib.DIR_FORWARD else "_grouped8_inv"
         else:
             name = "_grouped_fwd" if direction == _lib.DIR_FORWARD else "_grouped_inv"
         t = getattr(self, name)

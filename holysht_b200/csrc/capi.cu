@@ -12,6 +12,8 @@
 #include <cstdlib>
 #include <algorithm>
 #include <mutex>
+#include <utility>
+#include <vector>
 #include <string>
 
 #include "../../include/holysht_b200.h"
@@ -334,6 +336,47 @@ int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream
 
 // ---- streaming kernel (GROUPED8 tables) ----
 
+// Reduction split (cluster size) and number of clusters of a streaming launch.
+// One CTA per SM; clusters walk the work items (compute tile x batch group,
+// ordered by decreasing reduction length) in a snake order, so the split and
+// cluster count are chosen by simulating that assignment: the smallest
+// makespan in chunks (plus a fixed per-item cost for the pipeline ramp and the
+// epilogue), the smaller split on a tie.  An explicit ksplit is kept.
+std::pair<int, int> choose_stream_grid(const hsb::stream::Params& p, int chunk, bool forward) {
+  namespace st = hsb::stream;
+  std::vector<int> steps;  // reduction steps of every item, in item order
+  for (int jt = 0; jt < p.j_act; ++jt) {
+    const long long diag = std::min<long long>(32LL * (jt + p.mt_off), p.R);
+    const long long first = forward ? diag : 0;
+    const long long cnt = (p.R - first + st::kRows - 1) / st::kRows;
+    const int s = forward ? p.S : (int)(p.S - std::min<long long>(32LL * (jt + p.mt_off), p.S));
+    for (long long t = 0; t < cnt * p.n_bg; ++t) steps.push_back(s);
+  }
+  const long long items = (long long)steps.size();
+  const int sms = sm_count_of_current_device();
+  constexpr long long kItemCost = 2;  // chunks: pipeline ramp-up and the cluster epilogue
+  long long best = LLONG_MAX;
+  std::pair<int, int> choice{1, (int)std::max<long long>(1, std::min<long long>(items, sms))};
+  for (int ks = 1; ks <= 8; ks *= 2) {
+    if (p.ks != 0 && ks != p.ks) continue;
+    if (p.ks == 0 && ks > 1 && p.S / (2LL * ks) < 2LL * st::kMaxChunk) break;
+    const long long G = std::max<long long>(1, std::min<long long>(items, sms / ks));
+    std::vector<long long> load((size_t)G, 0);
+    for (long long i = 0; i < items; ++i) {
+      const long long round = i / G, pos = i % G;
+      const long long c = (round & 1) ? G - 1 - pos : pos;
+      const long long per = (steps[(size_t)i] + ks - 1) / ks;
+      load[(size_t)c] += (per + chunk - 1) / chunk + kItemCost;
+    }
+    const long long mk = *std::max_element(load.begin(), load.end());
+    if (mk < best) {
+      best = mk;
+      choice = {ks, (int)G};
+    }
+  }
+  return choice;
+}
+
 template <int KIND, int DIR, int NB>
 int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStream_t stream) {
   using Sm = hsb::stream::Smem<KIND, NB>;
@@ -350,19 +393,17 @@ int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStr
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
   hsb::stream::Params p = p_in;
-  if (p.n_compute == 0) p.ks = 1;  // a grid of zero writers only
-  if (p.ks == 0) {
-    // one CTA per SM: the largest split whose compute CTAs all fit in one wave,
-    // each cluster rank keeping at least two spectrum chunks of the reduction
-    const long long slots = sm_count_of_current_device();
-    const long long tiles = (long long)p.n_compute * p.n_bg;
-    int ks = 1;
-    while (ks < 8 && tiles * ks * 2 <= slots && p.S / (2LL * ks) >= 2LL * hsb::stream::kMaxChunk) ks *= 2;
-    p.ks = ks;
+  long long grid = 0;
+  if (p.n_compute == 0) {
+    p.ks = 1;  // a grid of zero writers only
+    grid = grid_tiles;
+  } else {
+    const std::pair<int, int> plan = choose_stream_grid(p, hsb::stream::Shape<KIND>::kChunk, DIR == 0);
+    p.ks = plan.first;
+    grid = (long long)plan.second * p.ks;
   }
-  if (grid_tiles * p.ks > INT_MAX / 2) return fail(HOLYSHT_ERR_INVALID, "problem too large for one launch");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid_tiles * p.ks), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(hsb::stream::kThreads, 1, 1);
   cfg.dynamicSmemBytes = Sm::kBytes;
   cfg.stream = stream;

@@ -233,38 +233,27 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   constexpr int kTabStages = S::kTabStages;
   constexpr int kChunk = Shape<KIND>::kChunk;
   constexpr int kStageFloats = kChunk * kStepFloats;  // one warp's table stage
-  constexpr int kSpecStageElems = kChunk * PB * 32;  // float2 per spectrum stage
+  constexpr int kSpecStageElems = kChunk * PB * 32;   // float2 per spectrum stage
+  static_assert((kSpecStages & (kSpecStages - 1)) == 0, "spectrum ring depth is a power of two");
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  float2* spec = reinterpret_cast<float2*>(smem_raw);                    // [stage][step][plane][lane]
-  float* tab = reinterpret_cast<float*>(smem_raw + S::kSpecBytes);       // [warp][stage][step floats]
-  float2* part = reinterpret_cast<float2*>(smem_raw);  // [source rank][owned row][NA][lane], after the loop
+  float2* spec = reinterpret_cast<float2*>(smem_raw);               // [stage][step][plane][lane]
+  float* tab = reinterpret_cast<float*>(smem_raw + S::kSpecBytes);  // [warp][stage][step floats]
+  float2* part = reinterpret_cast<float2*>(smem_raw);  // [source rank][owned row][NA][lane], after a tile
   __shared__ __align__(8) uint64_t full_bar[kSpecStages], empty_bar[kSpecStages];
   __shared__ __align__(8) uint64_t tab_bar[kCons][Smem<KIND, NB>::kTabStages];
 
   cg::cluster_group cluster = cg::this_cluster();
   const int ks = p.ks;
   const int rank = static_cast<int>(cluster.block_rank());
-  const int tile = blockIdx.x / ks;
-  const int bg = tile % p.n_bg;
-  int j, r0, r1;
-  const bool compute = decode<DIR>(p, tile / p.n_bg, j, r0, r1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b0 = bg * NB;
-  const int m0 = j * kMTile;
+  const int n_clusters = gridDim.x / ks;
+  const int cid = blockIdx.x / ks;  // this CTA's cluster: every rank walks the same items
+  const int n_items = p.n_compute * p.n_bg;
 
   // zeros first: fire-and-forget stores that drain while the table stream ramps up
   write_zero_units<DIR, NB, P>(p);
-  if (!compute) return;  // the grid holds no compute tile (launched with clusters of one)
-
-  const int m0g = m0 + p.m_off;
-  const int s_begin = DIR == 0 ? 0 : min(m0g, p.S);
-  const int nsteps = p.S - s_begin;
-  const int per = ((nsteps + ks * kChunk - 1) / (ks * kChunk)) * kChunk;
-  const int r_begin = min(p.S, s_begin + rank * per);
-  const int r_end = min(p.S, r_begin + per);
-  const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
-  const int n_valid = min(kCons, (r1 - r0 + kRowsPerWarp - 1) / kRowsPerWarp);  // warps with rows
+  if (cid >= n_items) return;  // uniform across the cluster
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSpecStages; ++i) {
@@ -276,12 +265,6 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
-
-  float2 acc[kRowsPerWarp][NA];
-#pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
-#pragma unroll
-    for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
 
   // ---- spectrum ring, staged by all threads ----
   // thread -> (batch, order) column and steps st_ls0, st_ls0 + kLsStep, ... of
@@ -295,24 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   static_assert(kThreads % (NB * 32) == 0, "spectrum staging map");
   const int st_b = (threadIdx.x >> 5) % NB;
   const int st_ls0 = threadIdx.x / (NB * 32);
-  const bool st_ok = m0 + lane < p.M && b0 + st_b < p.B;
-  const float2* st_src = p.in + (st_ok ? (long long)(b0 + st_b) * p.in_bs + m0 + lane : 0);
   float2* const st_dst = spec + (st_ls0 * PB + st_b * P) * 32 + lane;  // + slot * kSpecStageElems
-  auto stage = [&](int c, int slot) {
-    float2* dst = st_dst + slot * kSpecStageElems;
-    const int s0 = r_begin + c * kChunk + st_ls0;
-#pragma unroll
-    for (int it = 0; it < kStageIters; ++it) {
-      if (kChunk % kLsStep == 0 || st_ls0 + it * kLsStep < kChunk) {
-        const int s = s0 + it * kLsStep;
-        const bool ok = st_ok && s < r_end;
-        const float2* src = ok ? st_src + (long long)s * p.in_rs : p.in;
-#pragma unroll
-        for (int pl = 0; pl < P; ++pl)
-          cp_async8(dst + (it * kLsStep * PB + pl) * 32, ok ? src + pl * p.in_ps : p.in, ok);
-      }
-    }
-  };
   auto combine = [&](int slot) {
     float2* d = st_dst + slot * kSpecStageElems;
 #pragma unroll
@@ -329,193 +295,245 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(&full_bar[slot]))
                  : "memory");
   };
-
-  // ---- this warp's table ring (one stage per chunk) ----
-  const bool has_rows = warp < n_valid;
-  const int g = (r0 >> 3) + warp;  // row group of 8 (r0 is a multiple of 8)
-  const float* tsrc = p.table + (long long)(has_rows ? g : 0) * p.t_group + (long long)j * p.t_mt +
-                      (long long)r_begin * kStepFloats;
   float* my = tab + warp * kTabStages * kStageFloats;
-  const int nst = has_rows ? nchunks : 0;
-  auto issue_tab = [&](int q, int slot) {
-    const int n = min(kChunk, r_end - (r_begin + q * kChunk));
-    bulk_load(my + slot * kStageFloats, tsrc + (long long)q * kChunk * kStepFloats,
-              (unsigned)(n * kStepFloats * 4), &tab_bar[warp][slot]);
-  };
-  if (lane == 0)
-    for (int q = 0; q < kTabStages && q < nst; ++q) issue_tab(q, q);
-  int issued = min(kTabStages, nst);
 
-  auto step = [&](const float* ts, const float2* xs) {
-    // ts: this step's table block; xs: this step's staged spectrum planes
-    // (vector: planes 2b, 2b+1 hold u, v of batch b)
-    float w[kRowsPerWarp * T];
+  // running ring positions over all tiles of this CTA: spectrum chunks staged
+  // and consumed (global chunk g lives in slot g % kSpecStages, phase
+  // (g / kSpecStages) & 1), this warp's table stages (h: slot h % kTabStages)
+  int gbase = 0, tbase = 0;
+  bool alive = true;
+
+  // Items (compute tile x batch group) are ordered by decreasing reduction
+  // length; cluster c takes items c, 2G-1-c, 2G+c, ... (G clusters): long and
+  // short items pair up, which balances the triangular inverse direction.
+  for (int round = 0;; ++round) {
+    const int idx = round * n_clusters + ((round & 1) ? n_clusters - 1 - cid : cid);
+    if (idx >= n_items) break;
+    const int bg = idx % p.n_bg;
+    int j, r0, r1;
+    decode<DIR>(p, idx / p.n_bg, j, r0, r1);
+    const int b0 = bg * NB;
+    const int m0 = j * kMTile;
+    const int m0g = m0 + p.m_off;
+    const int s_begin = DIR == 0 ? 0 : min(m0g, p.S);
+    const int nsteps = p.S - s_begin;
+    const int per = ((nsteps + ks * kChunk - 1) / (ks * kChunk)) * kChunk;
+    const int r_begin = min(p.S, s_begin + rank * per);
+    const int r_end = min(p.S, r_begin + per);
+    const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
+    const int n_valid = min(kCons, (r1 - r0 + kRowsPerWarp - 1) / kRowsPerWarp);  // warps with rows
+
+    float2 acc[kRowsPerWarp][NA];
 #pragma unroll
-    for (int q = 0; q < Shape<KIND>::kQuads; ++q) {
-      const float4 v = reinterpret_cast<const float4*>(ts)[q * 32 + lane];
-      w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+    for (int i = 0; i < kRowsPerWarp; ++i)
+#pragma unroll
+      for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
+
+    const bool st_ok = m0 + lane < p.M && b0 + st_b < p.B;
+    const float2* st_src = p.in + (st_ok ? (long long)(b0 + st_b) * p.in_bs + m0 + lane : 0);
+    auto stage = [&](int c, int slot) {
+      float2* dst = st_dst + slot * kSpecStageElems;
+      const int s0 = r_begin + c * kChunk + st_ls0;
+#pragma unroll
+      for (int it = 0; it < kStageIters; ++it) {
+        if (kChunk % kLsStep == 0 || st_ls0 + it * kLsStep < kChunk) {
+          const int s = s0 + it * kLsStep;
+          const bool ok = st_ok && s < r_end;
+          const float2* src = ok ? st_src + (long long)s * p.in_rs : p.in;
+#pragma unroll
+          for (int pl = 0; pl < P; ++pl)
+            cp_async8(dst + (it * kLsStep * PB + pl) * 32, ok ? src + pl * p.in_ps : p.in, ok);
+        }
+      }
+    };
+    // stage chunk c of this tile (global chunk gbase + c), after the slot's previous reader is done
+    auto stage_chunk = [&](int c) -> bool {
+      const int g = gbase + c;
+      const int slot = g & (kSpecStages - 1);
+      if (g >= kSpecStages && !mbar_wait(&empty_bar[slot], ((g / kSpecStages) - 1) & 1)) return false;
+      stage(c, slot);
+      if constexpr (KIND != 1) publish_async(slot);
+      return true;
+    };
+
+    // ---- this warp's table ring (one stage per chunk) ----
+    const bool has_rows = warp < n_valid;
+    const int g8 = (r0 >> 3) + warp;  // row group of 8 (r0 is a multiple of 8)
+    const float* tsrc = p.table + (long long)(has_rows ? g8 : 0) * p.t_group + (long long)j * p.t_mt +
+                        (long long)r_begin * kStepFloats;
+    const int nst = has_rows ? nchunks : 0;
+    auto issue_tab = [&](int q) {
+      const int n = min(kChunk, r_end - (r_begin + q * kChunk));
+      const int slot = (tbase + q) % kTabStages;
+      bulk_load(my + slot * kStageFloats, tsrc + (long long)q * kChunk * kStepFloats,
+                (unsigned)(n * kStepFloats * 4), &tab_bar[warp][slot]);
+    };
+    if (lane == 0 && alive && nst > 0) {
+      // the ring memory was last written by the generic proxy (partial sums)
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      for (int q = 0; q < kTabStages && q < nst; ++q) issue_tab(q);
     }
-    float2 x[PB];
+    int issued = min(kTabStages, nst);
+
+    auto step = [&](const float* ts, const float2* xs) {
+      // ts: this step's table block; xs: this step's staged spectrum planes
+      // (vector: planes 2b, 2b+1 hold u, v of batch b)
+      float w[kRowsPerWarp * T];
 #pragma unroll
-    for (int a = 0; a < PB; ++a) x[a] = xs[a * 32 + lane];
+      for (int q = 0; q < Shape<KIND>::kQuads; ++q) {
+        const float4 v = reinterpret_cast<const float4*>(ts)[q * 32 + lane];
+        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+      }
+      float2 x[PB];
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
+      for (int a = 0; a < PB; ++a) x[a] = xs[a * 32 + lane];
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i) {
+        if constexpr (KIND == 1) {
+          const float wp = w[2 * i], wm = w[2 * i + 1];
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            acc[i][2 * b] = __ffma2_rn(make_float2(wp, wp), x[2 * b], acc[i][2 * b]);
+            acc[i][2 * b + 1] = __ffma2_rn(make_float2(wm, wm), x[2 * b + 1], acc[i][2 * b + 1]);
+          }
+        } else {
+          const float wv = w[i];
+#pragma unroll
+          for (int b = 0; b < NB; ++b) acc[i][b] = __ffma2_rn(make_float2(wv, wv), x[b], acc[i][b]);
+        }
+      }
+    };
+
+    int consumed = 0;  // table stages of this tile this warp has consumed
+    if (alive) {
+#pragma unroll
+      for (int q = 0; q < kSpecAhead; ++q) {
+        if (q < nchunks && alive) alive = stage_chunk(q);
+        if constexpr (KIND == 1) cp_async_commit();
+      }
       if constexpr (KIND == 1) {
-        const float wp = w[2 * i], wm = w[2 * i + 1];
+        if (nchunks > 0 && alive) {
+          cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk 0 have landed
+          combine(gbase & (kSpecStages - 1));
+          mbar_arrive(&full_bar[gbase & (kSpecStages - 1)]);
+        }
+      }
+    }
+    for (int c = 0; c < nchunks && alive; ++c) {
+      const int cn = c + kSpecAhead;
+      if (cn < nchunks && !stage_chunk(cn)) {
+        alive = false;
+        break;
+      }
+      if constexpr (KIND == 1) {
+        cp_async_commit();
+        if (c + 1 < nchunks) {
+          cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk c + 1 have landed
+          const int s1 = (gbase + c + 1) & (kSpecStages - 1);
+          combine(s1);
+          mbar_arrive(&full_bar[s1]);
+        }
+      }
+      const int g = gbase + c;
+      const int cs = g & (kSpecStages - 1);
+      if (!mbar_wait(&full_bar[cs], (g / kSpecStages) & 1)) {
+        alive = false;
+        break;
+      }
+      if (has_rows) {
+        const int h = tbase + c;
+        const int ts_ = h % kTabStages;
+        if (!mbar_wait(&tab_bar[warp][ts_], (h / kTabStages) & 1)) {
+          alive = false;
+          break;
+        }
+        const float2* xs = spec + cs * kSpecStageElems;
+        const float* tsb = my + ts_ * kStageFloats;
+        const int s0 = r_begin + c * kChunk;
+        if (s0 + kChunk <= r_end) {
+#pragma unroll
+          for (int ls = 0; ls < kChunk; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
+        } else {
+#pragma unroll 1
+          for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
+        }
+        ++consumed;
+        // stage consumed by every lane: refill it with chunk c + kTabStages
+        __syncwarp();
+        if (lane == 0 && issued < nst) {
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+          issue_tab(issued);
+        }
+        ++issued;
+      }
+      mbar_arrive(&empty_bar[cs]);
+    }
+    // nothing may still be writing into the rings when they become the partial-sum buffer
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    if (!alive && lane == 0 && has_rows) {
+      // a wait gave up: let this warp's table copies still in flight land first
+      const int done = min(issued, nst);
+      for (int q = consumed; q < done; ++q) {
+        const int h = tbase + q;
+        mbar_wait(&tab_bar[warp][h % kTabStages], (h / kTabStages) & 1);
+      }
+    }
+    __syncwarp();
+    gbase += nchunks;
+    tbase += nst;
+
+    if constexpr (KIND == 1) {
+      // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
+#pragma unroll
+      for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-          acc[i][2 * b] = __ffma2_rn(make_float2(wp, wp), x[2 * b], acc[i][2 * b]);
-          acc[i][2 * b + 1] = __ffma2_rn(make_float2(wm, wm), x[2 * b + 1], acc[i][2 * b + 1]);
+          const float2 pu = acc[i][2 * b], mv = acc[i][2 * b + 1];
+          acc[i][2 * b] = make_float2(0.5f * (mv.x + pu.x), 0.5f * (mv.y + pu.y));
+          acc[i][2 * b + 1] = make_float2(0.5f * (mv.y - pu.y), -0.5f * (mv.x - pu.x));
         }
-      } else {
-        const float wv = w[i];
-#pragma unroll
-        for (int b = 0; b < NB; ++b) acc[i][b] = __ffma2_rn(make_float2(wv, wv), x[b], acc[i][b]);
-      }
     }
-  };
 
-  bool alive = true;
-  // running ring positions: chunk c's spectrum slot/phase; the slot chunk
-  // c + kSpecAhead is staged into and the phase of the empty barrier it waits
-  // on; this warp's table slot/phase
-  int cs = 0, cph = 0, ps = kSpecAhead % kSpecStages, pph = (kSpecAhead / kSpecStages) & 1, ts_ = 0, tph = 0;
+    // ---- cluster reduction: every warp stores its rows' partial sums straight
+    // into the shared memory of the cluster rank that owns those rows (remote
+    // stores do not stall the warp), one cluster barrier, then each owner adds
+    // its ks slices in rank order (deterministic) from local shared memory.
+    const int rpr = kRows / ks;  // rows per owner rank, a multiple of 8
+    cluster.sync();              // every CTA of the cluster is done with its rings
+    {
+      const int owner = (warp * kRowsPerWarp) / rpr;
+      const int rl0 = warp * kRowsPerWarp - owner * rpr;
+      float2* dst = cluster.map_shared_rank(part, owner) + ((rank * rpr + rl0) * NA) * 32 + lane;
 #pragma unroll
-  for (int q = 0; q < kSpecAhead; ++q) {
-    if (q < nchunks) {
-      stage(q, q);
-      if constexpr (KIND != 1) publish_async(q);
-    }
-    if constexpr (KIND == 1) cp_async_commit();
-  }
-  if constexpr (KIND == 1) {
-    if (nchunks > 0) {
-      cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk 0 have landed
-      combine(0);
-      mbar_arrive(&full_bar[0]);
-    }
-  }
-  for (int c = 0; c < nchunks; ++c) {
-    const int cn = c + kSpecAhead;
-    if (cn < nchunks) {
-      // the slot chunk cn reuses was last read by chunk cn - kSpecStages
-      if (cn >= kSpecStages && !mbar_wait(&empty_bar[ps], pph ^ 1)) {
-        alive = false;
-        break;
-      }
-      stage(cn, ps);
-      if constexpr (KIND != 1) publish_async(ps);
-    }
-    if (++ps == kSpecStages) {
-      ps = 0;
-      pph ^= 1;
-    }
-    if constexpr (KIND == 1) {
-      cp_async_commit();
-      if (c + 1 < nchunks) {
-        cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk c + 1 have landed
-        const int s1 = cs + 1 == kSpecStages ? 0 : cs + 1;
-        combine(s1);
-        mbar_arrive(&full_bar[s1]);
-      }
-    }
-    if (!mbar_wait(&full_bar[cs], cph)) {
-      alive = false;
-      break;
-    }
-    if (has_rows) {
-      if (!mbar_wait(&tab_bar[warp][ts_], tph)) {
-        alive = false;
-        break;
-      }
-      const float2* xs = spec + cs * kSpecStageElems;
-      const float* tsb = my + ts_ * kStageFloats;
-      const int s0 = r_begin + c * kChunk;
-      if (s0 + kChunk <= r_end) {
+      for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-        for (int ls = 0; ls < kChunk; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
-      } else {
-#pragma unroll 1
-        for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
-      }
-      // stage consumed by every lane: refill it with chunk c + kTabStages
-      __syncwarp();
-      if (lane == 0 && issued < nst) {
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        issue_tab(issued, ts_);
-      }
-      ++issued;
-      if (++ts_ == kTabStages) {
-        ts_ = 0;
-        tph ^= 1;
-      }
+        for (int a = 0; a < NA; ++a) dst[(i * NA + a) * 32] = acc[i][a];
     }
-    mbar_arrive(&empty_bar[cs]);
-    if (++cs == kSpecStages) {
-      cs = 0;
-      cph ^= 1;
-    }
-  }
-  // nothing may still be writing into the rings when they become the partial-sum buffer
-  asm volatile("cp.async.wait_all;\n" ::: "memory");
-  if (!alive && lane == 0 && has_rows) {
-    // a wait gave up: let this warp's table copies still in flight land first
-    const int done = min(issued, nst);
-    for (int q = max(0, done - kTabStages); q < done; ++q)
-      mbar_wait(&tab_bar[warp][q % kTabStages], (q / kTabStages) & 1);
-  }
-  __syncwarp();
+    cluster.sync();
 
-  if constexpr (KIND == 1) {
-    // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i)
-#pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        const float2 pu = acc[i][2 * b], mv = acc[i][2 * b + 1];
-        acc[i][2 * b] = make_float2(0.5f * (mv.x + pu.x), 0.5f * (mv.y + pu.y));
-        acc[i][2 * b + 1] = make_float2(0.5f * (mv.y - pu.y), -0.5f * (mv.x - pu.x));
+    const int total = rpr * NA * 32;
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int col = e & 31;
+      const int a = (e >> 5) % NA;
+      const int rl = e / (NA * 32);
+      const int row = r0 + rank * rpr + rl;
+      const int mm = m0 + col;
+      if (row >= r1 || mm >= p.out_cols) continue;
+      float2 sum = make_float2(0.f, 0.f);
+      for (int q = 0; q < ks; ++q) {
+        const float2 v = part[((q * rpr + rl) * NA + a) * 32 + col];
+        sum.x += v.x;
+        sum.y += v.y;
       }
-  }
-
-  // ---- cluster reduction: every warp stores its rows' partial sums straight
-  // into the shared memory of the cluster rank that owns those rows (remote
-  // stores do not stall the warp), one cluster barrier, then each owner adds
-  // its ks slices in rank order (deterministic) from local shared memory.
-  const int rpr = kRows / ks;  // rows per owner rank, a multiple of 8
-  cluster.sync();              // every CTA of the cluster is done with its rings
-  {
-    const int owner = (warp * kRowsPerWarp) / rpr;
-    const int rl0 = warp * kRowsPerWarp - owner * rpr;
-    float2* dst = cluster.map_shared_rank(part, owner) + ((rank * rpr + rl0) * NA) * 32 + lane;
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i)
-#pragma unroll
-      for (int a = 0; a < NA; ++a) dst[(i * NA + a) * 32] = acc[i][a];
-  }
-  cluster.sync();
-
-  const int total = rpr * NA * 32;
-  for (int e = threadIdx.x; e < total; e += kThreads) {
-    const int col = e & 31;
-    const int a = (e >> 5) % NA;
-    const int rl = e / (NA * 32);
-    const int row = r0 + rank * rpr + rl;
-    const int mm = m0 + col;
-    if (row >= r1 || mm >= p.out_cols) continue;
-    float2 sum = make_float2(0.f, 0.f);
-    for (int q = 0; q < ks; ++q) {
-      const float2 v = part[((q * rpr + rl) * NA + a) * 32 + col];
-      sum.x += v.x;
-      sum.y += v.y;
+      sum.x *= p.scale;
+      sum.y *= p.scale;
+      if ((p.zero_imag_col0 && mm == 0) || mm == p.nyquist) sum.y = 0.f;
+      const int b = b0 + a / P, pl = a % P;
+      if (b < p.B)
+        static_cast<float2*>(p.out)[(long long)b * p.out_bs + (long long)pl * p.out_ps +
+                                    (long long)row * p.out_rs + mm] = sum;
     }
-    sum.x *= p.scale;
-    sum.y *= p.scale;
-    if ((p.zero_imag_col0 && mm == 0) || mm == p.nyquist) sum.y = 0.f;
-    const int b = b0 + a / P, pl = a % P;
-    if (b < p.B)
-      static_cast<float2*>(p.out)[(long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs +
-                                  mm] = sum;
+    __syncthreads();  // partial sums read: the next tile's copies may reuse the memory
   }
 }
 

@@ -105,9 +105,10 @@ class _OrderSharded(nn.Module):
         self.width_pad = max(b - a for a, b in self.ranges) or 1
         local = [t[:, :, lo:hi].contiguous() for t in dense_tables]  # [L, K, width]
         if hi > lo:
-            grouped = ops.group_table(tuple(local), _lib.DIR_FORWARD, m_offset=lo)  # (W0+W1, W0-W1) for vector
+            # streaming layout, (W0+W1, W0-W1) for vector, zero above the global diagonal
+            grouped = ops.group_table8(tuple(local), _lib.DIR_FORWARD, m_offset=lo)
         else:
-            grouped = torch.zeros((1, 1, 1, 32, 4, len(local)), dtype=torch.float32)
+            grouped = torch.zeros((1, 1, 1, 2 * len(local), 32, 4), dtype=torch.float32)
         self.register_buffer("table_local", grouped, persistent=False)
 
     def _forward(self, x: torch.Tensor, P: int) -> torch.Tensor:
@@ -127,7 +128,7 @@ class _OrderSharded(nn.Module):
                 input=spec[..., self.m_lo:], output=slab, w0=self.table_local, batch=B, nlat=self.nlat,
                 lmax=self.lmax, mmax=width, in_strides=(P * self.nlat * W, self.nlat * W, W),
                 out_strides=(P * self.lmax * self.width_pad, self.lmax * self.width_pad, self.width_pad),
-                out_cols=width, scale=2.0 * math.pi / self.nlon, grouped=True, m_offset=self.m_lo)
+                out_cols=width, scale=2.0 * math.pi / self.nlon, grouped8=True, m_offset=self.m_lo)
         full = gather_order_slabs(slab, self.ranges, self.group)
         shape = lead + ((2,) if P == 2 else ()) + (self.lmax, self.mmax)
         return full.reshape(shape)
