@@ -42,6 +42,7 @@ EXPORTS = (
     "holysht_legendre_dense_tc",
     "holysht_tc_error_word",
     "holysht_stream_error_word",
+    "holysht_stream_launch_plan",
     "holysht_legendre_dense_tc_noalloc",
     "holysht_legendre_forward_recurrence",
 )
@@ -117,6 +118,9 @@ def load() -> ctypes.CDLL:
                                            ctypes.c_float, i32, i64, vp, i64, vp], i32),
             "holysht_tc_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
             "holysht_stream_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
+            "holysht_stream_launch_plan": ([i32, i32, i64, i64, i64, i64, i64, i64, i32, i32,
+                                            ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                            ctypes.POINTER(ctypes.c_int)], i32),
             "holysht_legendre_forward_recurrence": ([vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64,
                                                      ctypes.c_float, vp], i32),
             "holysht_legendre_dense_tc_noalloc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,

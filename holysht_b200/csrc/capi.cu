@@ -342,7 +342,7 @@ int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream
 // cluster count are chosen by simulating that assignment: the smallest
 // makespan in chunks (plus a fixed per-item cost for the pipeline ramp and the
 // epilogue), the smaller split on a tie.  An explicit ksplit is kept.
-std::pair<int, int> choose_stream_grid(const hsb::stream::Params& p, int chunk, bool forward) {
+std::pair<int, int> choose_stream_grid(const hsb::stream::Params& p, int chunk, bool forward, int sms) {
   namespace st = hsb::stream;
   std::vector<int> steps;  // reduction steps of every item, in item order
   for (int jt = 0; jt < p.j_act; ++jt) {
@@ -353,7 +353,6 @@ std::pair<int, int> choose_stream_grid(const hsb::stream::Params& p, int chunk, 
     for (long long t = 0; t < cnt * p.n_bg; ++t) steps.push_back(s);
   }
   const long long items = (long long)steps.size();
-  const int sms = sm_count_of_current_device();
   constexpr long long kItemCost = 2;  // chunks: pipeline ramp-up and the cluster epilogue
   long long best = LLONG_MAX;
   std::pair<int, int> choice{1, (int)std::max<long long>(1, std::min<long long>(items, sms))};
@@ -398,7 +397,8 @@ int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStr
     p.ks = 1;  // a grid of zero writers only
     grid = grid_tiles;
   } else {
-    const std::pair<int, int> plan = choose_stream_grid(p, hsb::stream::Shape<KIND>::kChunk, DIR == 0);
+    const std::pair<int, int> plan =
+        choose_stream_grid(p, hsb::stream::Shape<KIND>::kChunk, DIR == 0, sm_count_of_current_device());
     p.ks = plan.first;
     grid = (long long)plan.second * p.ks;
   }
@@ -434,10 +434,9 @@ int stream_nb(const hsb::stream::Params& p, int nb, long long grid_tiles, cudaSt
   }
 }
 
-int run_stream_job(const Job& j, long long R, long long S, cudaStream_t stream) {
+// Kernel parameters of a streaming job (no CUDA call); *nb_out = batches per CTA.
+hsb::stream::Params make_stream_params(const Job& j, long long R, long long S, int* nb_out) {
   namespace st = hsb::stream;
-  if (j.ksplit != 0 && j.ksplit != 1 && j.ksplit != 2 && j.ksplit != 4 && j.ksplit != 8)
-    return fail(HOLYSHT_ERR_INVALID, "ksplit must be 0, 1, 2, 4 or 8");
   const long long T = j.kind == HOLYSHT_KIND_VECTOR ? 2 : 1;
   const long long step = 32LL * st::kRowsPerWarp * T;  // floats per (group, m tile, step)
   const long long mt_tab = (j.M + st::kMTile - 1) / st::kMTile;
@@ -480,6 +479,16 @@ int run_stream_job(const Job& j, long long R, long long S, cudaStream_t stream) 
   const int nb = next_pow2_at_least(j.B, 1, j.kind == HOLYSHT_KIND_VECTOR ? 4 : 8);
   p.n_bg = (int)((j.B + nb - 1) / nb);
   p.ks = j.ksplit ? j.ksplit : env_ksplit();
+  *nb_out = nb;
+  return p;
+}
+
+int run_stream_job(const Job& j, long long R, long long S, cudaStream_t stream) {
+  if (j.ksplit != 0 && j.ksplit != 1 && j.ksplit != 2 && j.ksplit != 4 && j.ksplit != 8)
+    return fail(HOLYSHT_ERR_INVALID, "ksplit must be 0, 1, 2, 4 or 8");
+  int nb = 1;
+  const hsb::stream::Params p = make_stream_params(j, R, S, &nb);
+  const long long n_compute = p.n_compute, n_zero = p.n_zero;
   // the grid holds the compute tiles; their CTAs also write the zero tiles
   if (n_compute + n_zero == 0) return ok();
   const long long grid_tiles = n_compute > 0 ? n_compute * p.n_bg : std::min<long long>(n_zero * p.n_bg, 148);
@@ -720,6 +729,50 @@ int holysht_tc_error_word(unsigned* value) {
   return ok();
 }
 
+
+int holysht_stream_launch_plan(int kind, int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                               int64_t out_cols, int64_t m_offset, int ksplit, int sm_count, int* ks_out,
+                               int* clusters_out, int* items_out) {
+  if (!ks_out || !clusters_out || !items_out) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  if (kind != HOLYSHT_KIND_SCALAR && kind != HOLYSHT_KIND_VECTOR)
+    return fail(HOLYSHT_ERR_INVALID, "the streaming kernel serves the SCALAR and VECTOR kinds");
+  if (direction != HOLYSHT_DIR_FORWARD && direction != HOLYSHT_DIR_INVERSE)
+    return fail(HOLYSHT_ERR_INVALID, "unknown direction %d", direction);
+  if (batch <= 0 || nlat <= 0 || lmax <= 0 || mmax <= 0 || out_cols < mmax || !fits_int(batch) || !fits_int(nlat) ||
+      !fits_int(lmax) || !fits_int(mmax) || !fits_int(out_cols))
+    return fail(HOLYSHT_ERR_INVALID, "extents must be positive, fit the tile range, out_cols >= mmax");
+  if (m_offset < 0 || m_offset % 32 != 0) return fail(HOLYSHT_ERR_INVALID, "m_offset must be a multiple of 32");
+  if (ksplit != 0 && ksplit != 1 && ksplit != 2 && ksplit != 4 && ksplit != 8)
+    return fail(HOLYSHT_ERR_INVALID, "ksplit must be 0, 1, 2, 4 or 8");
+  Job j = {};
+  j.kind = kind;
+  j.dir = direction;
+  j.B = batch;
+  j.K = nlat;
+  j.L = lmax;
+  j.M = mmax;
+  j.out_cols = out_cols;
+  j.m_off = m_offset;
+  j.ksplit = ksplit;
+  const long long R = direction == HOLYSHT_DIR_FORWARD ? lmax : nlat;
+  const long long S = direction == HOLYSHT_DIR_FORWARD ? nlat : lmax;
+  int nb = 1;
+  hsb::stream::Params p = make_stream_params(j, R, S, &nb);
+  p.ks = ksplit;  // the environment override is a launch-time setting
+  *items_out = p.n_compute * p.n_bg;
+  if (p.n_compute == 0) {
+    *ks_out = 1;
+    *clusters_out = 0;
+    return ok();
+  }
+  const int chunk = kind == HOLYSHT_KIND_VECTOR ? hsb::stream::Shape<hsb::KIND_VECTOR>::kChunk
+                                                : hsb::stream::Shape<hsb::KIND_SCALAR>::kChunk;
+  const std::pair<int, int> plan =
+      choose_stream_grid(p, chunk, direction == HOLYSHT_DIR_FORWARD, sm_count > 0 ? sm_count : sm_count_of_current_device());
+  *ks_out = plan.first;
+  *clusters_out = plan.second;
+  return ok();
+}
 
 int holysht_stream_error_word(unsigned* value) {
   if (!value) return fail(HOLYSHT_ERR_INVALID, "null pointer");

@@ -38,6 +38,7 @@ __all__ = [
     "group_table",
     "group_table8",
     "stream_error_word",
+    "stream_launch_plan",
     "legendre_dense_tc",
     "tc_error_word",
     "legendre_forward_recurrence",
@@ -448,6 +449,19 @@ def tc_error_word() -> int:
     v = ctypes.c_uint(0)
     _lib.check(_lib.load().holysht_tc_error_word(ctypes.byref(v)))
     return int(v.value)
+
+
+def stream_launch_plan(kind: int, direction: int, *, batch: int, nlat: int, lmax: int, mmax: int,
+                       out_cols: Optional[int] = None, m_offset: int = 0, ksplit: int = 0,
+                       sm_count: int = 0) -> dict:
+    """Launch plan of the streaming kernel (host-only): ``ks`` (cluster size /
+    reduction split), ``clusters`` and ``items`` (compute tile x batch group).
+    ``sm_count`` > 0 plans for that many SMs without a GPU."""
+    ks, cl, it = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.load().holysht_stream_launch_plan(
+        kind, direction, batch, nlat, lmax, mmax, mmax if out_cols is None else out_cols, m_offset, ksplit,
+        sm_count, ctypes.byref(ks), ctypes.byref(cl), ctypes.byref(it)))
+    return {"ks": ks.value, "clusters": cl.value, "items": it.value}
 
 
 def stream_error_word() -> int:

@@ -270,6 +270,17 @@ int holysht_tc_error_word(unsigned* value);
  * Synchronous. */
 int holysht_stream_error_word(unsigned* value);
 
+/* Launch plan of the streaming kernel (HOLYSHT_TABLE_GROUPED8) for a contraction
+ * of the given extents: reduction split *ks_out (cluster size), number of
+ * clusters *clusters_out and work items *items_out (compute tile x batch group).
+ * Clusters walk the items in snake order, longest reduction first; the plan is
+ * the split with the smallest simulated makespan.  sm_count > 0 plans for that
+ * many SMs without touching the GPU; 0 uses the current device.  ksplit 0
+ * chooses, else 1/2/4/8 is kept.  Host-only, no launch. */
+int holysht_stream_launch_plan(int kind, int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                               int64_t out_cols, int64_t m_offset, int ksplit, int sm_count, int* ks_out,
+                               int* clusters_out, int* items_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -188,3 +188,65 @@ def test_group_table8_layout():
                 assert gi[k // 8, m // 32, l, rk // 4, m % 32, rk % 4] == t * w0[l, k, m]
     # rows 11 .. 15 of the last group are zero: row 11 in quad 1, rows 12 .. 15 in quads 2, 3
     assert torch.all(g[1, :, :, 1, :, 2:] == 0) and torch.all(g[1, :, :, 2:, :, :] == 0)
+
+
+def test_group_table8_conjugate_and_scalar_forward():
+    L, K, M = 9, 3, 33
+    w0, w1 = torch.randn(L, K, M), torch.randn(L, K, M)
+    gc = hs.ops.group_table8((w0, w1), _lib.DIR_INVERSE, conj=True)  # rows are k
+    assert gc.shape == (1, 2, L, 4, 32, 4)
+    gs = hs.ops.group_table8(w0, _lib.DIR_FORWARD)
+    assert gs.shape == (2, 2, K, 2, 32, 4)
+    for l in range(L):
+        for k in range(K):
+            for m in range(M):
+                t = float(m <= l)
+                q, e = k // 2, 2 * (k % 2)
+                assert gc[0, m // 32, l, q, m % 32, e] == t * (w0[l, k, m] - w1[l, k, m])
+                assert gc[0, m // 32, l, q, m % 32, e + 1] == t * (w0[l, k, m] + w1[l, k, m])
+                r = l % 8
+                assert gs[l // 8, m // 32, k, r // 4, m % 32, r % 4] == t * w0[l, k, m]
+
+
+def _snake_loads(steps, ks, G, chunk):
+    loads = [0] * G
+    for i, s in enumerate(steps):
+        rnd, pos = divmod(i, G)
+        c = G - 1 - pos if rnd & 1 else pos
+        per = (s + ks - 1) // ks
+        loads[c] += (per + chunk - 1) // chunk + 2
+    return loads
+
+
+def test_stream_launch_plan_metric_shapes():
+    """The streaming kernel's launch plan (host-only, planned for 148 SMs)."""
+    plan = hs.ops.stream_launch_plan
+    V, S_, F, I = _lib.KIND_VECTOR, _lib.KIND_SCALAR, _lib.DIR_FORWARD, _lib.DIR_INVERSE
+    # 512x1024 b4: forward 72 tiles of 64 rows x 32 orders, split in clusters of 2 (144 CTAs)
+    assert plan(V, F, batch=4, nlat=512, lmax=512, mmax=513, sm_count=148) == {"ks": 2, "clusters": 72, "items": 72}
+    assert plan(S_, F, batch=4, nlat=512, lmax=512, mmax=513, sm_count=148) == {"ks": 2, "clusters": 72, "items": 72}
+    # inverse: 8 row tiles x 16 order tiles with reductions 512 - 32 j, 74 clusters of 2 in snake order
+    assert plan(V, I, batch=4, nlat=512, lmax=512, mmax=513, sm_count=148) == {"ks": 2, "clusters": 74, "items": 128}
+    # 256x512 (C1/C2): 20 tiles, split 4
+    assert plan(V, F, batch=4, nlat=256, lmax=256, mmax=257, sm_count=148) == {"ks": 4, "clusters": 20, "items": 20}
+    # batch groups multiply the items; an explicit split is kept
+    assert plan(S_, F, batch=64, nlat=512, lmax=512, mmax=513, sm_count=148)["items"] == 72 * 8
+    assert plan(V, F, batch=4, nlat=512, lmax=512, mmax=513, ksplit=4, sm_count=148)["ks"] == 4
+
+
+def test_stream_snake_assignment_balances_the_inverse():
+    # item reductions of the 512x1024 inverse, longest first (8 row tiles per order tile)
+    steps = [512 - 32 * j for j in range(16) for _ in range(8)]
+    loads = _snake_loads(steps, 2, 74, 4)
+    mean = sum(loads) / len(loads)
+    assert max(loads) <= 1.1 * mean
+    # one item per cluster instead leaves the longest tile alone: almost 2x the mean
+    assert max(_snake_loads(steps, 1, 128, 4)) >= 1.8 * (sum(_snake_loads(steps, 1, 128, 4)) / 128)
+
+
+def test_stream_launch_plan_rejects_bad_arguments():
+    with pytest.raises(RuntimeError, match="SCALAR and VECTOR"):
+        hs.ops.stream_launch_plan(_lib.KIND_REAL, _lib.DIR_FORWARD, batch=1, nlat=8, lmax=8, mmax=8, sm_count=148)
+    with pytest.raises(RuntimeError, match="ksplit"):
+        hs.ops.stream_launch_plan(_lib.KIND_VECTOR, _lib.DIR_FORWARD, batch=1, nlat=8, lmax=8, mmax=8, ksplit=3,
+                                  sm_count=148)
