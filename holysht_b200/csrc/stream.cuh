@@ -40,10 +40,16 @@ namespace stream {
 
 namespace cg = cooperative_groups;
 
-constexpr int kCons = 8;  // warps
-constexpr int kThreads = kCons * 32;
-constexpr int kRowsPerWarp = 8;
-constexpr int kRows = kCons * kRowsPerWarp;  // 64 output rows per CTA
+#ifndef HSB_STREAM_SPLIT
+#define HSB_STREAM_SPLIT 1
+#endif
+constexpr int kCons = 8;                       // row groups of 8 (one table ring each) per CTA
+constexpr int kSplit = HSB_STREAM_SPLIT;       // warps sharing one row group (1 or 2)
+constexpr int kWarps = kCons * kSplit;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRowsPerWarp = 8;                // rows of a table group
+constexpr int kWRows = kRowsPerWarp / kSplit;  // rows one warp accumulates
+constexpr int kRows = kCons * kRowsPerWarp;    // 64 output rows per CTA
 constexpr int kMTile = 32;
 #ifndef HSB_STREAM_CHUNK_V
 #define HSB_STREAM_CHUNK_V 4
@@ -242,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   float2* part = reinterpret_cast<float2*>(smem_raw);  // [source rank][owned row][NA][lane], after a tile
   __shared__ __align__(8) uint64_t full_bar[kSpecStages], empty_bar[kSpecStages];
   __shared__ __align__(8) uint64_t tab_bar[kCons][Smem<KIND, NB>::kTabStages];
+  __shared__ __align__(8) uint64_t tab_free[kCons][Smem<KIND, NB>::kTabStages];  // kSplit > 1: both warps read
 
   cg::cluster_group cluster = cg::this_cluster();
   const int ks = p.ks;
@@ -261,7 +268,10 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       mbar_init(&empty_bar[i], kThreads);
     }
     for (int w = 0; w < kCons; ++w)
-      for (int i = 0; i < kTabStages; ++i) mbar_init(&tab_bar[w][i], 1);
+      for (int i = 0; i < kTabStages; ++i) {
+        mbar_init(&tab_bar[w][i], 1);
+        mbar_init(&tab_free[w][i], kSplit * 32);
+      }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncthreads();
@@ -295,7 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(&full_bar[slot]))
                  : "memory");
   };
-  float* my = tab + warp * kTabStages * kStageFloats;
+  const int grp = warp / kSplit, half = warp % kSplit;  // row group, and which rows of it this warp takes
+  float* my = tab + grp * kTabStages * kStageFloats;
 
   // running ring positions over all tiles of this CTA: spectrum chunks staged
   // and consumed (global chunk g lives in slot g % kSpecStages, phase
@@ -321,11 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     const int r_begin = min(p.S, s_begin + rank * per);
     const int r_end = min(p.S, r_begin + per);
     const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
-    const int n_valid = min(kCons, (r1 - r0 + kRowsPerWarp - 1) / kRowsPerWarp);  // warps with rows
+    const int n_valid = min(kCons, (r1 - r0 + kRowsPerWarp - 1) / kRowsPerWarp);  // row groups with rows
 
-    float2 acc[kRowsPerWarp][NA];
+    float2 acc[kWRows][NA];
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i)
+    for (int i = 0; i < kWRows; ++i)
 #pragma unroll
       for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
 
@@ -357,8 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     };
 
     // ---- this warp's table ring (one stage per chunk) ----
-    const bool has_rows = warp < n_valid;
-    const int g8 = (r0 >> 3) + warp;  // row group of 8 (r0 is a multiple of 8)
+    const bool has_rows = grp < n_valid;
+    const int g8 = (r0 >> 3) + grp;  // row group of 8 (r0 is a multiple of 8)
     const float* tsrc = p.table + (long long)(has_rows ? g8 : 0) * p.t_group + (long long)j * p.t_mt +
                         (long long)r_begin * kStepFloats;
     const int nst = has_rows ? nchunks : 0;
@@ -366,9 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       const int n = min(kChunk, r_end - (r_begin + q * kChunk));
       const int slot = (tbase + q) % kTabStages;
       bulk_load(my + slot * kStageFloats, tsrc + (long long)q * kChunk * kStepFloats,
-                (unsigned)(n * kStepFloats * 4), &tab_bar[warp][slot]);
+                (unsigned)(n * kStepFloats * 4), &tab_bar[grp][slot]);
     };
-    if (lane == 0 && alive && nst > 0) {
+    if (half == 0 && lane == 0 && alive && nst > 0) {
       // the ring memory was last written by the generic proxy (partial sums)
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       for (int q = 0; q < kTabStages && q < nst; ++q) issue_tab(q);
@@ -378,17 +389,18 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     auto step = [&](const float* ts, const float2* xs) {
       // ts: this step's table block; xs: this step's staged spectrum planes
       // (vector: planes 2b, 2b+1 hold u, v of batch b)
-      float w[kRowsPerWarp * T];
+      constexpr int kQW = Shape<KIND>::kQuads / kSplit;  // quads of this warp's rows
+      float w[kWRows * T];
 #pragma unroll
-      for (int q = 0; q < Shape<KIND>::kQuads; ++q) {
-        const float4 v = reinterpret_cast<const float4*>(ts)[q * 32 + lane];
+      for (int q = 0; q < kQW; ++q) {
+        const float4 v = reinterpret_cast<const float4*>(ts)[(half * kQW + q) * 32 + lane];
         w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
       }
       float2 x[PB];
 #pragma unroll
       for (int a = 0; a < PB; ++a) x[a] = xs[a * 32 + lane];
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i) {
+      for (int i = 0; i < kWRows; ++i) {
         if constexpr (KIND == 1) {
           const float wp = w[2 * i], wm = w[2 * i + 1];
 #pragma unroll
@@ -443,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       if (has_rows) {
         const int h = tbase + c;
         const int ts_ = h % kTabStages;
-        if (!mbar_wait(&tab_bar[warp][ts_], (h / kTabStages) & 1)) {
+        if (!mbar_wait(&tab_bar[grp][ts_], (h / kTabStages) & 1)) {
           alive = false;
           break;
         }
@@ -458,11 +470,17 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
           for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
         }
         ++consumed;
-        // stage consumed by every lane: refill it with chunk c + kTabStages
+        // stage consumed by every lane (of both warps of the group): refill it
+        // with chunk c + kTabStages
         __syncwarp();
-        if (lane == 0 && issued < nst) {
-          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-          issue_tab(issued);
+        if constexpr (kSplit > 1) mbar_arrive(&tab_free[grp][ts_]);
+        if (half == 0 && lane == 0 && issued < nst) {
+          if (kSplit == 1 || mbar_wait(&tab_free[grp][ts_], (h / kTabStages) & 1)) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            issue_tab(issued);
+          } else {
+            alive = false;
+          }
         }
         ++issued;
       }
@@ -470,12 +488,12 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     }
     // nothing may still be writing into the rings when they become the partial-sum buffer
     asm volatile("cp.async.wait_all;\n" ::: "memory");
-    if (!alive && lane == 0 && has_rows) {
+    if (!alive && half == 0 && lane == 0 && has_rows) {
       // a wait gave up: let this warp's table copies still in flight land first
       const int done = min(issued, nst);
       for (int q = consumed; q < done; ++q) {
         const int h = tbase + q;
-        mbar_wait(&tab_bar[warp][h % kTabStages], (h / kTabStages) & 1);
+        mbar_wait(&tab_bar[grp][h % kTabStages], (h / kTabStages) & 1);
       }
     }
     __syncwarp();
@@ -485,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     if constexpr (KIND == 1) {
       // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i)
+      for (int i = 0; i < kWRows; ++i)
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
           const float2 pu = acc[i][2 * b], mv = acc[i][2 * b + 1];
@@ -501,11 +519,12 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     const int rpr = kRows / ks;  // rows per owner rank, a multiple of 8
     cluster.sync();              // every CTA of the cluster is done with its rings
     {
-      const int owner = (warp * kRowsPerWarp) / rpr;
-      const int rl0 = warp * kRowsPerWarp - owner * rpr;
+      const int row_local = grp * kRowsPerWarp + half * kWRows;  // first row of this warp in the tile
+      const int owner = row_local / rpr;
+      const int rl0 = row_local - owner * rpr;
       float2* dst = cluster.map_shared_rank(part, owner) + ((rank * rpr + rl0) * NA) * 32 + lane;
 #pragma unroll
-      for (int i = 0; i < kRowsPerWarp; ++i)
+      for (int i = 0; i < kWRows; ++i)
 #pragma unroll
         for (int a = 0; a < NA; ++a) dst[(i * NA + a) * 32] = acc[i][a];
     }
