@@ -261,6 +261,21 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     rec_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(rs, re_)))
     del rsht
+    # the inverse direction (InverseRealVectorSHT.forward, irfft included) on the same grid
+    isht = hs.InverseRealVectorSHT(NLAT, NLON).to(dev)
+    coef = vsht(x)
+    for _ in range(3):
+        isht(coef)
+    is_ = [torch.cuda.Event(enable_timing=True) for _ in range(sn)]
+    ie = [torch.cuda.Event(enable_timing=True) for _ in range(sn)]
+    for i in range(sn):
+        flush_l2()
+        is_[i].record(stream)
+        isht(coef)
+        ie[i].record(stream)
+    torch.cuda.synchronize(dev)
+    inv_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(is_, ie)))
+    del isht, coef
 
     # ---- end to end through the public API with host buffers ----
     xh = torch.empty((BATCH, 2, NLAT, NLON), dtype=torch.float32).pin_memory()
@@ -316,7 +331,8 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "flushed before every timed step: 256 MiB write, then a 256 MiB read so no dirty lines remain; tables 2x538 MB exceed L2"},
         "transforms_per_s": round(BATCH * world / (ms * 1e-3), 2),
         "secondary": {"RealSHT.forward_ms": round(scalar_ms, 5),
-                      "RealSHT.forward_recurrence_variant_ms": round(rec_ms, 5)},
+                      "RealSHT.forward_recurrence_variant_ms": round(rec_ms, 5),
+                      "InverseRealVectorSHT.forward_ms": round(inv_ms, 5)},
         "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * K,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",

@@ -184,3 +184,39 @@ def test_stream_rejects_flags_it_does_not_take():
     with pytest.raises(RuntimeError, match="GROUPED8"):
         run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, x, out, ops.group_table8((t, t), _lib.DIR_FORWARD), B, K, L, M,
             M, M, flags=_lib.FLAG_CONJ_W1)
+
+
+def test_stream_clusters_with_several_items_match():
+    """Persistent clusters: the 512 x 1024 inverse has 128 items for 74 clusters
+    (snake order, two items per cluster), and a forced split of 8 leaves 18
+    clusters for 72 forward items; both against the 4-row kernel."""
+    import holysht_b200 as hs
+
+    B, K, L, M = 4, 512, 512, 513
+    g = torch.Generator(DEV).manual_seed(7)
+    m = hs.RealVectorSHT(K, 2 * K).to(DEV)
+    assert ops.stream_launch_plan(_lib.KIND_VECTOR, _lib.DIR_INVERSE, batch=B, nlat=K, lmax=L, mmax=M)["clusters"] < 128
+    c = torch.complex(torch.randn((B, 2, L, M), device=DEV, generator=g), torch.randn((B, 2, L, M), device=DEV, generator=g))
+    c = c * (torch.arange(M, device=DEV)[None, :] <= torch.arange(L, device=DEV)[:, None])
+    t8 = ops.group_table8((m.w0_t, m.w1_t), _lib.DIR_INVERSE, conj=True)
+    t4 = ops.group_table((m.w0_t, m.w1_t), _lib.DIR_INVERSE, conj=True)
+    for ks in (0, 8):
+        o8 = torch.empty((B, 2, K, M), dtype=torch.complex64, device=DEV)
+        o4 = torch.empty_like(o8)
+        run(_lib.KIND_VECTOR, _lib.DIR_INVERSE, c, o8, t8, B, K, L, M, M, M, ks=ks)
+        ops.legendre_contract(kind=_lib.KIND_VECTOR, direction=_lib.DIR_INVERSE, input=c, output=o4, w0=t4, batch=B,
+                              nlat=K, lmax=L, mmax=M, in_strides=(2 * L * M, L * M, M), out_strides=(2 * K * M, K * M, M),
+                              out_cols=M, grouped=True)
+        a, b = o8.cpu().numpy().astype(np.complex128), o4.cpu().numpy().astype(np.complex128)
+        assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-6, ks
+    x = torch.randn((B, 2, K, 2 * K), device=DEV, generator=g)
+    spec = torch.fft.rfft(x, dim=-1)
+    W = spec.size(-1)
+    f8 = ops.group_table8((m.w0_t, m.w1_t), _lib.DIR_FORWARD)
+    outs = []
+    for ks in (0, 8):
+        o = torch.empty((B, 2, L, M), dtype=torch.complex64, device=DEV)
+        run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, spec, o, f8, B, K, L, M, W, M, ks=ks)
+        outs.append(o.cpu().numpy().astype(np.complex128))
+    assert np.linalg.norm(outs[0] - outs[1]) / np.linalg.norm(outs[1]) <= 1e-6
+    assert ops.stream_error_word() == 0
