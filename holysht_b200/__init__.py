@@ -118,8 +118,15 @@ class _GroupedTablesMixin:
             return TWO_PI * torch.fft.rfft(x.float(), dim=-1, norm="forward"), 1.0, True
         return torch.fft.rfft(x.float(), dim=-1), TWO_PI / self.nlon, False
 
+    def _apply(self, fn, *args, **kwargs):
+        # .to() / .cuda() / dtype casts move the tables: prepared launches must not outlive them
+        self.__dict__.pop("_contract_plans", None)
+        self.__dict__.pop("_fast_forward", None)
+        return super()._apply(fn, *args, **kwargs)
+
     def _drop_grouped(self) -> None:
         self.__dict__.pop("_contract_plans", None)
+        self.__dict__.pop("_fast_forward", None)
         self._grouped_fwd = None
         self._grouped_inv = None
         self._grouped8_fwd = None
@@ -174,6 +181,7 @@ class _GroupedTablesMixin:
             t = build(dense, direction, conj=conj)
             setattr(self, name, t)
             self.__dict__.pop("_contract_plans", None)  # prepared calls point at the old table
+            self.__dict__.pop("_fast_forward", None)
         return t, None, layout
 
 
@@ -222,6 +230,7 @@ def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_co
                                 grouped8=layout == "grouped8")
         plans[key] = plan
     plan.launch(inp, out)
+    return plan
 
 
 # ---------------------------------------------------------------------------
@@ -246,9 +255,56 @@ def _legendre_forward(spec, src, round_bf16: bool, scale: float):
         ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
                               lmax=L, mmax=M, scale=scale, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
     else:
-        _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
-             M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+        plan = _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
+                    M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
+        src.__dict__["_last_forward_plan"] = plan
     return out
+
+
+class _FastForward:
+    """The module forward for one input shape, once it has run through the
+    general path: rfft, output allocation and the prepared contraction (no
+    table lookups, checks or autograd).  Used only when no gradient is
+    wanted, for FP32 modules on the table path; dropped with the tables."""
+
+    __slots__ = ("plan", "spec_shape", "out_shape", "final_shape", "device")
+
+    def __init__(self, plan, spec_shape, out_shape, final_shape, device):
+        self.plan, self.spec_shape, self.out_shape = plan, spec_shape, out_shape
+        self.final_shape, self.device = final_shape, device
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        spec = torch.fft.rfft(x, dim=-1).view(self.spec_shape)
+        out = torch.empty(self.out_shape, dtype=torch.complex64, device=self.device)
+        self.plan.launch(spec, out)
+        return out.view(self.final_shape)
+
+
+def _module_forward(module, x: torch.Tensor, comp_dims: int) -> torch.Tensor:
+    """Forward of RealSHT (comp_dims 0) / RealVectorSHT (comp_dims 1)."""
+    fast_ok = not (x.requires_grad and torch.is_grad_enabled())
+    fast = module.__dict__.get("_fast_forward") if fast_ok else None
+    if fast is not None:
+        f = fast.get((x.shape, x.dtype, x.device))
+        if f is not None:
+            return f(x)
+    what = "RealVectorSHT" if comp_dims else "RealSHT"
+    _need_cuda(x, what)
+    assert x.shape[-2] == module.nlat and x.shape[-1] == module.nlon and (not comp_dims or x.shape[-3] == 2)
+    spec, scale, low = module._spectrum(x)
+    lead = spec.shape[:-2 - comp_dims]
+    flat = spec.reshape((-1,) + ((2,) if comp_dims else ()) + (module.nlat, spec.size(-1)))
+    module.__dict__.pop("_last_forward_plan", None)
+    out = _forward_coefficients(flat, module, low, scale)
+    final = lead + ((2,) if comp_dims else ()) + (module.lmax, module.mmax)
+    plan = module.__dict__.pop("_last_forward_plan", None)
+    if (fast_ok and plan is not None and not low and x.dtype == torch.float32 and x.is_contiguous()
+            and flat.data_ptr() == spec.data_ptr()):
+        cache = module.__dict__.setdefault("_fast_forward", {})
+        if len(cache) >= _MAX_PLANS:
+            cache.clear()
+        cache[(x.shape, x.dtype, x.device)] = _FastForward(plan, tuple(flat.shape), tuple(out.shape), final, x.device)
+    return out.reshape(final)
 
 
 def _forward_coefficients(spec, src, round_bf16: bool, scale: float):
@@ -603,13 +659,7 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
         return self.rec_seeds, self.rec_coef, self.rec_cos_theta
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        _need_cuda(x, "RealSHT")
-        assert x.shape[-2] == self.nlat and x.shape[-1] == self.nlon
-        spec, scale, low = self._spectrum(x)
-        lead = spec.shape[:-2]
-        spec = spec.reshape(-1, self.nlat, spec.size(-1))
-        out = _forward_coefficients(spec, self, low, scale)
-        return out.reshape(lead + (self.lmax, self.mmax))
+        return _module_forward(self, x, 0)
 
 
 class InverseRealSHT(_GroupedTablesMixin, nn.Module):
@@ -664,13 +714,7 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
         self._init_tables(("w0_t", "w1_t"), _lib.DIR_FORWARD)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        _need_cuda(x, "RealVectorSHT")
-        assert x.shape[-2] == self.nlat and x.shape[-1] == self.nlon and x.shape[-3] == 2
-        spec, scale, low = self._spectrum(x)
-        lead = spec.shape[:-3]
-        spec = spec.reshape(-1, 2, self.nlat, spec.size(-1))
-        out = _forward_coefficients(spec, self, low, scale)
-        return out.reshape(lead + (2, self.lmax, self.mmax))
+        return _module_forward(self, x, 1)
 
 
 class InverseRealVectorSHT(_GroupedTablesMixin, nn.Module):

@@ -11,6 +11,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <algorithm>
+#include <array>
+#include <map>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -342,7 +344,27 @@ int run_job_resolved(const Job& j, long long R, long long S, cudaStream_t stream
 // cluster count are chosen by simulating that assignment: the smallest
 // makespan in chunks (plus a fixed per-item cost for the pipeline ramp and the
 // epilogue), the smaller split on a tie.  An explicit ksplit is kept.
+std::pair<int, int> simulate_stream_grid(const hsb::stream::Params& p, int chunk, bool forward, int sms);
+
+// The plan depends on a handful of extents only: cached (the simulation walks every item).
 std::pair<int, int> choose_stream_grid(const hsb::stream::Params& p, int chunk, bool forward, int sms) {
+  using Key = std::array<long long, 10>;
+  static std::mutex mu;
+  static std::map<Key, std::pair<int, int>> cache;
+  const Key key = {p.R, p.S, p.M, p.j_act, p.mt_off, p.n_bg, p.ks, chunk, forward ? 1 : 0, sms};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const std::pair<int, int> plan = simulate_stream_grid(p, chunk, forward, sms);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 1024) cache.clear();
+  cache[key] = plan;
+  return plan;
+}
+
+std::pair<int, int> simulate_stream_grid(const hsb::stream::Params& p, int chunk, bool forward, int sms) {
   namespace st = hsb::stream;
   std::vector<int> steps;  // reduction steps of every item, in item order
   for (int jt = 0; jt < p.j_act; ++jt) {

@@ -220,3 +220,34 @@ def test_stream_clusters_with_several_items_match():
         outs.append(o.cpu().numpy().astype(np.complex128))
     assert np.linalg.norm(outs[0] - outs[1]) / np.linalg.norm(outs[1]) <= 1e-6
     assert ops.stream_error_word() == 0
+
+
+def test_module_fast_path_matches_the_general_path():
+    """Repeated no-grad forwards run a cached launch (rfft + one prepared
+    contraction); results equal the general path, per input shape, and the
+    cache is dropped when the tables change (state dict) or move (.to())."""
+    import holysht_b200 as hs
+
+    g = torch.Generator(DEV).manual_seed(11)
+    for cls, shape in ((hs.RealVectorSHT, (3, 2, 32, 64)), (hs.RealSHT, (2, 5, 32, 64))):
+        m = cls(32, 64).to(DEV)
+        x = torch.randn(shape, device=DEV, generator=g)
+        x2 = torch.randn((1,) + shape[1:], device=DEV, generator=g)
+        with torch.no_grad():
+            first = m(x)
+            again = m(x)             # cached launch
+            other = m(x2)            # a second shape
+        assert "_fast_forward" in m.__dict__ and len(m.__dict__["_fast_forward"]) == 2
+        general = m(x.clone().requires_grad_(True)).detach()  # autograd path
+        assert torch.equal(first, again) and torch.equal(first, general)
+        assert other.shape == (1,) + first.shape[1:]
+        # new tables through the state dict: the cached launch must not survive
+        sd = {k: v * 2 for k, v in m.state_dict().items()}
+        m.load_state_dict(sd)
+        with torch.no_grad():
+            doubled = m(x)
+        assert torch.allclose(doubled, 2 * first, rtol=1e-5, atol=1e-6)
+        m.to(DEV)
+        assert "_fast_forward" not in m.__dict__
+        with torch.no_grad():
+            assert torch.allclose(m(x), doubled)
