@@ -249,7 +249,10 @@ def _legendre_forward(spec, src, round_bf16: bool, scale: float):
     if getattr(src, "variant", "table") == "recurrence" and not round_bf16:
         # on-the-fly Legendre functions: no table stream
         seeds, coef, ct = src.recurrence_tables()
-        ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
+        if vector:
+            ops.legendre_vector_forward_recurrence(out, spec, seeds, coef, ct, scale)
+        else:
+            ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
     elif _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
         # large batch: the per-order contraction is a dense GEMM -> tcgen05
         ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
@@ -692,12 +695,20 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
 
 class RealVectorSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``RealVectorSHT``: [..., 2, nlat, nlon] -> [..., 2, lmax, mmax] complex64
-    (spheroidal, toroidal), both tables fused in one pass."""
+    (spheroidal, toroidal), both tables fused in one pass.
+
+    ``variant="recurrence"`` (an addition) generates the two vector tables on the
+    fly in the forward pass from the Legendre recurrences of orders m - 1 and
+    m + 1 (ladder identities) instead of streaming them (the backward pass uses
+    the tables)."""
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
                  grid: str = "equiangular", norm: str = "ortho", csphase: bool = True,
-                 dtype: str = "fp32"):
+                 dtype: str = "fp32", variant: str = "table"):
         super().__init__()
+        if variant not in ("table", "recurrence"):
+            raise ValueError(f"variant must be 'table' or 'recurrence', got {variant!r}")
+        self.variant = variant
         w_dtype = _w_dtype(dtype)
         w, L, M = _weights.vector_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
         _check_mmax(M, nlon)
@@ -712,6 +723,14 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
         self.register_buffer("w1_t", wt[1].permute(1, 2, 0).contiguous())
         self._mlk_name = "w0"
         self._init_tables(("w0_t", "w1_t"), _lib.DIR_FORWARD)
+        if variant == "recurrence":
+            seeds, coef, ct = _weights.vector_recurrence_tables(nlat, nlon, lmax, mmax, grid, norm, csphase)
+            self.register_buffer("rec_seeds", torch.from_numpy(seeds), persistent=False)
+            self.register_buffer("rec_coef", torch.from_numpy(coef), persistent=False)
+            self.register_buffer("rec_cos_theta", torch.from_numpy(ct), persistent=False)
+
+    def recurrence_tables(self):
+        return self.rec_seeds, self.rec_coef, self.rec_cos_theta
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return _module_forward(self, x, 1)

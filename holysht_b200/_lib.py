@@ -45,6 +45,7 @@ EXPORTS = (
     "holysht_stream_launch_plan",
     "holysht_legendre_dense_tc_noalloc",
     "holysht_legendre_forward_recurrence",
+    "holysht_legendre_vector_forward_recurrence",
 )
 
 
@@ -123,6 +124,8 @@ def load() -> ctypes.CDLL:
                                             ctypes.POINTER(ctypes.c_int)], i32),
             "holysht_legendre_forward_recurrence": ([vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64,
                                                      ctypes.c_float, vp], i32),
+            "holysht_legendre_vector_forward_recurrence": ([vp, vp, i64, i64, i64, vp, vp, vp, i64, i64, i64, i64,
+                                                            ctypes.c_float, vp], i32),
             "holysht_legendre_dense_tc_noalloc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,
                                                    ctypes.c_float, i32, i64, vp], i32),
         }

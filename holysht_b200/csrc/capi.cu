@@ -742,6 +742,46 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
   return check_launch("recurrence forward kernel");
 }
 
+int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int64_t spec_batch_stride,
+                                               int64_t spec_comp_stride, int64_t spec_row_stride, const float* seeds,
+                                               const float* coef, const float* cos_theta, int64_t batch,
+                                               int64_t nlat, int64_t lmax, int64_t mmax, float scale, void* stream) {
+  const long long B = batch, K = nlat, L = lmax, M = mmax;
+  if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  if (B == 0 || L == 0 || M == 0) return ok();
+  if (!out || !spec || !seeds || !coef || !cos_theta) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  if (K > (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt)
+    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d",
+                hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt);
+  if (!fits_int(B) || !fits_int(L) || !fits_int(M) || (B + hsb::rec::kNB - 1) / hsb::rec::kNB > 65535)
+    return fail(HOLYSHT_ERR_INVALID, "extent out of range");
+  if (spec_row_stride < M || spec_comp_stride < K * spec_row_stride || spec_batch_stride < 2 * spec_comp_stride)
+    return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
+  if ((reinterpret_cast<uintptr_t>(seeds) & 15) != 0)
+    return fail(HOLYSHT_ERR_INVALID, "seeds must be 16-byte aligned");
+  hsb::rec::VecRecParams p;
+  p.spec = static_cast<const float2*>(spec);
+  p.sbs = spec_batch_stride;
+  p.sps = spec_comp_stride;
+  p.srs = spec_row_stride;
+  p.seeds = seeds;
+  p.coef = coef;
+  p.x = cos_theta;
+  p.out = static_cast<float2*>(out);
+  p.B = (int)B;
+  p.K = (int)K;
+  p.L = (int)L;
+  p.M = (int)M;
+  p.nseg = (int)((L + hsb::rec::kSeg - 1) / hsb::rec::kSeg);
+  p.scale = scale;
+  const int threads = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
+  const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
+  dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
+  hsb::rec::recurrence_vector_forward_kernel<<<grid, threads < 32 ? 32 : threads, 0,
+                                               static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("vector recurrence forward kernel");
+}
+
 int holysht_tc_error_word(unsigned* value) {
   if (!value) return fail(HOLYSHT_ERR_INVALID, "null pointer");
   unsigned zero = 0;

@@ -173,5 +173,164 @@ __global__ void __launch_bounds__(kMaxWarps * 32) recurrence_forward_kernel(cons
   }
 }
 
+// ---------------------------------------------------------------------------
+// Vector forward with on-the-fly tables.  The vector tables of order m are
+// ladder combinations of the Legendre functions of orders m - 1 and m + 1:
+//   W0[l, k] = alpha_l Q^{m-1}_l + beta_l Q^{m+1}_l
+//   W1[l, k] = gamma_l Q^{m-1}_{l+1} + delta_l Q^{m+1}_{l+1},   Q^{m'}_l = w_k P_l^{m'}(x_k)
+// Both recurrences run upwards in l in fp32 from float64 checkpoints every
+// kSeg degrees (the state is (Q_l, Q_{l+1}) for each order), and the
+// contraction is evaluated in the (W0 + W1, W0 - W1) form with u = c0 + i c1,
+// v = c0 - i c1:  sph - i tor = sum_k (W0 + W1) u,  sph + i tor = sum_k (W0 - W1) v.
+struct VecRecParams {
+  const float2* spec;  // element (b, component, k, m) at b*sbs + p*sps + k*srs + m
+  long long sbs, sps, srs;
+  const float* seeds;  // [M][nseg][K][4]: Q^{m-1}_{l0}, Q^{m-1}_{l0+1}, Q^{m+1}_{l0}, Q^{m+1}_{l0+1}
+  const float* coef;   // [M][L][8]: a, b (order m-1), a, b (order m+1) at degree l+2; alpha, beta, gamma, delta
+  const float* x;      // [K] cos(theta_k)
+  float2* out;         // [B][2][L][M]
+  int B, K, L, M, nseg;
+  float scale;
+};
+
+// grid: x = order m, y = block of kSegPerCta segments, z = batch group of kNB
+__global__ void __launch_bounds__(kMaxWarps * 32) recurrence_vector_forward_kernel(const VecRecParams p) {
+  __shared__ float red[kMaxWarps][32];
+  __shared__ float cf[kSegPerCta * kSeg][8];
+  const int m = blockIdx.x;
+  const int b0 = blockIdx.z * kNB;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int lm = p.L - m;
+  const int nseg = lm > 0 ? (lm + kSeg - 1) / kSeg : 0;
+  const int c_begin = blockIdx.y * kSegPerCta;
+  const long long plane = (long long)p.L * p.M;
+
+  if (blockIdx.y == 0) {
+    // rows l < m of both components (every row of an order without degrees) are exact zeros
+    const int zrows = lm > 0 ? m : p.L;
+    for (int e = tid; e < zrows * kNB * 2; e += blockDim.x) {
+      const int l = e / (kNB * 2), r = e % (kNB * 2), b = b0 + r / 2, pc = r % 2;
+      if (b < p.B) p.out[((long long)b * 2 + pc) * plane + (long long)l * p.M + m] = make_float2(0.f, 0.f);
+    }
+  }
+  if (c_begin >= nseg) return;  // uniform per CTA
+  const int c_end = min(nseg, c_begin + kSegPerCta);
+  const int l_first = m + c_begin * kSeg;
+  const int ndeg = min(p.L, m + c_end * kSeg) - l_first;
+  for (int e = tid; e < kSegPerCta * kSeg * 8; e += blockDim.x) {
+    const int dl = e / 8, f = e % 8;
+    cf[dl][f] = dl < ndeg ? p.coef[((long long)m * p.L + l_first + dl) * 8 + f] : 0.f;
+  }
+
+  // this thread's latitudes and u, v of its kNB batches (scaled)
+  const int k0 = tid * kKpt;
+  float xk[kKpt];
+  float2 U[kKpt][kNB], V[kKpt][kNB];
+#pragma unroll
+  for (int i = 0; i < kKpt; ++i) {
+    const int k = k0 + i;
+    xk[i] = k < p.K ? p.x[k] : 0.f;
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      float2 c0 = make_float2(0.f, 0.f), c1 = c0;
+      if (k < p.K && b0 + b < p.B) {
+        const float2* s = p.spec + (long long)(b0 + b) * p.sbs + (long long)k * p.srs + m;
+        c0 = s[0];
+        c1 = s[p.sps];
+      }
+      U[i][b] = make_float2((c0.x - c1.y) * p.scale, (c0.y + c1.x) * p.scale);
+      V[i][b] = make_float2((c0.x + c1.y) * p.scale, (c0.y - c1.x) * p.scale);
+    }
+  }
+  __syncthreads();  // coefficients staged
+
+  for (int c = c_begin; c < c_end; ++c) {
+    const int lseg = m + c * kSeg;
+    const float* sd = p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 4;
+    float qm0[kKpt], qm1[kKpt], qp0[kKpt], qp1[kKpt];
+#pragma unroll
+    for (int i = 0; i < kKpt; ++i) {
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + i < p.K) s4 = reinterpret_cast<const float4*>(sd)[i];
+      qm0[i] = s4.x;
+      qm1[i] = s4.y;
+      qp0[i] = s4.z;
+      qp1[i] = s4.w;
+    }
+#pragma unroll
+    for (int qb = 0; qb < kSeg; qb += 2) {
+      float v[32];  // 2 degrees x (4 batches x (u, v) x re/im)
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const float* k8 = cf[lseg + qb + q2 - l_first];
+        const float am = k8[0], bm = k8[1], ap = k8[2], bp = k8[3];
+        const float al = k8[4], be = k8[5], ga = k8[6], de = k8[7];
+        float2 au[kNB], av[kNB];
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) au[b] = av[b] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < kKpt; ++i) {
+          const float w0 = fmaf(al, qm0[i], be * qp0[i]);
+          const float w1 = fmaf(ga, qm1[i], de * qp1[i]);
+          const float wp = w0 + w1, wm = w0 - w1;
+#pragma unroll
+          for (int b = 0; b < kNB; ++b) {
+            au[b] = __ffma2_rn(make_float2(wp, wp), U[i][b], au[b]);
+            av[b] = __ffma2_rn(make_float2(wm, wm), V[i][b], av[b]);
+          }
+          // both recurrences to degree l + 2
+          const float nm = fmaf(am * xk[i], qm1[i], -bm * qm0[i]);
+          const float np = fmaf(ap * xk[i], qp1[i], -bp * qp0[i]);
+          qm0[i] = qm1[i];
+          qm1[i] = nm;
+          qp0[i] = qp1[i];
+          qp1[i] = np;
+        }
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) {
+          v[q2 * 16 + b * 4 + 0] = au[b].x;
+          v[q2 * 16 + b * 4 + 1] = au[b].y;
+          v[q2 * 16 + b * 4 + 2] = av[b].x;
+          v[q2 * 16 + b * 4 + 3] = av[b].y;
+        }
+      }
+      // warp transpose-reduce: lane j ends with value j summed over the warp
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < d; ++i) {
+          const float send = upper ? v[i] : v[i + d];
+          const float keep = upper ? v[i + d] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+      float sum = v[0];
+      if (nwarps > 1) {
+        red[warp][lane] = sum;
+        __syncthreads();
+        sum = 0.f;
+        if (warp == 0)
+          for (int w = 0; w < nwarps; ++w) sum += red[w][lane];
+      }
+      if (warp == 0) {
+        // lane j: degree qb + (j >> 4), batch (j >> 2) & 3, (u, v) product (j >> 1) & 1, re/im j & 1
+        const float other = __shfl_xor_sync(0xffffffffu, sum, 2);
+        const int q2 = lane >> 4, b = (lane >> 2) & 3, which = (lane >> 1) & 1, ri = lane & 1;
+        const int l = lseg + qb + q2;
+        if (which == 0 && l < p.L && b0 + b < p.B) {
+          const float pu = sum, mv = other;  // Wp u and Wm v, component ri
+          float* o = reinterpret_cast<float*>(p.out + (long long)(b0 + b) * 2 * plane + (long long)l * p.M + m);
+          o[ri] = 0.5f * (mv + pu);  // sph = (Wm v + Wp u) / 2
+          // tor = -i (Wm v - Wp u) / 2: re from the imaginary parts, im from the real parts
+          o[2 * plane + (1 - ri)] = ri ? 0.5f * (mv - pu) : -0.5f * (mv - pu);
+        }
+      }
+      if (nwarps > 1) __syncthreads();
+    }
+  }
+}
+
 }  // namespace rec
 }  // namespace hsb

@@ -42,6 +42,7 @@ __all__ = [
     "legendre_dense_tc",
     "tc_error_word",
     "legendre_forward_recurrence",
+    "legendre_vector_forward_recurrence",
 ]
 
 
@@ -469,6 +470,29 @@ def stream_error_word() -> int:
     v = ctypes.c_uint(0)
     _lib.check(_lib.load().holysht_stream_error_word(ctypes.byref(v)))
     return int(v.value)
+
+
+def legendre_vector_forward_recurrence(output: torch.Tensor, spec: torch.Tensor, seeds: torch.Tensor,
+                                       coef: torch.Tensor, cos_theta: torch.Tensor, scale: float = 1.0) -> None:
+    """Vector forward with on-the-fly tables (``holysht_legendre_vector_forward_recurrence``):
+    output [B, 2, L, M] complex64 from an rfft-layout spectrum [B, 2, K, W >= M];
+    ``seeds``, ``coef`` and ``cos_theta`` from
+    :func:`holysht_b200.weights.vector_recurrence_tables`."""
+    dev = _cuda(output, spec, seeds, coef, cos_theta)
+    _require(spec.dtype == torch.complex64 and output.dtype == torch.complex64, "spectrum and output are complex64")
+    _require(spec.dim() == 4 and spec.size(1) == 2 and spec.stride(3) == 1,
+             "spectrum must be [B, 2, K, W] with contiguous orders")
+    _contig(output, seeds, coef, cos_theta)
+    M, nseg, K, four = seeds.shape
+    L = coef.size(1)
+    B = spec.size(0)
+    _require(four == 4 and tuple(coef.shape) == (M, L, 8) and cos_theta.numel() == K, "inconsistent tables")
+    _require(spec.size(2) == K and spec.size(3) >= M, "spectrum must be [B, 2, nlat, >= mmax]")
+    _require(tuple(output.shape) == (B, 2, L, M), "output must be [B, 2, lmax, mmax]")
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_legendre_vector_forward_recurrence(
+            _p(output), _p(spec), spec.stride(0), spec.stride(1), spec.stride(2), _p(seeds), _p(coef),
+            _p(cos_theta), B, K, L, M, float(scale), _stream(dev)))
 
 
 def legendre_forward_recurrence(output: torch.Tensor, spec: torch.Tensor, seeds: torch.Tensor, coef: torch.Tensor,

@@ -303,3 +303,75 @@ def scalar_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular
             coef[k, l, 0] = a
             coef[k, l, 1] = b
     return seeds, coef, x.astype(np.float32)
+
+
+def vector_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True):
+    """Inputs of the vector recurrence kernel (float64 built, float32 returned).
+
+    The vector tables of order m are ladder combinations of the Legendre
+    functions of orders m - 1 and m + 1 (the same identities as
+    :func:`dlegendre`).  With Q^{m'}_l(x_k) = w_k P_l^{m'}(x_k) (normalised,
+    Schmidt factor included, no Condon-Shortley phase):
+
+        W0[m, l, k] = alpha Q^{m-1}_l + beta Q^{m+1}_l
+        W1[m, l, k] = gamma Q^{m-1}_{l+1} + delta Q^{m+1}_{l+1}
+
+    which are ``vector_forward``'s tables (1/(l(l+1)) scaling, phase and the
+    sign of the second table folded into alpha .. delta).  The kernel runs both
+    recurrences upwards in l in float32, re-seeded every 16 degrees.
+
+    * seeds [mmax, ceil(lmax/16), nlat, 4]: Q^{m-1} at l0, l0+1 and Q^{m+1} at
+      l0, l0+1 for l0 = m + 16c (zero where the order does not exist);
+    * coef [mmax, lmax, 8]: a, b of order m-1 and a, b of order m+1 for
+      Q_{l+2} = a x Q_{l+1} - b Q_l, then alpha, beta, gamma, delta of degree l;
+    * cos_theta [nlat]."""
+    lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
+    theta, w = nodes_and_weights(nlat, grid)
+    x = np.cos(theta)
+    nseg = (lmax + SEGMENT - 1) // SEGMENT
+    seeds = np.zeros((mmax, nseg, nlat, 4), dtype=np.float32)
+    coef = np.zeros((mmax, lmax, 8), dtype=np.float32)
+    m_all = np.arange(mmax)
+    for l, row in _legendre_rows(mmax + 1, lmax + 1, x, _norm_seed(norm, False)):
+        q = row * _schmidt(norm, False, l) * w[None, :]  # [mmax + 1, K]: Q^{m'}_l
+        for off in (0, 1):  # checkpoint degrees l0 = l - off
+            d = l - off - m_all
+            sel = (d >= 0) & (d % SEGMENT == 0) & (l - off < lmax)
+            ms = m_all[sel]
+            c = d[sel] // SEGMENT
+            lower = ms >= 1
+            seeds[ms[lower], c[lower], :, off] = q[ms[lower] - 1].astype(np.float32)
+            seeds[ms, c, :, 2 + off] = q[ms + 1].astype(np.float32)
+
+    def rec(mp, lt):  # a, b of order mp at degree lt (lt >= mp + 1), Schmidt-rescaled
+        mp = np.asarray(mp, np.float64)
+        a = np.sqrt((4.0 * lt * lt - 1.0) / (lt * lt - mp * mp))
+        b = np.sqrt(np.maximum((lt - 1.0) ** 2 - mp * mp, 0.0) * (2.0 * lt + 1.0)
+                    / ((2.0 * lt - 3.0) * (lt * lt - mp * mp)))
+        f = _schmidt(norm, False, lt)
+        return a * f / _schmidt(norm, False, lt - 1), b * f / _schmidt(norm, False, lt - 2)
+
+    sign = np.ones(mmax)
+    if csphase:
+        sign[1::2] = -1.0
+    for l in range(lmax):
+        ms = m_all[m_all <= l]
+        mf = ms.astype(np.float64)
+        lt = l + 2.0
+        am, bm = rec(np.maximum(mf - 1.0, 0.0), lt)
+        am[ms == 0] = 0.0
+        bm[ms == 0] = 0.0
+        ap, bp = rec(mf + 1.0, lt)
+        s = sign[ms] * (1.0 / (l * (l + 1.0)) if l > 0 else 1.0)
+        alpha = 0.5 * np.sqrt((l + mf) * (l - mf + 1.0))
+        beta = -0.5 * np.sqrt(np.maximum((l - mf) * (l + mf + 1.0), 0.0))
+        F = 0.5 * math.sqrt((2.0 * l + 1.0) / (2.0 * l + 3.0))
+        gamma = F * np.sqrt(np.maximum((l - mf + 1.0) * (l - mf + 2.0), 0.0))
+        delta = F * np.sqrt((l + mf + 1.0) * (l + mf + 2.0))
+        z = ms == 0  # order 0: dP/dtheta = -sqrt(l(l+1)) P^1, m P / sin(theta) = 0
+        alpha[z] = 0.0
+        beta[z] = -math.sqrt(l * (l + 1.0))
+        gamma[z] = 0.0
+        delta[z] = 0.0
+        coef[ms, l] = np.stack([am, bm, ap, bp, alpha * s, beta * s, -gamma * s, -delta * s], axis=1)
+    return seeds, coef, x.astype(np.float32)

@@ -242,6 +242,20 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
                                         int64_t nlat, int64_t lmax, int64_t mmax, float scale,
                                         void* stream);
 
+/* Vector forward (RealVectorSHT's contraction) with on-the-fly tables: the
+ * orders m - 1 and m + 1 Legendre recurrences run in fp32 from float64
+ * checkpoints every 16 degrees and are combined by the ladder identities into
+ * (W0 + W1, W0 - W1) per degree.  out [B][2][lmax][mmax] complex64 (contiguous),
+ * spec: element (b, component, k, m) at b*spec_batch_stride +
+ * c*spec_comp_stride + k*spec_row_stride + m (the rfft layout), seeds
+ * [mmax][ceil(lmax/16)][nlat][4] (16-byte aligned), coef [mmax][lmax][8],
+ * cos_theta [nlat], all from holysht_b200.weights.vector_recurrence_tables.
+ * Output = scale * contraction; exact zeros for m > l.  nlat <= 1024. */
+int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int64_t spec_batch_stride,
+                                               int64_t spec_comp_stride, int64_t spec_row_stride, const float* seeds,
+                                               const float* coef, const float* cos_theta, int64_t batch,
+                                               int64_t nlat, int64_t lmax, int64_t mmax, float scale, void* stream);
+
 /* Same contraction as holysht_legendre_dense_tc, for callers that cannot
  * allocate device memory (a host whose own allocator owns the GPU memory, a
  * loop that must not allocate per call, a plugin handed no allocator).  No

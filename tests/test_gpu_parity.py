@@ -472,3 +472,24 @@ def test_recurrence_variant_matches_oracle(nlat, nlon, grid, norm, cs):
     assert_fp32_close(out, _module_oracle_scalar(m, x.astype(np.float64)))
     upper = np.arange(m.mmax)[None, :] > np.arange(m.lmax)[:, None]
     assert np.all(out.cpu().numpy()[:, upper] == 0)
+
+
+@pytest.mark.parametrize("nlat,nlon,grid,norm,cs", [
+    (512, 1024, "equiangular", "ortho", True),
+    (96, 192, "legendre-gauss", "schmidt", False),
+    (33, 64, "lobatto", "four-pi", True),
+    (130, 256, "equiangular", "ortho", True),
+])
+def test_vector_recurrence_variant_matches_oracle(nlat, nlon, grid, norm, cs):
+    rng = np.random.default_rng(nlat + 1)
+    x = rng.standard_normal((5, 2, nlat, nlon)).astype(np.float32)  # 5 batches: two batch groups
+    m = hs.RealVectorSHT(nlat, nlon, grid=grid, norm=norm, csphase=cs, variant="recurrence").to(DEV)
+    out = m(torch.from_numpy(x).to(DEV))
+    assert_fp32_close(out, _module_oracle_vector(m, x.astype(np.float64)))
+    upper = np.arange(m.mmax)[None, :] > np.arange(m.lmax)[:, None]
+    assert np.all(out.cpu().numpy()[:, :, upper] == 0)
+    # the table variant of the same transform
+    t = hs.RealVectorSHT(nlat, nlon, grid=grid, norm=norm, csphase=cs).to(DEV)
+    ref = t(torch.from_numpy(x).to(DEV)).cpu().numpy().astype(np.complex128)
+    got = out.cpu().numpy().astype(np.complex128)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-6
