@@ -250,3 +250,30 @@ def test_stream_launch_plan_rejects_bad_arguments():
     with pytest.raises(RuntimeError, match="ksplit"):
         hs.ops.stream_launch_plan(_lib.KIND_VECTOR, _lib.DIR_FORWARD, batch=1, nlat=8, lmax=8, mmax=8, ksplit=3,
                                   sm_count=148)
+
+
+@pytest.mark.parametrize("nlat,grid,norm,cs", [(24, "equiangular", "ortho", True),
+                                               (33, "legendre-gauss", "schmidt", False),
+                                               (40, "lobatto", "four-pi", True)])
+def test_vector_recurrence_tables_reproduce_the_vector_tables(nlat, grid, norm, cs):
+    """The vector recurrence kernel's inputs, evaluated with its own scheme
+    (two recurrences re-seeded every 16 degrees, ladder combination per degree)
+    in float64, give RealVectorSHT's tables."""
+    from holysht_b200 import weights as W
+
+    nlon = 2 * nlat
+    seeds, coef, x = W.vector_recurrence_tables(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+    ref, L, M = W.vector_forward(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+    got = np.zeros_like(ref)
+    x64 = x.astype(np.float64)
+    for m in range(min(M, L)):
+        for l in range(m, L):
+            d = l - m
+            if d % W.SEGMENT == 0:
+                qm0, qm1, qp0, qp1 = (seeds[m, d // W.SEGMENT, :, i].astype(np.float64) for i in range(4))
+            am, bm, ap, bp, al, be, ga, de = coef[m, l].astype(np.float64)
+            got[0, m, l] = al * qm0 + be * qp0
+            got[1, m, l] = ga * qm1 + de * qp1
+            qm0, qm1 = qm1, am * x64 * qm1 - bm * qm0
+            qp0, qp1 = qp1, ap * x64 * qp1 - bp * qp0
+    assert np.abs(got - ref).max() <= 1e-6 * np.abs(ref).max()
