@@ -1,6 +1,9 @@
-"""Run the recurrence-variant RealSHT forward (512x1024, batch 4) for profilers.
+"""Run the recurrence-variant forward (512x1024, batch 4) for profilers.
 
-    python -m holysht_b200.tools.profile_recurrence [reps]
+    python -m holysht_b200.tools.profile_recurrence [reps] [vector]
+
+RealSHT(variant="recurrence") by default, RealVectorSHT(variant="recurrence")
+with ``vector``.
 """
 from __future__ import annotations
 
@@ -13,9 +16,14 @@ import holysht_b200 as hs
 
 def main(argv):
     reps = int(argv[1]) if len(argv) > 1 else 3
+    vector = "vector" in argv
     dev = torch.device("cuda")
-    m = hs.RealSHT(512, 1024, variant="recurrence").to(dev)
-    x = torch.randn(4, 512, 1024, device=dev)
+    if vector:
+        m = hs.RealVectorSHT(512, 1024, variant="recurrence").to(dev)
+        x = torch.randn(4, 2, 512, 1024, device=dev)
+    else:
+        m = hs.RealSHT(512, 1024, variant="recurrence").to(dev)
+        x = torch.randn(4, 512, 1024, device=dev)
     with torch.no_grad():
         for _ in range(reps):
             m(x)
@@ -26,7 +34,8 @@ def main(argv):
             m(x)
         e[1].record()
         torch.cuda.synchronize()
-    print("recurrence RealSHT 512x1024 b4 ms", round(e[0].elapsed_time(e[1]) / 10, 4))
+    print("recurrence", "RealVectorSHT" if vector else "RealSHT", "512x1024 b4 ms",
+          round(e[0].elapsed_time(e[1]) / 10, 4))
 
 
 if __name__ == "__main__":
