@@ -11,21 +11,29 @@
 // so one warp's step is one contiguous 1 KB (scalar) / 2 KB (vector) block in
 // which every 16-byte read of the 32 lanes is a conflict-free 512-byte row.
 //
-// CTA = 8 warps x 8 rows (64 output rows) x 32 orders x NB batches; the
-// reduction is split over a thread-block cluster of ks CTAs whose partial sums
-// meet in distributed shared memory (fixed rank order: deterministic).
+// CTA = 8 warps x 8 rows (64 output rows) x 32 orders x NB batches, one CTA per
+// SM; the reduction is split over a thread-block cluster of ks CTAs.
 //   * every warp streams its own table block into a private ring of
 //     shared-memory stages with cp.async.bulk (one elected lane, mbarrier
 //     transaction counts), so the table never occupies registers and HBM
 //     requests stay in flight without any per-load instruction;
-//   * the input spectrum (shared by the 8 warps) goes through a 3-deep ring
-//     staged by all threads with cp.async; each thread's copies arrive on the
-//     chunk's full mbarrier when they land (cp.async.mbarrier.arrive.noinc),
-//     and an empty mbarrier per stage keeps a stage from being refilled before
-//     every warp has read it: no __syncthreads in the main loop;
+//   * the input spectrum (shared by the 8 warps) goes through a 4-stage ring
+//     staged 3 chunks ahead by all threads with cp.async.  Scalar: each
+//     thread's copies arrive on the chunk's full mbarrier when they land
+//     (cp.async.mbarrier.arrive.noinc).  Vector: the thread that staged a
+//     (c0, c1) pair forms u = c0 + i c1, v = c0 - i c1 in place once its copies
+//     have landed, then arrives.  An empty mbarrier per stage keeps a stage from
+//     being refilled before every warp has read it: no __syncthreads in the
+//     main loop;
 //   * 8 rows per warp halve the spectrum reads per FMA relative to 4 rows; the
-//     vector kind forms u = c0 + i c1, v = c0 - i c1 in registers; the FMAs
-//     are packed f32x2 (FFMA2).
+//     FMAs are packed f32x2 (FFMA2);
+//   * persistent over work items (compute tile x batch group, longest
+//     reduction first): cluster c takes items c, 2G-1-c, 2G+c, ... (snake
+//     order), which balances the triangular inverse direction; ring positions
+//     and mbarrier phases carry over from item to item;
+//   * each item ends with a cluster reduction: every warp stores its partial
+//     sums into the shared memory of the rank that owns its rows, one cluster
+//     barrier, and the owner adds the ks slices in rank order (deterministic).
 // Every mbarrier wait is bounded; a wait that gives up sets bit 0 of
 // g_stream_error and the CTA skips the rest of its reduction (its output is
 // then garbage, and the host reads the error word).
