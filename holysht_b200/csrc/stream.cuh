@@ -216,8 +216,8 @@ __device__ __forceinline__ bool decode(const Params& p, int t, int& j, int& r0, 
 
 // Exact zeros of the output outside the compute tiles (rows above the
 // diagonal, and m tiles with no l >= m inside the table), spread over the
-// grid's CTAs before their own tiles: the grid holds compute tiles only, so no
-// SM is taken by a CTA that only writes zeros.
+// grid's CTAs, written once the first tile's copies are in flight: the grid
+// holds compute tiles only, so no SM is taken by a CTA that only writes zeros.
 template <int DIR, int NB, int P>
 __device__ __forceinline__ void write_zero_units(const Params& p) {
   const int nz = p.n_zero * p.n_bg;
@@ -266,9 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   const int cid = blockIdx.x / ks;  // this CTA's cluster: every rank walks the same items
   const int n_items = p.n_compute * p.n_bg;
 
-  // zeros first: fire-and-forget stores that drain while the table stream ramps up
-  write_zero_units<DIR, NB, P>(p);
-  if (cid >= n_items) return;  // uniform across the cluster
+  if (cid >= n_items) {  // uniform across the cluster: this CTA only writes its share of the zeros
+    write_zero_units<DIR, NB, P>(p);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSpecStages; ++i) {
@@ -431,6 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         if (q < nchunks && alive) alive = stage_chunk(q);
         if constexpr (KIND == 1) cp_async_commit();
       }
+      // the first item's copies are in flight: now the zeros (fire-and-forget
+      // stores that drain while the table stream ramps up)
+      if (round == 0) write_zero_units<DIR, NB, P>(p);
       if constexpr (KIND == 1) {
         if (nchunks > 0 && alive) {
           cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk 0 have landed
