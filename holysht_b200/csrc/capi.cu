@@ -65,6 +65,17 @@ int sm_count_of_current_device() {
   return n;
 }
 
+// Test hook of the streaming kernel (HOLYSHT_TEST_STALL_CHUNK, read once): the
+// first CTA's warp 0 skips this table stage, so a bounded wait runs out and the
+// error word is set; the kernel still finishes.  Off (-1) by default.
+int env_stall_chunk() {
+  static int v = [] {
+    const char* s = std::getenv("HOLYSHT_TEST_STALL_CHUNK");
+    return (s && *s) ? std::atoi(s) : -1;
+  }();
+  return v;
+}
+
 int env_ksplit() {
   static int v = [] {
     const char* s = std::getenv("HOLYSHT_KSPLIT");
@@ -501,6 +512,7 @@ hsb::stream::Params make_stream_params(const Job& j, long long R, long long S, i
   const int nb = next_pow2_at_least(j.B, 1, j.kind == HOLYSHT_KIND_VECTOR ? 4 : 8);
   p.n_bg = (int)((j.B + nb - 1) / nb);
   p.ks = j.ksplit ? j.ksplit : env_ksplit();
+  p.stall_chunk = env_stall_chunk();
   *nb_out = nb;
   return p;
 }

@@ -102,6 +102,7 @@ struct Params {
   int zero_imag_col0, nyquist;
   int n_mt, j_act, n_compute, n_zero, n_bg, ks;
   int m_off, mt_off;
+  int stall_chunk;  // test hook, -1 = off: warp 0 of the first CTA never issues this table stage
 };
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
@@ -383,6 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
                         (long long)r_begin * kStepFloats;
     const int nst = has_rows ? nchunks : 0;
     auto issue_tab = [&](int q) {
+      // test hook: the stage is never requested, so its wait runs out (bounded)
+      if (q == p.stall_chunk && round == 0 && blockIdx.x == 0 && warp == 0) return;
       const int n = min(kChunk, r_end - (r_begin + q * kChunk));
       const int slot = (tbase + q) % kTabStages;
       bulk_load(my + slot * kStageFloats, tsrc + (long long)q * kChunk * kStepFloats,

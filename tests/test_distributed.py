@@ -158,3 +158,45 @@ def test_order_sharded_vector_two_gpus_nccl():
         p.join(timeout=300)
         assert p.exitcode == 0
     assert dict(result) == {0: True, 1: True}
+
+
+def _faulty_gloo_worker(rank, world, port, result):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    try:
+        if rank == 1:
+            raise RuntimeError("injected fault before the gather")  # this rank never joins the collective
+        slab = torch.zeros((1, 1, 4, 8), dtype=torch.complex64)
+        try:
+            hd.gather_order_slabs(slab, [(0, 8), (8, 16)])
+            result.put((rank, "no error"))
+        except Exception as e:  # the collective gives up after the process-group timeout
+            result.put((rank, type(e).__name__))
+    except RuntimeError as e:
+        result.put((rank, "raised: " + str(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_rank_failure_before_the_gather_is_reported_not_hung():
+    """Host-side fault injection on CPU ranks: rank 1 raises before the
+    all-gather; rank 0's collective ends with an error after the short
+    process-group timeout instead of waiting forever."""
+    ctx = mp.get_context("spawn")
+    result = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_faulty_gloo_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(result.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1].startswith("raised:")
+    assert got[0] != "no error"
