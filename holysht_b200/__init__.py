@@ -156,17 +156,15 @@ class _GroupedTablesMixin:
         """(table, None, layout) for one contraction direction.
 
         ``layout`` "grouped8" (``ops.group_table8``, the streaming kernel) is
-        the default for both directions; "grouped" (``ops.group_table``, 4-row
-        groups) serves the forward of the BF16/FP16 modules, whose forward
-        rounds the spectrum in the kernel.  ``HOLYSHT_TABLE_LAYOUT=grouped``
-        selects the 4-row kernel everywhere."""
+        the default for both directions (BF16/FP16 modules included: the
+        kernel rounds the staged spectrum); "grouped" (``ops.group_table``,
+        4-row groups) is the 4-row kernel, which ``HOLYSHT_TABLE_LAYOUT=grouped``
+        selects everywhere."""
         if layout is None:
             import os
 
-            low = bool(getattr(self, "_use_bf16", False) or getattr(self, "_use_fp16", False))
-            rounds = direction == _lib.DIR_FORWARD and low  # the forward rounds the spectrum in the kernel
             stream = os.environ.get("HOLYSHT_TABLE_LAYOUT", "grouped8") != "grouped"
-            layout = "grouped8" if stream and not rounds else "grouped"
+            layout = "grouped8" if stream else "grouped"
         if layout == "grouped8":
             name = "_grouped8_fwd" if direction == _lib.DIR_FORWARD else "_grouped8_inv"
         else:

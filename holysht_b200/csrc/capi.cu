@@ -241,10 +241,9 @@ int run_job(const Job& j, cudaStream_t stream) {
   if (j.grouped8) {
     if (j.kind == HOLYSHT_KIND_REAL)
       return fail(HOLYSHT_ERR_INVALID, "the GROUPED8 table layout is for complex contractions");
-    if (j.flags & (HOLYSHT_FLAG_CONJ_W1 | HOLYSHT_FLAG_ROUND_BF16))
+    if (j.flags & HOLYSHT_FLAG_CONJ_W1)
       return fail(HOLYSHT_ERR_INVALID,
-                  "the GROUPED8 layout takes neither HOLYSHT_FLAG_CONJ_W1 (build the table from "
-                  "(W0, -W1)) nor HOLYSHT_FLAG_ROUND_BF16");
+                  "the GROUPED8 layout does not take HOLYSHT_FLAG_CONJ_W1 (build the table from (W0, -W1))");
     return run_stream_job(j, R, S, stream);
   }
   Job jj = j;
@@ -513,6 +512,7 @@ hsb::stream::Params make_stream_params(const Job& j, long long R, long long S, i
   p.n_bg = (int)((j.B + nb - 1) / nb);
   p.ks = j.ksplit ? j.ksplit : env_ksplit();
   p.stall_chunk = env_stall_chunk();
+  p.round_bf16 = (j.flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0;
   *nb_out = nb;
   return p;
 }

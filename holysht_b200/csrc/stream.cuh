@@ -40,6 +40,7 @@
 #pragma once
 
 #include <cooperative_groups.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -103,6 +104,7 @@ struct Params {
   int n_mt, j_act, n_compute, n_zero, n_bg, ks;
   int m_off, mt_off;
   int stall_chunk;  // test hook, -1 = off: warp 0 of the first CTA never issues this table stage
+  int round_bf16;   // round the staged spectrum to bfloat16 (after the caller's scaling)
 };
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
@@ -299,15 +301,29 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   const int st_b = (threadIdx.x >> 5) % NB;
   const int st_ls0 = threadIdx.x / (NB * 32);
   float2* const st_dst = spec + (st_ls0 * PB + st_b * P) * 32 + lane;  // + slot * kSpecStageElems
+  // the staged values need a pass by the thread that staged them (after its
+  // own copies landed) for the vector kind (u, v) and for bfloat16 rounding;
+  // otherwise the copies publish themselves
+  const bool sync_stage = KIND == 1 || p.round_bf16 != 0;
+  auto bf16 = [](float v) { return __bfloat162float(__float2bfloat16_rn(v)); };
   auto combine = [&](int slot) {
     float2* d = st_dst + slot * kSpecStageElems;
 #pragma unroll
     for (int it = 0; it < kStageIters; ++it) {
       if (kChunk % kLsStep == 0 || st_ls0 + it * kLsStep < kChunk) {
         float2* e = d + it * kLsStep * PB * 32;
-        const float2 c0 = e[0], c1 = e[32];
-        e[0] = make_float2(c0.x - c1.y, c0.y + c1.x);   // u = c0 + i c1
-        e[32] = make_float2(c0.x + c1.y, c0.y - c1.x);  // v = c0 - i c1
+        if constexpr (KIND == 1) {
+          float2 c0 = e[0], c1 = e[32];
+          if (p.round_bf16) {
+            c0 = make_float2(bf16(c0.x), bf16(c0.y));
+            c1 = make_float2(bf16(c1.x), bf16(c1.y));
+          }
+          e[0] = make_float2(c0.x - c1.y, c0.y + c1.x);   // u = c0 + i c1
+          e[32] = make_float2(c0.x + c1.y, c0.y - c1.x);  // v = c0 - i c1
+        } else {
+          const float2 c0 = e[0];
+          e[0] = make_float2(bf16(c0.x), bf16(c0.y));
+        }
       }
     }
   };
@@ -373,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       const int slot = g & (kSpecStages - 1);
       if (g >= kSpecStages && !mbar_wait(&empty_bar[slot], ((g / kSpecStages) - 1) & 1)) return false;
       stage(c, slot);
-      if constexpr (KIND != 1) publish_async(slot);
+      if (!sync_stage) publish_async(slot);
       return true;
     };
 
@@ -433,12 +449,12 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
 #pragma unroll
       for (int q = 0; q < kSpecAhead; ++q) {
         if (q < nchunks && alive) alive = stage_chunk(q);
-        if constexpr (KIND == 1) cp_async_commit();
+        if (sync_stage) cp_async_commit();
       }
       // the first item's copies are in flight: now the zeros (fire-and-forget
       // stores that drain while the table stream ramps up)
       if (round == 0) write_zero_units<DIR, NB, P>(p);
-      if constexpr (KIND == 1) {
+      if (sync_stage) {
         if (nchunks > 0 && alive) {
           cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk 0 have landed
           combine(gbase & (kSpecStages - 1));
@@ -452,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         alive = false;
         break;
       }
-      if constexpr (KIND == 1) {
+      if (sync_stage) {
         cp_async_commit();
         if (c + 1 < nchunks) {
           cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk c + 1 have landed

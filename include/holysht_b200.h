@@ -179,8 +179,7 @@ typedef struct holysht_contract_desc {
  * sph - i tor = (W0 + W1)(c0 + i c1) and sph + i tor = (W0 - W1)(c0 - i c1),
  * half the multiplies of the direct form); the conjugate map is a table built
  * from (W0, -W1), and HOLYSHT_FLAG_CONJ_W1 is rejected with this layout. */
-/* GROUPED8 (SCALAR and VECTOR kinds, complex64 input, no CONJ_W1 / ROUND_BF16
- * flags): rows in groups of 8, each lane's 8 rows x T tables as quads of 4 floats:
+/* GROUPED8 (SCALAR and VECTOR kinds, complex64 input, no CONJ_W1 flag): rows in groups of 8, each lane's 8 rows x T tables as quads of 4 floats:
  *   T8[g][mt][s][q][lane][4], g < ceil(R/8), q < 2T,
  *   VECTOR: quad q = (row 2q: t0, t1, row 2q+1: t0, t1), t0 = W0 + W1, t1 = W0 - W1
  *   SCALAR: quad q = rows 4q .. 4q+3

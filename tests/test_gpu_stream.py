@@ -251,3 +251,27 @@ def test_module_fast_path_matches_the_general_path():
         assert "_fast_forward" not in m.__dict__
         with torch.no_grad():
             assert torch.allclose(m(x), doubled)
+
+
+@pytest.mark.parametrize("kind", [_lib.KIND_SCALAR, _lib.KIND_VECTOR])
+def test_stream_rounds_the_spectrum_to_bf16(kind):
+    """HOLYSHT_FLAG_ROUND_BF16: the staged (already scaled) spectrum is rounded to
+    bfloat16 and contracted in FP32: FP32-exact against the float64 oracle on the
+    rounded spectrum."""
+    rng = np.random.default_rng(21 + kind)
+    B, K, L, M = 5, 70, 64, 65
+    P = 2 if kind == _lib.KIND_VECTOR else 1
+    w0, w1 = tri_table(rng, L, K, M), tri_table(rng, L, K, M)
+    x = cplx(rng, (B, P, K, M)) if P == 2 else cplx(rng, (B, K, M))
+    xr = torch.from_numpy(x).view(torch.float32).bfloat16().float().view(torch.complex64).numpy()
+    if P == 2:
+        tab = ops.group_table8((torch.from_numpy(w0).to(DEV), torch.from_numpy(w1).to(DEV)), _lib.DIR_FORWARD)
+        ref = orc.vector_legendre_forward(xr.astype(np.complex128), w0.astype(np.float64), w1.astype(np.float64))
+        out = torch.empty((B, 2, L, M), dtype=torch.complex64, device=DEV)
+    else:
+        tab = ops.group_table8(torch.from_numpy(w0).to(DEV), _lib.DIR_FORWARD)
+        ref = orc.legendre_forward(xr.astype(np.complex128), w0.astype(np.float64))
+        out = torch.empty((B, L, M), dtype=torch.complex64, device=DEV)
+    run(kind, _lib.DIR_FORWARD, torch.from_numpy(x).to(DEV), out, tab, B, K, L, M, M, M, flags=_lib.FLAG_ROUND_BF16)
+    assert_fp32_close(out, ref)
+    assert ops.stream_error_word() == 0
