@@ -604,26 +604,33 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
         acc[i][2 * b + 1] = make_float2(0.5f * (mv.y - pu.y), -0.5f * (mv.x - pu.x));
       }
   }
-  // ---- cluster reduction of the partial sums through distributed smem ----
-  __syncthreads();
+  // ---- cluster reduction: every warp stores its rows' partial sums into the
+  // shared memory of the cluster rank that owns those rows (remote stores do not
+  // stall the warp), one cluster barrier, then each owner adds the ks slices in
+  // rank order (deterministic) from local shared memory.
+  const int rpr = kRows / ks;  // rows per owner rank, a multiple of kRowsPerWarp
+  cluster.sync();              // every CTA is done with its staging buffers (part aliases them)
+  {
+    const int row_local = warp * kRowsPerWarp;
+    const int owner = row_local / rpr;
+    const int rl0 = row_local - owner * rpr;
+    float2* dst = cluster.map_shared_rank(part, owner) + ((rank * rpr + rl0) * NA) * 32 + lane;
 #pragma unroll
-  for (int i = 0; i < kRowsPerWarp; ++i)
+    for (int i = 0; i < kRowsPerWarp; ++i)
 #pragma unroll
-    for (int a = 0; a < NA; ++a) part[((warp * kRowsPerWarp + i) * NA + a) * 32 + lane] = acc[i][a];
+      for (int a = 0; a < NA; ++a) dst[(i * NA + a) * 32] = acc[i][a];
+  }
   cluster.sync();
 
-  const int rpr = kRows / ks;
   const int total = rpr * NA * 32;
   for (int e = threadIdx.x; e < total; e += kThreads) {
     const int col = e & 31;
     const int a = (e >> 5) % NA;
     const int rl = e / (NA * 32);
     const int rloc = rank * rpr + rl;
-    const int idx = (rloc * NA + a) * 32 + col;
     float2 sum = make_float2(0.f, 0.f);
     for (int q = 0; q < ks; ++q) {
-      const float2* pq = cluster.map_shared_rank(part, q);
-      const float2 v = pq[idx];
+      const float2 v = part[((q * rpr + rl) * NA + a) * 32 + col];
       sum.x += v.x;
       sum.y += v.y;
     }
@@ -648,7 +655,6 @@ __global__ void __launch_bounds__(kThreads, KIND == KIND_VECTOR ? HSB_VECTOR_MIN
             sum;
     }
   }
-  cluster.sync();  // keep this CTA's partials alive until every peer has read them
 }
 
 }  // namespace hsb
