@@ -237,6 +237,13 @@ def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_co
 
 def _legendre_forward(spec, src, round_bf16: bool, scale: float):
     """coef = scale * Legendre(spec[..., :mmax]) (the body of the module forward)."""
+    return _legendre_forward_planned(spec, src, round_bf16, scale)[0]
+
+
+def _legendre_forward_planned(spec, src, round_bf16: bool, scale: float):
+    """(coef, the prepared contraction it ran or None): the table path returns
+    its ``ops.ContractPlan`` so the caller can reuse it."""
+    plan = None
     vector = src.vector
     B, K = spec.size(0), spec.size(-2)
     if K != src.nlat:
@@ -258,8 +265,7 @@ def _legendre_forward(spec, src, round_bf16: bool, scale: float):
     else:
         plan = _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
                     M, scale, _lib.FLAG_ROUND_BF16 if round_bf16 else 0)
-        src.__dict__["_last_forward_plan"] = plan
-    return out
+    return out, plan
 
 
 class _FastForward:
@@ -295,11 +301,11 @@ def _module_forward(module, x: torch.Tensor, comp_dims: int) -> torch.Tensor:
     spec, scale, low = module._spectrum(x)
     lead = spec.shape[:-2 - comp_dims]
     flat = spec.reshape((-1,) + ((2,) if comp_dims else ()) + (module.nlat, spec.size(-1)))
-    module.__dict__.pop("_last_forward_plan", None)
-    out = _forward_coefficients(flat, module, low, scale)
     final = lead + ((2,) if comp_dims else ()) + (module.lmax, module.mmax)
-    plan = module.__dict__.pop("_last_forward_plan", None)
-    if (fast_ok and plan is not None and not low and x.dtype == torch.float32 and x.is_contiguous()
+    if not fast_ok:
+        return _forward_coefficients(flat, module, low, scale).reshape(final)
+    out, plan = _legendre_forward_planned(flat, module, low, scale)
+    if (plan is not None and not low and x.dtype == torch.float32 and x.is_contiguous()
             and flat.data_ptr() == spec.data_ptr()):
         cache = module.__dict__.setdefault("_fast_forward", {})
         if len(cache) >= _MAX_PLANS:
