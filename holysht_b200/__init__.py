@@ -64,6 +64,15 @@ def _need_cuda(x: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what}: holysht_b200 runs on CUDA tensors only (no CPU fallback)")
 
 
+def _flat_batch(shape, trailing: int) -> int:
+    """Number of slices in the leading dimensions (``reshape(-1, ...)`` cannot
+    infer it for an empty tensor)."""
+    n = 1
+    for d in shape[: len(shape) - trailing]:
+        n *= d
+    return n
+
+
 def _strides3(t: torch.Tensor, vector: bool):
     """(batch, component, row) element strides of a [B,(2),R,C] tensor."""
     if vector:
@@ -300,7 +309,8 @@ def _module_forward(module, x: torch.Tensor, comp_dims: int) -> torch.Tensor:
     assert x.shape[-2] == module.nlat and x.shape[-1] == module.nlon and (not comp_dims or x.shape[-3] == 2)
     spec, scale, low = module._spectrum(x)
     lead = spec.shape[:-2 - comp_dims]
-    flat = spec.reshape((-1,) + ((2,) if comp_dims else ()) + (module.nlat, spec.size(-1)))
+    flat = spec.reshape((_flat_batch(spec.shape, 2 + comp_dims),) + ((2,) if comp_dims else ())
+                        + (module.nlat, spec.size(-1)))
     final = lead + ((2,) if comp_dims else ()) + (module.lmax, module.mmax)
     if not fast_ok:
         return _forward_coefficients(flat, module, low, scale).reshape(final)
@@ -552,7 +562,7 @@ def fused_sht_forward(x: torch.Tensor, weights: torch.Tensor, mmax: int,
     _need_cuda(x, "fused_sht_forward")
     spec = torch.fft.rfft(x.float(), dim=-1)
     lead = spec.shape[:-2]
-    spec = spec.reshape(-1, spec.size(-2), spec.size(-1))
+    spec = spec.reshape(_flat_batch(spec.shape, 2), spec.size(-2), spec.size(-1))
     wt = _as_weight_t(weights, weight_t)
     if wt.size(2) != int(mmax):
         raise RuntimeError(f"weight_t has mmax={wt.size(2)}, expected {int(mmax)}")
@@ -565,7 +575,7 @@ def fused_sht_inverse(coeffs: torch.Tensor, pct: torch.Tensor, nlon: int,
     """Legendre -> irfft: [B, lmax, mmax] complex64 -> [B, nlat, nlon] float32."""
     _need_cuda(coeffs, "fused_sht_inverse")
     lead = coeffs.shape[:-2]
-    c = coeffs.reshape(-1, coeffs.size(-2), coeffs.size(-1))
+    c = coeffs.reshape(_flat_batch(coeffs.shape, 2), coeffs.size(-2), coeffs.size(-1))
     if c.dtype != torch.complex64:
         c = c.to(torch.complex64)
     spec = _SpectrumLegendreInverse.apply(c, _DenseTables(_as_weight_t(pct, pct_t)), int(nlon))
@@ -585,7 +595,7 @@ def _prepare_irfft_input(x: torch.Tensor, nlon: int, active_mmax: Optional[int] 
         out = torch.zeros(x.shape[:-1] + (full,), dtype=x.dtype, device=x.device)
         n = min(full, x.size(-1))
         out[..., :n] = x[..., :n]
-    flat = out.reshape(-1, out.size(-2), out.size(-1))
+    flat = out.reshape(_flat_batch(out.shape, 2), out.size(-2), out.size(-1))
     ops.sht_prepare_irfft(flat, active_mmax, nlon)
     return flat.reshape(out.shape)
 
@@ -689,7 +699,7 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
         _need_cuda(x, "InverseRealSHT")
         assert x.shape[-2] == self.lmax and x.shape[-1] == self.mmax
         lead = x.shape[:-2]
-        c = x.reshape(-1, self.lmax, self.mmax)
+        c = x.reshape(_flat_batch(x.shape, 2), self.lmax, self.mmax)
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
         spec = _SpectrumLegendreInverse.apply(c, self, self.nlon)
@@ -762,7 +772,7 @@ class InverseRealVectorSHT(_GroupedTablesMixin, nn.Module):
         _need_cuda(x, "InverseRealVectorSHT")
         assert x.shape[-2] == self.lmax and x.shape[-1] == self.mmax and x.shape[-3] == 2
         lead = x.shape[:-3]
-        c = x.reshape(-1, 2, self.lmax, self.mmax)
+        c = x.reshape(_flat_batch(x.shape, 3), 2, self.lmax, self.mmax)
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
         spec = _SpectrumLegendreInverse.apply(c, self, self.nlon)

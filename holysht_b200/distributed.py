@@ -118,7 +118,7 @@ class _OrderSharded(nn.Module):
             raise RuntimeError("order-sharded transforms are forward-only; use the single-GPU modules for training")
         spec = torch.fft.rfft(x.float(), dim=-1)
         lead = spec.shape[: -3] if P == 2 else spec.shape[:-2]
-        spec = spec.reshape((-1, P, self.nlat, spec.size(-1)))
+        spec = spec.reshape((int(math.prod(lead)), P, self.nlat, spec.size(-1)))
         B, W = spec.size(0), spec.size(-1)
         slab = torch.zeros((B, P, self.lmax, self.width_pad), dtype=torch.complex64, device=x.device)
         width = self.m_hi - self.m_lo

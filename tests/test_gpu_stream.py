@@ -275,3 +275,30 @@ def test_stream_rounds_the_spectrum_to_bf16(kind):
     run(kind, _lib.DIR_FORWARD, torch.from_numpy(x).to(DEV), out, tab, B, K, L, M, M, M, flags=_lib.FLAG_ROUND_BF16)
     assert_fp32_close(out, ref)
     assert ops.stream_error_word() == 0
+
+
+def test_empty_batches_are_no_ops():
+    """Zero batches through the reference-named operators, the streaming entry
+    and the modules: empty outputs, no error, nothing launched that reads."""
+    import holysht_b200 as hs
+
+    K, L, M = 16, 12, 13
+    w = torch.zeros((L, K, M), device=DEV)
+    ops.fused_legendre_forward(torch.empty((0, L, M), dtype=torch.complex64, device=DEV),
+                               torch.empty((0, K, M), dtype=torch.complex64, device=DEV), w)
+    ops.fused_vector_legendre_inverse(torch.empty((0, 2, K, M), dtype=torch.complex64, device=DEV),
+                                      torch.empty((0, 2, L, M), dtype=torch.complex64, device=DEV), w, w)
+    run(_lib.KIND_VECTOR, _lib.DIR_FORWARD, torch.empty((0, 2, K, M), dtype=torch.complex64, device=DEV),
+        torch.empty((0, 2, L, M), dtype=torch.complex64, device=DEV), ops.group_table8((w, w), _lib.DIR_FORWARD),
+        0, K, L, M, M, M)
+    for cls, shape in ((hs.RealSHT, (0, 16, 32)), (hs.RealVectorSHT, (0, 2, 16, 32))):
+        m = cls(16, 32).to(DEV)
+        with torch.no_grad():
+            for _ in range(2):  # the general path, then the cached launch
+                out = m(torch.empty(shape, device=DEV))
+                assert out.shape == shape[:-2] + (m.lmax, m.mmax) and out.numel() == 0
+    inv = hs.InverseRealVectorSHT(16, 32).to(DEV)
+    y = inv(torch.empty((0, 2, inv.lmax, inv.mmax), dtype=torch.complex64, device=DEV))
+    assert y.shape == (0, 2, 16, 32)
+    torch.cuda.synchronize()
+    assert ops.stream_error_word() == 0
