@@ -64,6 +64,22 @@ def _need_cuda(x: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what}: holysht_b200 runs on CUDA tensors only (no CPU fallback)")
 
 
+def _rfft(x: torch.Tensor, norm: str = "backward") -> torch.Tensor:
+    """``torch.fft.rfft`` over the last dimension; cuFFT rejects a zero-sized
+    batch, whose spectrum is just an empty tensor of the right shape."""
+    if x.numel() == 0:
+        return torch.empty(x.shape[:-1] + (x.size(-1) // 2 + 1,), dtype=torch.complex64, device=x.device)
+    return torch.fft.rfft(x, dim=-1, norm=norm)
+
+
+def _irfft(spec: torch.Tensor, n: int) -> torch.Tensor:
+    """``torch.fft.irfft(..., norm="forward")`` over the last dimension, empty
+    batches included."""
+    if spec.numel() == 0:
+        return torch.empty(spec.shape[:-1] + (n,), dtype=torch.float32, device=spec.device)
+    return torch.fft.irfft(spec, n=n, dim=-1, norm="forward")
+
+
 def _flat_batch(shape, trailing: int) -> int:
     """Number of slices in the leading dimensions (``reshape(-1, ...)`` cannot
     infer it for an empty tensor)."""
@@ -124,8 +140,8 @@ class _GroupedTablesMixin:
         before the kernel rounds it."""
         low = bool(getattr(self, "_use_bf16", False) or getattr(self, "_use_fp16", False))
         if low:
-            return TWO_PI * torch.fft.rfft(x.float(), dim=-1, norm="forward"), 1.0, True
-        return torch.fft.rfft(x.float(), dim=-1), TWO_PI / self.nlon, False
+            return TWO_PI * _rfft(x.float(), "forward"), 1.0, True
+        return _rfft(x.float()), TWO_PI / self.nlon, False
 
     def _apply(self, fn, *args, **kwargs):
         # .to() / .cuda() / dtype casts move the tables: prepared launches must not outlive them
@@ -290,7 +306,7 @@ class _FastForward:
         self.final_shape, self.device = final_shape, device
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        spec = torch.fft.rfft(x, dim=-1).view(self.spec_shape)
+        spec = _rfft(x).view(self.spec_shape)
         out = torch.empty(self.out_shape, dtype=torch.complex64, device=self.device)
         self.plan.launch(spec, out)
         return out.view(self.final_shape)
@@ -560,7 +576,7 @@ def fused_sht_forward(x: torch.Tensor, weights: torch.Tensor, mmax: int,
                       weight_t: Optional[torch.Tensor] = None) -> torch.Tensor:
     """rfft -> Legendre: [B, nlat, nlon] float32 -> [B, lmax, mmax] complex64."""
     _need_cuda(x, "fused_sht_forward")
-    spec = torch.fft.rfft(x.float(), dim=-1)
+    spec = _rfft(x.float())
     lead = spec.shape[:-2]
     spec = spec.reshape(_flat_batch(spec.shape, 2), spec.size(-2), spec.size(-1))
     wt = _as_weight_t(weights, weight_t)
@@ -579,7 +595,7 @@ def fused_sht_inverse(coeffs: torch.Tensor, pct: torch.Tensor, nlon: int,
     if c.dtype != torch.complex64:
         c = c.to(torch.complex64)
     spec = _SpectrumLegendreInverse.apply(c, _DenseTables(_as_weight_t(pct, pct_t)), int(nlon))
-    y = torch.fft.irfft(spec, n=int(nlon), dim=-1, norm="forward")
+    y = _irfft(spec, int(nlon))
     return y.reshape(lead + y.shape[-2:])
 
 
@@ -703,7 +719,7 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
         spec = _SpectrumLegendreInverse.apply(c, self, self.nlon)
-        y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
+        y = _irfft(spec, self.nlon)
         return y.reshape(lead + (self.nlat, self.nlon))
 
 
@@ -776,7 +792,7 @@ class InverseRealVectorSHT(_GroupedTablesMixin, nn.Module):
         if c.dtype != torch.complex64:
             c = c.to(torch.complex64)
         spec = _SpectrumLegendreInverse.apply(c, self, self.nlon)
-        y = torch.fft.irfft(spec, n=self.nlon, dim=-1, norm="forward")
+        y = _irfft(spec, self.nlon)
         return y.reshape(lead + (2, self.nlat, self.nlon))
 
 

@@ -116,7 +116,9 @@ class _OrderSharded(nn.Module):
             raise RuntimeError("holysht_b200 runs on CUDA tensors only (no CPU fallback)")
         if torch.is_grad_enabled() and x.requires_grad:
             raise RuntimeError("order-sharded transforms are forward-only; use the single-GPU modules for training")
-        spec = torch.fft.rfft(x.float(), dim=-1)
+        from . import _rfft
+
+        spec = _rfft(x.float())
         lead = spec.shape[: -3] if P == 2 else spec.shape[:-2]
         spec = spec.reshape((int(math.prod(lead)), P, self.nlat, spec.size(-1)))
         B, W = spec.size(0), spec.size(-1)
