@@ -33,7 +33,7 @@ sys.path.insert(0, str(ROOT))
 NLAT, NLON, BATCH = 512, 1024, 4
 METRIC = "RealVectorSHT.forward ms @512x1024 b4 fp32"
 UNIT = "ms"
-PUBLISHED_GB10_MS = 6.855  # HOLYSHT RealVectorSHT.forward 512x1024 b4 on GB10
+PUBLISHED_GB10_MS = 6.855  # the published HOLYSHT RealVectorSHT.forward 512x1024 b4 time on GB10
 PROFILE = ROOT / "profiles" / "stream_vector_fwd_512x1024_b4.md"
 
 

@@ -17,7 +17,7 @@
 // 128-byte row segment and each table element is read from HBM exactly once
 // per batch group; only the l >= m triangle is ever loaded.
 //
-// Work decomposition (see DESIGN.md for the roofline):
+// Work decomposition:
 //   * a CTA owns a 32-order m-tile x 32 output rows (8 warps x 4 rows) x a
 //     batch group of NB batches;
 //   * the reduction axis is split across a thread-block cluster of KS CTAs;

@@ -1,6 +1,6 @@
 """Multi-GPU partitions of the forward transforms (one process per GPU).
 
-Two partitions (SURVEY §8e):
+Two partitions:
 
 * batch x channel (:func:`shard_batch`): every rank transforms its own slice
   of the leading dimensions with a full table replica; no collective.  This is

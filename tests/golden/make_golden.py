@@ -1,7 +1,7 @@
 """Generate golden fixtures from the reference's own CPU code path.
 
 Run from the repository root in a container where the reference checkout is
-mounted (default ``/root/reference``; override with ``HOLYSHT_REFERENCE``):
+mounted (its path in ``HOLYSHT_REFERENCE``, else the default in ``main``):
 
     python tests/golden/make_golden.py
 
