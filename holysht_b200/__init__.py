@@ -240,7 +240,8 @@ def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_co
         flags &= ~_lib.FLAG_CONJ_W1
     # the descriptor of a repeated call is built and checked once (ops.ContractPlan)
     key = (direction, B, M, tuple(in_vec_strides), tuple(out_vec_strides), out_cols, scale, flags, nlon, layout,
-           w0.data_ptr(), None if w1 is None else w1.data_ptr(), inp.dtype, out.dtype, inp.device.index)
+           w0.data_ptr(), None if w1 is None else w1.data_ptr(), inp.dtype, out.dtype, inp.device.index,
+           tuple(inp.shape), inp.stride(), tuple(out.shape), out.stride())
     plans = src.__dict__.setdefault("_contract_plans", {})
     plan = plans.get(key)
     if plan is None:

@@ -14,6 +14,7 @@ scale, writes irfft-ready buffers and runs the conjugate-transpose vector map.
 from __future__ import annotations
 
 import ctypes
+import threading
 from typing import Optional
 
 import torch
@@ -320,29 +321,35 @@ class ContractPlan:
     """A prepared :func:`legendre_contract` call: the descriptor is built and
     checked once, :meth:`launch` only fills in the input and output pointers
     (for callers that launch the same contraction repeatedly, such as the
-    modules' forward).  ``input_like`` / ``output_like`` fix the dtypes and the
-    device; later tensors must match them and the strides given here."""
+    modules' forward).  ``input_like`` / ``output_like`` fix the dtypes, shapes,
+    strides and the device; later tensors must match them.  One plan may be
+    launched from several threads (the descriptor is filled and passed under a
+    lock; the launch itself is asynchronous)."""
 
-    __slots__ = ("_desc", "_dev", "_in_dtype", "_out_dtype", "_keep")
+    __slots__ = ("_desc", "_dev", "_in_sig", "_out_sig", "_keep", "_lock")
 
     def __init__(self, *, input_like: torch.Tensor, output_like: torch.Tensor, **kw):
         self._desc = _contract_desc(input=input_like, output=output_like, **kw)
         self._dev = input_like.device.index
-        self._in_dtype, self._out_dtype = input_like.dtype, output_like.dtype
+        self._in_sig = (input_like.dtype, tuple(input_like.shape), input_like.stride())
+        self._out_sig = (output_like.dtype, tuple(output_like.shape), output_like.stride())
         self._keep = (kw.get("w0"), kw.get("w1"))  # the tables stay alive with the plan
+        self._lock = threading.Lock()
 
     def launch(self, input: torch.Tensor, output: torch.Tensor) -> None:
         _require(input.is_cuda and input.device.index == self._dev and output.device == input.device
-                 and input.dtype == self._in_dtype and output.dtype == self._out_dtype,
+                 and (input.dtype, tuple(input.shape), input.stride()) == self._in_sig
+                 and (output.dtype, tuple(output.shape), output.stride()) == self._out_sig,
                  "tensors do not match the contraction plan")
-        d = self._desc
-        d.in_, d.out = input.data_ptr(), output.data_ptr()
         lib = _lib.load()
-        if torch.cuda.current_device() == self._dev:
-            _lib.check(lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev)))
-        else:
-            with torch.cuda.device(self._dev):
+        with self._lock:
+            d = self._desc
+            d.in_, d.out = input.data_ptr(), output.data_ptr()
+            if torch.cuda.current_device() == self._dev:
                 _lib.check(lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev)))
+            else:
+                with torch.cuda.device(self._dev):
+                    _lib.check(lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev)))
 
 
 def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,

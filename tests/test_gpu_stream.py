@@ -253,6 +253,49 @@ def test_module_fast_path_matches_the_general_path():
             assert torch.allclose(m(x), doubled)
 
 
+def test_prepared_launch_checks_tensors_and_is_thread_safe():
+    """A prepared contraction rejects tensors whose shape or strides differ
+    from the ones it was built for, and one module's cached forward driven
+    from several threads at once gives each caller its own result."""
+    import threading
+
+    import holysht_b200 as hs
+
+    m = hs.RealVectorSHT(32, 64).to(DEV)
+    g = torch.Generator(DEV).manual_seed(5)
+    xs = [torch.randn((3, 2, 32, 64), device=DEV, generator=g) for _ in range(4)]
+    with torch.no_grad():
+        expected = [m(x) for x in xs]
+    fast = m.__dict__["_fast_forward"][(xs[0].shape, xs[0].dtype, xs[0].device)]
+    spec = torch.fft.rfft(xs[0], dim=-1)
+    with pytest.raises(RuntimeError, match="do not match"):
+        fast.plan.launch(spec[:2], torch.empty((2, 2, m.lmax, m.mmax), dtype=torch.complex64, device=DEV))
+    with pytest.raises(RuntimeError, match="do not match"):
+        fast.plan.launch(spec, torch.empty((3, 2, m.mmax, m.lmax), dtype=torch.complex64, device=DEV).transpose(-1, -2))
+
+    got = [[] for _ in xs]
+    errors = []
+
+    def worker(i):
+        try:
+            with torch.no_grad():
+                for _ in range(25):
+                    got[i].append(m(xs[i]))
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(len(xs))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    for i, outs in enumerate(got):
+        assert len(outs) == 25 and all(torch.equal(o, expected[i]) for o in outs)
+    assert ops.stream_error_word() == 0
+
+
 @pytest.mark.parametrize("kind", [_lib.KIND_SCALAR, _lib.KIND_VECTOR])
 def test_stream_rounds_the_spectrum_to_bf16(kind):
     """HOLYSHT_FLAG_ROUND_BF16: the staged (already scaled) spectrum is rounded to
