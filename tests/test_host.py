@@ -123,6 +123,21 @@ def test_cpu_tensors_fail_loudly():
         hs.ops.fused_legendre_forward(out, out, m.weight_t)
 
 
+def test_missing_library_fails_loudly(tmp_path):
+    """Without the native library the package raises; nothing falls back to a
+    CPU or PyTorch implementation."""
+    import subprocess
+    import sys
+
+    code = ("import torch, holysht_b200 as hs\n"
+            "try:\n    hs._lib.load()\nexcept RuntimeError as e:\n    print('raised', e)\n")
+    env = dict(__import__("os").environ, HOLYSHT_B200_LIBRARY=str(tmp_path / "absent.so"))
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.startswith("raised") and "not found" in r.stdout
+
+
 def test_graphed_module_passthrough_on_cpu():
     inner = torch.nn.Identity()
     g = hs.GraphedModule(inner)
