@@ -18,8 +18,6 @@ ROOT = PKG.parent
 SOURCES = [PKG / "csrc" / "capi.cu"]
 HEADERS = [*(PKG / "csrc").glob("*.cuh"), ROOT / "include" / "holysht_b200.h"]
 LIB = PKG / "libholysht_b200.so"
-PROBE_SRCS = [PKG / "csrc" / "fp32_probe.cu", PKG / "csrc" / "bulk_probe.cu"]
-PROBE_LIB = PKG / "libholysht_b200_probe.so"
 
 
 def nvcc() -> str:
@@ -45,11 +43,6 @@ def command(verbose: bool = False) -> list[str]:
     return cmd
 
 
-def probe_command() -> list[str]:
-    return [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-            "-shared", "-Xcompiler", "-fPIC", "-o", str(PROBE_LIB), *map(str, PROBE_SRCS), "-lcudart"]
-
-
 def up_to_date() -> bool:
     if not LIB.exists():
         return False
@@ -64,10 +57,6 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             raise RuntimeError(f"nvcc failed:\n{res.stdout}\n{res.stderr}")
         if verbose:
             sys.stderr.write(res.stderr)
-    if force or not PROBE_LIB.exists() or any(p.stat().st_mtime > PROBE_LIB.stat().st_mtime for p in PROBE_SRCS):
-        res = subprocess.run(probe_command(), capture_output=True, text=True)
-        if res.returncode != 0:
-            raise RuntimeError(f"nvcc failed on the FP32 probe:\n{res.stdout}\n{res.stderr}")
     return LIB
 
 

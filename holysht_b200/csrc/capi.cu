@@ -604,8 +604,17 @@ bool make_map_3d(CUtensorMap* map, const void* base, unsigned long long d0, unsi
 
 long long align256(long long v) { return (v + 255) & ~255LL; }
 
+// Bytes of the dense path's scratch (Xt [M][2B][S] and D [M][R][2B], fp32), or -1
+// when the size does not fit in 62 bits (each product is checked factor by factor).
 long long tc_workspace(long long B, long long R, long long S, long long M) {
-  return align256(M * 2 * B * S * 4) + align256(M * R * 2 * B * 4);
+  const long long lim = 1LL << 62;
+  auto mul = [lim](long long a, long long b, long long* r) {
+    return !__builtin_mul_overflow(a, b, r) && *r < lim;
+  };
+  long long a = 0, b = 0;
+  if (!mul(M, 2, &a) || !mul(a, B, &a) || !mul(a, S, &a) || !mul(a, 4, &a)) return -1;
+  if (!mul(M, R, &b) || !mul(b, 2, &b) || !mul(b, B, &b) || !mul(b, 4, &b)) return -1;
+  return align256(a) + align256(b);
 }
 
 }  // namespace
@@ -620,7 +629,9 @@ int holysht_legendre_dense_tc_workspace(int direction, int64_t batch, int64_t nl
   if (batch < 0 || nlat < 0 || lmax < 0 || mmax < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
   const bool fwd = direction == HOLYSHT_DIR_FORWARD;
   const long long Mrows = mmax < lmax ? mmax : lmax;
-  *bytes = tc_workspace(batch, fwd ? lmax : nlat, fwd ? nlat : lmax, Mrows);
+  const long long need = tc_workspace(batch, fwd ? lmax : nlat, fwd ? nlat : lmax, Mrows);
+  if (need < 0) return fail(HOLYSHT_ERR_INVALID, "extents too large: the workspace size overflows");
+  *bytes = need;
   return ok();
 }
 
@@ -651,7 +662,8 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
   if ((flags & HOLYSHT_FLAG_IRFFT_PREP) && (fwd || nlon <= 0 || out_cols > nlon / 2 + 1))
     return fail(HOLYSHT_ERR_INVALID, "irfft preparation is for the inverse with out_cols <= nlon/2+1");
   const long long Mrows = M < L ? M : L;
-  if (workspace_bytes < tc_workspace(B, R, S, Mrows)) return fail(HOLYSHT_ERR_INVALID, "workspace too small");
+  const long long need = tc_workspace(B, R, S, Mrows);
+  if (need < 0 || workspace_bytes < need) return fail(HOLYSHT_ERR_INVALID, "workspace too small");
   if (in_row_stride < M || in_batch_stride < S * in_row_stride || out_row_stride < out_cols ||
       out_batch_stride < R * out_row_stride)
     return fail(HOLYSHT_ERR_INVALID, "input or output strides too small");
@@ -1014,26 +1026,18 @@ constexpr long long kNoAllocScratchBytes = 64LL << 20;  // 64 MiB
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kMaxDevices] = {};
-
-// Device address of the scratch array on the current device; looked up once per
-// device (the host-side name of the array is not a device address).
+// Device address of the scratch array in the current device's context.  The
+// host-side name of the array is not a device address.  It is looked up on
+// every call (a cheap host-side query), so a context that was destroyed and
+// re-created (cudaDeviceReset) never receives a stale address.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return fail(HOLYSHT_ERR_CUDA, "no current CUDA device for the built-in scratch");
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      cudaGetLastError();
-      return fail(HOLYSHT_ERR_CUDA, "cannot get the address of the built-in scratch: %s", cudaGetErrorString(e));
-    }
-    g_noalloc_ptr[dev] = p;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    return fail(HOLYSHT_ERR_CUDA, "cannot get the address of the built-in scratch: %s", cudaGetErrorString(e));
   }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return HOLYSHT_OK;
 }
 }  // namespace

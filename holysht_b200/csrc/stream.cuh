@@ -35,8 +35,11 @@
 //     sums into the shared memory of the rank that owns its rows, one cluster
 //     barrier, and the owner adds the ks slices in rank order (deterministic).
 // Every mbarrier wait is bounded; a wait that gives up sets bit 0 of
-// g_stream_error and the CTA skips the rest of its reduction (its output is
-// then garbage, and the host reads the error word).
+// g_stream_error and the CTA skips the rest of its reduction: it waits for its
+// outstanding cp.async copies (cp.async.wait_all) and, warp by warp, for the
+// table bulk copies it issued but did not consume (bounded), issues no new
+// copy, and still reaches every cluster barrier.  After bit 0 is set the
+// output of that launch is undefined; the host reads the error word.
 #pragma once
 
 #include <cooperative_groups.h>

@@ -261,9 +261,10 @@ int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int6
  * counterpart in the reference.  The scratch is a 64 MiB array built into the
  * library (held on every GPU that loads it until the process exits); problems
  * whose holysht_legendre_dense_tc_workspace size exceeds 64 MiB are rejected
- * with HOLYSHT_ERR_INVALID.  The first call on a device looks the array's
- * device address up (cudaGetSymbolAddress); make that first call before any
- * stream capture.  All calls share the one array: calls that overlap on the
+ * with HOLYSHT_ERR_INVALID.  Every call looks the array's device address up
+ * in the current context (cudaGetSymbolAddress), so after cudaDeviceReset the
+ * next call uses the re-created context's copy of the array; make the first
+ * call on a device before any stream capture.  All calls share the one array: calls that overlap on the
  * GPU (other streams, other host threads) race on it and must be serialised
  * by the caller.  Nothing in the array carries over between calls: every
  * scratch element a call reads was written earlier in the same call.  No

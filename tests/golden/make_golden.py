@@ -1,9 +1,9 @@
 """Generate golden fixtures from the reference's own CPU code path.
 
-Run from the repository root in a container where the reference checkout is
-mounted (its path in ``HOLYSHT_REFERENCE``, else the default in ``main``):
+Run from the repository root with the reference checkout's path in
+``HOLYSHT_REFERENCE`` (required; there is no default):
 
-    python tests/golden/make_golden.py
+    HOLYSHT_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 The reference package ``torch-ext/holysht/__init__.py`` is imported from a
 temporary copy (importing it in place would create a build directory inside
@@ -87,7 +87,9 @@ CASES = [
 
 
 def main():
-    ref_root = Path(os.environ.get("HOLYSHT_REFERENCE", "/root/reference"))
+    if not os.environ.get("HOLYSHT_REFERENCE"):
+        raise SystemExit("set HOLYSHT_REFERENCE to the reference checkout's root")
+    ref_root = Path(os.environ["HOLYSHT_REFERENCE"])
     hs, tmp = _import_reference(ref_root)
     torch.manual_seed(1234)
     rng = np.random.default_rng(1234)

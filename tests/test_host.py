@@ -59,6 +59,21 @@ def test_invalid_arguments_are_rejected_without_gpu():
         _lib.check(lib.holysht_sht_prepare_irfft(None, -1, 4, 4, 6, None))
 
 
+
+def test_dense_workspace_size_overflow_is_rejected():
+    """Extents whose workspace size would wrap in 64 bits are refused instead of
+    yielding a small size that a smaller buffer would pass."""
+    lib = _lib.load()
+    n = ctypes.c_int64(0)
+    big = 1 << 40
+    st = lib.holysht_legendre_dense_tc_workspace(_lib.DIR_FORWARD, big, big, big, big, ctypes.byref(n))
+    assert st == _lib.HOLYSHT_ERR_INVALID and b"overflow" in lib.holysht_last_error()
+    st = lib.holysht_legendre_dense_tc_workspace(_lib.DIR_FORWARD, 65535, 1 << 31, 1 << 31, 1 << 31,
+                                                 ctypes.byref(n))
+    assert st == _lib.HOLYSHT_ERR_INVALID
+    assert lib.holysht_legendre_dense_tc_workspace(_lib.DIR_FORWARD, 4, 64, 64, 65, ctypes.byref(n)) == 0
+    assert n.value > 0
+
 @pytest.mark.parametrize("grid", ["equiangular", "legendre-gauss", "lobatto"])
 @pytest.mark.parametrize("norm", ["ortho", "schmidt", "four-pi"])
 def test_package_tables_match_oracle(grid, norm):

@@ -86,3 +86,34 @@ def test_noalloc_rejects_problems_larger_than_its_scratch():
     assert st == _lib.HOLYSHT_ERR_INVALID
     msg = _lib.load().holysht_last_error().decode()
     assert "built-in scratch" in msg and "64 MiB" in msg
+
+
+def _workspace_entry_nan(direction, out, inp, table, nlat, lmax, mmax, scale=1.0, flags=0, nlon=0):
+    """The workspace entry point with its workspace pre-filled with NaN, so any
+    scratch element read before it is written shows up in the output."""
+    lib = _lib.load()
+    nbytes = ctypes.c_int64(0)
+    _lib.check(lib.holysht_legendre_dense_tc_workspace(direction, inp.size(0), nlat, lmax, mmax,
+                                                       ctypes.byref(nbytes)))
+    ws = torch.full((max(nbytes.value, 4) // 4,), float("nan"), dtype=torch.float32, device=DEV)
+    _lib.check(lib.holysht_legendre_dense_tc(
+        direction, out.data_ptr(), out.stride(0), out.stride(1), out.size(2), inp.data_ptr(), inp.stride(0),
+        inp.stride(1), table.data_ptr(), inp.size(0), nlat, lmax, mmax, ctypes.c_float(scale), flags, nlon,
+        ws.data_ptr(), nbytes.value, torch.cuda.current_stream().cuda_stream))
+
+
+def test_noalloc_larger_problem_then_smaller_problem():
+    """A large call leaves its rows in the shared scratch; a following smaller
+    call with a different row count and batch must not read any of them."""
+    rng = np.random.default_rng(77)
+    for B, K, L, M in ((160, 128, 192, 129), (24, 32, 48, 33)):
+        w, spec, _ = _problem(rng, B, K, L, M)
+        fwd_table = torch.from_numpy(np.ascontiguousarray(w.transpose(2, 0, 1))).to(DEV)
+        ref = torch.empty((B, L, M), dtype=torch.complex64, device=DEV)
+        _workspace_entry_nan(_lib.DIR_FORWARD, ref, spec, fwd_table, K, L, M, scale=1.25)
+        got = torch.full((B, L, M), complex(np.nan, np.nan), dtype=torch.complex64, device=DEV)
+        assert _noalloc(_lib.DIR_FORWARD, got, spec, fwd_table, K, L, M, scale=1.25) == _lib.HOLYSHT_OK
+        assert torch.isfinite(torch.view_as_real(ref)).all()
+        _close(got, ref)
+    torch.cuda.synchronize()
+    assert ops.tc_error_word() == 0
