@@ -114,8 +114,8 @@ class _DenseTables:
 
 class _GroupedTablesMixin:
     """Module mixin: dense buffers plus cached row-grouped copies per direction
-    (``ops.group_table``), built for the transform's own direction at
-    construction and for the other direction on first backward.  The copies
+    (``ops.group_table8`` / ``ops.group_table``), built on the first
+    contraction in that direction on the tables' device.  The copies
     are non-persistent buffers (they follow ``.to()``) and are dropped when a
     state dict is loaded into the dense buffers."""
 
@@ -127,7 +127,9 @@ class _GroupedTablesMixin:
         self.register_buffer("_grouped_inv", None, persistent=False)
         self.register_buffer("_grouped8_fwd", None, persistent=False)
         self.register_buffer("_grouped8_inv", None, persistent=False)
-        self.table(hot_direction)
+        # the streaming copies are built on first use, on the tables' device
+        # (a GPU builds them in milliseconds; the host takes tens of seconds
+        # at 1024 x 2048)
         self.register_load_state_dict_post_hook(lambda module, _keys: module._drop_grouped())
 
     def _spectrum(self, x: torch.Tensor):

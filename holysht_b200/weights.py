@@ -23,6 +23,7 @@ from __future__ import annotations
 import math
 
 import numpy as np
+import torch
 
 GRIDS = ("equiangular", "legendre-gauss", "lobatto")
 NORMS = ("ortho", "four-pi", "schmidt")
@@ -97,32 +98,37 @@ def nodes_and_weights(nlat: int, grid: str):
 
 def _legendre_rows(n_m: int, n_l: int, x: np.ndarray, seed: float):
     """Yield (l, row) with row[m, k] = P_l^m(x_k) (no Condon-Shortley phase,
-    zero for m > l), for l = 0 .. n_l-1 and all m < n_m at once.
+    zero for m > l), for l = 0 .. n_l-1 and all m < n_m at once, as float64
+    torch tensors on the host (row is only valid until the next step).
 
     The recurrence runs upwards in l for every order simultaneously, keeping
-    only the two previous rows, so memory stays O(n_m * nlat)."""
-    sin_t = np.sqrt((1.0 + x) * (1.0 - x))
-    K = x.size
-    mm = np.arange(n_m, dtype=np.float64)
-    sect = np.full(K, seed)  # P_l^l at the current l
-    prev2 = np.zeros((n_m, K))
-    prev1 = np.zeros((n_m, K))
+    only the two previous rows, so memory stays O(n_m * nlat); the row updates
+    are multi-threaded torch operations."""
+    xt = torch.from_numpy(np.ascontiguousarray(x, np.float64))
+    sin_t = torch.sqrt((1.0 + xt) * (1.0 - xt))
+    K = xt.numel()
+    mm = torch.arange(n_m, dtype=torch.float64)
+    sect = torch.full((K,), float(seed), dtype=torch.float64)  # P_l^l at the current l
+    prev2 = torch.zeros((n_m, K), dtype=torch.float64)
+    prev1 = torch.zeros((n_m, K), dtype=torch.float64)
+    row = torch.zeros((n_m, K), dtype=torch.float64)
     for l in range(n_l):
-        row = np.zeros((n_m, K))
         if l > 0:
             sect = math.sqrt((2.0 * l + 1.0) / (2.0 * l)) * sin_t * sect
+        row.zero_()
         if l >= 2:
             k = min(l - 1, n_m)
             m = mm[:k]
-            a = np.sqrt((4.0 * l * l - 1.0) / (l * l - m * m))
-            b = np.sqrt(((l - 1.0) ** 2 - m * m) * (2.0 * l + 1.0) / ((2.0 * l - 3.0) * (l * l - m * m)))
-            row[:k] = a[:, None] * x[None, :] * prev1[:k] - b[:, None] * prev2[:k]
+            a = torch.sqrt((4.0 * l * l - 1.0) / (l * l - m * m))
+            b = torch.sqrt(((l - 1.0) ** 2 - m * m) * (2.0 * l + 1.0) / ((2.0 * l - 3.0) * (l * l - m * m)))
+            torch.mul(prev1[:k], xt[None, :], out=row[:k])
+            row[:k].mul_(a[:, None]).addcmul_(prev2[:k], b[:, None], value=-1.0)
         if l >= 1 and l - 1 < n_m:
-            row[l - 1] = math.sqrt(2.0 * l + 1.0) * x * prev1[l - 1]
+            row[l - 1] = math.sqrt(2.0 * l + 1.0) * xt * prev1[l - 1]
         if l < n_m:
             row[l] = sect
         yield l, row
-        prev2, prev1 = prev1, row
+        prev2, prev1, row = prev1, row, prev2
 
 
 def _norm_seed(norm: str, inverse: bool) -> float:
@@ -138,60 +144,72 @@ def _schmidt(norm: str, inverse: bool, l: int) -> float:
     return s if inverse else 1.0 / s
 
 
+def _torch_dtype(dtype):
+    return torch.float32 if np.dtype(dtype) == np.float32 else torch.float64
+
+
 def legendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
              inverse: bool = False, csphase: bool = True, kscale=None,
              dtype=np.float64) -> np.ndarray:
     """[mmax, lmax, nlat] normalised associated Legendre functions, each
     latitude optionally multiplied by ``kscale`` (the quadrature weights)."""
     x = np.cos(theta)
-    out = np.zeros((mmax, lmax, x.size), dtype=dtype)
-    sign = np.ones(mmax)
+    out = torch.zeros((mmax, lmax, x.size), dtype=_torch_dtype(dtype))
+    sign = torch.ones(mmax, dtype=torch.float64)
     if csphase:
         sign[1::2] = -1.0
-    ks = np.ones(x.size) if kscale is None else np.asarray(kscale, np.float64)
+    ks = torch.ones(x.size, dtype=torch.float64) if kscale is None else torch.from_numpy(
+        np.asarray(kscale, np.float64))
+    f = sign[:, None] * ks[None, :]
     for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, inverse)):
-        out[:, l, :] = row * (sign * _schmidt(norm, inverse, l))[:, None] * ks[None, :]
-    return out
+        out[:, l, :] = row * f * _schmidt(norm, inverse, l)
+    return out.numpy()
 
 
 def dlegendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
               inverse: bool = False, csphase: bool = True, kscale=None, lscale=None,
-              dtype=np.float64) -> np.ndarray:
+              dtype=np.float64, sign1: float = 1.0) -> np.ndarray:
     """[2, mmax, lmax, nlat]: dP/dtheta and m P / sin(theta), optionally
-    multiplied by ``kscale[k]`` and ``lscale[l]``."""
+    multiplied by ``kscale[k]`` and ``lscale[l]``; the second table is also
+    multiplied by ``sign1``."""
     x = np.cos(theta)
     K = x.size
-    out = np.zeros((2, mmax, lmax, K), dtype=dtype)
-    m = np.arange(mmax, dtype=np.float64)
-    sign = np.ones(mmax)
+    out = torch.zeros((2, mmax, lmax, K), dtype=_torch_dtype(dtype))
+    m = torch.arange(mmax, dtype=torch.float64)
+    sign = torch.ones(mmax, dtype=torch.float64)
     if csphase:
         sign[1::2] = -1.0
-    ks = np.ones(K) if kscale is None else np.asarray(kscale, np.float64)
+    ks = torch.ones(K, dtype=torch.float64) if kscale is None else torch.from_numpy(np.asarray(kscale, np.float64))
     rows = _legendre_rows(mmax + 1, lmax + 1, x, _norm_seed(norm, inverse))
-    _, cur = next(rows)
+    _, first = next(rows)
+    cur = first.clone()
+    d0 = torch.empty((mmax, K), dtype=torch.float64)
+    d1 = torch.empty((mmax, K), dtype=torch.float64)
     for l in range(lmax):
         _, nxt = next(rows)
-        cur = cur * _schmidt(norm, inverse, l)
-        nxt_s = nxt * _schmidt(norm, inverse, l + 1)
-        lower = np.zeros((mmax, K))
-        lower[1:] = cur[: mmax - 1]
-        upper = cur[1 : mmax + 1]
-        d0 = 0.5 * (np.sqrt(np.maximum((l + m) * (l - m + 1.0), 0.0))[:, None] * lower
-                    - np.sqrt(np.maximum((l - m) * (l + m + 1.0), 0.0))[:, None] * upper)
-        d0[0] = -math.sqrt(l * (l + 1.0)) * cur[1]
-        lower1 = np.zeros((mmax, K))
-        lower1[1:] = nxt_s[: mmax - 1]
-        upper1 = nxt_s[1 : mmax + 1]
-        d1 = 0.5 * math.sqrt((2.0 * l + 1.0) / (2.0 * l + 3.0)) * (
-            np.sqrt(np.maximum((l - m + 1.0) * (l - m + 2.0), 0.0))[:, None] * lower1
-            + np.sqrt((l + m + 1.0) * (l + m + 2.0))[:, None] * upper1)
+        cs = _schmidt(norm, inverse, l)
+        ns = _schmidt(norm, inverse, l + 1)
+        # d0 = (sqrt((l+m)(l-m+1)) P^{m-1}_l - sqrt((l-m)(l+m+1)) P^{m+1}_l) / 2
+        ca = 0.5 * cs * torch.sqrt(torch.clamp((l + m) * (l - m + 1.0), min=0.0))
+        cb = 0.5 * cs * torch.sqrt(torch.clamp((l - m) * (l + m + 1.0), min=0.0))
+        torch.mul(cur[1: mmax + 1], cb[:, None], out=d0)
+        d0.neg_()
+        d0[1:].addcmul_(cur[: mmax - 1], ca[1:, None])
+        d0[0] = -math.sqrt(l * (l + 1.0)) * cs * cur[1]
+        # d1 = F (sqrt((l-m+1)(l-m+2)) P^{m-1}_{l+1} + sqrt((l+m+1)(l+m+2)) P^{m+1}_{l+1})
+        F = 0.5 * math.sqrt((2.0 * l + 1.0) / (2.0 * l + 3.0)) * ns
+        ga = F * torch.sqrt(torch.clamp((l - m + 1.0) * (l - m + 2.0), min=0.0))
+        gb = F * torch.sqrt((l + m + 1.0) * (l + m + 2.0))
+        torch.mul(nxt[1: mmax + 1], gb[:, None], out=d1)
+        d1[1:].addcmul_(nxt[: mmax - 1], ga[1:, None])
         d1[0] = 0.0
-        keep = (m <= l)[:, None]
-        f = (sign * (1.0 if lscale is None else lscale[l]))[:, None] * ks[None, :]
-        out[0, :, l, :] = np.where(keep, d0, 0.0) * f
-        out[1, :, l, :] = np.where(keep, d1, 0.0) * f
-        cur = nxt
-    return out
+        keep = (m <= l).to(torch.float64)
+        fs = sign * keep * (1.0 if lscale is None else float(lscale[l]))
+        f = fs[:, None] * ks[None, :]
+        out[0, :, l, :] = d0 * f
+        out[1, :, l, :] = d1 * f * sign1
+        cur.copy_(nxt)
+    return out.numpy()
 
 
 def _try_torch_harmonics():
@@ -245,8 +263,7 @@ def vector_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="o
     ll = np.arange(lmax, dtype=np.float64)
     lscale = np.ones(lmax)
     lscale[1:] = 1.0 / (ll[1:] * (ll[1:] + 1.0))
-    d = dlegendre(mmax, lmax, theta, norm, False, csphase, kscale=w, lscale=lscale, dtype=dtype)
-    d[1] = -d[1]
+    d = dlegendre(mmax, lmax, theta, norm, False, csphase, kscale=w, lscale=lscale, dtype=dtype, sign1=-1.0)
     return d, lmax, mmax
 
 
@@ -287,6 +304,7 @@ def scalar_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular
         sign[1::2] = -1.0
     m_all = np.arange(mmax)
     for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, False)):
+        row = row.numpy()
         f = _schmidt(norm, False, l)
         vals = row * (sign * f)[:, None] * w[None, :]          # [mmax, K]
         d = l - m_all
@@ -333,6 +351,7 @@ def vector_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular
     coef = np.zeros((mmax, lmax, 8), dtype=np.float32)
     m_all = np.arange(mmax)
     for l, row in _legendre_rows(mmax + 1, lmax + 1, x, _norm_seed(norm, False)):
+        row = row.numpy()
         q = row * _schmidt(norm, False, l) * w[None, :]  # [mmax + 1, K]: Q^{m'}_l
         for off in (0, 1):  # checkpoint degrees l0 = l - off
             d = l - off - m_all
