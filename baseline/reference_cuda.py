@@ -28,7 +28,6 @@ import json
 import os
 import sys
 import tempfile
-import types
 from pathlib import Path
 
 import numpy as np
@@ -39,31 +38,13 @@ ROOT = HERE.parent
 REF_PKG = HERE / "_ref" / "torch-ext"
 
 
-def _stand_in_torch_harmonics():
-    sys.path.insert(0, str(ROOT))
-    from holysht_b200 import weights as W
-
-    th = types.ModuleType("torch_harmonics")
-
-    def make(builder, attr):
-        class _T:
-            def __init__(self, nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True):
-                t, self.lmax, self.mmax = builder(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
-                self.nlat, self.nlon = nlat, nlon
-                setattr(self, attr, torch.from_numpy(t))
-        return _T
-
-    th.RealSHT = make(W.scalar_forward, "weights")
-    th.InverseRealSHT = make(W.scalar_inverse, "pct")
-    th.RealVectorSHT = make(W.vector_forward, "weights")
-    th.InverseRealVectorSHT = make(W.vector_inverse, "dpct")
-    return th
-
-
 def _import_reference():
     if not (REF_PKG / "holysht" / "_ops.py").exists():
         raise RuntimeError("baseline/_ref is not prepared (run baseline/prepare_reference.py here first)")
-    sys.modules["torch_harmonics"] = _stand_in_torch_harmonics()
+    sys.path.insert(0, str(ROOT))
+    from baseline.reference_cpu import stand_in_torch_harmonics
+
+    sys.modules["torch_harmonics"] = stand_in_torch_harmonics()
     sys.path.insert(0, str(REF_PKG))
     import holysht  # the reference package
 

@@ -319,9 +319,10 @@ def run_ours(args, rank, world, local_rank):
     achieved = abytes / (kernel_ms * 1e-3) / 1e9
     traffic = _traffic_from_profile()
 
-    cpu = None
+    cpu = ref_cuda = None
     if rank == 0 and world == 1:
         cpu = cpu_baseline(vsht, x)
+        ref_cuda = reference_cuda_bar()
 
     if world > 1:
         dist.destroy_process_group()
@@ -358,33 +359,104 @@ def run_ours(args, rank, world, local_rank):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if ref_cuda is not None:
+        line["secondary"]["reference_cuda"] = ref_cuda
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(vsht, x):
-    """The oracle's restatement of the reference CPU path on the same workload
-    (full batch; a few repetitions, about 10-20 s of CPU work)."""
+def _reference_cpu_forward(vsht=None):
+    """(callable x -> coefficients, kind, description) of the reference's CPU path.
+
+    Preferred: the reference's own ``RealVectorSHT.forward`` on torch CPU,
+    imported unmodified from ``baseline/_ref`` (``baseline/reference_cpu.py``;
+    rfft + its einsum contractions) with the tables this project uses.  If
+    ``baseline/_ref`` was not staged, the oracle's fp32 restatement of that
+    path (rfft + per-order GEMMs)."""
+    import numpy as np
+    import torch
+
+    from baseline import reference_cpu
+
+    if reference_cpu.available():
+        hs_ref = reference_cpu.load()
+        mod = hs_ref.RealVectorSHT(NLAT, NLON)
+
+        def fn(xh):
+            with torch.no_grad():
+                return mod(torch.from_numpy(xh)).numpy()
+        return fn, "reference", ("the reference's RealVectorSHT.forward on torch CPU "
+                                 "(torch-ext/holysht/__init__.py:1504-1693, CPU branch)")
+    from oracle import sht_oracle as orc
+
+    if vsht is not None:
+        w = np.stack([vsht.w0.float().cpu().numpy(), vsht.w1.float().cpu().numpy()])
+    else:
+        w = orc.vector_forward_tables(NLAT, NLON).astype(np.float32)
+    return orc.CpuForwardBaseline(w, vector=True), "port", "oracle restatement: rfft + per-order fp32 GEMMs"
+
+
+def _time_cpu(fn, xh, steps, warmup, budget_s):
+    for _ in range(max(warmup, 1)):
+        fn(xh)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < 3 or (len(times) < steps and time.perf_counter() < t_end):
+        t = time.perf_counter()
+        fn(xh)
+        times.append((time.perf_counter() - t) * 1e3)
+    return statistics.median(times), len(times)
+
+
+def _check_against_oracle(out, xh):
+    """Relative L2 of a CPU-path result against the float64 oracle on slice 0."""
     import numpy as np
 
     from oracle import sht_oracle as orc
 
+    w = orc.vector_forward_tables(NLAT, NLON)
+    ref = orc.vector_sht_forward(xh[:1].astype(np.float64), w)
+    return float(np.linalg.norm(out[:1] - ref) / np.linalg.norm(ref))
+
+
+def cpu_baseline(vsht, x):
+    """The reference's CPU path on the same workload, on this host's cores
+    (about 10 s of CPU work), checked once against the float64 oracle."""
+    import torch
+
     _use_all_cores()
-    w = np.stack([vsht.w0.float().cpu().numpy(), vsht.w1.float().cpu().numpy()])
-    fn = orc.CpuForwardBaseline(w, vector=True)
+    fn, kind, what = _reference_cpu_forward(vsht)
     xh = x.cpu().numpy()
-    fn(xh)
-    times = []
-    t_end = time.perf_counter() + 10.0
-    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 20):
-        t = time.perf_counter()
-        fn(xh)
-        times.append((time.perf_counter() - t) * 1e3)
-    return {"value": round(statistics.median(times), 3), "unit": UNIT, "cores": _blas_threads(), "kind": "port",
-            "sample": f"full workload (4,2,512,1024), median of {len(times)} runs"}
+    ms, n = _time_cpu(fn, xh, 20, 1, 10.0)
+    rel = _check_against_oracle(fn(xh), xh)
+    return {"value": round(ms, 3), "unit": UNIT, "cores": torch.get_num_threads() if kind == "reference"
+            else _blas_threads(), "kind": kind,
+            "sample": f"full workload (4,2,512,1024), median of {n} runs; {what}",
+            "rel_l2_vs_oracle": rel}
+
+
+def reference_cuda_bar():
+    """The reference's own CUDA path timed on this GPU (``baseline/reference_cuda.py``)
+    in a child process, so this process never loads the reference's library.
+    None when ``baseline/_ref`` was not staged; an error string if the child failed."""
+    script = ROOT / "baseline" / "reference_cuda.py"
+    if not (ROOT / "baseline" / "_ref" / "torch-ext" / "holysht" / "_ops.py").exists():
+        return None
+    try:
+        res = subprocess.run([sys.executable, str(script), "--steps", "20", "--warmup", "5"], capture_output=True,
+                             text=True, timeout=600, cwd=str(ROOT))
+    except subprocess.TimeoutExpired:
+        return {"error": "timed out after 600 s"}
+    for ln in reversed(res.stdout.splitlines()):
+        if ln.startswith("{"):
+            return json.loads(ln)
+    return {"error": f"rc={res.returncode}: {res.stderr.strip().splitlines()[-1:]}"}
 
 
 def _use_all_cores():
     """Give the CPU baseline every host core (torchrun sets OMP_NUM_THREADS=1)."""
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
     try:
         from threadpoolctl import threadpool_limits
 
@@ -405,33 +477,27 @@ def _blas_threads():
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args, rank, world):
+    """The reference arm: the reference's own CPU path (see _reference_cpu_forward)
+    on the same workload and seed, every host core, rank 0 only; each step is
+    one full forward (about 0.1-0.2 s)."""
     if rank != 0:
         return
     import numpy as np
-
-    from oracle import sht_oracle as orc
+    import torch
 
     _use_all_cores()
-    w = orc.vector_forward_tables(NLAT, NLON).astype(np.float32)
-    fn = orc.CpuForwardBaseline(w, vector=True)
+    fn, kind, what = _reference_cpu_forward()
     rng = np.random.default_rng(1)
     x = rng.standard_normal((BATCH, 2, NLAT, NLON)).astype(np.float32)
-    for _ in range(max(args.warmup, 1)):
-        fn(x)
-    times = []
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        fn(x)
-        times.append((time.perf_counter() - t) * 1e3)
-    ms = sum(times) / len(times)
-    cores = _blas_threads()
+    ms, n = _time_cpu(fn, x, args.steps, args.warmup, 120.0)
+    cores = torch.get_num_threads() if kind == "reference" else _blas_threads()
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(ms, 4),
         "unit": UNIT,
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": n,
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": False,
@@ -441,8 +507,8 @@ def run_reference(args, rank, world):
         "data": "synthetic N(0,1), seed 1",
         "config": {"workload": "RealVectorSHT.forward 512x1024 equiangular lmax=512 mmax=513 ortho csphase, batch 4",
                    "global_batch": BATCH, "parallelism": "host CPU"},
-        "cpu_baseline": {"value": round(ms, 4), "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": "full workload per step: rfft + per-order fp32 GEMMs (numpy/BLAS)"},
+        "cpu_baseline": {"value": round(ms, 4), "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"full workload per step, median of {n} steps; {what}"},
         "e2e": {"value": round(ms, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

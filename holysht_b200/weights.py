@@ -213,6 +213,8 @@ def dlegendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
 
 
 def _try_torch_harmonics():
+    """torch-harmonics when importable (``restated=True`` in the builders below
+    skips it and always uses the float64 restatement)."""
     try:
         import torch_harmonics  # noqa: F401
         return torch_harmonics
@@ -228,9 +230,9 @@ def _resolve(nlat, nlon, lmax, mmax, grid, norm):
 
 
 def scalar_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64):
+                   dtype=np.float64, restated=False):
     """RealSHT ``weights`` [mmax, lmax, nlat] (float64) and (lmax, mmax)."""
-    th = _try_torch_harmonics()
+    th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.RealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
         return ref.weights.double().numpy().astype(dtype), ref.lmax, ref.mmax
@@ -240,9 +242,9 @@ def scalar_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="o
 
 
 def scalar_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64):
+                   dtype=np.float64, restated=False):
     """InverseRealSHT ``pct`` [mmax, lmax, nlat]."""
-    th = _try_torch_harmonics()
+    th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.InverseRealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
         return ref.pct.double().numpy().astype(dtype), ref.lmax, ref.mmax
@@ -252,9 +254,9 @@ def scalar_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="o
 
 
 def vector_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64):
+                   dtype=np.float64, restated=False):
     """RealVectorSHT ``weights`` [2, mmax, lmax, nlat]."""
-    th = _try_torch_harmonics()
+    th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.RealVectorSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
         return ref.weights.double().numpy().astype(dtype), ref.lmax, ref.mmax
@@ -268,9 +270,9 @@ def vector_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="o
 
 
 def vector_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64):
+                   dtype=np.float64, restated=False):
     """InverseRealVectorSHT ``dpct`` [2, mmax, lmax, nlat]."""
-    th = _try_torch_harmonics()
+    th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.InverseRealVectorSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
         return ref.dpct.double().numpy().astype(dtype), ref.lmax, ref.mmax
