@@ -38,6 +38,9 @@ EXPORTS = (
     "holysht_fused_vector_forward_recompose_real",
     "holysht_sht_prepare_irfft",
     "holysht_legendre_contract",
+    "holysht_legendre_contract_peers",
+    "holysht_peer_barrier",
+    "holysht_peer_error_word",
     "holysht_legendre_dense_tc_workspace",
     "holysht_legendre_dense_tc",
     "holysht_tc_error_word",
@@ -114,6 +117,10 @@ def load() -> ctypes.CDLL:
             "holysht_fused_vector_forward_recompose_real": ([vp, vp, vp, i64, i64, i64, vp], i32),
             "holysht_sht_prepare_irfft": ([vp, i64, i64, i64, i64, vp], i32),
             "holysht_legendre_contract": ([ctypes.POINTER(ContractDesc), vp], i32),
+            "holysht_peer_barrier": ([ctypes.POINTER(vp), i32, i32, ctypes.c_uint, vp], i32),
+            "holysht_peer_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
+            "holysht_legendre_contract_peers": ([ctypes.POINTER(ContractDesc), ctypes.POINTER(vp), i32, i64, vp, vp],
+                                                i32),
             "holysht_legendre_dense_tc_workspace": ([i32, i64, i64, i64, i64, ctypes.POINTER(ctypes.c_int64)], i32),
             "holysht_legendre_dense_tc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,
                                            ctypes.c_float, i32, i64, vp, i64, vp], i32),

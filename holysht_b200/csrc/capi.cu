@@ -24,6 +24,7 @@
 #include "tc_dense.cuh"
 #include "recurrence.cuh"
 #include "stream.cuh"
+#include "peer.cuh"
 
 namespace {
 
@@ -163,6 +164,11 @@ struct Job {
   int grouped;   // HOLYSHT_TABLE_GROUPED
   int grouped8;  // HOLYSHT_TABLE_GROUPED8 (streaming kernel)
   long long m_off;
+  // output to several GPUs (holysht_legendre_contract_peers); n_peers == 0: out only
+  void* const* peers;
+  int n_peers;
+  long long col_off;
+  void* mc;
 };
 
 template <int KIND, int DIR, typename TIN, bool GROUPED>
@@ -220,7 +226,7 @@ int run_job(const Job& j, cudaStream_t stream) {
   const long long R = j.dir == HOLYSHT_DIR_FORWARD ? j.L : j.K;
   const long long S = j.dir == HOLYSHT_DIR_FORWARD ? j.K : j.L;
   if (j.B == 0 || R == 0 || j.out_cols == 0) return ok();
-  if (!j.out) return fail(HOLYSHT_ERR_INVALID, "output pointer is null");
+  if (!j.out && j.n_peers == 0) return fail(HOLYSHT_ERR_INVALID, "output pointer is null");
   if (S > 0 && j.M > 0 && (!j.in || !j.w0)) return fail(HOLYSHT_ERR_INVALID, "input or table pointer is null");
   if (j.kind == HOLYSHT_KIND_VECTOR && !j.grouped && !j.grouped8 && S > 0 && j.M > 0 && !j.w1)
     return fail(HOLYSHT_ERR_INVALID, "vector contraction needs both tables");
@@ -513,6 +519,10 @@ hsb::stream::Params make_stream_params(const Job& j, long long R, long long S, i
   p.ks = j.ksplit ? j.ksplit : env_ksplit();
   p.stall_chunk = env_stall_chunk();
   p.round_bf16 = (j.flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0;
+  p.n_peers = j.n_peers;
+  p.col_off = (int)j.col_off;
+  p.mc = static_cast<float2*>(j.mc);
+  for (int q = 0; q < j.n_peers; ++q) p.peer[q] = static_cast<float2*>(j.peers[q]);
   *nb_out = nb;
   return p;
 }
@@ -869,6 +879,33 @@ int holysht_stream_error_word(unsigned* value) {
   return ok();
 }
 
+int holysht_peer_barrier(void* const* signal, int n_ranks, int rank, unsigned epoch, void* stream) {
+  if (!signal) return fail(HOLYSHT_ERR_INVALID, "signal is null");
+  if (n_ranks < 1 || n_ranks > 8 || rank < 0 || rank >= n_ranks)
+    return fail(HOLYSHT_ERR_INVALID, "rank %d of %d ranks (1..8)", rank, n_ranks);
+  if (epoch == 0) return fail(HOLYSHT_ERR_INVALID, "epoch starts at 1");
+  hsb::peer::BarrierParams p = {};
+  for (int q = 0; q < n_ranks; ++q) {
+    if (!signal[q] || (reinterpret_cast<uintptr_t>(signal[q]) & 3))
+      return fail(HOLYSHT_ERR_INVALID, "signal[%d] is null or misaligned", q);
+    p.signal[q] = static_cast<unsigned*>(signal[q]);
+  }
+  p.n_ranks = n_ranks;
+  p.rank = rank;
+  p.epoch = epoch;
+  hsb::peer::barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("peer_barrier");
+}
+
+int holysht_peer_error_word(unsigned* value) {
+  if (!value) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  unsigned zero = 0;
+  if (cudaMemcpyFromSymbol(value, hsb::peer::g_peer_error, sizeof(unsigned)) != cudaSuccess ||
+      cudaMemcpyToSymbol(hsb::peer::g_peer_error, &zero, sizeof(unsigned)) != cudaSuccess)
+    return fail(HOLYSHT_ERR_CUDA, "cannot read the peer barrier's error word");
+  return ok();
+}
+
 int holysht_version(void) { return 100; }
 
 const char* holysht_last_error(void) { return g_last_error.c_str(); }
@@ -925,9 +962,40 @@ int holysht_fused_vector_legendre_inverse(void* out, const void* in, const float
   return run_job(j, static_cast<cudaStream_t>(stream));
 }
 
-int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
+namespace {
+int contract_impl(const holysht_contract_desc* d, void* const* peers, int n_peers, long long col_off, void* mc,
+                  void* stream);
+}  // namespace
+
+int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream) {
+  return contract_impl(desc, nullptr, 0, 0, nullptr, stream);
+}
+
+int holysht_legendre_contract_peers(const holysht_contract_desc* desc, void* const* peer_out, int n_peers,
+                                    int64_t out_col_offset, void* multicast_out, void* stream) {
+  if (!desc) return fail(HOLYSHT_ERR_INVALID, "descriptor is null");
+  if (n_peers < 1 || n_peers > 8) return fail(HOLYSHT_ERR_INVALID, "n_peers must be 1..8 (got %d)", n_peers);
+  if (!peer_out) return fail(HOLYSHT_ERR_INVALID, "peer_out is null");
+  for (int q = 0; q < n_peers; ++q)
+    if (!peer_out[q]) return fail(HOLYSHT_ERR_INVALID, "peer_out[%d] is null", q);
+  if (desc->table_layout != HOLYSHT_TABLE_GROUPED8)
+    return fail(HOLYSHT_ERR_INVALID, "output to several GPUs needs the GROUPED8 table layout");
+  if (out_col_offset < 0 || !fits_int(out_col_offset + desc->out_cols))
+    return fail(HOLYSHT_ERR_INVALID, "out_col_offset out of range");
+  if (multicast_out && (reinterpret_cast<uintptr_t>(multicast_out) & 7))
+    return fail(HOLYSHT_ERR_INVALID, "multicast_out must be 8-byte aligned");
+  return contract_impl(desc, peer_out, n_peers, out_col_offset, multicast_out, stream);
+}
+
+namespace {
+int contract_impl(const holysht_contract_desc* d, void* const* peers, int n_peers, long long col_off, void* mc,
+                  void* stream) {
   if (!d) return fail(HOLYSHT_ERR_INVALID, "descriptor is null");
   Job j = {};
+  j.peers = peers;
+  j.n_peers = n_peers;
+  j.col_off = col_off;
+  j.mc = mc;
   j.kind = d->kind;
   j.dir = d->direction;
   j.in_dtype = d->in_dtype;
@@ -965,6 +1033,7 @@ int holysht_legendre_contract(const holysht_contract_desc* d, void* stream) {
     return fail(HOLYSHT_ERR_INVALID, "irfft preparation needs nlon > 0 and out_cols <= nlon/2+1");
   return run_job(j, static_cast<cudaStream_t>(stream));
 }
+}  // namespace
 
 int holysht_fused_vector_forward_pack_real(float* s0, float* s1, const void* in, int64_t batch,
                                            int64_t nlat, int64_t mmax, void* stream) {

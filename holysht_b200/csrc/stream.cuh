@@ -108,7 +108,36 @@ struct Params {
   int m_off, mt_off;
   int stall_chunk;  // test hook, -1 = off: warp 0 of the first CTA never issues this table stage
   int round_bf16;   // round the staged spectrum to bfloat16 (after the caller's scaling)
+  // Output to several GPUs (order-partitioned transforms): with n_peers > 0 every
+  // output element is stored at column col_off + m of each peer[q] buffer (same
+  // strides as out, plain peer stores over NVLink), or, when mc is set, once
+  // through the NVLink multicast address mc (multimem.st: the switch delivers it
+  // to every GPU's buffer).  n_peers == 0: the element goes to out.
+  float2* peer[8];
+  float2* mc;
+  int n_peers;
+  int col_off;
 };
+
+__device__ __forceinline__ void multimem_store(float2* addr, float2 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};\n" ::"l"(addr), "f"(v.x), "f"(v.y)
+               : "memory");
+}
+
+// Store one output element (offset in elements, strides of out).
+__device__ __forceinline__ void store_out(const Params& p, long long off, float2 v) {
+  if (p.n_peers == 0) {
+    static_cast<float2*>(p.out)[off] = v;
+    return;
+  }
+  off += p.col_off;
+  if (p.mc != nullptr) {
+    multimem_store(p.mc + off, v);
+    return;
+  }
+#pragma unroll 1
+  for (int q = 0; q < p.n_peers; ++q) p.peer[q][off] = v;
+}
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
   return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -238,8 +267,8 @@ __device__ __forceinline__ void write_zero_units(const Params& p) {
       const int row = r0 + e / (NB * P * 32);
       const int mm = m0 + col, b = b0 + a / P, pl = a % P;
       if (mm < p.out_cols && b < p.B)
-        static_cast<float2*>(p.out)[(long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs +
-                                    mm] = make_float2(0.f, 0.f);
+        store_out(p, (long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs + mm,
+                  make_float2(0.f, 0.f));
     }
   }
 }
@@ -580,11 +609,13 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       }
       sum.x *= p.scale;
       sum.y *= p.scale;
-      if ((p.zero_imag_col0 && mm == 0) || mm == p.nyquist) sum.y = 0.f;
+      // irfft preparation acts on global columns (an order slice written to
+      // peers starts at column col_off)
+      const int gcol = mm + (p.n_peers ? p.col_off : 0);
+      if ((p.zero_imag_col0 && gcol == 0) || gcol == p.nyquist) sum.y = 0.f;
       const int b = b0 + a / P, pl = a % P;
       if (b < p.B)
-        static_cast<float2*>(p.out)[(long long)b * p.out_bs + (long long)pl * p.out_ps +
-                                    (long long)row * p.out_rs + mm] = sum;
+        store_out(p, (long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs + mm, sum);
     }
     __syncthreads();  // partial sums read: the next tile's copies may reuse the memory
   }

@@ -374,6 +374,26 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
         _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))
 
 
+def legendre_contract_peers(peer_ptrs, *, out_col_offset: int = 0, multicast_ptr: int = 0, **kwargs) -> None:
+    """:func:`legendre_contract` (``grouped8`` tables) with every output element
+    stored at column ``out_col_offset + m`` of each buffer in ``peer_ptrs``
+    (device addresses valid on this GPU: its own buffer and peers' buffers
+    mapped into it, all laid out like ``output``), or once through the NVLink
+    multicast address ``multicast_ptr`` when it is not 0
+    (``holysht_legendre_contract_peers``).  ``output`` is this GPU's own buffer
+    (used for checks only).  The caller orders the stores with the peers
+    (a cross-GPU barrier) before anyone reads them."""
+    _require(kwargs.get("grouped8", False), "output to several GPUs needs grouped8 tables")
+    n = len(peer_ptrs)
+    _require(1 <= n <= 8, "1 to 8 peer buffers")
+    d = _contract_desc(**kwargs)
+    arr = (ctypes.c_void_p * n)(*[int(p) for p in peer_ptrs])
+    dev = kwargs["input"].device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_legendre_contract_peers(
+            ctypes.byref(d), arr, n, int(out_col_offset), ctypes.c_void_p(int(multicast_ptr) or None), _stream(dev)))
+
+
 def _contract_desc(*, kind, direction, input, output, w0, w1=None, batch, nlat, lmax, mmax, in_strides,
                    out_strides, out_cols, scale=1.0, flags=0, nlon=0, ksplit=0, w_strides=None, grouped=False,
                    m_offset=0, grouped8=False):

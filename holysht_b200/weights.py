@@ -96,22 +96,25 @@ def nodes_and_weights(nlat: int, grid: str):
     return np.flip(np.arccos(x)).copy(), np.asarray(w, np.float64)
 
 
-def _legendre_rows(n_m: int, n_l: int, x: np.ndarray, seed: float):
+def _legendre_rows(n_m: int, n_l: int, x: np.ndarray, seed: float, device=None):
     """Yield (l, row) with row[m, k] = P_l^m(x_k) (no Condon-Shortley phase,
     zero for m > l), for l = 0 .. n_l-1 and all m < n_m at once, as float64
-    torch tensors on the host (row is only valid until the next step).
+    torch tensors on ``device`` (default: the host; row is only valid until
+    the next step).
 
     The recurrence runs upwards in l for every order simultaneously, keeping
     only the two previous rows, so memory stays O(n_m * nlat); the row updates
     are multi-threaded torch operations."""
-    xt = torch.from_numpy(np.ascontiguousarray(x, np.float64))
+    dev = torch.device("cpu") if device is None else torch.device(device)
+    f64 = dict(dtype=torch.float64, device=dev)
+    xt = torch.from_numpy(np.ascontiguousarray(x, np.float64)).to(dev)
     sin_t = torch.sqrt((1.0 + xt) * (1.0 - xt))
     K = xt.numel()
-    mm = torch.arange(n_m, dtype=torch.float64)
-    sect = torch.full((K,), float(seed), dtype=torch.float64)  # P_l^l at the current l
-    prev2 = torch.zeros((n_m, K), dtype=torch.float64)
-    prev1 = torch.zeros((n_m, K), dtype=torch.float64)
-    row = torch.zeros((n_m, K), dtype=torch.float64)
+    mm = torch.arange(n_m, **f64)
+    sect = torch.full((K,), float(seed), **f64)  # P_l^l at the current l
+    prev2 = torch.zeros((n_m, K), **f64)
+    prev1 = torch.zeros((n_m, K), **f64)
+    row = torch.zeros((n_m, K), **f64)
     for l in range(n_l):
         if l > 0:
             sect = math.sqrt((2.0 * l + 1.0) / (2.0 * l)) * sin_t * sect
@@ -150,41 +153,47 @@ def _torch_dtype(dtype):
 
 def legendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
              inverse: bool = False, csphase: bool = True, kscale=None,
-             dtype=np.float64) -> np.ndarray:
+             dtype=np.float64, device=None):
     """[mmax, lmax, nlat] normalised associated Legendre functions, each
-    latitude optionally multiplied by ``kscale`` (the quadrature weights)."""
+    latitude optionally multiplied by ``kscale`` (the quadrature weights).
+    A numpy array, or a torch tensor on ``device`` when one is given."""
     x = np.cos(theta)
-    out = torch.zeros((mmax, lmax, x.size), dtype=_torch_dtype(dtype))
-    sign = torch.ones(mmax, dtype=torch.float64)
+    dev = torch.device("cpu") if device is None else torch.device(device)
+    out = torch.zeros((mmax, lmax, x.size), dtype=_torch_dtype(dtype), device=dev)
+    sign = torch.ones(mmax, dtype=torch.float64, device=dev)
     if csphase:
         sign[1::2] = -1.0
     ks = torch.ones(x.size, dtype=torch.float64) if kscale is None else torch.from_numpy(
         np.asarray(kscale, np.float64))
-    f = sign[:, None] * ks[None, :]
-    for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, inverse)):
+    f = sign[:, None] * ks.to(dev)[None, :]
+    for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, inverse), device):
         out[:, l, :] = row * f * _schmidt(norm, inverse, l)
-    return out.numpy()
+    return out if device is not None else out.numpy()
 
 
 def dlegendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
               inverse: bool = False, csphase: bool = True, kscale=None, lscale=None,
-              dtype=np.float64, sign1: float = 1.0) -> np.ndarray:
+              dtype=np.float64, sign1: float = 1.0, device=None):
     """[2, mmax, lmax, nlat]: dP/dtheta and m P / sin(theta), optionally
     multiplied by ``kscale[k]`` and ``lscale[l]``; the second table is also
-    multiplied by ``sign1``."""
+    multiplied by ``sign1``.  A numpy array, or a torch tensor on ``device``
+    when one is given."""
     x = np.cos(theta)
     K = x.size
-    out = torch.zeros((2, mmax, lmax, K), dtype=_torch_dtype(dtype))
-    m = torch.arange(mmax, dtype=torch.float64)
-    sign = torch.ones(mmax, dtype=torch.float64)
+    dev = torch.device("cpu") if device is None else torch.device(device)
+    f64 = dict(dtype=torch.float64, device=dev)
+    out = torch.zeros((2, mmax, lmax, K), dtype=_torch_dtype(dtype), device=dev)
+    m = torch.arange(mmax, **f64)
+    sign = torch.ones(mmax, **f64)
     if csphase:
         sign[1::2] = -1.0
-    ks = torch.ones(K, dtype=torch.float64) if kscale is None else torch.from_numpy(np.asarray(kscale, np.float64))
-    rows = _legendre_rows(mmax + 1, lmax + 1, x, _norm_seed(norm, inverse))
+    ks = (torch.ones(K, dtype=torch.float64) if kscale is None
+          else torch.from_numpy(np.asarray(kscale, np.float64))).to(dev)
+    rows = _legendre_rows(mmax + 1, lmax + 1, x, _norm_seed(norm, inverse), device)
     _, first = next(rows)
     cur = first.clone()
-    d0 = torch.empty((mmax, K), dtype=torch.float64)
-    d1 = torch.empty((mmax, K), dtype=torch.float64)
+    d0 = torch.empty((mmax, K), **f64)
+    d1 = torch.empty((mmax, K), **f64)
     for l in range(lmax):
         _, nxt = next(rows)
         cs = _schmidt(norm, inverse, l)
@@ -209,7 +218,7 @@ def dlegendre(mmax: int, lmax: int, theta: np.ndarray, norm: str = "ortho",
         out[0, :, l, :] = d0 * f
         out[1, :, l, :] = d1 * f * sign1
         cur.copy_(nxt)
-    return out.numpy()
+    return out if device is not None else out.numpy()
 
 
 def _try_torch_harmonics():
@@ -222,6 +231,13 @@ def _try_torch_harmonics():
         return None
 
 
+def _from_th(t, dtype, device):
+    """A torch-harmonics table as numpy (``device`` None) or a tensor on ``device``."""
+    if device is None:
+        return t.double().numpy().astype(dtype)
+    return t.to(device=device, dtype=_torch_dtype(dtype))
+
+
 def _resolve(nlat, nlon, lmax, mmax, grid, norm):
     _check(grid, norm)
     lmax = lmax or default_lmax(nlat, grid)
@@ -230,55 +246,56 @@ def _resolve(nlat, nlon, lmax, mmax, grid, norm):
 
 
 def scalar_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64, restated=False):
+                   dtype=np.float64, restated=False, device=None):
     """RealSHT ``weights`` [mmax, lmax, nlat] (float64) and (lmax, mmax)."""
     th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.RealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
-        return ref.weights.double().numpy().astype(dtype), ref.lmax, ref.mmax
+        return _from_th(ref.weights, dtype, device), ref.lmax, ref.mmax
     lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
     theta, w = nodes_and_weights(nlat, grid)
-    return legendre(mmax, lmax, theta, norm, False, csphase, kscale=w, dtype=dtype), lmax, mmax
+    return legendre(mmax, lmax, theta, norm, False, csphase, kscale=w, dtype=dtype, device=device), lmax, mmax
 
 
 def scalar_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64, restated=False):
+                   dtype=np.float64, restated=False, device=None):
     """InverseRealSHT ``pct`` [mmax, lmax, nlat]."""
     th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.InverseRealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
-        return ref.pct.double().numpy().astype(dtype), ref.lmax, ref.mmax
+        return _from_th(ref.pct, dtype, device), ref.lmax, ref.mmax
     lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
     theta, _ = nodes_and_weights(nlat, grid)
-    return legendre(mmax, lmax, theta, norm, True, csphase, dtype=dtype), lmax, mmax
+    return legendre(mmax, lmax, theta, norm, True, csphase, dtype=dtype, device=device), lmax, mmax
 
 
 def vector_forward(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64, restated=False):
+                   dtype=np.float64, restated=False, device=None):
     """RealVectorSHT ``weights`` [2, mmax, lmax, nlat]."""
     th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.RealVectorSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
-        return ref.weights.double().numpy().astype(dtype), ref.lmax, ref.mmax
+        return _from_th(ref.weights, dtype, device), ref.lmax, ref.mmax
     lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
     theta, w = nodes_and_weights(nlat, grid)
     ll = np.arange(lmax, dtype=np.float64)
     lscale = np.ones(lmax)
     lscale[1:] = 1.0 / (ll[1:] * (ll[1:] + 1.0))
-    d = dlegendre(mmax, lmax, theta, norm, False, csphase, kscale=w, lscale=lscale, dtype=dtype, sign1=-1.0)
+    d = dlegendre(mmax, lmax, theta, norm, False, csphase, kscale=w, lscale=lscale, dtype=dtype, sign1=-1.0,
+                  device=device)
     return d, lmax, mmax
 
 
 def vector_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
-                   dtype=np.float64, restated=False):
+                   dtype=np.float64, restated=False, device=None):
     """InverseRealVectorSHT ``dpct`` [2, mmax, lmax, nlat]."""
     th = None if restated else _try_torch_harmonics()
     if th is not None:
         ref = th.InverseRealVectorSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=csphase)
-        return ref.dpct.double().numpy().astype(dtype), ref.lmax, ref.mmax
+        return _from_th(ref.dpct, dtype, device), ref.lmax, ref.mmax
     lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
     theta, _ = nodes_and_weights(nlat, grid)
-    return dlegendre(mmax, lmax, theta, norm, True, csphase, dtype=dtype), lmax, mmax
+    return dlegendre(mmax, lmax, theta, norm, True, csphase, dtype=dtype, device=device), lmax, mmax
 
 
 SEGMENT = 16  # degrees between recurrence checkpoints (matches the kernel)

@@ -194,6 +194,37 @@ typedef struct holysht_contract_desc {
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
+/* The same contraction (HOLYSHT_TABLE_GROUPED8 layout only) with its output
+ * stored on several GPUs at once: no counterpart in the reference, which has
+ * no multi-GPU code; it is the fused "contract + all-gather" step of the
+ * order-partitioned transform.  Every output element (b, c, row, m) is stored
+ * at column out_col_offset + m of each of the n_peers (1..8) buffers in
+ * peer_out (device pointers valid in the calling context: this GPU's own
+ * buffer and the peers' buffers mapped into it, all with desc's output
+ * strides), by plain stores over NVLink; when multicast_out is not null it is
+ * the NVLink multicast address of those buffers and each element is stored
+ * once through it (multimem.st), the switch delivering it to every GPU.
+ * desc->out is ignored.  The call only launches: the caller orders the
+ * stores with every peer (for example a cross-GPU barrier on the same stream)
+ * before any GPU reads its buffer. */
+/* Cross-GPU barrier on `stream` for the ranks that share the stores of
+ * holysht_legendre_contract_peers (no counterpart in the reference).
+ * signal[q] is rank q's array of n_ranks (1..8) 32-bit words as mapped on this
+ * GPU (zero-initialised once; epochs start at 1 and increase by one per
+ * barrier).  Each rank stores `epoch` into word `rank` of every array with
+ * system-scope release semantics (ordering its earlier stores, the peer
+ * stores of the contraction included) and waits with acquire semantics until
+ * every word of its own array has reached `epoch`.  The wait is bounded: a
+ * peer that does not arrive sets bit 0 of the word holysht_peer_error_word
+ * reads, and the kernel returns instead of hanging. */
+int holysht_peer_barrier(void* const* signal, int n_ranks, int rank, unsigned epoch, void* stream);
+
+/* Reads and clears the peer barrier's device error word (synchronous). */
+int holysht_peer_error_word(unsigned* value);
+
+int holysht_legendre_contract_peers(const holysht_contract_desc* desc, void* const* peer_out, int n_peers,
+                                    int64_t out_col_offset, void* multicast_out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Dense tensor-core contraction (no counterpart operator in the reference; the
  * reference's TF32 wmma forward, cuda/fused_legendre.cu:635-714, is its

@@ -70,6 +70,38 @@ def _gloo_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
+def _gloo_width_worker(rank, world, port, result):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ranges = [(0, 32), (32, 45)]
+        a, b = ranges[rank]
+        slab = torch.full((1, 1, 3, 32), complex(5.0, 5.0), dtype=torch.complex64)
+        slab[..., : b - a] = complex(rank + 1, 0)
+        got = hd.gather_order_slabs(slab, ranges, out_width=50)
+        ok = got.shape == (1, 1, 3, 50) and bool((got[..., :32] == 1).all()) and bool((got[..., 32:45] == 2).all())
+        result[rank] = ok and bool((got[..., 45:] == 0).all())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_order_slabs_pads_zero_columns_gloo():
+    """The inverse direction gathers into the irfft width: columns past the
+    last order range are zero on every rank."""
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    result = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_width_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert dict(result) == {0: True, 1: True}
+
+
 def test_gather_order_slabs_gloo_two_ranks():
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
@@ -123,6 +155,23 @@ def test_order_sharded_modules_single_rank():
     x = torch.randn(2, 2, 64, 128, device=dev)
     _close(hd.OrderShardedRealVectorSHT(64, 128).to(dev)(x), hs.RealVectorSHT(64, 128).to(dev)(x))
     _close(hd.OrderShardedRealSHT(64, 128).to(dev)(x[:, 0]), hs.RealSHT(64, 128).to(dev)(x[:, 0]))
+    c = hs.RealVectorSHT(64, 128).to(dev)(x)
+    _close(hd.OrderShardedInverseRealVectorSHT(64, 128, table_device=dev)(c),
+           hs.InverseRealVectorSHT(64, 128).to(dev)(c))
+    _close(hd.OrderShardedInverseRealSHT(64, 128, table_device=dev)(c[:, 0]),
+           hs.InverseRealSHT(64, 128).to(dev)(c[:, 0]))
+    # gradients through the sharded forward equal the module's
+    for sharded, single, inp in ((hd.OrderShardedRealVectorSHT(64, 128, table_device=dev), hs.RealVectorSHT(64, 128),
+                                  x),
+                                 (hd.OrderShardedInverseRealSHT(64, 128, table_device=dev), hs.InverseRealSHT(64, 128),
+                                  c[:, 0])):
+        got = []
+        for mod in (sharded, single.to(dev)):
+            t = inp.clone().requires_grad_(True)
+            y = mod(t)
+            (y.abs().square().sum() if y.is_complex() else y.square().sum()).backward()
+            got.append(t.grad)
+        _close(got[0], got[1])
 
 
 def _nccl_worker(rank, world, port, result):
@@ -133,31 +182,86 @@ def _nccl_worker(rank, world, port, result):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    out = {}
     try:
+        nlat, nlon = 128, 256
         g = torch.Generator(device=dev).manual_seed(5)
-        x = torch.randn(2, 2, 128, 256, device=dev, generator=g)
-        got = hd.OrderShardedRealVectorSHT(128, 256).to(dev)(x)
-        ref = hs.RealVectorSHT(128, 256).to(dev)(x)
-        err = float((got - ref).abs().max()) / float(ref.abs().max())
-        result[rank] = err < 1e-5
+        x = torch.randn(3, 2, nlat, nlon, device=dev, generator=g)
+        c = torch.randn(3, 2, nlat, nlon // 2 + 1, device=dev, dtype=torch.complex64, generator=g)
+        tri = torch.arange(nlon // 2 + 1, device=dev)[None, :] <= torch.arange(nlat, device=dev)[:, None]
+        c = c * tri
+        ref_v = hs.RealVectorSHT(nlat, nlon).to(dev)
+        ref_s = hs.RealSHT(nlat, nlon).to(dev)
+        ref_iv = hs.InverseRealVectorSHT(nlat, nlon).to(dev)
+        ref_is = hs.InverseRealSHT(nlat, nlon).to(dev)
+
+        def rel(a, b):
+            return float((a - b).abs().max()) / float(b.abs().max())
+
+        def grads(mod, inp):
+            t = inp.clone().requires_grad_(True)
+            y = mod(t)
+            w = torch.linspace(0.5, 1.5, y.numel(), device=dev).reshape(y.shape)
+            (y.abs().square() * w).sum().backward() if y.is_complex() else (y.square() * w).sum().backward()
+            return y.detach(), t.grad
+
+        for comm in ("nccl", "peer", "auto"):
+            kw = dict(comm=comm, table_device=dev)
+            v = hd.OrderShardedRealVectorSHT(nlat, nlon, **kw).to(dev)
+            s = hd.OrderShardedRealSHT(nlat, nlon, **kw).to(dev)
+            iv = hd.OrderShardedInverseRealVectorSHT(nlat, nlon, **kw).to(dev)
+            is_ = hd.OrderShardedInverseRealSHT(nlat, nlon, **kw).to(dev)
+            errs = []
+            for _ in range(3):  # several calls: the exchange buffers alternate
+                errs.append(rel(v(x), ref_v(x)))
+                errs.append(rel(s(x[:, 0]), ref_s(x[:, 0])))
+                errs.append(rel(iv(c), ref_iv(c)))
+                errs.append(rel(is_(c[:, 0]), ref_is(c[:, 0])))
+            for sharded, single, inp in ((v, ref_v, x), (s, ref_s, x[:, 0]), (iv, ref_iv, c), (is_, ref_is, c[:, 0])):
+                ys, gs = grads(sharded, inp)
+                yr, gr = grads(single, inp)
+                errs += [rel(ys, yr), rel(gs, gr)]
+            torch.cuda.synchronize(dev)
+            out[comm] = (v.comm, max(errs), hd.peer_error_word())
+        result[rank] = out
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.gpu
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_order_sharded_vector_two_gpus_nccl():
+def _run_nccl(world):
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     result = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, result)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, result)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=300)
+        p.join(timeout=600)
         assert p.exitcode == 0
-    assert dict(result) == {0: True, 1: True}
+    res = dict(result)
+    assert sorted(res) == list(range(world))
+    for rank, per in res.items():
+        for comm, (used, err, perr) in per.items():
+            assert err < 1e-5, (rank, comm, used, err)
+            assert perr == 0, (rank, comm, used)
+        assert per["nccl"][0] == "nccl" and per["peer"][0] == "peer"
+    return res
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_order_sharded_transforms_two_gpus():
+    """Forward and inverse, scalar and vector, values and gradients, with each
+    exchange (NCCL all-gather, peer stores, and the automatic choice, which is
+    the multicast store where NVSwitch offers it) against the single-GPU modules."""
+    _run_nccl(2)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_order_sharded_transforms_four_gpus():
+    _run_nccl(4)
 
 
 def _faulty_gloo_worker(rank, world, port, result):

@@ -221,3 +221,18 @@ def test_c5_vector_full_size():
     assert out[3][:, upper].abs().max().item() == 0.0
     del out, x
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("builder", ["scalar_forward", "scalar_inverse", "vector_forward", "vector_inverse"])
+def test_tables_built_on_the_gpu_match_the_host(builder):
+    """The float64 table recurrence run on the GPU (used to build large sharded
+    tables quickly) gives the host's tables."""
+    from holysht_b200 import weights as W
+
+    fn = getattr(W, builder)
+    for grid in ("equiangular", "legendre-gauss"):
+        host, L, M = fn(48, 96, grid=grid, restated=True)
+        dev, L2, M2 = fn(48, 96, grid=grid, restated=True, device=DEV)
+        assert (L, M) == (L2, M2) and dev.device.type == "cuda"
+        d = dev.cpu().numpy()
+        assert np.max(np.abs(d - host)) <= 1e-13 * np.max(np.abs(host))
