@@ -43,6 +43,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-c5", action="store_true", help="skip the 1024x2048 secondary measurements")
     return ap.parse_args()
 
 
@@ -160,7 +161,7 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    vsht = hs.RealVectorSHT(NLAT, NLON).to(dev)
+    vsht = hs.RealVectorSHT(NLAT, NLON, table_device=dev)
     L, M = vsht.lmax, vsht.mmax
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     x = torch.randn((BATCH, 2, NLAT, NLON), generator=gen, device=dev)
@@ -232,7 +233,7 @@ def run_ours(args, rank, world, local_rank):
     clocks.stop()
 
     # ---- secondary: RealSHT.forward on the same grid ----
-    ssht = hs.RealSHT(NLAT, NLON).to(dev)
+    ssht = hs.RealSHT(NLAT, NLON, table_device=dev)
     xs = torch.randn((BATCH, NLAT, NLON), generator=gen, device=dev)
     for _ in range(3):
         ssht(xs)
@@ -276,7 +277,7 @@ def run_ours(args, rank, world, local_rank):
     vrec_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(vs_, ve)))
     del vrsht
     # the inverse direction (InverseRealVectorSHT.forward, irfft included) on the same grid
-    isht = hs.InverseRealVectorSHT(NLAT, NLON).to(dev)
+    isht = hs.InverseRealVectorSHT(NLAT, NLON, table_device=dev)
     coef = vsht(x)
     for _ in range(3):
         isht(coef)
@@ -290,6 +291,9 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     inv_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(is_, ie)))
     del isht, coef
+
+    # ---- the 1024 x 2048 configuration on all ranks (both partitions) ----
+    c5 = run_c5(rank, world, dev, barrier, max_over_ranks) if not args.skip_c5 else {}
 
     # ---- end to end through the public API with host buffers ----
     xh = torch.empty((BATCH, 2, NLAT, NLON), dtype=torch.float32).pin_memory()
@@ -311,7 +315,28 @@ def run_ours(args, rank, world, local_rank):
         oh.copy_(vsht(xd), non_blocking=True)
         ee[i].record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(es, ee)))
+    e2e_seq_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(es, ee)))
+    # the same K transforms through holysht_b200.pipeline.HostStream: upload of
+    # batch i+1 and download of batch i-1 overlap the transform of batch i
+    from holysht_b200.pipeline import HostStream
+
+    ring = 4
+    hin = [torch.empty_like(xh).pin_memory() for _ in range(ring)]
+    for i, h in enumerate(hin):
+        h.copy_(torch.randn((BATCH, 2, NLAT, NLON), generator=gen, device=dev).cpu())
+    hout = [torch.empty_like(oh).pin_memory() for _ in range(K)]
+    inputs = [hin[i % ring] for i in range(K)]
+    pipe = HostStream(vsht, dev)
+    pipe.run(inputs[:3], hout[:3])
+    barrier()
+    ps, pe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    ps.record(stream)
+    pipe.run(inputs, hout)
+    pe.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(ps.elapsed_time(pe) / K)
+    e2e_ok = bool(torch.allclose(hout[K - 1], vsht(hin[(K - 1) % ring].to(dev)).cpu()))
     h2d = xh.numel() * 4
     d2h = oh.numel() * 8
 
@@ -348,8 +373,11 @@ def run_ours(args, rank, world, local_rank):
         "secondary": {"RealSHT.forward_ms": round(scalar_ms, 5),
                       "RealSHT.forward_recurrence_variant_ms": round(rec_ms, 5),
                       "RealVectorSHT.forward_recurrence_variant_ms": round(vrec_ms, 5),
-                      "InverseRealVectorSHT.forward_ms": round(inv_ms, 5)},
-        "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                      "InverseRealVectorSHT.forward_ms": round(inv_ms, 5), **c5},
+        "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "how": (f"{K} steps through holysht_b200.pipeline.HostStream (pinned host in/out; upload, transform "
+                        "and download of consecutive steps overlap on three streams), total / K"),
+                "matches_device_result": e2e_ok, "sequential_ms": round(e2e_seq_ms, 5)},
         "gpu_launches": launches_per_step * K,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
@@ -432,6 +460,73 @@ def cpu_baseline(vsht, x):
             else _blas_threads(), "kind": kind,
             "sample": f"full workload (4,2,512,1024), median of {n} runs; {what}",
             "rel_l2_vs_oracle": rel}
+
+
+def _timed(fn, steps, dev, barrier, max_over_ranks, warmup=2):
+    """Mean CUDA-event ms of ``fn`` over ``steps`` calls (after ``warmup``),
+    bracketed by barriers; the max over ranks."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    return max_over_ranks(s.elapsed_time(e) / steps)
+
+
+def run_c5(rank, world, dev, barrier, max_over_ranks):
+    """The 1024 x 2048 configuration (lmax 1024, mmax 1025) on ``world`` GPUs,
+    both partitions of the north star:
+
+    * RealSHT on (16, 64, 1024, 2048): batch x channel partition, 1024/world
+      slices per rank, each with a full table replica, no collective (the
+      tcgen05 dense path);
+    * RealVectorSHT on (16, 2, 1024, 2048): order partition (each rank holds
+      1/world of the tables), the input replicated, the coefficients exchanged
+      by the fused multicast/peer store + barrier, and by the NCCL all-gather
+      for comparison.
+
+    Inputs are larger than L2 (no flush needed).  Returns secondary fields."""
+    import torch
+
+    import holysht_b200 as hs
+    from holysht_b200 import distributed as hd
+
+    nlat, nlon = 1024, 2048
+    res = {}
+    # -- scalar, batch x channel partition
+    sl = hd.shard_batch(16 * 64, rank, world)
+    n = sl.stop - sl.start
+    m = hs.RealSHT(nlat, nlon, table_device=dev)
+    gen = torch.Generator(device=dev).manual_seed(4 + rank)
+    x = torch.randn((n, nlat, nlon), generator=gen, device=dev)
+    with torch.no_grad():
+        ms = _timed(lambda: m(x), 3, dev, barrier, max_over_ranks)
+    res["C5_RealSHT_batch_split"] = {"ms": round(ms, 4), "slices_per_rank": n,
+                                     "transforms_per_s": round(16 * 64 / (ms * 1e-3), 1),
+                                     "path": "tcgen05 dense" if n >= 128 else "streaming"}
+    del m, x
+    torch.cuda.empty_cache()
+    # -- vector, order partition (replicated input: the same seed on every rank)
+    gen = torch.Generator(device=dev).manual_seed(4)
+    xv = torch.randn((16, 2, nlat, nlon), generator=gen, device=dev)
+    for comm in (("auto", "nccl") if world > 1 else ("auto",)):
+        v = hd.OrderShardedRealVectorSHT(nlat, nlon, comm=comm, table_device=dev, return_buffer=True)
+        with torch.no_grad():
+            ms = _timed(lambda: v(xv), 5, dev, barrier, max_over_ranks)
+        key = "C5_RealVectorSHT_order_split" + ("" if comm == "auto" else "_nccl")
+        res[key] = {"ms": round(ms, 4), "comm": v.comm, "orders": list(v.ranges[rank]),
+                    "transforms_per_s": round(16 / (ms * 1e-3), 1)}
+        del v
+        torch.cuda.empty_cache()
+    return res
 
 
 def reference_cuda_bar():

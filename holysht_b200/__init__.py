@@ -663,24 +663,28 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
     with the FP32 table in FP32 (the reference's BF16 path, ``__init__.py:1289-1337``).
     ``variant="recurrence"`` (an addition) computes the Legendre functions on the
     fly in the forward pass instead of streaming the table (the backward pass
-    uses the table).
+    uses the table).  ``table_device`` (an addition, every module) runs the
+    float64 table recurrence on that device and keeps the tables there (a GPU
+    builds the 1024 x 2048 tables in about a second; default: the host, as the
+    reference does through torch-harmonics).
     """
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
                  grid: str = "equiangular", norm: str = "ortho", csphase: bool = True,
-                 dtype: str = "fp32", variant: str = "table"):
+                 dtype: str = "fp32", variant: str = "table", table_device=None):
         super().__init__()
         if variant not in ("table", "recurrence"):
             raise ValueError(f"variant must be 'table' or 'recurrence', got {variant!r}")
         self.variant = variant
         w_dtype = _w_dtype(dtype)
-        w, L, M = _weights.scalar_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        w, L, M = _weights.scalar_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32,
+                                          device=table_device)
         _check_mmax(M, nlon)
         self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
         self.grid, self.norm, self.csphase = grid, norm, csphase
         self._use_bf16 = dtype == "bf16"
         self._use_fp16 = dtype == "fp16"
-        wt = torch.from_numpy(w)
+        wt = torch.from_numpy(w) if table_device is None else w
         self.register_buffer("weights", wt.to(w_dtype))
         self.register_buffer("weight_t", wt.permute(1, 2, 0).contiguous())
         self._mlk_name = "weights"
@@ -702,13 +706,14 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``InverseRealSHT``: [..., lmax, mmax] complex -> [..., nlat, nlon] real."""
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
-                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True):
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True, table_device=None):
         super().__init__()
-        p, L, M = _weights.scalar_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        p, L, M = _weights.scalar_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32,
+                                          device=table_device)
         _check_mmax(M, nlon)
         self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
         self.grid, self.norm, self.csphase = grid, norm, csphase
-        pt = torch.from_numpy(p)
+        pt = torch.from_numpy(p) if table_device is None else p
         self.register_buffer("pct", pt)
         self.register_buffer("pct_t", pt.permute(1, 2, 0).contiguous())
         self._mlk_name = "pct"
@@ -737,19 +742,20 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
                  grid: str = "equiangular", norm: str = "ortho", csphase: bool = True,
-                 dtype: str = "fp32", variant: str = "table"):
+                 dtype: str = "fp32", variant: str = "table", table_device=None):
         super().__init__()
         if variant not in ("table", "recurrence"):
             raise ValueError(f"variant must be 'table' or 'recurrence', got {variant!r}")
         self.variant = variant
         w_dtype = _w_dtype(dtype)
-        w, L, M = _weights.vector_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        w, L, M = _weights.vector_forward(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32,
+                                          device=table_device)
         _check_mmax(M, nlon)
         self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
         self.grid, self.norm, self.csphase = grid, norm, csphase
         self._use_bf16 = dtype == "bf16"
         self._use_fp16 = dtype == "fp16"
-        wt = torch.from_numpy(w)
+        wt = torch.from_numpy(w) if table_device is None else w
         self.register_buffer("w0", wt[0].to(w_dtype))
         self.register_buffer("w1", wt[1].to(w_dtype))
         self.register_buffer("w0_t", wt[0].permute(1, 2, 0).contiguous())
@@ -773,13 +779,14 @@ class InverseRealVectorSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``InverseRealVectorSHT``: [..., 2, lmax, mmax] -> [..., 2, nlat, nlon]."""
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
-                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True):
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True, table_device=None):
         super().__init__()
-        d, L, M = _weights.vector_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32)
+        d, L, M = _weights.vector_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32,
+                                          device=table_device)
         _check_mmax(M, nlon)
         self.nlat, self.nlon, self.lmax, self.mmax = nlat, nlon, L, M
         self.grid, self.norm, self.csphase = grid, norm, csphase
-        dt = torch.from_numpy(d)
+        dt = torch.from_numpy(d) if table_device is None else d
         self.register_buffer("d0", dt[0].contiguous())
         self.register_buffer("d1", dt[1].contiguous())
         self.register_buffer("d0_t", dt[0].permute(1, 2, 0).contiguous())

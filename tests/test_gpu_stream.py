@@ -345,3 +345,21 @@ def test_empty_batches_are_no_ops():
     assert y.shape == (0, 2, 16, 32)
     torch.cuda.synchronize()
     assert ops.stream_error_word() == 0
+
+
+def test_host_stream_pipeline_matches_module_calls():
+    """holysht_b200.pipeline.HostStream: pinned host batches in, pinned host
+    results out, copies overlapped with the transforms; every result equals the
+    module's own output for that batch."""
+    import holysht_b200 as hs
+    from holysht_b200.pipeline import HostStream
+
+    dev = torch.device("cuda")
+    m = hs.RealVectorSHT(64, 128).to(dev)
+    ins = [torch.randn(3, 2, 64, 128).pin_memory() for _ in range(5)]
+    outs = [torch.empty(3, 2, 64, 65, dtype=torch.complex64).pin_memory() for _ in range(5)]
+    HostStream(m, dev).run(ins, outs)
+    for i, o in zip(ins, outs):
+        torch.testing.assert_close(o, m(i.to(dev)).cpu(), rtol=0, atol=0)
+    with pytest.raises(ValueError, match="pinned"):
+        HostStream(m, dev).run([torch.randn(3, 2, 64, 128)], [outs[0]])
