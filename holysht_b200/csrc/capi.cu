@@ -77,6 +77,13 @@ int env_stall_chunk() {
   return v;
 }
 
+// Integer environment variable (read on every call: experiment switches that
+// a process may flip between launches).
+int env_int(const char* name, int dflt) {
+  const char* s = std::getenv(name);
+  return (s && *s) ? std::atoi(s) : dflt;
+}
+
 int env_ksplit() {
   static int v = [] {
     const char* s = std::getenv("HOLYSHT_KSPLIT");
@@ -748,9 +755,8 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
   if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
   if (B == 0 || L == 0 || M == 0) return ok();
   if (!out || !spec || !seeds || !coef || !cos_theta) return fail(HOLYSHT_ERR_INVALID, "null pointer");
-  if (K > (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt)
-    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d",
-                hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt);
+  if (K > (long long)hsb::rec::kMaxWarps * 32 * 16)
+    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d", hsb::rec::kMaxWarps * 32 * 16);
   if (!fits_int(B) || !fits_int(L) || !fits_int(M) || (B + 3) / 4 > 65535)
     return fail(HOLYSHT_ERR_INVALID, "extent out of range");
   if (spec_row_stride < M || spec_batch_stride < K * spec_row_stride)
@@ -769,10 +775,19 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
   p.M = (int)M;
   p.nseg = (int)((L + hsb::rec::kSeg - 1) / hsb::rec::kSeg);
   p.scale = scale;
-  const int threads = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
+  // latitudes per thread: 16 (8 for small grids, so a warp still covers them)
+  const int kpt = (K <= 256 || env_int("HSB_REC_KPT8", 0)) ? 8 : 16;
+  const int threads = (int)(((K + kpt - 1) / kpt + 31) / 32 * 32);
   const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
   dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
-  hsb::rec::recurrence_forward_kernel<<<grid, threads < 32 ? 32 : threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  if (env_int("HSB_REC_LEGACY", 0)) {
+    const int t4 = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
+    hsb::rec::recurrence_forward_kernel<<<grid, t4 < 32 ? 32 : t4, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  } else if (kpt == 8) {
+    hsb::rec::recurrence_forward_pair_kernel<8><<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  } else {
+    hsb::rec::recurrence_forward_pair_kernel<16><<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  }
   return check_launch("recurrence forward kernel");
 }
 

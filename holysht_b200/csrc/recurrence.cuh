@@ -174,6 +174,153 @@ __global__ void __launch_bounds__(kMaxWarps * 32) recurrence_forward_kernel(cons
 }
 
 // ---------------------------------------------------------------------------
+// Paired-latitude scalar kernel (the one the library launches).  Same maths
+// and checkpoints as recurrence_forward_kernel, organised for the FP32 pipe:
+//   * each thread holds KPT latitudes as KPT/2 pairs; the recurrence and the
+//     contraction run on packed f32x2 operations whose two halves are the two
+//     latitudes of a pair (fma.rn.f32x2 with no operand duplication: the
+//     pair of Legendre values multiplies a pair of spectrum values directly);
+//   * KPT = 16 latitudes per thread (one warp per 512 latitudes), so the
+//     per-degree warp reduction (a transpose-reduce every 4 degrees) is
+//     amortised over 4x the multiply-adds of the 4-latitude kernel;
+//   * the CTA's recurrence coefficients (a, -b) sit in shared memory.
+template <int KPT>
+__global__ void __launch_bounds__(kMaxWarps * 32) recurrence_forward_pair_kernel(const RecParams p) {
+  constexpr int NP = KPT / 2;
+  __shared__ float red[kMaxWarps][32];
+  __shared__ float2 cab[kSegPerCta * kSeg];
+  const int m = blockIdx.x;
+  const int b0 = blockIdx.z * kNB;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int lm = p.L - m;
+  const int nseg = lm > 0 ? (lm + kSeg - 1) / kSeg : 0;
+  const int c_begin = blockIdx.y * kSegPerCta;
+
+  if (blockIdx.y == 0) {
+    const int zrows = lm > 0 ? m : p.L;
+    for (int e = tid; e < zrows * kNB; e += blockDim.x) {
+      const int l = e / kNB, b = b0 + e % kNB;
+      if (b < p.B) p.out[((long long)b * p.L + l) * p.M + m] = make_float2(0.f, 0.f);
+    }
+  }
+  if (c_begin >= nseg) return;  // uniform per CTA
+  const int c_end = min(nseg, c_begin + kSegPerCta);
+  const int l_first = m + c_begin * kSeg;
+  const int ndeg = min(p.L, m + c_end * kSeg) - l_first;
+  for (int e = tid; e < kSegPerCta * kSeg; e += blockDim.x) {
+    float2 ab = make_float2(0.f, 0.f);
+    if (e < ndeg) {
+      const float* c2 = p.coef + ((long long)m * p.L + l_first + e) * 2;
+      ab = make_float2(c2[0], -c2[1]);
+    }
+    cab[e] = ab;
+  }
+
+  const int k0 = tid * KPT;
+  float2 xp[NP];
+  float2 Xr[NP][kNB], Xi[NP][kNB];  // (latitude 2i, 2i+1) pairs of the scaled spectrum
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int k = k0 + 2 * i;
+    xp[i] = make_float2(k < p.K ? p.x[k] : 0.f, k + 1 < p.K ? p.x[k + 1] : 0.f);
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+      if (b0 + b < p.B) {
+        const float2* row = p.spec + (long long)(b0 + b) * p.sbs + m;
+        if (k < p.K) s0 = row[(long long)k * p.srs];
+        if (k + 1 < p.K) s1 = row[(long long)(k + 1) * p.srs];
+      }
+      Xr[i][b] = make_float2(s0.x * p.scale, s1.x * p.scale);
+      Xi[i][b] = make_float2(s0.y * p.scale, s1.y * p.scale);
+    }
+  }
+  __syncthreads();  // coefficients staged
+
+  for (int c = c_begin; c < c_end; ++c) {
+    const int lseg = m + c * kSeg;
+    const float* sd = p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 2;
+    float2 p1[NP], p2[NP];  // P at degrees l-1 and l-2 of each latitude pair
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      // (P at lseg, P at lseg + 1) of latitudes 2i and 2i+1: 8-byte aligned pairs
+      // (a 16-byte load would be misaligned for odd nlat)
+      const float2* sd2 = reinterpret_cast<const float2*>(sd);
+      const float2 a = k0 + 2 * i < p.K ? sd2[2 * i] : make_float2(0.f, 0.f);
+      const float2 bq = k0 + 2 * i + 1 < p.K ? sd2[2 * i + 1] : make_float2(0.f, 0.f);
+      p2[i] = make_float2(a.x, bq.x);  // degree lseg
+      p1[i] = make_float2(a.y, bq.y);  // degree lseg + 1
+    }
+#pragma unroll
+    for (int qb = 0; qb < kSeg; qb += 4) {
+      float v[32];  // 4 degrees x (4 batches x re/im)
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int q = qb + q4;
+        float2 pl[NP];
+        if (q == 0) {
+#pragma unroll
+          for (int i = 0; i < NP; ++i) pl[i] = p2[i];
+        } else if (q == 1) {
+#pragma unroll
+          for (int i = 0; i < NP; ++i) pl[i] = p1[i];
+        } else {
+          const float2 ab = cab[lseg + q - l_first];
+          const float2 a2 = make_float2(ab.x, ab.x), nb2 = make_float2(ab.y, ab.y);
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            pl[i] = __ffma2_rn(a2, __fmul2_rn(xp[i], p1[i]), __fmul2_rn(nb2, p2[i]));
+            p2[i] = p1[i];
+            p1[i] = pl[i];
+          }
+        }
+        float2 ar[kNB], ai[kNB];
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) ar[b] = ai[b] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < NP; ++i)
+#pragma unroll
+          for (int b = 0; b < kNB; ++b) {
+            ar[b] = __ffma2_rn(pl[i], Xr[i][b], ar[b]);
+            ai[b] = __ffma2_rn(pl[i], Xi[i][b], ai[b]);
+          }
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) {
+          v[q4 * 8 + 2 * b] = ar[b].x + ar[b].y;
+          v[q4 * 8 + 2 * b + 1] = ai[b].x + ai[b].y;
+        }
+      }
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < d; ++i) {
+          const float send = upper ? v[i] : v[i + d];
+          const float keep = upper ? v[i + d] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+      float sum = v[0];
+      if (nwarps > 1) {
+        red[warp][lane] = sum;
+        __syncthreads();
+        sum = 0.f;
+        if (warp == 0)
+          for (int w = 0; w < nwarps; ++w) sum += red[w][lane];
+      }
+      if (warp == 0) {
+        const int q4 = lane >> 3, b = (lane >> 1) & 3, ri = lane & 1;
+        const int l = lseg + qb + q4;
+        if (l < p.L && b0 + b < p.B)
+          reinterpret_cast<float*>(p.out)[(((long long)(b0 + b) * p.L + l) * p.M + m) * 2 + ri] = sum;
+      }
+      if (nwarps > 1) __syncthreads();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Vector forward with on-the-fly tables.  The vector tables of order m are
 // ladder combinations of the Legendre functions of orders m - 1 and m + 1:
 //   W0[l, k] = alpha_l Q^{m-1}_l + beta_l Q^{m+1}_l

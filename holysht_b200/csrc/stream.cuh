@@ -85,9 +85,20 @@ constexpr int kMaxChunk = HSB_STREAM_CHUNK_V > HSB_STREAM_CHUNK_S ? HSB_STREAM_C
 #ifndef HSB_STREAM_SPEC_AHEAD
 #define HSB_STREAM_SPEC_AHEAD 3
 #endif
-constexpr int kSpecStages = HSB_STREAM_SPEC_STAGES;  // spectrum ring depth
-constexpr int kSpecAhead = HSB_STREAM_SPEC_AHEAD;    // chunks staged ahead of the one being read
-static_assert(kSpecStages >= kSpecAhead + 1 && kSpecAhead >= 1, "spectrum ring too shallow");
+#ifndef HSB_STREAM_SPEC_STAGES_V
+#define HSB_STREAM_SPEC_STAGES_V HSB_STREAM_SPEC_STAGES
+#endif
+#ifndef HSB_STREAM_SPEC_AHEAD_V
+#define HSB_STREAM_SPEC_AHEAD_V HSB_STREAM_SPEC_AHEAD
+#endif
+// spectrum ring depth and chunks staged ahead of the one being read, per kind
+template <int KIND>
+struct SpecRing {
+  static constexpr int kStages = KIND == 1 ? HSB_STREAM_SPEC_STAGES_V : HSB_STREAM_SPEC_STAGES;
+  static constexpr int kAhead = KIND == 1 ? HSB_STREAM_SPEC_AHEAD_V : HSB_STREAM_SPEC_AHEAD;
+  static_assert(kStages >= kAhead + 1 && kAhead >= 1, "spectrum ring too shallow");
+  static_assert((kStages & (kStages - 1)) == 0, "spectrum ring depth is a power of two");
+};
 constexpr int kSmemLimit = 227 * 1024 - 2048;  // dynamic shared memory per CTA, minus static and reserve
 constexpr unsigned kWaitLimit = 1u << 22;
 
@@ -201,7 +212,7 @@ struct Smem {
   static constexpr int P = Shape<KIND>::P;
   static constexpr int PB = NB * P;
   static constexpr int NA = NB * P;  // complex accumulators per row
-  static constexpr int kSpecBytes = kSpecStages * Shape<KIND>::kChunk * PB * 32 * 8;
+  static constexpr int kSpecBytes = SpecRing<KIND>::kStages * Shape<KIND>::kChunk * PB * 32 * 8;
   static constexpr int kStageBytes = kCons * Shape<KIND>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
   // table ring depth: the configured one, or as many as fit next to the spectrum ring
   static constexpr int kWant = KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S;
@@ -283,7 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   constexpr int kChunk = Shape<KIND>::kChunk;
   constexpr int kStageFloats = kChunk * kStepFloats;  // one warp's table stage
   constexpr int kSpecStageElems = kChunk * PB * 32;   // float2 per spectrum stage
-  static_assert((kSpecStages & (kSpecStages - 1)) == 0, "spectrum ring depth is a power of two");
+  constexpr int kSpecStages = SpecRing<KIND>::kStages;
+  constexpr int kSpecAhead = SpecRing<KIND>::kAhead;
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float2* spec = reinterpret_cast<float2*>(smem_raw);               // [stage][step][plane][lane]
