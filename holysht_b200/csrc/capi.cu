@@ -775,12 +775,13 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
   p.M = (int)M;
   p.nseg = (int)((L + hsb::rec::kSeg - 1) / hsb::rec::kSeg);
   p.scale = scale;
-  // latitudes per thread: 16 (8 for small grids, so a warp still covers them)
-  const int kpt = (K <= 256 || env_int("HSB_REC_KPT8", 0)) ? 8 : 16;
+  // latitudes per thread: 8 (measured faster than 16 at 512 x 1024: more
+  // resident warps); HSB_REC_KPT16=1 selects 16 (needed above 2048 latitudes)
+  const int kpt = (K > 2048 || (K > 256 && env_int("HSB_REC_KPT16", 0))) ? 16 : 8;
   const int threads = (int)(((K + kpt - 1) / kpt + 31) / 32 * 32);
   const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
   dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
-  if (env_int("HSB_REC_LEGACY", 0)) {
+  if (env_int("HSB_REC_LEGACY", 0) && K <= (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt) {
     const int t4 = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
     hsb::rec::recurrence_forward_kernel<<<grid, t4 < 32 ? 32 : t4, 0, static_cast<cudaStream_t>(stream)>>>(p);
   } else if (kpt == 8) {
@@ -799,9 +800,8 @@ int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int6
   if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
   if (B == 0 || L == 0 || M == 0) return ok();
   if (!out || !spec || !seeds || !coef || !cos_theta) return fail(HOLYSHT_ERR_INVALID, "null pointer");
-  if (K > (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt)
-    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d",
-                hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt);
+  if (K > (long long)hsb::rec::kMaxWarps * 32 * 8)
+    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d", hsb::rec::kMaxWarps * 32 * 8);
   if (!fits_int(B) || !fits_int(L) || !fits_int(M) || (B + hsb::rec::kNB - 1) / hsb::rec::kNB > 65535)
     return fail(HOLYSHT_ERR_INVALID, "extent out of range");
   if (spec_row_stride < M || spec_comp_stride < K * spec_row_stride || spec_batch_stride < 2 * spec_comp_stride)
@@ -823,9 +823,14 @@ int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int6
   p.M = (int)M;
   p.nseg = (int)((L + hsb::rec::kSeg - 1) / hsb::rec::kSeg);
   p.scale = scale;
-  const int threads = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
   const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
   dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
+  if (!env_int("HSB_REC_LEGACY", 0) || K > (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt) {
+    const int t8 = (int)(((K + 7) / 8 + 31) / 32 * 32);
+    hsb::rec::recurrence_vector_forward_pair_kernel<8><<<grid, t8, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("recurrence_vector_forward");
+  }
+  const int threads = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
   hsb::rec::recurrence_vector_forward_kernel<<<grid, threads < 32 ? 32 : threads, 0,
                                                static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("vector recurrence forward kernel");

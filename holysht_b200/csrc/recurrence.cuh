@@ -479,5 +479,159 @@ __global__ void __launch_bounds__(kMaxWarps * 32) recurrence_vector_forward_kern
   }
 }
 
+// Paired-latitude vector kernel (the one the library launches): the maths of
+// recurrence_vector_forward_kernel with both recurrences, the table
+// combinations and the contraction on packed f32x2 operations over latitude
+// pairs (no operand duplication) and KPT latitudes per thread, which halves the
+// share of the per-degree warp reductions relative to 4 latitudes per thread.
+template <int KPT>
+__global__ void __launch_bounds__(kMaxWarps * 32) recurrence_vector_forward_pair_kernel(const VecRecParams p) {
+  constexpr int NP = KPT / 2;
+  __shared__ float red[kMaxWarps][32];
+  __shared__ float cf[kSegPerCta * kSeg][8];  // am, -bm, ap, -bp, alpha, beta, gamma, delta
+  const int m = blockIdx.x;
+  const int b0 = blockIdx.z * kNB;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int lm = p.L - m;
+  const int nseg = lm > 0 ? (lm + kSeg - 1) / kSeg : 0;
+  const int c_begin = blockIdx.y * kSegPerCta;
+  const long long plane = (long long)p.L * p.M;
+
+  if (blockIdx.y == 0) {
+    const int zrows = lm > 0 ? m : p.L;
+    for (int e = tid; e < zrows * kNB * 2; e += blockDim.x) {
+      const int l = e / (kNB * 2), r = e % (kNB * 2), b = b0 + r / 2, pc = r % 2;
+      if (b < p.B) p.out[((long long)b * 2 + pc) * plane + (long long)l * p.M + m] = make_float2(0.f, 0.f);
+    }
+  }
+  if (c_begin >= nseg) return;  // uniform per CTA
+  const int c_end = min(nseg, c_begin + kSegPerCta);
+  const int l_first = m + c_begin * kSeg;
+  const int ndeg = min(p.L, m + c_end * kSeg) - l_first;
+  for (int e = tid; e < kSegPerCta * kSeg * 8; e += blockDim.x) {
+    const int dl = e / 8, f = e % 8;
+    float v = dl < ndeg ? p.coef[((long long)m * p.L + l_first + dl) * 8 + f] : 0.f;
+    cf[dl][f] = (f == 1 || f == 3) ? -v : v;
+  }
+
+  const int k0 = tid * KPT;
+  float2 xp[NP];
+  float2 ur[NP][kNB], ui[NP][kNB], vr[NP][kNB], vi[NP][kNB];  // latitude pairs of u = c0 + i c1, v = c0 - i c1
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int k = k0 + 2 * i;
+    xp[i] = make_float2(k < p.K ? p.x[k] : 0.f, k + 1 < p.K ? p.x[k + 1] : 0.f);
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      float2 c0a = make_float2(0.f, 0.f), c1a = c0a, c0b = c0a, c1b = c0a;
+      if (b0 + b < p.B) {
+        const float2* base = p.spec + (long long)(b0 + b) * p.sbs + m;
+        if (k < p.K) {
+          c0a = base[(long long)k * p.srs];
+          c1a = base[(long long)k * p.srs + p.sps];
+        }
+        if (k + 1 < p.K) {
+          c0b = base[(long long)(k + 1) * p.srs];
+          c1b = base[(long long)(k + 1) * p.srs + p.sps];
+        }
+      }
+      const float sc = p.scale;
+      ur[i][b] = make_float2((c0a.x - c1a.y) * sc, (c0b.x - c1b.y) * sc);
+      ui[i][b] = make_float2((c0a.y + c1a.x) * sc, (c0b.y + c1b.x) * sc);
+      vr[i][b] = make_float2((c0a.x + c1a.y) * sc, (c0b.x + c1b.y) * sc);
+      vi[i][b] = make_float2((c0a.y - c1a.x) * sc, (c0b.y - c1b.x) * sc);
+    }
+  }
+  __syncthreads();  // coefficients staged
+
+  for (int c = c_begin; c < c_end; ++c) {
+    const int lseg = m + c * kSeg;
+    const float4* sd = reinterpret_cast<const float4*>(p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 4);
+    float2 qm0[NP], qm1[NP], qp0[NP], qp1[NP];
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const float4 a = k0 + 2 * i < p.K ? sd[2 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 bq = k0 + 2 * i + 1 < p.K ? sd[2 * i + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      qm0[i] = make_float2(a.x, bq.x);
+      qm1[i] = make_float2(a.y, bq.y);
+      qp0[i] = make_float2(a.z, bq.z);
+      qp1[i] = make_float2(a.w, bq.w);
+    }
+#pragma unroll
+    for (int qb = 0; qb < kSeg; qb += 2) {
+      float v[32];  // 2 degrees x (4 batches x (u, v) x re/im)
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const float* k8 = cf[lseg + qb + q2 - l_first];
+        const float2 am = make_float2(k8[0], k8[0]), nbm = make_float2(k8[1], k8[1]);
+        const float2 ap = make_float2(k8[2], k8[2]), nbp = make_float2(k8[3], k8[3]);
+        const float2 al = make_float2(k8[4], k8[4]), be = make_float2(k8[5], k8[5]);
+        const float2 ga = make_float2(k8[6], k8[6]), de = make_float2(k8[7], k8[7]);
+        float2 wp[NP], wm[NP];
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          const float2 w0 = __ffma2_rn(al, qm0[i], __fmul2_rn(be, qp0[i]));
+          const float2 w1 = __ffma2_rn(ga, qm1[i], __fmul2_rn(de, qp1[i]));
+          wp[i] = __fadd2_rn(w0, w1);
+          wm[i] = __fadd2_rn(w0, make_float2(-w1.x, -w1.y));
+          // both recurrences to degree l + 2
+          const float2 nm = __ffma2_rn(am, __fmul2_rn(xp[i], qm1[i]), __fmul2_rn(nbm, qm0[i]));
+          const float2 np = __ffma2_rn(ap, __fmul2_rn(xp[i], qp1[i]), __fmul2_rn(nbp, qp0[i]));
+          qm0[i] = qm1[i];
+          qm1[i] = nm;
+          qp0[i] = qp1[i];
+          qp1[i] = np;
+        }
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) {
+          float2 aur = make_float2(0.f, 0.f), aui = aur, avr = aur, avi = aur;
+#pragma unroll
+          for (int i = 0; i < NP; ++i) {
+            aur = __ffma2_rn(wp[i], ur[i][b], aur);
+            aui = __ffma2_rn(wp[i], ui[i][b], aui);
+            avr = __ffma2_rn(wm[i], vr[i][b], avr);
+            avi = __ffma2_rn(wm[i], vi[i][b], avi);
+          }
+          v[q2 * 16 + b * 4 + 0] = aur.x + aur.y;
+          v[q2 * 16 + b * 4 + 1] = aui.x + aui.y;
+          v[q2 * 16 + b * 4 + 2] = avr.x + avr.y;
+          v[q2 * 16 + b * 4 + 3] = avi.x + avi.y;
+        }
+      }
+#pragma unroll
+      for (int d = 16; d >= 1; d >>= 1) {
+        const bool upper = (lane & d) != 0;
+#pragma unroll
+        for (int i = 0; i < d; ++i) {
+          const float send = upper ? v[i] : v[i + d];
+          const float keep = upper ? v[i + d] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+      float sum = v[0];
+      if (nwarps > 1) {
+        red[warp][lane] = sum;
+        __syncthreads();
+        sum = 0.f;
+        if (warp == 0)
+          for (int w = 0; w < nwarps; ++w) sum += red[w][lane];
+      }
+      if (warp == 0) {
+        const float other = __shfl_xor_sync(0xffffffffu, sum, 2);
+        const int q2 = lane >> 4, b = (lane >> 2) & 3, which = (lane >> 1) & 1, ri = lane & 1;
+        const int l = lseg + qb + q2;
+        if (which == 0 && l < p.L && b0 + b < p.B) {
+          const float pu = sum, mv = other;
+          float* o = reinterpret_cast<float*>(p.out + (long long)(b0 + b) * 2 * plane + (long long)l * p.M + m);
+          o[ri] = 0.5f * (mv + pu);
+          o[2 * plane + (1 - ri)] = ri ? 0.5f * (mv - pu) : -0.5f * (mv - pu);
+        }
+      }
+      if (nwarps > 1) __syncthreads();
+    }
+  }
+}
+
 }  // namespace rec
 }  // namespace hsb
