@@ -149,9 +149,13 @@ class _GroupedTablesMixin:
         # .to() / .cuda() / dtype casts move the tables: prepared launches must not outlive them
         self.__dict__.pop("_contract_plans", None)
         self.__dict__.pop("_fast_forward", None)
+        self.__dict__.pop("_dense_split_fwd", None)
+        self.__dict__.pop("_dense_split_inv", None)
         return super()._apply(fn, *args, **kwargs)
 
     def _drop_grouped(self) -> None:
+        self.__dict__.pop("_dense_split_fwd", None)
+        self.__dict__.pop("_dense_split_inv", None)
         self.__dict__.pop("_contract_plans", None)
         self.__dict__.pop("_fast_forward", None)
         self._grouped_fwd = None
@@ -177,6 +181,17 @@ class _GroupedTablesMixin:
                 self.register_buffer("_dense_inv", t, persistent=False)
             else:
                 self._dense_inv = t
+        return t
+
+    def dense_table_split(self, direction: int) -> torch.Tensor:
+        """The tensor-core path's table split into tf32 and residual planes
+        (``ops.split_dense_table``), built once per direction on first use."""
+        name = "_dense_split_fwd" if direction == _lib.DIR_FORWARD else "_dense_split_inv"
+        t = self.__dict__.get(name)
+        dense = self.dense_table(direction)
+        if t is None or t.device != dense.device:
+            t = ops.split_dense_table(dense)
+            self.__dict__[name] = t
         return t
 
     def table(self, direction: int, layout=None):
@@ -228,7 +243,38 @@ def _dense_tc_eligible(src, B: int, direction: int) -> bool:
     force = os.environ.get("HOLYSHT_DENSE_TC", "")
     if force in ("0", "1"):
         return force == "1"
+    ref = _reference_backend()
+    if ref is not None:
+        return ref
     return B >= DENSE_TC_MIN_BATCH
+
+
+_REF_FLAGS_WARNED = set()
+
+
+def _reference_backend():
+    """The reference's backend environment flags (``torch-ext/holysht/__init__.py:253-288``),
+    mapped onto this package's paths: ``HOLYSHT_FORCE_BACKEND`` = ``tc_tf32`` / ``tc_bf16``
+    forces the tensor-core path (True), ``fma`` / ``tma`` the streaming kernel (False),
+    ``auto`` or unset chooses by batch size (None).  ``HOLYSHT_FORCE_VECTOR_STRATEGY``
+    and the ``HOLYSHT_AUTOTUNE*`` flags select among reference kernels that have no
+    counterpart here (one kernel per case, nothing timed at run time): they are
+    accepted, ignored, and reported once with a warning."""
+    import os
+    import warnings
+
+    for name in ("HOLYSHT_FORCE_VECTOR_STRATEGY", "HOLYSHT_AUTOTUNE", "HOLYSHT_AUTOTUNE_REBENCH",
+                 "HOLYSHT_AUTOTUNE_CACHE_PATH"):
+        if os.environ.get(name) and name not in _REF_FLAGS_WARNED:
+            _REF_FLAGS_WARNED.add(name)
+            warnings.warn(f"{name} is a reference autotuning flag; holysht_b200 has a fixed kernel choice "
+                          "and ignores it")
+    raw = os.environ.get("HOLYSHT_FORCE_BACKEND", "").strip().lower()
+    if raw in ("tc_tf32", "tc_bf16"):
+        return True
+    if raw in ("fma", "tma"):
+        return False
+    return None
 
 
 _MAX_PLANS = 32  # prepared contraction calls cached per table source
@@ -288,7 +334,7 @@ def _legendre_forward_planned(spec, src, round_bf16: bool, scale: float):
             ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
     elif _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
         # large batch: the per-order contraction is a dense GEMM -> tcgen05
-        ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table(_lib.DIR_FORWARD), nlat=K,
+        ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table_split(_lib.DIR_FORWARD), nlat=K,
                               lmax=L, mmax=M, scale=scale, flags=_lib.FLAG_ROUND_BF16 if round_bf16 else 0)
     else:
         plan = _run(src, _lib.DIR_FORWARD, spec, out, B, M, _strides3(spec, vector), _strides3(out, vector),
@@ -372,7 +418,7 @@ class _SpectrumLegendreForward(torch.autograd.Function):
         shape = (B, 2, K, W) if vector else (B, K, W)
         gspec = torch.empty(shape, device=g.device, dtype=torch.complex64)
         if _dense_tc_eligible(src, B, _lib.DIR_INVERSE):
-            ops.legendre_dense_tc(_lib.DIR_INVERSE, gspec, g, src.dense_table(_lib.DIR_INVERSE), nlat=K,
+            ops.legendre_dense_tc(_lib.DIR_INVERSE, gspec, g, src.dense_table_split(_lib.DIR_INVERSE), nlat=K,
                                   lmax=src.lmax, mmax=src.mmax, scale=ctx.scale)
         else:
             _run(src, _lib.DIR_INVERSE, g, gspec, B, src.mmax, _strides3(g, vector), _strides3(gspec, vector),
@@ -396,7 +442,7 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
         shape = (B, 2, K, W) if vector else (B, K, W)
         spec = torch.empty(shape, device=c.device, dtype=torch.complex64)
         if _dense_tc_eligible(src, B, _lib.DIR_INVERSE):
-            ops.legendre_dense_tc(_lib.DIR_INVERSE, spec, c, src.dense_table(_lib.DIR_INVERSE), nlat=K, lmax=L,
+            ops.legendre_dense_tc(_lib.DIR_INVERSE, spec, c, src.dense_table_split(_lib.DIR_INVERSE), nlat=K, lmax=L,
                                   mmax=M, scale=1.0, flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
         else:
             _run(src, _lib.DIR_INVERSE, c, spec, B, M, _strides3(c, vector), _strides3(spec, vector),
@@ -419,7 +465,7 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
         shape = (B, 2, L, M) if vector else (B, L, M)
         gc = torch.empty(shape, device=g.device, dtype=torch.complex64)
         if _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
-            ops.legendre_dense_tc(_lib.DIR_FORWARD, gc, g, src.dense_table(_lib.DIR_FORWARD), nlat=K, lmax=L,
+            ops.legendre_dense_tc(_lib.DIR_FORWARD, gc, g, src.dense_table_split(_lib.DIR_FORWARD), nlat=K, lmax=L,
                                   mmax=M, scale=1.0)
         else:
             _run(src, _lib.DIR_FORWARD, g, gc, B, M, _strides3(g, vector), _strides3(gc, vector),

@@ -21,7 +21,7 @@ HOLYSHT_ERR_UNSUPPORTED = 3
 DTYPE_C64, DTYPE_F32, DTYPE_BF16 = 0, 1, 2
 KIND_SCALAR, KIND_VECTOR, KIND_REAL = 0, 1, 2
 DIR_FORWARD, DIR_INVERSE = 0, 1
-FLAG_CONJ_W1, FLAG_ROUND_BF16, FLAG_IRFFT_PREP = 1, 2, 4
+FLAG_CONJ_W1, FLAG_ROUND_BF16, FLAG_IRFFT_PREP, FLAG_TABLE_SPLIT = 1, 2, 4, 16
 TABLE_STRIDED, TABLE_GROUPED, TABLE_GROUPED8 = 0, 1, 2
 
 # every symbol include/holysht_b200.h declares
@@ -42,6 +42,8 @@ EXPORTS = (
     "holysht_peer_barrier",
     "holysht_peer_error_word",
     "holysht_legendre_dense_tc_workspace",
+    "holysht_legendre_dense_tc_workspace_ex",
+    "holysht_legendre_dense_tc_split_table",
     "holysht_legendre_dense_tc",
     "holysht_tc_error_word",
     "holysht_stream_error_word",
@@ -121,6 +123,9 @@ def load() -> ctypes.CDLL:
             "holysht_peer_error_word": ([ctypes.POINTER(ctypes.c_uint)], i32),
             "holysht_legendre_contract_peers": ([ctypes.POINTER(ContractDesc), ctypes.POINTER(vp), i32, i64, vp, vp],
                                                 i32),
+            "holysht_legendre_dense_tc_workspace_ex": ([i32, i64, i64, i64, i64, i32,
+                                                        ctypes.POINTER(ctypes.c_int64)], i32),
+            "holysht_legendre_dense_tc_split_table": ([vp, vp, i64, vp], i32),
             "holysht_legendre_dense_tc_workspace": ([i32, i64, i64, i64, i64, ctypes.POINTER(ctypes.c_int64)], i32),
             "holysht_legendre_dense_tc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,
                                            ctypes.c_float, i32, i64, vp, i64, vp], i32),

@@ -621,22 +621,51 @@ bool make_map_3d(CUtensorMap* map, const void* base, unsigned long long d0, unsi
 
 long long align256(long long v) { return (v + 255) & ~255LL; }
 
-// Bytes of the dense path's scratch (Xt [M][2B][S] and D [M][R][2B], fp32), or -1
-// when the size does not fit in 62 bits (each product is checked factor by factor).
-long long tc_workspace(long long B, long long R, long long S, long long M) {
+// Bytes of the dense path's scratch: the split spectrum Xt hi/lo [2][M][2B][S],
+// the GEMM output D [M][R][2B] and, unless the caller passes a split table, the
+// split table [2][M][R][S] (fp32 each); -1 when the size does not fit in 62
+// bits (each product is checked factor by factor).
+long long tc_workspace(long long B, long long R, long long S, long long M, bool split_table = true) {
   const long long lim = 1LL << 62;
   auto mul = [lim](long long a, long long b, long long* r) {
     return !__builtin_mul_overflow(a, b, r) && *r < lim;
   };
-  long long a = 0, b = 0;
+  long long a = 0, b = 0, c = 0;
   if (!mul(M, 2, &a) || !mul(a, B, &a) || !mul(a, S, &a) || !mul(a, 4, &a)) return -1;
   if (!mul(M, R, &b) || !mul(b, 2, &b) || !mul(b, B, &b) || !mul(b, 4, &b)) return -1;
-  return align256(a) + align256(b);
+  if (!mul(M, R, &c) || !mul(c, S, &c) || !mul(c, 4, &c)) return -1;
+  const long long total = 2 * align256(a) + align256(b) + (split_table ? 2 * align256(c) : 0);
+  return total < lim ? total : -1;
 }
 
 }  // namespace
 
 extern "C" {
+
+int holysht_legendre_dense_tc_workspace_ex(int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                           int flags, int64_t* bytes) {
+  if (!bytes) return fail(HOLYSHT_ERR_INVALID, "bytes pointer is null");
+  if (direction != HOLYSHT_DIR_FORWARD && direction != HOLYSHT_DIR_INVERSE)
+    return fail(HOLYSHT_ERR_INVALID, "unknown direction %d", direction);
+  if (batch < 0 || nlat < 0 || lmax < 0 || mmax < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  const bool fwd = direction == HOLYSHT_DIR_FORWARD;
+  const long long Mrows = mmax < lmax ? mmax : lmax;
+  const long long need = tc_workspace(batch, fwd ? lmax : nlat, fwd ? nlat : lmax, Mrows,
+                                      !(flags & HOLYSHT_FLAG_TABLE_SPLIT));
+  if (need < 0) return fail(HOLYSHT_ERR_INVALID, "extents too large: the workspace size overflows");
+  *bytes = need;
+  return ok();
+}
+
+int holysht_legendre_dense_tc_split_table(const float* table, float* split, int64_t count, void* stream) {
+  if (count < 0) return fail(HOLYSHT_ERR_INVALID, "negative count");
+  if (count == 0) return ok();
+  if (!table || !split) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  const long long blocks = std::min<long long>((count + 255) / 256, 148LL * 16);
+  hsb::tc::split_tf32_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, split,
+                                                                                             split + count, count);
+  return check_launch("split_tf32");
+}
 
 int holysht_legendre_dense_tc_workspace(int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
                                         int64_t* bytes) {
@@ -660,9 +689,10 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (direction != HOLYSHT_DIR_FORWARD && direction != HOLYSHT_DIR_INVERSE)
     return fail(HOLYSHT_ERR_INVALID, "unknown direction %d", direction);
-  if (flags & ~(HOLYSHT_FLAG_ROUND_BF16 | HOLYSHT_FLAG_IRFFT_PREP))
+  if (flags & ~(HOLYSHT_FLAG_ROUND_BF16 | HOLYSHT_FLAG_IRFFT_PREP | HOLYSHT_FLAG_TABLE_SPLIT))
     return fail(HOLYSHT_ERR_INVALID, "unsupported flags 0x%x", flags);
   const bool fwd = direction == HOLYSHT_DIR_FORWARD;
+  const bool presplit = (flags & HOLYSHT_FLAG_TABLE_SPLIT) != 0;
   const long long B = batch, K = nlat, L = lmax, M = mmax;
   if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
   if (out_cols < M) return fail(HOLYSHT_ERR_INVALID, "out_cols (%lld) < mmax (%lld)", (long long)out_cols, M);
@@ -679,25 +709,41 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
   if ((flags & HOLYSHT_FLAG_IRFFT_PREP) && (fwd || nlon <= 0 || out_cols > nlon / 2 + 1))
     return fail(HOLYSHT_ERR_INVALID, "irfft preparation is for the inverse with out_cols <= nlon/2+1");
   const long long Mrows = M < L ? M : L;
-  const long long need = tc_workspace(B, R, S, Mrows);
+  const long long need = tc_workspace(B, R, S, Mrows, !presplit);
   if (need < 0 || workspace_bytes < need) return fail(HOLYSHT_ERR_INVALID, "workspace too small");
   if (in_row_stride < M || in_batch_stride < S * in_row_stride || out_row_stride < out_cols ||
       out_batch_stride < R * out_row_stride)
     return fail(HOLYSHT_ERR_INVALID, "input or output strides too small");
   const long long N = 2 * B;
-  float* xt = static_cast<float*>(workspace);
-  float* D = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256(Mrows * N * S * 4));
+  char* ws = static_cast<char*>(workspace);
+  float* xt = reinterpret_cast<float*>(ws);
+  float* xt_lo = reinterpret_cast<float*>(ws + align256(Mrows * N * S * 4));
+  float* D = reinterpret_cast<float*>(ws + 2 * align256(Mrows * N * S * 4));
+  const float* a_hi = table;
+  const float* a_lo = table + M * R * S;  // a split table: [2][mmax][R][S]
 
-  if (Mrows > 0) {  // input -> Xt [Mrows][2B][S]
+  if (Mrows > 0) {  // input -> Xt [Mrows][2B][S], split into tf32 hi and residual lo
+    if (!presplit) {  // split the table's first Mrows orders into the workspace
+      float* t_hi = reinterpret_cast<float*>(ws + 2 * align256(Mrows * N * S * 4) + align256(Mrows * R * N * 4));
+      float* t_lo = reinterpret_cast<float*>(reinterpret_cast<char*>(t_hi) + align256(Mrows * R * S * 4));
+      const long long cnt = Mrows * R * S;
+      const long long blocks = std::min<long long>((cnt + 255) / 256, 148LL * 16);
+      hsb::tc::split_tf32_kernel<<<(unsigned)blocks, 256, 0, stream>>>(table, t_hi, t_lo, cnt);
+      if (int st = check_launch("split_tf32")) return st;
+      a_hi = t_hi;
+      a_lo = t_lo;
+    }
     dim3 grid((unsigned)((Mrows + 31) / 32), (unsigned)((S + 31) / 32), (unsigned)B), block(32, 8);
-    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(in), xt, (int)B, (int)S,
-                                                             (int)Mrows, in_batch_stride, in_row_stride, scale,
-                                                             (flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0);
+    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(in), xt, xt_lo, (int)B,
+                                                             (int)S, (int)Mrows, in_batch_stride, in_row_stride,
+                                                             scale, (flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0);
     if (int st = check_launch("transpose_in")) return st;
     // table: forward [M][L][K] (rows l, reduce k); inverse [M][K][L] (rows k, reduce l)
-    CUtensorMap map_a, map_b;
-    if (!make_map_3d(&map_a, table, S, R, Mrows, hsb::tc::kBK, hsb::tc::kBM) ||
-        !make_map_3d(&map_b, xt, S, N, Mrows, hsb::tc::kBK, hsb::tc::kBN))
+    CUtensorMap map_a, map_b, map_a_lo, map_b_lo;
+    if (!make_map_3d(&map_a, a_hi, S, R, Mrows, hsb::tc::kBK, hsb::tc::kBM) ||
+        !make_map_3d(&map_a_lo, a_lo, S, R, Mrows, hsb::tc::kBK, hsb::tc::kBM) ||
+        !make_map_3d(&map_b, xt, S, N, Mrows, hsb::tc::kBK, hsb::tc::kBN) ||
+        !make_map_3d(&map_b_lo, xt_lo, S, N, Mrows, hsb::tc::kBK, hsb::tc::kBN))
       return fail(HOLYSHT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable or rejected the tensors");
     hsb::tc::DenseParams p;
     p.R = (int)R;
@@ -730,8 +776,8 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
       configured.fetch_or(bit);
     }
     if (tiles > 0) {
-      hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(map_a, map_b,
-                                                                                                        p);
+      hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(
+          map_a, map_b, map_a_lo, map_b_lo, p);
       if (int st = check_launch("dense tcgen05 kernel")) return st;
     }
   }

@@ -6,19 +6,21 @@
 // W[m][l][k] (k contiguous, the module's `weights` buffer) and X_m the
 // spectrum of order m transposed to Xt[m][n][k] (n = 2*batch + re/im).
 //
-// FP32 accuracy from TF32 tensor cores: each operand is split in shared
-// memory into hi = rna_tf32(x) and lo = x - hi; the products hi*hi + hi*lo +
-// lo*hi of one 32-wide k block go to a TMEM accumulator that starts from zero,
-// and the block sums are added into fp32 registers with round-to-nearest
-// (the tensor core's own accumulation truncates, an error that grows with the
-// chain length; the lo*lo term is below fp32 resolution).  Two TMEM slots
-// alternate so the warps drain one block while the tensor core runs the next.
+// FP32 accuracy from TF32 tensor cores: each operand is stored split in
+// global memory, hi = rna_tf32(x) and lo = x - hi (the table once per module,
+// the spectrum by the input transpose); the products hi*hi + hi*lo + lo*hi of
+// one 32-wide k block go to a TMEM accumulator that starts from zero, and the
+// block sums are added into fp32 registers with round-to-nearest (the tensor
+// core's own accumulation truncates, an error that grows with the chain
+// length; the lo*lo term is below fp32 resolution).  Two TMEM slots alternate
+// so the warps drain one block while the tensor core runs the next.
 //
 // CTA: one order m, 128 output rows l (TMEM lanes), 256 columns n (TMEM
-// columns), the full k range in 32-wide blocks.  Pipeline per k block:
-// TMA (cp.async.bulk.tensor, SWIZZLE_128B, K-major) -> all threads split the
-// stage in place -> one thread issues 4 k-steps x 3 tcgen05.mma (kind::tf32,
-// cta_group::1) -> tcgen05.commit frees the stage.  Two stages in flight.
+// columns), the full k range in 32-wide blocks.  Pipeline per k block: one
+// thread issues four TMA copies (cp.async.bulk.tensor, SWIZZLE_128B, K-major:
+// A hi, A lo, B hi, B lo) -> one thread issues 4 k-steps x 3 tcgen05.mma
+// (kind::tf32, cta_group::1) -> tcgen05.commit frees the stage.  Two stages in
+// flight; no thread rewrites a stage.
 // Epilogue: tcgen05.ld 32x32b -> coalesced row stores of D[m][l][n].
 // Every mbarrier wait is bounded; a timeout sets a device error word and the
 // CTA drains and releases its TMEM instead of hanging.
@@ -173,6 +175,7 @@ __device__ __forceinline__ bool decode(const DenseParams& p, int t, int& m, int&
 
 __global__ void __launch_bounds__(kThreads, 1)
     dense_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_a_lo, const __grid_constant__ CUtensorMap map_b_lo,
                         const DenseParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -220,10 +223,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const unsigned tmem = *tmem_slot;
   constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
 
+  // both operands arrive already split (tf32 hi and fp32 residual lo planes)
   auto issue_loads = [&](int kb, int s) {
-    mbar_expect_tx(&full[s], kABytes + kBBytes);
+    mbar_expect_tx(&full[s], 2 * (kABytes + kBBytes));
     tma_load_3d(a_hi(s), &map_a, &full[s], (kb0 + kb) * kBK, l0, m);
+    tma_load_3d(a_lo(s), &map_a_lo, &full[s], (kb0 + kb) * kBK, l0, m);
     tma_load_3d(b_hi(s), &map_b, &full[s], (kb0 + kb) * kBK, n0, m);
+    tma_load_3d(b_lo(s), &map_b_lo, &full[s], (kb0 + kb) * kBK, n0, m);
   };
   if (tid == 0) issue_loads(0, 0);
 
@@ -278,29 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (kb + 1 >= kStages) mbar_wait(&empty[s2], ((kb + 1) / kStages - 1) & 1);  // MMAs of kb-1 done
       issue_loads(kb + 1, s2);
     }
-    mbar_wait(&full[s], ph);
-    // split the stage in place: hi = rna_tf32(x) where x was, lo = x - hi alongside
-    {
-      float4* ah = reinterpret_cast<float4*>(a_hi(s));
-      float4* al = reinterpret_cast<float4*>(a_lo(s));
-      for (int i = tid; i < kABytes / 16; i += kThreads) {
-        const float4 v = ah[i];
-        const float4 h = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
-        ah[i] = h;
-        al[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-      }
-      float4* bh = reinterpret_cast<float4*>(b_hi(s));
-      float4* bl = reinterpret_cast<float4*>(b_lo(s));
-      for (int i = tid; i < kBBytes / 16; i += kThreads) {
-        const float4 v = bh[i];
-        const float4 h = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
-        bh[i] = h;
-        bl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-    __syncthreads();
     if (warp == 1 && lane == 0) {
+      mbar_wait(&full[s], ph);  // the stage's four operand tiles have landed
       const int slot = kb & 1;
       if (kb >= 2) mbar_wait(&d1_free[slot], ((kb >> 1) - 1) & 1);  // block kb-2 drained
       asm volatile("tcgen05.fence::after_thread_sync;\n");
@@ -347,9 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // input [B][S][W] complex (orders < M used) -> Xt [M][2B][S] fp32 * scale,
-// optionally rounded to bf16 (after scaling)
-__global__ void transpose_in_kernel(const float2* __restrict__ in, float* __restrict__ xt, int B, int S, int M,
-                                    long long in_bs, long long in_rs, float scale, int round_bf16) {
+// optionally rounded to bf16 (after scaling), stored split: xt = rna_tf32(x),
+// xt_lo = x - xt (the residual is exact in fp32)
+__global__ void transpose_in_kernel(const float2* __restrict__ in, float* __restrict__ xt, float* __restrict__ xt_lo,
+                                    int B, int S, int M, long long in_bs, long long in_rs, float scale,
+                                    int round_bf16) {
   __shared__ float2 tile[32][33];
   const int b = blockIdx.z;
   const int m0 = blockIdx.x * 32, s0 = blockIdx.y * 32;
@@ -368,9 +355,12 @@ __global__ void transpose_in_kernel(const float2* __restrict__ in, float* __rest
         re = __bfloat162float(__float2bfloat16_rn(re));
         im = __bfloat162float(__float2bfloat16_rn(im));
       }
-      float* row = xt + ((long long)m * (2LL * B) + 2LL * b) * S;
-      row[sidx] = re;
-      row[S + sidx] = im;
+      const long long off = ((long long)m * (2LL * B) + 2LL * b) * S;
+      const float hre = rna_tf32(re), him = rna_tf32(im);
+      xt[off + sidx] = hre;
+      xt[off + S + sidx] = him;
+      xt_lo[off + sidx] = re - hre;
+      xt_lo[off + S + sidx] = im - him;
     }
   }
 }
@@ -402,6 +392,17 @@ __global__ void transpose_out_kernel(const float* __restrict__ D, float2* __rest
       if ((zero_im0 && m == 0) || m == nyquist) v.y = 0.f;
       out[(long long)b * out_bs + (long long)r * out_rs + m] = v;
     }
+  }
+}
+
+// table [n] -> hi [n] = rna_tf32(x), lo [n] = x - hi
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                  long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const float h = rna_tf32(v);
+    hi[i] = h;
+    lo[i] = v - h;
   }
 }
 

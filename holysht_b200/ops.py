@@ -443,6 +443,18 @@ def _contract_desc(*, kind, direction, input, output, w0, w1=None, batch, nlat, 
     return d
 
 
+def split_dense_table(table: torch.Tensor) -> torch.Tensor:
+    """[2, *table.shape] split of a dense-path table (``holysht_legendre_dense_tc_split_table``):
+    plane 0 the tf32-rounded values, plane 1 the fp32 residuals."""
+    _cuda(table)
+    _require(table.dtype == torch.float32 and table.is_contiguous(), "table must be contiguous float32")
+    out = torch.empty((2,) + tuple(table.shape), dtype=torch.float32, device=table.device)
+    with torch.cuda.device(table.device):
+        _lib.check(_lib.load().holysht_legendre_dense_tc_split_table(_p(table), _p(out), table.numel(),
+                                                                     _stream(table.device)))
+    return out
+
+
 def legendre_dense_tc(direction: int, output: torch.Tensor, input: torch.Tensor, table: torch.Tensor,
                       *, nlat: int, lmax: int, mmax: int, scale: float = 1.0, flags: int = 0,
                       nlon: int = 0) -> None:
@@ -459,11 +471,15 @@ def legendre_dense_tc(direction: int, output: torch.Tensor, input: torch.Tensor,
              "input and output must be [B, rows, cols] with contiguous orders")
     fwd = direction == _lib.DIR_FORWARD
     want = (mmax, lmax, nlat) if fwd else (mmax, nlat, lmax)
-    _require(tuple(table.shape) == want, f"table must be {want}")
+    if tuple(table.shape) == (2,) + want:  # a split_dense_table() table
+        flags |= _lib.FLAG_TABLE_SPLIT
+    else:
+        _require(tuple(table.shape) == want, f"table must be {want} or a split (2, {want}) table")
     B = input.size(0)
     lib = _lib.load()
     nbytes = ctypes.c_int64(0)
-    _lib.check(lib.holysht_legendre_dense_tc_workspace(direction, B, nlat, lmax, mmax, ctypes.byref(nbytes)))
+    _lib.check(lib.holysht_legendre_dense_tc_workspace_ex(direction, B, nlat, lmax, mmax, int(flags),
+                                                          ctypes.byref(nbytes)))
     with torch.cuda.device(dev):
         ws = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=dev)
         _lib.check(lib.holysht_legendre_dense_tc(

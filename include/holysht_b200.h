@@ -242,8 +242,26 @@ int holysht_legendre_contract_peers(const holysht_contract_desc* desc, void* con
  * layout), inverse [mmax][nlat][lmax] (the same table transposed per order);
  * the reduction extent (nlat forward, lmax inverse) must be a multiple of 4.
  * workspace: caller-allocated device memory (256-byte aligned) of at least
- * the size holysht_legendre_dense_tc_workspace reports; it holds the
- * transposed input and the GEMM output between the three launches. */
+ * the size holysht_legendre_dense_tc_workspace reports; it holds the split
+ * table (unless HOLYSHT_FLAG_TABLE_SPLIT), the transposed input split into
+ * tf32 and residual planes, and the GEMM output between the launches. */
+/* HOLYSHT_FLAG_TABLE_SPLIT (holysht_legendre_dense_tc only): `table` is the
+ * split table [2][mmax][R][S] that holysht_legendre_dense_tc_split_table
+ * writes (plane 0: the tf32-rounded table, plane 1: the fp32 residual), so
+ * the call does not split it again; the workspace then needs only the size
+ * holysht_legendre_dense_tc_workspace_ex reports with this flag. */
+#define HOLYSHT_FLAG_TABLE_SPLIT 16
+
+/* Split a dense-path table of `count` floats for HOLYSHT_FLAG_TABLE_SPLIT:
+ * split[i] = rna_tf32(table[i]), split[count + i] = table[i] - split[i].
+ * No counterpart in the reference (its tensor-core path rounds to TF32). */
+int holysht_legendre_dense_tc_split_table(const float* table, float* split, int64_t count, void* stream);
+
+/* Workspace bytes of holysht_legendre_dense_tc for the given flags (only
+ * HOLYSHT_FLAG_TABLE_SPLIT changes the size).  Host-only. */
+int holysht_legendre_dense_tc_workspace_ex(int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                           int flags, int64_t* bytes);
+
 int holysht_legendre_dense_tc_workspace(int direction, int64_t batch, int64_t nlat, int64_t lmax,
                                         int64_t mmax, int64_t* bytes);
 int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride,

@@ -307,3 +307,22 @@ def test_vector_recurrence_tables_reproduce_the_vector_tables(nlat, grid, norm, 
             qm0, qm1 = qm1, am * x64 * qm1 - bm * qm0
             qp0, qp1 = qp1, ap * x64 * qp1 - bp * qp0
     assert np.abs(got - ref).max() <= 1e-6 * np.abs(ref).max()
+
+
+def test_reference_backend_flags_map_onto_the_paths(monkeypatch):
+    """HOLYSHT_FORCE_BACKEND of the reference picks the tensor-core path (tc_*) or the
+    streaming kernel (fma/tma); its autotune flags are ignored with a warning."""
+    import holysht_b200 as hs_mod
+
+    m = hs.RealSHT(16, 32)
+    monkeypatch.delenv("HOLYSHT_DENSE_TC", raising=False)
+    monkeypatch.setenv("HOLYSHT_FORCE_BACKEND", "tc_tf32")
+    assert hs_mod._dense_tc_eligible(m, 1, _lib.DIR_FORWARD)
+    monkeypatch.setenv("HOLYSHT_FORCE_BACKEND", "tma")
+    assert not hs_mod._dense_tc_eligible(m, 4096, _lib.DIR_FORWARD)
+    monkeypatch.setenv("HOLYSHT_FORCE_BACKEND", "auto")
+    assert hs_mod._dense_tc_eligible(m, 4096, _lib.DIR_FORWARD)
+    monkeypatch.setenv("HOLYSHT_AUTOTUNE", "1")
+    hs_mod._REF_FLAGS_WARNED.discard("HOLYSHT_AUTOTUNE")
+    with pytest.warns(UserWarning, match="HOLYSHT_AUTOTUNE"):
+        hs_mod._dense_tc_eligible(m, 1, _lib.DIR_FORWARD)
