@@ -607,7 +607,8 @@ EncodeTiledFn encode_tiled() {
 
 // 3-D fp32 tensor map (inner dim contiguous), 128-byte swizzle, zero OOB fill
 bool make_map_3d(CUtensorMap* map, const void* base, unsigned long long d0, unsigned long long d1,
-                 unsigned long long d2, unsigned box0, unsigned box1) {
+                 unsigned long long d2, unsigned box0, unsigned box1,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return false;
   cuuint64_t dims[3] = {d0, d1, d2};
@@ -615,7 +616,7 @@ bool make_map_3d(CUtensorMap* map, const void* base, unsigned long long d0, unsi
   cuuint32_t box[3] = {box0, box1, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -739,11 +740,16 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
                                                              scale, (flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0);
     if (int st = check_launch("transpose_in")) return st;
     // table: forward [M][L][K] (rows l, reduce k); inverse [M][K][L] (rows k, reduce l)
+    // the warp-specialised kernel moves 16-wide k blocks (64-byte swizzle);
+    // HSB_TC_LEGACY=1 runs the earlier 32-wide, 8-warp kernel
+    const bool legacy = env_int("HSB_TC_LEGACY", 0) != 0;
+    const unsigned bk = legacy ? hsb::tc::kBK : hsb::tc::kBK2;
+    const CUtensorMapSwizzle sw = legacy ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap map_a, map_b, map_a_lo, map_b_lo;
-    if (!make_map_3d(&map_a, a_hi, S, R, Mrows, hsb::tc::kBK, hsb::tc::kBM) ||
-        !make_map_3d(&map_a_lo, a_lo, S, R, Mrows, hsb::tc::kBK, hsb::tc::kBM) ||
-        !make_map_3d(&map_b, xt, S, N, Mrows, hsb::tc::kBK, hsb::tc::kBN) ||
-        !make_map_3d(&map_b_lo, xt_lo, S, N, Mrows, hsb::tc::kBK, hsb::tc::kBN))
+    if (!make_map_3d(&map_a, a_hi, S, R, Mrows, bk, hsb::tc::kBM, sw) ||
+        !make_map_3d(&map_a_lo, a_lo, S, R, Mrows, bk, hsb::tc::kBM, sw) ||
+        !make_map_3d(&map_b, xt, S, N, Mrows, bk, hsb::tc::kBN, sw) ||
+        !make_map_3d(&map_b_lo, xt_lo, S, N, Mrows, bk, hsb::tc::kBN, sw))
       return fail(HOLYSHT_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable or rejected the tensors");
     hsb::tc::DenseParams p;
     p.R = (int)R;
@@ -771,13 +777,19 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
     const unsigned long long bit = 1ull << (dev & 63);
     if (!(configured.load() & bit)) {
       if (cudaFuncSetAttribute(hsb::tc::dense_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               hsb::tc::kSmemBytes) != cudaSuccess)
+                               hsb::tc::kSmemBytes) != cudaSuccess ||
+          cudaFuncSetAttribute(hsb::tc::dense_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               hsb::tc::kWsSmemBytes) != cudaSuccess)
         return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the tensor-core kernel");
       configured.fetch_or(bit);
     }
     if (tiles > 0) {
-      hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(
-          map_a, map_b, map_a_lo, map_b_lo, p);
+      if (legacy)
+        hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(
+            map_a, map_b, map_a_lo, map_b_lo, p);
+      else
+        hsb::tc::dense_ws_kernel<<<(unsigned)tiles, hsb::tc::kWsThreads, hsb::tc::kWsSmemBytes, stream>>>(
+            map_a, map_b, map_a_lo, map_b_lo, p);
       if (int st = check_launch("dense tcgen05 kernel")) return st;
     }
   }

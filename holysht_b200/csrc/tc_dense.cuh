@@ -331,6 +331,173 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialised variant (the one the library launches).  Same tile, same
+// split-TF32 products and per-block draining, with the pipeline roles on
+// separate warps so no role waits for another's unrelated work:
+//   warp 0      TMA producer: four copies per stage into a 4-deep ring;
+//   warp 1      MMA issuer: 2 k-steps x 3 tcgen05.mma per stage, commits;
+//   warps 2..9  drain: each owns 32 TMEM lanes x 128 columns of the
+//               accumulator and adds every finished block into registers.
+// A stage is 16 k-values (64-byte rows, SWIZZLE_64B), 48 KiB for A hi/lo and
+// B hi/lo, so four stages (192 KiB) keep three stages of loads in flight while
+// the tensor core works on the fourth.
+constexpr int kBK2 = 16;
+constexpr int kStages2 = 4;
+constexpr int kWsThreads = 320;
+constexpr int kA2 = kBM * kBK2 * 4;   // 8 KiB
+constexpr int kB2 = kBN * kBK2 * 4;   // 16 KiB
+constexpr int kStage2 = 2 * kA2 + 2 * kB2;
+constexpr int kWsSmemBytes = kStages2 * kStage2 + 1024 + 256;
+
+// UMMA shared-memory descriptor: K-major, SWIZZLE_64B (8-row groups of
+// 64-byte rows, 512 bytes apart), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw64_desc(unsigned smem_addr) {
+  const uint64_t start = (smem_addr & 0x3FFFFu) >> 4;
+  const uint64_t lbo = 1;
+  const uint64_t sbo = 512u >> 4;
+  return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (4ull << 61);
+}
+
+__global__ void __launch_bounds__(kWsThreads, 1)
+    dense_ws_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    const __grid_constant__ CUtensorMap map_a_lo, const __grid_constant__ CUtensorMap map_b_lo,
+                    const DenseParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages2 * kStage2);
+  uint64_t* empty = full + kStages2;
+  uint64_t* d_full = empty + kStages2;
+  uint64_t* d_free = d_full + 2;
+  unsigned* tmem_slot = reinterpret_cast<unsigned*>(d_free + 2);
+
+  int m, lt, nt;
+  if (!decode(p, blockIdx.x, m, lt, nt)) return;  // uniform per CTA
+  const int l0 = (p.inverse ? 0 : m) + lt * kBM;
+  const int n0 = nt * kBN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb0 = p.inverse ? m / kBK2 : 0;  // inverse: the table is zero for l < m
+  const int nk = (p.S + kBK2 - 1) / kBK2 - kb0;
+
+  auto a_hi = [&](int s) { return smem + s * kStage2; };
+  auto a_lo = [&](int s) { return smem + s * kStage2 + kA2; };
+  auto b_hi = [&](int s) { return smem + s * kStage2 + 2 * kA2; };
+  auto b_lo = [&](int s) { return smem + s * kStage2 + 2 * kA2 + kB2; };
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&d_full[q], 1);
+      mbar_init(&d_free[q], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  const unsigned tmem = *tmem_slot;
+  constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages2;
+        if (kb >= kStages2 && !mbar_wait(&empty[s], ((kb / kStages2) - 1) & 1)) break;
+        mbar_expect_tx(&full[s], kStage2);
+        const int kc = (kb0 + kb) * kBK2;
+        tma_load_3d(a_hi(s), &map_a, &full[s], kc, l0, m);
+        tma_load_3d(a_lo(s), &map_a_lo, &full[s], kc, l0, m);
+        tma_load_3d(b_hi(s), &map_b, &full[s], kc, n0, m);
+        tma_load_3d(b_lo(s), &map_b_lo, &full[s], kc, n0, m);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages2;
+        const int slot = kb & 1;
+        if (!mbar_wait(&full[s], (kb / kStages2) & 1)) break;
+        if (kb >= 2 && !mbar_wait(&d_free[slot], ((kb >> 1) - 1) & 1)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;\n");
+        const unsigned d = tmem + (unsigned)(slot * kBN);
+        const unsigned ahi = smem_u32(a_hi(s)), alo = smem_u32(a_lo(s));
+        const unsigned bhi = smem_u32(b_hi(s)), blo = smem_u32(b_lo(s));
+#pragma unroll
+        for (int j = 0; j < kBK2 / 8; ++j) {  // 8 tf32 = 32 bytes per k-step
+          const unsigned off = j * 32;
+          mma_tf32(d, sw64_desc(ahi + off), sw64_desc(bhi + off), idesc, j > 0 ? 1u : 0u);
+          mma_tf32(d, sw64_desc(ahi + off), sw64_desc(blo + off), idesc, 1u);
+          mma_tf32(d, sw64_desc(alo + off), sw64_desc(bhi + off), idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+        mma_commit(&d_full[slot]);
+      }
+    }
+  } else {  // drain warps 2..9
+    const int dw = warp - 2;
+    const int quarter = warp & 3;  // the TMEM lanes this warp may read
+    const int col_half = dw >> 2;
+    const unsigned trow = tmem + ((unsigned)(quarter * 32) << 16) + (unsigned)(col_half * (kBN / 2));
+    float acc[kBN / 2];
+#pragma unroll
+    for (int c = 0; c < kBN / 2; ++c) acc[c] = 0.f;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int slot = kb & 1;
+      const bool okw = mbar_wait(&d_full[slot], (kb >> 1) & 1);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, okw)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;\n");
+#pragma unroll
+      for (int cc = 0; cc < kBN / 2; cc += 32) {
+        unsigned r[32];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+              "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+              "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+              "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(trow + (unsigned)(slot * kBN + cc)));
+        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+        for (int q = 0; q < 32; ++q) acc[cc + q] += __uint_as_float(r[q]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;\n");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&d_free[slot]);
+    }
+    const int row = l0 + quarter * 32 + lane;
+    const int nb = n0 + col_half * (kBN / 2);
+    if (row < p.R) {
+      float* dst = p.D + ((size_t)m * p.R + row) * p.N + nb;
+      if (nb + kBN / 2 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < kBN / 8; ++q)
+          reinterpret_cast<float4*>(dst)[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kBN / 2; ++q)
+          if (nb + q < p.N) dst[q] = acc[q];
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // input [B][S][W] complex (orders < M used) -> Xt [M][2B][S] fp32 * scale,
 // optionally rounded to bf16 (after scaling), stored split: xt = rna_tf32(x),
 // xt_lo = x - xt (the residual is exact in fp32)
