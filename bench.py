@@ -129,11 +129,14 @@ def _peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def algorithmic_bytes(L, K, M, B, tables):
+def algorithmic_bytes(L, K, M, B, tables, table_rows=None):
     """Bytes one forward Legendre launch must move: the l >= m triangle of each
-    table (fp32), the spectrum read (complex64, orders < M) and the output."""
+    table (fp32) over ``table_rows`` latitudes (K, or ceil(K/2) when the kernel
+    folds the southern half by equatorial parity), the spectrum read
+    (complex64, orders < M, all K rows) and the output."""
     pairs = sum(max(L - m, 0) for m in range(M))
-    return tables * pairs * K * 4 + B * tables * K * M * 8 + B * tables * L * M * 8
+    rows = K if table_rows is None else table_rows
+    return tables * pairs * rows * 4 + B * tables * K * M * 8 + B * tables * L * M * 8
 
 
 def run_ours(args, rank, world, local_rank):
@@ -214,7 +217,7 @@ def run_ours(args, rank, world, local_rank):
                           w0=table, batch=BATCH, nlat=NLAT, lmax=L, mmax=M,
                           in_strides=(2 * NLAT * W, NLAT * W, W), out_strides=(2 * L * M, L * M, M),
                           out_cols=M, scale=2 * math.pi / NLON, grouped=layout == "grouped",
-                          grouped8=layout == "grouped8")
+                          grouped8=layout in ("grouped8", "parity"), parity=layout == "parity")
 
     for _ in range(3):
         kernel()
@@ -229,7 +232,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(ks, ke))
     kernel_ms = max_over_ranks(kernel_ms)
-    abytes = algorithmic_bytes(L, NLAT, M, BATCH, 2)
+    abytes = algorithmic_bytes(L, NLAT, M, BATCH, 2, (NLAT + 1) // 2 if layout == "parity" else NLAT)
     clocks.stop()
 
     # ---- secondary: RealSHT.forward on the same grid ----

@@ -127,6 +127,7 @@ class _GroupedTablesMixin:
         self.register_buffer("_grouped_inv", None, persistent=False)
         self.register_buffer("_grouped8_fwd", None, persistent=False)
         self.register_buffer("_grouped8_inv", None, persistent=False)
+        self.register_buffer("_grouped8p_fwd", None, persistent=False)
         # the streaming copies are built on first use, on the tables' device
         # (a GPU builds them in milliseconds; the host takes tens of seconds
         # at 1024 x 2048)
@@ -162,6 +163,8 @@ class _GroupedTablesMixin:
         self._grouped_inv = None
         self._grouped8_fwd = None
         self._grouped8_inv = None
+        self._grouped8p_fwd = None
+        self.__dict__.pop("_symmetric", None)
         if hasattr(self, "_dense_inv"):
             self._dense_inv = None
 
@@ -194,6 +197,27 @@ class _GroupedTablesMixin:
             self.__dict__[name] = t
         return t
 
+    def _equatorial_symmetry(self) -> bool:
+        """True when the forward tables obey the equatorial parity the folded
+        (``"parity"``) layout relies on: W(K-1-k) = s W(k) for the scalar table
+        and W1, W0(K-1-k) = -s W0(k), s = (-1)^(l+m), to 1e-6 of the largest
+        entry (every grid this package builds is symmetric; tables loaded from
+        elsewhere are checked)."""
+        sym = self.__dict__.get("_symmetric")
+        if sym is None:
+            dense = [getattr(self, n) for n in self._table_names]
+            L, K, M = dense[0].shape
+            dev = dense[0].device
+            sgn = 1.0 - 2.0 * ((torch.arange(L, device=dev)[:, None, None]
+                                + torch.arange(M, device=dev)[None, None, :]) % 2).float()
+            sym = True
+            for i, d in enumerate(dense):
+                f = -sgn if (self.vector and i == 0) else sgn
+                err = (d.flip(1) - f * d).abs().max()
+                sym = sym and bool(err <= 1e-6 * d.abs().max().clamp_min(1e-30))
+            self.__dict__["_symmetric"] = sym
+        return sym
+
     def table(self, direction: int, layout=None):
         """(table, None, layout) for one contraction direction.
 
@@ -207,6 +231,22 @@ class _GroupedTablesMixin:
 
             stream = os.environ.get("HOLYSHT_TABLE_LAYOUT", "grouped8") != "grouped"
             layout = "grouped8" if stream else "grouped"
+            if (stream and direction == _lib.DIR_FORWARD and os.environ.get("HOLYSHT_PARITY", "1") != "0"
+                    and self._equatorial_symmetry()):
+                layout = "parity"
+        if layout == "parity":
+            t = self._grouped8p_fwd
+            dense = tuple(getattr(self, n) for n in self._table_names)
+            if t is None or t.device != dense[0].device:
+                half = (self.nlat + 1) // 2
+                north = [d[:, :half, :].contiguous() for d in dense]
+                if self.vector and direction != self._hot_direction:
+                    north[1] = -north[1]  # the conjugate map (autograd of an inverse transform)
+                t = ops.group_table8(tuple(north) if self.vector else north[0], direction, combine=False)
+                self._grouped8p_fwd = t
+                self.__dict__.pop("_contract_plans", None)
+                self.__dict__.pop("_fast_forward", None)
+            return t, None, layout
         if layout == "grouped8":
             name = "_grouped8_fwd" if direction == _lib.DIR_FORWARD else "_grouped8_inv"
         else:
@@ -299,7 +339,7 @@ def _run(src, direction, inp, out, B, M, in_vec_strides, out_vec_strides, out_co
                                 direction=direction, w0=w0, w1=w1, batch=B, nlat=src.nlat, lmax=src.lmax, mmax=M,
                                 in_strides=in_vec_strides, out_strides=out_vec_strides, out_cols=out_cols,
                                 scale=scale, flags=flags, nlon=nlon, grouped=layout == "grouped",
-                                grouped8=layout == "grouped8")
+                                grouped8=layout in ("grouped8", "parity"), parity=layout == "parity")
         plans[key] = plan
     plan.launch(inp, out)
     return plan

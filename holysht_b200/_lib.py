@@ -22,7 +22,7 @@ DTYPE_C64, DTYPE_F32, DTYPE_BF16 = 0, 1, 2
 KIND_SCALAR, KIND_VECTOR, KIND_REAL = 0, 1, 2
 DIR_FORWARD, DIR_INVERSE = 0, 1
 FLAG_CONJ_W1, FLAG_ROUND_BF16, FLAG_IRFFT_PREP, FLAG_TABLE_SPLIT = 1, 2, 4, 16
-TABLE_STRIDED, TABLE_GROUPED, TABLE_GROUPED8 = 0, 1, 2
+TABLE_STRIDED, TABLE_GROUPED, TABLE_GROUPED8, TABLE_GROUPED8_PARITY = 0, 1, 2, 3
 
 # every symbol include/holysht_b200.h declares
 EXPORTS = (

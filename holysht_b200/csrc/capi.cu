@@ -169,7 +169,8 @@ struct Job {
   float scale;
   int ksplit;
   int grouped;   // HOLYSHT_TABLE_GROUPED
-  int grouped8;  // HOLYSHT_TABLE_GROUPED8 (streaming kernel)
+  int grouped8;  // HOLYSHT_TABLE_GROUPED8 / _PARITY (streaming kernel)
+  int parity;    // HOLYSHT_TABLE_GROUPED8_PARITY: northern-half table, reduction over ceil(K/2) rows
   long long m_off;
   // output to several GPUs (holysht_legendre_contract_peers); n_peers == 0: out only
   void* const* peers;
@@ -257,6 +258,11 @@ int run_job(const Job& j, cudaStream_t stream) {
     if (j.flags & HOLYSHT_FLAG_CONJ_W1)
       return fail(HOLYSHT_ERR_INVALID,
                   "the GROUPED8 layout does not take HOLYSHT_FLAG_CONJ_W1 (build the table from (W0, -W1))");
+    if (j.parity) {
+      if (j.dir != HOLYSHT_DIR_FORWARD)
+        return fail(HOLYSHT_ERR_INVALID, "the GROUPED8_PARITY layout is for the forward direction");
+      return run_stream_job(j, R, (S + 1) / 2, stream);  // reduction over the northern rows
+    }
     return run_stream_job(j, R, S, stream);
   }
   Job jj = j;
@@ -421,11 +427,11 @@ std::pair<int, int> simulate_stream_grid(const hsb::stream::Params& p, int chunk
   return choice;
 }
 
-template <int KIND, int DIR, int NB>
+template <int KIND, int DIR, int NB, bool PAR = false>
 int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStream_t stream) {
-  using Sm = hsb::stream::Smem<KIND, NB>;
+  using Sm = hsb::stream::Smem<KIND, NB, PAR>;
   static std::atomic<unsigned long long> configured{0};
-  auto kernel = hsb::stream::stream_kernel<KIND, DIR, NB>;
+  auto kernel = hsb::stream::stream_kernel<KIND, DIR, NB, PAR>;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
@@ -443,7 +449,7 @@ int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStr
     grid = grid_tiles;
   } else {
     const std::pair<int, int> plan =
-        choose_stream_grid(p, hsb::stream::Shape<KIND>::kChunk, DIR == 0, sm_count_of_current_device());
+        choose_stream_grid(p, hsb::stream::Shape<KIND, PAR>::kChunk, DIR == 0, sm_count_of_current_device());
     p.ks = plan.first;
     grid = (long long)plan.second * p.ks;
   }
@@ -469,6 +475,18 @@ int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStr
 
 template <int KIND, int DIR>
 int stream_nb(const hsb::stream::Params& p, int nb, long long grid_tiles, cudaStream_t stream) {
+  if constexpr (DIR == 0) {
+    if (p.kfull > 0) {  // parity-folded forward
+      switch (nb) {
+        case 1: return launch_stream<KIND, DIR, 1, true>(p, grid_tiles, stream);
+        case 2: return launch_stream<KIND, DIR, 2, true>(p, grid_tiles, stream);
+        case 4: return launch_stream<KIND, DIR, 4, true>(p, grid_tiles, stream);
+        default:
+          if constexpr (KIND == hsb::KIND_SCALAR) return launch_stream<KIND, DIR, 8, true>(p, grid_tiles, stream);
+          return launch_stream<KIND, DIR, 4, true>(p, grid_tiles, stream);
+      }
+    }
+  }
   switch (nb) {
     case 1: return launch_stream<KIND, DIR, 1>(p, grid_tiles, stream);
     case 2: return launch_stream<KIND, DIR, 2>(p, grid_tiles, stream);
@@ -525,6 +543,7 @@ hsb::stream::Params make_stream_params(const Job& j, long long R, long long S, i
   p.n_bg = (int)((j.B + nb - 1) / nb);
   p.ks = j.ksplit ? j.ksplit : env_ksplit();
   p.stall_chunk = env_stall_chunk();
+  p.kfull = j.parity ? (int)j.K : 0;
   p.round_bf16 = (j.flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0;
   p.n_peers = j.n_peers;
   p.col_off = (int)j.col_off;
@@ -1097,12 +1116,13 @@ int contract_impl(const holysht_contract_desc* d, void* const* peers, int n_peer
   j.w_ks = d->w_k_stride;
   j.w_mt = d->w_m_tile_stride ? d->w_m_tile_stride : hsb::kMTile;
   j.grouped = d->table_layout == HOLYSHT_TABLE_GROUPED;
-  j.grouped8 = d->table_layout == HOLYSHT_TABLE_GROUPED8;
+  j.grouped8 = d->table_layout == HOLYSHT_TABLE_GROUPED8 || d->table_layout == HOLYSHT_TABLE_GROUPED8_PARITY;
+  j.parity = d->table_layout == HOLYSHT_TABLE_GROUPED8_PARITY;
   j.m_off = d->m_offset;
   if (j.m_off < 0 || j.m_off % hsb::kMTile != 0 || !fits_int(j.m_off))
     return fail(HOLYSHT_ERR_INVALID, "m_offset must be a non-negative multiple of 32");
   if (d->table_layout != HOLYSHT_TABLE_STRIDED && d->table_layout != HOLYSHT_TABLE_GROUPED &&
-      d->table_layout != HOLYSHT_TABLE_GROUPED8)
+      d->table_layout != HOLYSHT_TABLE_GROUPED8 && d->table_layout != HOLYSHT_TABLE_GROUPED8_PARITY)
     return fail(HOLYSHT_ERR_INVALID, "unknown table_layout %d", d->table_layout);
   j.nlon = d->nlon;
   j.scale = d->scale;

@@ -119,6 +119,7 @@ struct Params {
   int m_off, mt_off;
   int stall_chunk;  // test hook, -1 = off: warp 0 of the first CTA never issues this table stage
   int round_bf16;   // round the staged spectrum to bfloat16 (after the caller's scaling)
+  int kfull;        // PAR launches: the full latitude count K (S is ceil(K / 2))
   // Output to several GPUs (order-partitioned transforms): with n_peers > 0 every
   // output element is stored at column col_off + m of each peer[q] buffer (same
   // strides as out, plain peer stores over NVLink), or, when mc is set, once
@@ -198,24 +199,38 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src, bool ok) {
                "r"(ok ? 8 : 0));
 }
 
-template <int KIND>
+// PAR (equatorial parity, forward direction): the reduction runs over the
+// northern latitudes k < ceil(K/2) only, with the table's southern half
+// folded in by symmetry, W(K-1-k) = s W(k) (W1 and the scalar table) and
+// W0(K-1-k) = -s W0(k), s = (-1)^(l+m), which every grid here has.  The
+// staged spectrum then holds, per step, batch and lane, the combinations of
+// rows k and K-1-k that even-l and odd-l rows multiply (two sets).
+template <int KIND, bool PAR = false>
 struct Shape {
   static constexpr int P = KIND == 1 ? 2 : 1;  // components (KIND_VECTOR = 1)
   static constexpr int T = KIND == 1 ? 2 : 1;  // interleaved tables
   static constexpr int kStepFloats = 32 * kRowsPerWarp * T;  // one warp's step
   static constexpr int kQuads = kRowsPerWarp * T / 4;
-  static constexpr int kChunk = KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S;
+  static constexpr int kChunk = PAR ? (KIND == 1 ? 2 : 4) : (KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S);
 };
 
-template <int KIND, int NB>
+// staged spectrum float2 per lane per step: the planes, or with PAR two
+// parity sets per batch of (A, iB, iC, -D) (vector) / one value (scalar)
+template <int KIND, int NB, bool PAR>
+constexpr int spec_per_step() {
+  return PAR ? (KIND == 1 ? 8 * NB : 2 * NB) : NB * Shape<KIND>::P;
+}
+
+template <int KIND, int NB, bool PAR = false>
 struct Smem {
   static constexpr int P = Shape<KIND>::P;
   static constexpr int PB = NB * P;
+  static constexpr int SX = spec_per_step<KIND, NB, PAR>();
   static constexpr int NA = NB * P;  // complex accumulators per row
-  static constexpr int kSpecBytes = SpecRing<KIND>::kStages * Shape<KIND>::kChunk * PB * 32 * 8;
-  static constexpr int kStageBytes = kCons * Shape<KIND>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
+  static constexpr int kSpecBytes = SpecRing<KIND>::kStages * Shape<KIND, PAR>::kChunk * SX * 32 * 8;
+  static constexpr int kStageBytes = kCons * Shape<KIND, PAR>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
   // table ring depth: the configured one, or as many as fit next to the spectrum ring
-  static constexpr int kWant = KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S;
+  static constexpr int kWant = PAR ? 3 : (KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S);
   static constexpr int kFit = (kSmemLimit - kSpecBytes) / kStageBytes;
   static constexpr int kTabStages = kWant < kFit ? kWant : kFit;
   static_assert(kTabStages >= 2, "table ring needs two stages");
@@ -284,16 +299,18 @@ __device__ __forceinline__ void write_zero_units(const Params& p) {
   }
 }
 
-template <int KIND, int DIR, int NB>
+template <int KIND, int DIR, int NB, bool PAR = false>
 __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
-  using S = Smem<KIND, NB>;
-  constexpr int P = S::P, PB = S::PB, NA = S::NA;
+  static_assert(!PAR || DIR == 0, "parity folding is for the forward direction");
+  static_assert(!PAR || kSplit == 1, "parity folding needs whole row groups per warp (row parity = index parity)");
+  using S = Smem<KIND, NB, PAR>;
+  constexpr int P = S::P, PB = S::PB, NA = S::NA, SX = S::SX;
   constexpr int T = Shape<KIND>::T;
   constexpr int kStepFloats = Shape<KIND>::kStepFloats;
   constexpr int kTabStages = S::kTabStages;
-  constexpr int kChunk = Shape<KIND>::kChunk;
+  constexpr int kChunk = Shape<KIND, PAR>::kChunk;
   constexpr int kStageFloats = kChunk * kStepFloats;  // one warp's table stage
-  constexpr int kSpecStageElems = kChunk * PB * 32;   // float2 per spectrum stage
+  constexpr int kSpecStageElems = kChunk * SX * 32;   // float2 per spectrum stage
   constexpr int kSpecStages = SpecRing<KIND>::kStages;
   constexpr int kSpecAhead = SpecRing<KIND>::kAhead;
 
@@ -302,8 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   float* tab = reinterpret_cast<float*>(smem_raw + S::kSpecBytes);  // [warp][stage][step floats]
   float2* part = reinterpret_cast<float2*>(smem_raw);  // [source rank][owned row][NA][lane], after a tile
   __shared__ __align__(8) uint64_t full_bar[kSpecStages], empty_bar[kSpecStages];
-  __shared__ __align__(8) uint64_t tab_bar[kCons][Smem<KIND, NB>::kTabStages];
-  __shared__ __align__(8) uint64_t tab_free[kCons][Smem<KIND, NB>::kTabStages];  // kSplit > 1: both warps read
+  __shared__ __align__(8) uint64_t tab_bar[kCons][S::kTabStages];
+  __shared__ __align__(8) uint64_t tab_free[kCons][S::kTabStages];  // kSplit > 1: both warps read
 
   cg::cluster_group cluster = cg::this_cluster();
   const int ks = p.ks;
@@ -344,17 +361,58 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   static_assert(kThreads % (NB * 32) == 0, "spectrum staging map");
   const int st_b = (threadIdx.x >> 5) % NB;
   const int st_ls0 = threadIdx.x / (NB * 32);
-  float2* const st_dst = spec + (st_ls0 * PB + st_b * P) * 32 + lane;  // + slot * kSpecStageElems
+  // PAR: the thread's raw copies (rows k and K-1-k) land in its own staged
+  // positions and its combine pass overwrites them (no other thread reads them)
+  float2* const st_dst = PAR ? spec + st_ls0 * SX * 32 + (KIND == 1 ? st_b * 128 + 2 * lane : st_b * 32 + lane)
+                             : spec + (st_ls0 * PB + st_b * P) * 32 + lane;  // + slot * kSpecStageElems
   // the staged values need a pass by the thread that staged them (after its
   // own copies landed) for the vector kind (u, v) and for bfloat16 rounding;
   // otherwise the copies publish themselves
-  const bool sync_stage = KIND == 1 || p.round_bf16 != 0;
+  const bool sync_stage = PAR || KIND == 1 || p.round_bf16 != 0;
   auto bf16 = [](float v) { return __bfloat162float(__float2bfloat16_rn(v)); };
-  auto combine = [&](int slot) {
+  auto rnd = [&](float2 c) { return p.round_bf16 ? make_float2(bf16(c.x), bf16(c.y)) : c; };
+  auto cadd = [](float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); };
+  auto csub = [](float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); };
+  auto ci = [](float2 a) { return make_float2(-a.y, a.x); };  // i * a
+  auto combine = [&](int slot, int c_first_step) {
     float2* d = st_dst + slot * kSpecStageElems;
 #pragma unroll
     for (int it = 0; it < kStageIters; ++it) {
       if (kChunk % kLsStep == 0 || st_ls0 + it * kLsStep < kChunk) {
+        if constexpr (PAR) {
+          // step s of the chunk; the equator row (odd K) pairs with itself
+          const bool eq = (p.kfull & 1) && c_first_step + st_ls0 + it * kLsStep == p.S - 1;
+          const bool odd_lane = (lane & 1) != 0;  // m = m0 + lane with m0 even
+          if constexpr (KIND == 1) {
+            float4* e = reinterpret_cast<float4*>(d + it * kLsStep * SX * 32);
+            // raw: [set 0][pair 0] = (c0, c1) at row k, [set 0][pair 1] = (c0, c1) at row K-1-k
+            const float4 r0 = e[0], r1 = e[32];
+            const float2 c0 = rnd(make_float2(r0.x, r0.y)), c1 = rnd(make_float2(r0.z, r0.w));
+            const float2 d0 = eq ? make_float2(0.f, 0.f) : rnd(make_float2(r1.x, r1.y));
+            const float2 d1 = eq ? make_float2(0.f, 0.f) : rnd(make_float2(r1.z, r1.w));
+            const float2 P0 = cadd(c0, d0), M0 = eq ? make_float2(0.f, 0.f) : csub(c0, d0);
+            const float2 P1 = cadd(c1, d1), M1 = eq ? make_float2(0.f, 0.f) : csub(c1, d1);
+            // even l + m: (A, iB, iC, -D) = (M0, iP1, iP0, -M1); odd: (P0, iM1, iM0, -P1)
+            const float2 nM1 = make_float2(-M1.x, -M1.y), nP1 = make_float2(-P1.x, -P1.y);
+            const float4 e_ab = make_float4(M0.x, M0.y, ci(P1).x, ci(P1).y);
+            const float4 e_cd = make_float4(ci(P0).x, ci(P0).y, nM1.x, nM1.y);
+            const float4 o_ab = make_float4(P0.x, P0.y, ci(M1).x, ci(M1).y);
+            const float4 o_cd = make_float4(ci(M0).x, ci(M0).y, nP1.x, nP1.y);
+            // set 0 is what even rows (even l) read: E where m is even, O where m is odd
+            e[0] = odd_lane ? o_ab : e_ab;
+            e[32] = odd_lane ? o_cd : e_cd;
+            e[NB * 64] = odd_lane ? e_ab : o_ab;
+            e[NB * 64 + 32] = odd_lane ? e_cd : o_cd;
+          } else {
+            float2* e = d + it * kLsStep * SX * 32;
+            const float2 x = rnd(e[0]);
+            const float2 y = eq ? make_float2(0.f, 0.f) : rnd(e[NB * 32]);
+            const float2 pl = cadd(x, y), mi = csub(x, y);
+            e[0] = odd_lane ? mi : pl;          // even rows: P where m is even
+            e[NB * 32] = odd_lane ? pl : mi;    // odd rows
+          }
+          continue;
+        }
         float2* e = d + it * kLsStep * PB * 32;
         if constexpr (KIND == 1) {
           float2 c0 = e[0], c1 = e[32];
@@ -421,6 +479,20 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
           const int s = s0 + it * kLsStep;
           const bool ok = st_ok && s < r_end;
           const float2* src = ok ? st_src + (long long)s * p.in_rs : p.in;
+          if constexpr (PAR) {
+            const float2* src2 = ok ? st_src + (long long)(p.kfull - 1 - s) * p.in_rs : p.in;
+            float2* e = dst + it * kLsStep * SX * 32;
+            if constexpr (KIND == 1) {  // (c0, c1) of row k, then of row K-1-k, as float4s
+              cp_async8(e, ok ? src : p.in, ok);
+              cp_async8(e + 1, ok ? src + p.in_ps : p.in, ok);
+              cp_async8(e + 64, ok ? src2 : p.in, ok);
+              cp_async8(e + 65, ok ? src2 + p.in_ps : p.in, ok);
+            } else {
+              cp_async8(e, ok ? src : p.in, ok);
+              cp_async8(e + NB * 32, ok ? src2 : p.in, ok);
+            }
+            continue;
+          }
 #pragma unroll
           for (int pl = 0; pl < P; ++pl)
             cp_async8(dst + (it * kLsStep * PB + pl) * 32, ok ? src + pl * p.in_ps : p.in, ok);
@@ -468,6 +540,45 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         const float4 v = reinterpret_cast<const float4*>(ts)[(half * kQW + q) * 32 + lane];
         w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
       }
+      if constexpr (PAR) {
+        // set 0 feeds the warp's even rows, set 1 its odd rows (kWRows == 8)
+#pragma unroll
+        for (int set = 0; set < 2; ++set) {
+          if constexpr (KIND == 1) {
+            const float4* xv = reinterpret_cast<const float4*>(xs) + set * NB * 64 + lane;
+            float4 ab[NB], cd[NB];
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+              ab[b] = xv[b * 64];
+              cd[b] = xv[b * 64 + 32];
+            }
+#pragma unroll
+            for (int i = set; i < kWRows; i += 2) {
+              const float w0 = w[2 * i], w1 = w[2 * i + 1];
+#pragma unroll
+              for (int b = 0; b < NB; ++b) {
+                // sph += W0 A + W1 (i B),  tor += W1 (i C) + W0 (-D)
+                acc[i][2 * b] = __ffma2_rn(make_float2(w0, w0), make_float2(ab[b].x, ab[b].y), acc[i][2 * b]);
+                acc[i][2 * b] = __ffma2_rn(make_float2(w1, w1), make_float2(ab[b].z, ab[b].w), acc[i][2 * b]);
+                acc[i][2 * b + 1] =
+                    __ffma2_rn(make_float2(w1, w1), make_float2(cd[b].x, cd[b].y), acc[i][2 * b + 1]);
+                acc[i][2 * b + 1] =
+                    __ffma2_rn(make_float2(w0, w0), make_float2(cd[b].z, cd[b].w), acc[i][2 * b + 1]);
+              }
+            }
+          } else {
+            float2 xv[NB];
+#pragma unroll
+            for (int b = 0; b < NB; ++b) xv[b] = xs[(set * NB + b) * 32 + lane];
+#pragma unroll
+            for (int i = set; i < kWRows; i += 2) {
+#pragma unroll
+              for (int b = 0; b < NB; ++b) acc[i][b] = __ffma2_rn(make_float2(w[i], w[i]), xv[b], acc[i][b]);
+            }
+          }
+        }
+        return;
+      }
       float2 x[PB];
 #pragma unroll
       for (int a = 0; a < PB; ++a) x[a] = xs[a * 32 + lane];
@@ -501,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       if (sync_stage) {
         if (nchunks > 0 && alive) {
           cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk 0 have landed
-          combine(gbase & (kSpecStages - 1));
+          combine(gbase & (kSpecStages - 1), r_begin);
           mbar_arrive(&full_bar[gbase & (kSpecStages - 1)]);
         }
       }
@@ -517,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         if (c + 1 < nchunks) {
           cp_async_wait<kSpecAhead - 1>();  // this thread's copies of chunk c + 1 have landed
           const int s1 = (gbase + c + 1) & (kSpecStages - 1);
-          combine(s1);
+          combine(s1, r_begin + (c + 1) * kChunk);
           mbar_arrive(&full_bar[s1]);
         }
       }
@@ -539,10 +650,10 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         const int s0 = r_begin + c * kChunk;
         if (s0 + kChunk <= r_end) {
 #pragma unroll
-          for (int ls = 0; ls < kChunk; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
+          for (int ls = 0; ls < kChunk; ++ls) step(tsb + ls * kStepFloats, xs + ls * SX * 32);
         } else {
 #pragma unroll 1
-          for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * PB * 32);
+          for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * SX * 32);
         }
         ++consumed;
         // stage consumed by every lane (of both warps of the group): refill it
@@ -575,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     gbase += nchunks;
     tbase += nst;
 
-    if constexpr (KIND == 1) {
+    if constexpr (KIND == 1 && !PAR) {
       // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
 #pragma unroll
       for (int i = 0; i < kWRows; ++i)

@@ -272,7 +272,7 @@ def group_table(tables, direction: int, conj: bool = False, m_offset: int = 0) -
     return out
 
 
-def group_table8(tables, direction: int, conj: bool = False, m_offset: int = 0) -> torch.Tensor:
+def group_table8(tables, direction: int, conj: bool = False, m_offset: int = 0, combine: bool = True) -> torch.Tensor:
     """Table in the ``HOLYSHT_TABLE_GROUPED8`` layout of the streaming kernel.
 
     Rows (l for ``DIR_FORWARD``, k for ``DIR_INVERSE``) in groups of 8; per
@@ -284,7 +284,7 @@ def group_table8(tables, direction: int, conj: bool = False, m_offset: int = 0) 
     diagonal (l < m_offset + column)."""
     if torch.is_tensor(tables):
         tables = (tables,)
-    if len(tables) == 2:
+    if len(tables) == 2 and combine:  # combine=False keeps (W0, W1) as they are
         w0, w1 = tables
         s1 = -1.0 if conj else 1.0
         tables = (w0 + s1 * w1, w0 - s1 * w1)
@@ -357,18 +357,21 @@ def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output:
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
                       scale: float = 1.0, flags: int = 0, nlon: int = 0, ksplit: int = 0,
                       w_strides=None, grouped: bool = False, m_offset: int = 0,
-                      grouped8: bool = False) -> None:
+                      grouped8: bool = False, parity: bool = False) -> None:
     """Strided contraction; strides are (batch, component, row) in elements.
 
     ``w0``/``w1`` are either dense [lmax, nlat, mmax] tables (m contiguous) or
     m-tiled tables from :func:`tile_table` ([lmax, ceil(mmax/32), nlat, 32]);
     ``w_strides`` = (l, k, m-tile) strides in floats overrides the inference.
     ``grouped``: ``w0`` is a :func:`group_table` table (``w1`` unused);
-    ``grouped8``: ``w0`` is a :func:`group_table8` table (streaming kernel)."""
+    ``grouped8``: ``w0`` is a :func:`group_table8` table (streaming kernel);
+    ``parity`` (forward, with ``grouped8``): ``w0`` holds the northern rows only
+    (:func:`group_table8` of ``table[:, :ceil(nlat/2)]``, vector tables not
+    combined), for grids symmetric about the equator."""
     d = _contract_desc(kind=kind, direction=direction, input=input, output=output, w0=w0, w1=w1, batch=batch,
                        nlat=nlat, lmax=lmax, mmax=mmax, in_strides=in_strides, out_strides=out_strides,
                        out_cols=out_cols, scale=scale, flags=flags, nlon=nlon, ksplit=ksplit, w_strides=w_strides,
-                       grouped=grouped, m_offset=m_offset, grouped8=grouped8)
+                       grouped=grouped, m_offset=m_offset, grouped8=grouped8, parity=parity)
     dev = input.device
     with torch.cuda.device(dev):
         _lib.check(_lib.load().holysht_legendre_contract(ctypes.byref(d), _stream(dev)))
@@ -396,7 +399,7 @@ def legendre_contract_peers(peer_ptrs, *, out_col_offset: int = 0, multicast_ptr
 
 def _contract_desc(*, kind, direction, input, output, w0, w1=None, batch, nlat, lmax, mmax, in_strides,
                    out_strides, out_cols, scale=1.0, flags=0, nlon=0, ksplit=0, w_strides=None, grouped=False,
-                   m_offset=0, grouped8=False):
+                   m_offset=0, grouped8=False, parity=False):
     """Checked ``holysht_contract_desc`` for :func:`legendre_contract` / :class:`ContractPlan`."""
     _cuda(output, input, w0)
     if w1 is not None:
@@ -437,7 +440,7 @@ def _contract_desc(*, kind, direction, input, output, w0, w1=None, batch, nlat, 
     d.nlon = nlon
     d.scale = scale
     d.ksplit = ksplit
-    d.table_layout = (_lib.TABLE_GROUPED8 if grouped8 else
+    d.table_layout = (_lib.TABLE_GROUPED8_PARITY if (grouped8 and parity) else _lib.TABLE_GROUPED8 if grouped8 else
                       _lib.TABLE_GROUPED if grouped else _lib.TABLE_STRIDED)
     d.m_offset = m_offset
     return d

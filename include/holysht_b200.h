@@ -191,6 +191,15 @@ typedef struct holysht_contract_desc {
 #define HOLYSHT_TABLE_STRIDED 0
 #define HOLYSHT_TABLE_GROUPED 1
 #define HOLYSHT_TABLE_GROUPED8 2
+/* GROUPED8_PARITY (forward direction, SCALAR and VECTOR kinds): the GROUPED8
+ * layout of the northern rows k < ceil(nlat/2) only (S = ceil(nlat/2) steps),
+ * for grids symmetric about the equator, where the table obeys
+ * W(nlat-1-k) = (-1)^(l+m) W(k) (scalar, and W1 of the vector map) and
+ * W0(nlat-1-k) = -(-1)^(l+m) W0(k).  The vector tables are stored as they are
+ * (t0 = W0, t1 = W1, not their sum and difference).  The kernel reads input
+ * rows k and nlat-1-k together (half the table bytes, and for the scalar
+ * kind half the multiply-adds).  No counterpart in the reference. */
+#define HOLYSHT_TABLE_GROUPED8_PARITY 3
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
