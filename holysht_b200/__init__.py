@@ -231,7 +231,12 @@ class _GroupedTablesMixin:
 
             stream = os.environ.get("HOLYSHT_TABLE_LAYOUT", "grouped8") != "grouped"
             layout = "grouped8" if stream else "grouped"
-            if (stream and direction == _lib.DIR_FORWARD and os.environ.get("HOLYSHT_PARITY", "1") != "0"
+            # the folded layout halves the table bytes; it is the scalar default
+            # (61.5 -> 55.3 us at 512 x 1024 b4).  For the vector map it was measured
+            # slower (124.9 vs 118.8 us: twice the staged spectrum per step), so it is
+            # used there only with HOLYSHT_PARITY=2; HOLYSHT_PARITY=0 turns it off.
+            par = os.environ.get("HOLYSHT_PARITY", "1")
+            if (stream and direction == _lib.DIR_FORWARD and par != "0" and (par == "2" or not self.vector)
                     and self._equatorial_symmetry()):
                 layout = "parity"
         if layout == "parity":

@@ -363,3 +363,47 @@ def test_host_stream_pipeline_matches_module_calls():
         torch.testing.assert_close(o, m(i.to(dev)).cpu(), rtol=0, atol=0)
     with pytest.raises(ValueError, match="pinned"):
         HostStream(m, dev).run([torch.randn(3, 2, 64, 128)], [outs[0]])
+
+
+@pytest.mark.parametrize("vector", [False, True])
+@pytest.mark.parametrize("nlat,nlon,grid", [(33, 64, "equiangular"), (48, 96, "legendre-gauss"),
+                                            (31, 64, "lobatto"), (512, 1024, "equiangular")])
+def test_parity_folded_forward_matches_oracle(monkeypatch, vector, nlat, nlon, grid):
+    """The equatorial-parity layout (northern half of the table, rows k and
+    K-1-k read together; odd nlat has an equator row paired with itself)
+    against the float64 oracle, for both kinds and every grid family."""
+    import holysht_b200 as hs
+
+    monkeypatch.setenv("HOLYSHT_PARITY", "2")
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(nlat + 7 * vector)
+    shape = (5, 2, nlat, nlon) if vector else (5, nlat, nlon)
+    x = rng.standard_normal(shape).astype(np.float32)
+    m = (hs.RealVectorSHT if vector else hs.RealSHT)(nlat, nlon, grid=grid).to(dev)
+    assert m.table(_lib.DIR_FORWARD)[2] == "parity"
+    with torch.no_grad():
+        got = m(torch.from_numpy(x).to(dev)).cpu().numpy()
+    if vector:
+        w = np.stack([m.w0.double().cpu().numpy(), m.w1.double().cpu().numpy()])
+        ref = orc.vector_sht_forward(x.astype(np.float64), w)
+    else:
+        ref = orc.sht_forward(x.astype(np.float64), m.weights.double().cpu().numpy())
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert rel <= 1e-6, rel
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+    upper = np.arange(m.mmax)[None, :] > np.arange(m.lmax)[:, None]
+    assert np.all(got[..., upper] == 0)
+
+
+def test_parity_layout_is_skipped_for_asymmetric_tables():
+    """Tables without the equatorial symmetry (e.g. loaded from elsewhere)
+    fall back to the full layout."""
+    import holysht_b200 as hs
+
+    m = hs.RealSHT(16, 32).to("cuda")
+    assert m.table(_lib.DIR_FORWARD)[2] == "parity"
+    with torch.no_grad():
+        m.weight_t[:, 0, :] += 1.0
+        m.weights.copy_(m.weight_t.permute(2, 0, 1))
+    m._drop_grouped()
+    assert m.table(_lib.DIR_FORWARD)[2] == "grouped8"
