@@ -753,15 +753,19 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
       a_hi = t_hi;
       a_lo = t_lo;
     }
+    // kernels: 0 = split B in shared memory (default), 1 = pre-split B planes,
+    // 2 = the first 8-warp kernel (HSB_TC_MODE selects; 1 and 2 for comparison)
+    const int mode = env_int("HSB_TC_MODE", env_int("HSB_TC_LEGACY", 0) ? 2 : 1);
     dim3 grid((unsigned)((Mrows + 31) / 32), (unsigned)((S + 31) / 32), (unsigned)B), block(32, 8);
-    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(in), xt, xt_lo, (int)B,
+    hsb::tc::transpose_in_kernel<<<grid, block, 0, stream>>>(static_cast<const float2*>(in), xt,
+                                                             mode == 0 ? nullptr : xt_lo, (int)B,
                                                              (int)S, (int)Mrows, in_batch_stride, in_row_stride,
                                                              scale, (flags & HOLYSHT_FLAG_ROUND_BF16) ? 1 : 0);
     if (int st = check_launch("transpose_in")) return st;
     // table: forward [M][L][K] (rows l, reduce k); inverse [M][K][L] (rows k, reduce l)
     // the warp-specialised kernel moves 16-wide k blocks (64-byte swizzle);
     // HSB_TC_LEGACY=1 runs the earlier 32-wide, 8-warp kernel
-    const bool legacy = env_int("HSB_TC_LEGACY", 0) != 0;
+    const bool legacy = mode == 2;
     const unsigned bk = legacy ? hsb::tc::kBK : hsb::tc::kBK2;
     const CUtensorMapSwizzle sw = legacy ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap map_a, map_b, map_a_lo, map_b_lo;
@@ -797,6 +801,8 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
     if (!(configured.load() & bit)) {
       if (cudaFuncSetAttribute(hsb::tc::dense_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                hsb::tc::kSmemBytes) != cudaSuccess ||
+          cudaFuncSetAttribute(hsb::tc::dense_ws3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               hsb::tc::kWs3SmemBytes) != cudaSuccess ||
           cudaFuncSetAttribute(hsb::tc::dense_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                hsb::tc::kWsSmemBytes) != cudaSuccess)
         return fail(HOLYSHT_ERR_UNSUPPORTED, "cannot configure the tensor-core kernel");
@@ -806,8 +812,11 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
       if (legacy)
         hsb::tc::dense_tf32x3_kernel<<<(unsigned)tiles, hsb::tc::kThreads, hsb::tc::kSmemBytes, stream>>>(
             map_a, map_b, map_a_lo, map_b_lo, p);
-      else
+      else if (mode == 1)
         hsb::tc::dense_ws_kernel<<<(unsigned)tiles, hsb::tc::kWsThreads, hsb::tc::kWsSmemBytes, stream>>>(
+            map_a, map_b, map_a_lo, map_b_lo, p);
+      else
+        hsb::tc::dense_ws3_kernel<<<(unsigned)tiles, hsb::tc::kWsThreads, hsb::tc::kWs3SmemBytes, stream>>>(
             map_a, map_b, map_a_lo, map_b_lo, p);
       if (int st = check_launch("dense tcgen05 kernel")) return st;
     }

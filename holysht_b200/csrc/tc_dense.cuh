@@ -498,6 +498,183 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   }
 }
 
+// Variant with the spectrum tile split in shared memory (the library's
+// default): the input transpose writes one fp32 plane (half the bytes of a
+// split plane pair) and the drain warps split each raw B tile into tf32 hi and
+// residual lo, two stages ahead of the MMA (they convert stage kb + 2 before
+// draining block kb).  Stage = A hi, A lo, B raw, B hi, B lo = 64 KiB; three
+// stages.
+constexpr int kStages3 = 3;
+constexpr int kStage3 = 2 * kA2 + 3 * kB2;
+constexpr int kWs3SmemBytes = kStages3 * kStage3 + 1024 + 256;
+
+__global__ void __launch_bounds__(kWsThreads, 1)
+    dense_ws3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    const __grid_constant__ CUtensorMap map_a_lo, const __grid_constant__ CUtensorMap map_b_lo,
+                    const DenseParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages3 * kStage3);
+  uint64_t* empty = full + kStages3;
+  uint64_t* conv = empty + kStages3;
+  uint64_t* d_full = conv + kStages3;
+  uint64_t* d_free = d_full + 2;
+  unsigned* tmem_slot = reinterpret_cast<unsigned*>(d_free + 2);
+
+  int m, lt, nt;
+  if (!decode(p, blockIdx.x, m, lt, nt)) return;  // uniform per CTA
+  const int l0 = (p.inverse ? 0 : m) + lt * kBM;
+  const int n0 = nt * kBN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb0 = p.inverse ? m / kBK2 : 0;  // inverse: the table is zero for l < m
+  const int nk = (p.S + kBK2 - 1) / kBK2 - kb0;
+
+  auto a_hi = [&](int s) { return smem + s * kStage3; };
+  auto a_lo = [&](int s) { return smem + s * kStage3 + kA2; };
+  auto b_hi = [&](int s) { return smem + s * kStage3 + 2 * kA2; };
+  auto b_lo = [&](int s) { return smem + s * kStage3 + 2 * kA2 + kB2; };
+  auto b_raw = [&](int s) { return smem + s * kStage3 + 2 * kA2 + 2 * kB2; };
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages3; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 8);
+    }
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&d_full[q], 1);
+      mbar_init(&d_free[q], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  const unsigned tmem = *tmem_slot;
+  constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages3;
+        if (kb >= kStages3 && !mbar_wait(&empty[s], ((kb / kStages3) - 1) & 1)) break;
+        mbar_expect_tx(&full[s], 2 * kA2 + kB2);
+        const int kc = (kb0 + kb) * kBK2;
+        tma_load_3d(a_hi(s), &map_a, &full[s], kc, l0, m);
+        tma_load_3d(a_lo(s), &map_a_lo, &full[s], kc, l0, m);
+        tma_load_3d(b_raw(s), &map_b, &full[s], kc, n0, m);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages3;
+        const int slot = kb & 1;
+        if (!mbar_wait(&full[s], (kb / kStages3) & 1)) break;
+        if (!mbar_wait(&conv[s], (kb / kStages3) & 1)) break;  // B split by the drain warps
+        if (kb >= 2 && !mbar_wait(&d_free[slot], ((kb >> 1) - 1) & 1)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;\n");
+        const unsigned d = tmem + (unsigned)(slot * kBN);
+        const unsigned ahi = smem_u32(a_hi(s)), alo = smem_u32(a_lo(s));
+        const unsigned bhi = smem_u32(b_hi(s)), blo = smem_u32(b_lo(s));
+#pragma unroll
+        for (int j = 0; j < kBK2 / 8; ++j) {  // 8 tf32 = 32 bytes per k-step
+          const unsigned off = j * 32;
+          mma_tf32(d, sw64_desc(ahi + off), sw64_desc(bhi + off), idesc, j > 0 ? 1u : 0u);
+          mma_tf32(d, sw64_desc(ahi + off), sw64_desc(blo + off), idesc, 1u);
+          mma_tf32(d, sw64_desc(alo + off), sw64_desc(bhi + off), idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+        mma_commit(&d_full[slot]);
+      }
+    }
+  } else {  // drain warps 2..9
+    const int dw = warp - 2;
+    const int quarter = warp & 3;  // the TMEM lanes this warp may read
+    const int col_half = dw >> 2;
+    const unsigned trow = tmem + ((unsigned)(quarter * 32) << 16) + (unsigned)(col_half * (kBN / 2));
+    float acc[kBN / 2];
+#pragma unroll
+    for (int c = 0; c < kBN / 2; ++c) acc[c] = 0.f;
+    // split the raw B tile of stage kb into tf32 hi and fp32 residual lo, in the
+    // same (swizzled) positions, for the tensor core
+    const int dtid = tid - 64;
+    auto convert = [&](int kb) -> bool {
+      const int s = kb % kStages3;
+      const bool ok = mbar_wait(&full[s], (kb / kStages3) & 1);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, ok)) return false;
+      const float4* raw = reinterpret_cast<const float4*>(b_raw(s));
+      float4* hi = reinterpret_cast<float4*>(b_hi(s));
+      float4* lo = reinterpret_cast<float4*>(b_lo(s));
+#pragma unroll
+      for (int i = dtid; i < kB2 / 16; i += 256) {
+        const float4 v = raw[i];
+        const float4 h = make_float4(rna_tf32(v.x), rna_tf32(v.y), rna_tf32(v.z), rna_tf32(v.w));
+        hi[i] = h;
+        lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+      return true;
+    };
+    bool alive = convert(0) && (nk < 2 || convert(1));
+    for (int kb = 0; kb < nk && alive; ++kb) {
+      if (kb + 2 < nk && !convert(kb + 2)) break;
+      const int slot = kb & 1;
+      const bool okw = mbar_wait(&d_full[slot], (kb >> 1) & 1);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, okw)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;\n");
+#pragma unroll
+      for (int cc = 0; cc < kBN / 2; cc += 32) {
+        unsigned r[32];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+              "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+              "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+              "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(trow + (unsigned)(slot * kBN + cc)));
+        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+        for (int q = 0; q < 32; ++q) acc[cc + q] += __uint_as_float(r[q]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;\n");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&d_free[slot]);
+    }
+    const int row = l0 + quarter * 32 + lane;
+    const int nb = n0 + col_half * (kBN / 2);
+    if (row < p.R) {
+      float* dst = p.D + ((size_t)m * p.R + row) * p.N + nb;
+      if (nb + kBN / 2 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < kBN / 8; ++q)
+          reinterpret_cast<float4*>(dst)[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kBN / 2; ++q)
+          if (nb + q < p.N) dst[q] = acc[q];
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // input [B][S][W] complex (orders < M used) -> Xt [M][2B][S] fp32 * scale,
 // optionally rounded to bf16 (after scaling), stored split: xt = rna_tf32(x),
 // xt_lo = x - xt (the residual is exact in fp32)
@@ -523,11 +700,16 @@ __global__ void transpose_in_kernel(const float2* __restrict__ in, float* __rest
         im = __bfloat162float(__float2bfloat16_rn(im));
       }
       const long long off = ((long long)m * (2LL * B) + 2LL * b) * S;
-      const float hre = rna_tf32(re), him = rna_tf32(im);
-      xt[off + sidx] = hre;
-      xt[off + S + sidx] = him;
-      xt_lo[off + sidx] = re - hre;
-      xt_lo[off + S + sidx] = im - him;
+      if (xt_lo == nullptr) {  // one fp32 plane: the GEMM kernel splits it
+        xt[off + sidx] = re;
+        xt[off + S + sidx] = im;
+      } else {
+        const float hre = rna_tf32(re), him = rna_tf32(im);
+        xt[off + sidx] = hre;
+        xt[off + S + sidx] = him;
+        xt_lo[off + sidx] = re - hre;
+        xt_lo[off + S + sidx] = im - him;
+      }
     }
   }
 }
