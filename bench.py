@@ -338,7 +338,14 @@ def run_ours(args, rank, world, local_rank):
     pipe.run(inputs, hout)
     pe.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(ps.elapsed_time(pe) / K)
+    e2e_local = ps.elapsed_time(pe) / K
+    e2e_ms = max_over_ranks(e2e_local)
+    e2e_ranks = [e2e_local]
+    if world > 1:
+        t = torch.zeros(world, device=dev, dtype=torch.float64)
+        t[rank] = e2e_local
+        dist.all_reduce(t)
+        e2e_ranks = [round(v, 5) for v in t.tolist()]
     e2e_ok = bool(torch.allclose(hout[K - 1], vsht(hin[(K - 1) % ring].to(dev)).cpu()))
     h2d = xh.numel() * 4
     d2h = oh.numel() * 8
@@ -380,7 +387,8 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "how": (f"{K} steps through holysht_b200.pipeline.HostStream (pinned host in/out; upload, transform "
                         "and download of consecutive steps overlap on three streams), total / K"),
-                "matches_device_result": e2e_ok, "sequential_ms": round(e2e_seq_ms, 5)},
+                "matches_device_result": e2e_ok, "sequential_ms": round(e2e_seq_ms, 5),
+                "per_rank_ms": e2e_ranks},
         "gpu_launches": launches_per_step * K,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),

@@ -732,9 +732,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       }
       sum.x *= p.scale;
       sum.y *= p.scale;
-      // irfft preparation acts on global columns (an order slice written to
-      // peers starts at column col_off)
-      const int gcol = mm + (p.n_peers ? p.col_off : 0);
+      // irfft preparation acts on global orders: column mm holds order m_off + mm
+      // (an order slice of a partitioned transform starts at m_off)
+      const int gcol = mm + p.m_off;
       if ((p.zero_imag_col0 && gcol == 0) || gcol == p.nyquist) sum.y = 0.f;
       const int b = b0 + a / P, pl = a % P;
       if (b < p.B)

@@ -198,8 +198,7 @@ class _Exchange:
         self._signal = (t, h, [p + base for p in h.buffer_ptrs])
         dist.barrier(group=self.group)  # every rank's signal array is zero before any barrier
         if self.mode == "auto":
-            self.mode = "multicast" if (h.has_multicast_support() if callable(h.has_multicast_support)
-                                        else h.has_multicast_support) and h.multicast_ptr else "peer"
+            self.mode = "multicast" if h.multicast_ptr else "peer"
 
     def buffer(self, shape):
         """(local complex64 tensor, peer pointers, multicast pointer) of the next
