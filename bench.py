@@ -1,17 +1,20 @@
 """Benchmark: RealVectorSHT.forward at 512 x 1024, batch 4, FP32 (the
 reference's headline metric, README.md:79), on N GPUs of one node.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-c5]
 
 One step = one RealVectorSHT.forward (rfft on cuFFT + the fused vector
 Legendre kernel) over a (4, 2, 512, 1024) float32 batch resident in HBM.
 Multi-GPU: batch partition with no collective (every rank transforms its own
 batch of 4, weak scaling); the timing is device time (CUDA events), the max
-over ranks.  The L2 is flushed (256 MiB write) before every timed step.
+over ranks.  The L2 is flushed (256 MiB write, then 256 MiB read) before
+every timed step.  Secondary fields: the scalar, inverse and recurrence
+forwards, the 1024 x 2048 configuration under both multi-GPU partitions, and
+(N = 1) the reference's own CUDA path timed in a child process.
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's
-CPU path restated by the oracle (rfft + per-order GEMMs in numpy/BLAS, all
-host cores) on the same workload, rank 0 only.
+own CPU forward (imported unmodified from ``baseline/_ref``; the oracle's
+restatement when that is absent) on the same workload, rank 0 only.
 """
 from __future__ import annotations
 
