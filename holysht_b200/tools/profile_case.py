@@ -1,7 +1,7 @@
 """Run one Legendre contraction of the module paths at the benchmark size, for
 profilers (ncu -k regex:contract_kernel) and quick timing.
 
-    python -m holysht_b200.tools.profile_case {vector|scalar} [reps] [ksplit] [grouped|grouped8|strided] [inv]
+    python -m holysht_b200.tools.profile_case {vector|scalar} [reps] [ksplit] [grouped|grouped8|parity|strided] [inv]
 
 Builds RealVectorSHT/RealSHT(512, 1024) on cuda:0, runs ``reps`` warm-up
 launches of the forward (or, with ``inv``, the inverse-direction) contraction
@@ -45,10 +45,13 @@ def main(argv):
         Rin, W = L, M
         out = torch.empty((B, P, NLAT, NLON // 2 + 1), dtype=torch.complex64, device=dev)
         Rout, ocols = NLAT, NLON // 2 + 1
-    grouped8 = layout == "grouped8"
-    if layout == "grouped":
+    grouped8 = layout in ("grouped8", "parity")
+    parity = layout == "parity"
+    if parity:
+        w0, w1, grouped = m.table(direction, "parity")[0], None, False
+    elif layout == "grouped":
         w0, w1, grouped = m.table(direction, "grouped")[0], None, True
-    elif grouped8:
+    elif layout == "grouped8":
         from holysht_b200.ops import group_table8
         tabs = dense if kind == "vector" else dense[0]
         w0, w1, grouped = group_table8(tabs, direction, conj=(kind == "vector" and direction == _lib.DIR_INVERSE)), None, False
@@ -60,7 +63,7 @@ def main(argv):
                           batch=B, nlat=NLAT, lmax=L, mmax=M,
                           in_strides=(P * Rin * W, Rin * W, W), out_strides=(P * Rout * ocols, Rout * ocols, ocols),
                           out_cols=ocols, scale=2 * math.pi / NLON, ksplit=ks, grouped=grouped,
-                          grouped8=grouped8)
+                          grouped8=grouped8, parity=parity)
 
     for _ in range(reps):
         launch()
