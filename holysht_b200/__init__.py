@@ -128,6 +128,7 @@ class _GroupedTablesMixin:
         self.register_buffer("_grouped8_fwd", None, persistent=False)
         self.register_buffer("_grouped8_inv", None, persistent=False)
         self.register_buffer("_grouped8p_fwd", None, persistent=False)
+        self.register_buffer("_grouped8p_inv", None, persistent=False)
         # the streaming copies are built on first use, on the tables' device
         # (a GPU builds them in milliseconds; the host takes tens of seconds
         # at 1024 x 2048)
@@ -164,6 +165,7 @@ class _GroupedTablesMixin:
         self._grouped8_fwd = None
         self._grouped8_inv = None
         self._grouped8p_fwd = None
+        self._grouped8p_inv = None
         self.__dict__.pop("_symmetric", None)
         if hasattr(self, "_dense_inv"):
             self._dense_inv = None
@@ -235,12 +237,14 @@ class _GroupedTablesMixin:
             # (61.5 -> 55.3 us at 512 x 1024 b4).  For the vector map it was measured
             # slower (124.9 vs 118.8 us: twice the staged spectrum per step), so it is
             # used there only with HOLYSHT_PARITY=2; HOLYSHT_PARITY=0 turns it off.
+            # the scalar inverse direction folds too (half the table bytes, half the FMAs)
             par = os.environ.get("HOLYSHT_PARITY", "1")
-            if (stream and direction == _lib.DIR_FORWARD and par != "0" and (par == "2" or not self.vector)
+            if (stream and par != "0" and (not self.vector or (par == "2" and direction == _lib.DIR_FORWARD))
                     and self._equatorial_symmetry()):
                 layout = "parity"
         if layout == "parity":
-            t = self._grouped8p_fwd
+            pname = "_grouped8p_fwd" if direction == _lib.DIR_FORWARD else "_grouped8p_inv"
+            t = getattr(self, pname)
             dense = tuple(getattr(self, n) for n in self._table_names)
             if t is None or t.device != dense[0].device:
                 half = (self.nlat + 1) // 2
@@ -248,7 +252,7 @@ class _GroupedTablesMixin:
                 if self.vector and direction != self._hot_direction:
                     north[1] = -north[1]  # the conjugate map (autograd of an inverse transform)
                 t = ops.group_table8(tuple(north) if self.vector else north[0], direction, combine=False)
-                self._grouped8p_fwd = t
+                setattr(self, pname, t)
                 self.__dict__.pop("_contract_plans", None)
                 self.__dict__.pop("_fast_forward", None)
             return t, None, layout

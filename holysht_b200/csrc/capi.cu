@@ -259,9 +259,10 @@ int run_job(const Job& j, cudaStream_t stream) {
       return fail(HOLYSHT_ERR_INVALID,
                   "the GROUPED8 layout does not take HOLYSHT_FLAG_CONJ_W1 (build the table from (W0, -W1))");
     if (j.parity) {
-      if (j.dir != HOLYSHT_DIR_FORWARD)
-        return fail(HOLYSHT_ERR_INVALID, "the GROUPED8_PARITY layout is for the forward direction");
-      return run_stream_job(j, R, (S + 1) / 2, stream);  // reduction over the northern rows
+      if (j.dir == HOLYSHT_DIR_FORWARD) return run_stream_job(j, R, (S + 1) / 2, stream);  // northern steps
+      if (j.kind != HOLYSHT_KIND_SCALAR)
+        return fail(HOLYSHT_ERR_INVALID, "the GROUPED8_PARITY inverse is for the scalar kind");
+      return run_stream_job(j, (R + 1) / 2, S, stream);  // northern output rows, mirrored in the epilogue
     }
     return run_stream_job(j, R, S, stream);
   }
@@ -427,11 +428,11 @@ std::pair<int, int> simulate_stream_grid(const hsb::stream::Params& p, int chunk
   return choice;
 }
 
-template <int KIND, int DIR, int NB, bool PAR = false>
+template <int KIND, int DIR, int NB, int FOLD = 0>
 int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStream_t stream) {
-  using Sm = hsb::stream::Smem<KIND, NB, PAR>;
+  using Sm = hsb::stream::Smem<KIND, NB, FOLD>;
   static std::atomic<unsigned long long> configured{0};
-  auto kernel = hsb::stream::stream_kernel<KIND, DIR, NB, PAR>;
+  auto kernel = hsb::stream::stream_kernel<KIND, DIR, NB, FOLD>;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
@@ -449,7 +450,7 @@ int launch_stream(const hsb::stream::Params& p_in, long long grid_tiles, cudaStr
     grid = grid_tiles;
   } else {
     const std::pair<int, int> plan =
-        choose_stream_grid(p, hsb::stream::Shape<KIND, PAR>::kChunk, DIR == 0, sm_count_of_current_device());
+        choose_stream_grid(p, hsb::stream::Shape<KIND, FOLD>::kChunk, DIR == 0, sm_count_of_current_device());
     p.ks = plan.first;
     grid = (long long)plan.second * p.ks;
   }
@@ -478,12 +479,20 @@ int stream_nb(const hsb::stream::Params& p, int nb, long long grid_tiles, cudaSt
   if constexpr (DIR == 0) {
     if (p.kfull > 0) {  // parity-folded forward
       switch (nb) {
-        case 1: return launch_stream<KIND, DIR, 1, true>(p, grid_tiles, stream);
-        case 2: return launch_stream<KIND, DIR, 2, true>(p, grid_tiles, stream);
-        case 4: return launch_stream<KIND, DIR, 4, true>(p, grid_tiles, stream);
+        case 1: return launch_stream<KIND, DIR, 1, 1>(p, grid_tiles, stream);
+        case 2: return launch_stream<KIND, DIR, 2, 1>(p, grid_tiles, stream);
+        case 4: return launch_stream<KIND, DIR, 4, 1>(p, grid_tiles, stream);
         default:
-          if constexpr (KIND == hsb::KIND_SCALAR) return launch_stream<KIND, DIR, 8, true>(p, grid_tiles, stream);
-          return launch_stream<KIND, DIR, 4, true>(p, grid_tiles, stream);
+          if constexpr (KIND == hsb::KIND_SCALAR) return launch_stream<KIND, DIR, 8, 1>(p, grid_tiles, stream);
+          return launch_stream<KIND, DIR, 4, 1>(p, grid_tiles, stream);
+      }
+    }
+  } else if constexpr (KIND == hsb::KIND_SCALAR) {
+    if (p.kfull > 0) {  // parity-folded scalar inverse (at most 4 batches per CTA: twice the accumulators)
+      switch (nb) {
+        case 1: return launch_stream<KIND, DIR, 1, 2>(p, grid_tiles, stream);
+        case 2: return launch_stream<KIND, DIR, 2, 2>(p, grid_tiles, stream);
+        default: return launch_stream<KIND, DIR, 4, 2>(p, grid_tiles, stream);
       }
     }
   }
@@ -539,7 +548,8 @@ hsb::stream::Params make_stream_params(const Job& j, long long R, long long S, i
   }
   p.n_compute = (int)n_compute;
   p.n_zero = (int)n_zero;
-  const int nb = next_pow2_at_least(j.B, 1, j.kind == HOLYSHT_KIND_VECTOR ? 4 : 8);
+  const bool fold_inv = j.parity && j.dir == HOLYSHT_DIR_INVERSE;  // twice the accumulators: at most 4 batches
+  const int nb = next_pow2_at_least(j.B, 1, (j.kind == HOLYSHT_KIND_VECTOR || fold_inv) ? 4 : 8);
   p.n_bg = (int)((j.B + nb - 1) / nb);
   p.ks = j.ksplit ? j.ksplit : env_ksplit();
   p.stall_chunk = env_stall_chunk();

@@ -238,20 +238,28 @@ __global__ void __launch_bounds__(kMaxWarps * 32) recurrence_forward_pair_kernel
   }
   __syncthreads();  // coefficients staged
 
+  // checkpoints of segment c: (P at lseg, P at lseg + 1) of latitudes 2i and 2i+1
+  // (8-byte aligned pairs: a 16-byte load would be misaligned for odd nlat).
+  // The next segment's are loaded while this one is computed.
+  float2 sa[NP], sb[NP];
+  auto load_seeds = [&](int c) {
+    const float2* sd2 = reinterpret_cast<const float2*>(p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 2);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      sa[i] = k0 + 2 * i < p.K ? sd2[2 * i] : make_float2(0.f, 0.f);
+      sb[i] = k0 + 2 * i + 1 < p.K ? sd2[2 * i + 1] : make_float2(0.f, 0.f);
+    }
+  };
+  load_seeds(c_begin);
   for (int c = c_begin; c < c_end; ++c) {
     const int lseg = m + c * kSeg;
-    const float* sd = p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 2;
     float2 p1[NP], p2[NP];  // P at degrees l-1 and l-2 of each latitude pair
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
-      // (P at lseg, P at lseg + 1) of latitudes 2i and 2i+1: 8-byte aligned pairs
-      // (a 16-byte load would be misaligned for odd nlat)
-      const float2* sd2 = reinterpret_cast<const float2*>(sd);
-      const float2 a = k0 + 2 * i < p.K ? sd2[2 * i] : make_float2(0.f, 0.f);
-      const float2 bq = k0 + 2 * i + 1 < p.K ? sd2[2 * i + 1] : make_float2(0.f, 0.f);
-      p2[i] = make_float2(a.x, bq.x);  // degree lseg
-      p1[i] = make_float2(a.y, bq.y);  // degree lseg + 1
+      p2[i] = make_float2(sa[i].x, sb[i].x);  // degree lseg
+      p1[i] = make_float2(sa[i].y, sb[i].y);  // degree lseg + 1
     }
+    if (c + 1 < c_end) load_seeds(c + 1);
 #pragma unroll
     for (int qb = 0; qb < kSeg; qb += 4) {
       float v[32];  // 4 degrees x (4 batches x re/im)

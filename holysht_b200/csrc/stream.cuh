@@ -47,6 +47,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace hsb {
 namespace stream {
 
@@ -205,32 +207,34 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src, bool ok) {
 // W0(K-1-k) = -s W0(k), s = (-1)^(l+m), which every grid here has.  The
 // staged spectrum then holds, per step, batch and lane, the combinations of
 // rows k and K-1-k that even-l and odd-l rows multiply (two sets).
-template <int KIND, bool PAR = false>
+template <int KIND, int FOLD = 0>
 struct Shape {
   static constexpr int P = KIND == 1 ? 2 : 1;  // components (KIND_VECTOR = 1)
   static constexpr int T = KIND == 1 ? 2 : 1;  // interleaved tables
   static constexpr int kStepFloats = 32 * kRowsPerWarp * T;  // one warp's step
   static constexpr int kQuads = kRowsPerWarp * T / 4;
-  static constexpr int kChunk = PAR ? (KIND == 1 ? 2 : 4) : (KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S);
+  static constexpr int kChunk = FOLD == 1 ? (KIND == 1 ? 2 : 4) : (KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S);
 };
 
 // staged spectrum float2 per lane per step: the planes, or with PAR two
 // parity sets per batch of (A, iB, iC, -D) (vector) / one value (scalar)
-template <int KIND, int NB, bool PAR>
+template <int KIND, int NB, int FOLD>
 constexpr int spec_per_step() {
-  return PAR ? (KIND == 1 ? 8 * NB : 2 * NB) : NB * Shape<KIND>::P;
+  return FOLD == 1 ? (KIND == 1 ? 8 * NB : 2 * NB) : NB * Shape<KIND>::P;
 }
 
-template <int KIND, int NB, bool PAR = false>
+// FOLD: 0 none, 1 forward parity fold, 2 inverse parity fold (scalar: every
+// row accumulates its even-step and odd-step sums apart, NA = 2 NB)
+template <int KIND, int NB, int FOLD = 0>
 struct Smem {
   static constexpr int P = Shape<KIND>::P;
   static constexpr int PB = NB * P;
-  static constexpr int SX = spec_per_step<KIND, NB, PAR>();
-  static constexpr int NA = NB * P;  // complex accumulators per row
-  static constexpr int kSpecBytes = SpecRing<KIND>::kStages * Shape<KIND, PAR>::kChunk * SX * 32 * 8;
-  static constexpr int kStageBytes = kCons * Shape<KIND, PAR>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
+  static constexpr int SX = spec_per_step<KIND, NB, FOLD>();
+  static constexpr int NA = (FOLD == 2 ? 2 : 1) * NB * P;  // complex accumulators per row
+  static constexpr int kSpecBytes = SpecRing<KIND>::kStages * Shape<KIND, FOLD>::kChunk * SX * 32 * 8;
+  static constexpr int kStageBytes = kCons * Shape<KIND, FOLD>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
   // table ring depth: the configured one, or as many as fit next to the spectrum ring
-  static constexpr int kWant = PAR ? 3 : (KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S);
+  static constexpr int kWant = FOLD == 1 ? 3 : (KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S);
   static constexpr int kFit = (kSmemLimit - kSpecBytes) / kStageBytes;
   static constexpr int kTabStages = kWant < kFit ? kWant : kFit;
   static_assert(kTabStages >= 2, "table ring needs two stages");
@@ -292,23 +296,33 @@ __device__ __forceinline__ void write_zero_units(const Params& p) {
       const int a = (e >> 5) % (NB * P);
       const int row = r0 + e / (NB * P * 32);
       const int mm = m0 + col, b = b0 + a / P, pl = a % P;
-      if (mm < p.out_cols && b < p.B)
+      if (mm < p.out_cols && b < p.B) {
         store_out(p, (long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs + mm,
                   make_float2(0.f, 0.f));
+        // inverse fold: the tile's rows are the northern rows; zero their mirrors too
+        if (DIR == 1 && p.kfull > 0 && p.kfull - 1 - row != row)
+          store_out(p, (long long)b * p.out_bs + (long long)pl * p.out_ps +
+                           (long long)(p.kfull - 1 - row) * p.out_rs + mm,
+                    make_float2(0.f, 0.f));
+      }
     }
   }
 }
 
-template <int KIND, int DIR, int NB, bool PAR = false>
+template <int KIND, int DIR, int NB, int FOLD = 0>
 __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
-  static_assert(!PAR || DIR == 0, "parity folding is for the forward direction");
+  constexpr bool PAR = FOLD == 1;   // forward fold
+  constexpr bool IPAR = FOLD == 2;  // inverse fold
+  static_assert(!PAR || DIR == 0, "the forward parity fold is for the forward direction");
+  static_assert(!IPAR || (DIR == 1 && KIND == 0), "the inverse parity fold is for the scalar inverse direction");
   static_assert(!PAR || kSplit == 1, "parity folding needs whole row groups per warp (row parity = index parity)");
-  using S = Smem<KIND, NB, PAR>;
+  using S = Smem<KIND, NB, FOLD>;
   constexpr int P = S::P, PB = S::PB, NA = S::NA, SX = S::SX;
   constexpr int T = Shape<KIND>::T;
   constexpr int kStepFloats = Shape<KIND>::kStepFloats;
   constexpr int kTabStages = S::kTabStages;
-  constexpr int kChunk = Shape<KIND, PAR>::kChunk;
+  constexpr int kChunk = Shape<KIND, FOLD>::kChunk;
+  static_assert(!IPAR || kChunk % 2 == 0, "the inverse fold alternates accumulators by step");
   constexpr int kStageFloats = kChunk * kStepFloats;  // one warp's table stage
   constexpr int kSpecStageElems = kChunk * SX * 32;   // float2 per spectrum stage
   constexpr int kSpecStages = SpecRing<KIND>::kStages;
@@ -530,7 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     }
     int issued = min(kTabStages, nst);
 
-    auto step = [&](const float* ts, const float2* xs) {
+    auto step = [&](const float* ts, const float2* xs, auto hc) {
+      // hc: step parity within the chunk (inverse fold: which accumulator half)
+      constexpr int H = decltype(hc)::value;
       // ts: this step's table block; xs: this step's staged spectrum planes
       // (vector: planes 2b, 2b+1 hold u, v of batch b)
       constexpr int kQW = Shape<KIND>::kQuads / kSplit;  // quads of this warp's rows
@@ -594,7 +610,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         } else {
           const float wv = w[i];
 #pragma unroll
-          for (int b = 0; b < NB; ++b) acc[i][b] = __ffma2_rn(make_float2(wv, wv), x[b], acc[i][b]);
+          for (int b = 0; b < NB; ++b)
+            acc[i][(IPAR ? H * NB : 0) + b] =
+                __ffma2_rn(make_float2(wv, wv), x[b], acc[i][(IPAR ? H * NB : 0) + b]);
         }
       }
     };
@@ -650,10 +668,19 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         const int s0 = r_begin + c * kChunk;
         if (s0 + kChunk <= r_end) {
 #pragma unroll
-          for (int ls = 0; ls < kChunk; ++ls) step(tsb + ls * kStepFloats, xs + ls * SX * 32);
+          for (int ls = 0; ls < kChunk; ls += 2) {
+            step(tsb + ls * kStepFloats, xs + ls * SX * 32, std::integral_constant<int, 0>{});
+            if (kChunk > 1)
+              step(tsb + (ls + 1) * kStepFloats, xs + (ls + 1) * SX * 32, std::integral_constant<int, 1>{});
+          }
         } else {
 #pragma unroll 1
-          for (int ls = 0; ls < r_end - s0; ++ls) step(tsb + ls * kStepFloats, xs + ls * SX * 32);
+          for (int ls = 0; ls < r_end - s0; ++ls) {
+            if (ls & 1)
+              step(tsb + ls * kStepFloats, xs + ls * SX * 32, std::integral_constant<int, 1>{});
+            else
+              step(tsb + ls * kStepFloats, xs + ls * SX * 32, std::integral_constant<int, 0>{});
+          }
         }
         ++consumed;
         // stage consumed by every lane (of both warps of the group): refill it
@@ -686,6 +713,20 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     gbase += nchunks;
     tbase += nst;
 
+    if constexpr (IPAR) {
+      // accumulator halves: A = steps l with l = r_begin (mod 2), B = the others.
+      // With e / o the sums over even / odd l + m (m = m0 + lane, m0 even), the
+      // northern row k receives e + o and its mirror K-1-k receives e - o.
+      const bool a_is_even = ((r_begin + lane) & 1) == 0;
+#pragma unroll
+      for (int i = 0; i < kWRows; ++i)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const float2 A = acc[i][b], Bv = acc[i][NB + b];
+          acc[i][b] = make_float2(A.x + Bv.x, A.y + Bv.y);
+          acc[i][NB + b] = a_is_even ? make_float2(A.x - Bv.x, A.y - Bv.y) : make_float2(Bv.x - A.x, Bv.y - A.y);
+        }
+    }
     if constexpr (KIND == 1 && !PAR) {
       // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
 #pragma unroll
@@ -736,6 +777,13 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       // (an order slice of a partitioned transform starts at m_off)
       const int gcol = mm + p.m_off;
       if ((p.zero_imag_col0 && gcol == 0) || gcol == p.nyquist) sum.y = 0.f;
+      if constexpr (IPAR) {  // a < NB: northern row; a >= NB: its mirror (not the equator twice)
+        const int b = b0 + a % NB;
+        const int orow = a < NB ? row : p.kfull - 1 - row;
+        if (b < p.B && (a < NB || orow != row))
+          store_out(p, (long long)b * p.out_bs + (long long)orow * p.out_rs + mm, sum);
+        continue;
+      }
       const int b = b0 + a / P, pl = a % P;
       if (b < p.B)
         store_out(p, (long long)b * p.out_bs + (long long)pl * p.out_ps + (long long)row * p.out_rs + mm, sum);
