@@ -237,10 +237,17 @@ class _GroupedTablesMixin:
             # (61.5 -> 55.3 us at 512 x 1024 b4).  For the vector map it was measured
             # slower (124.9 vs 118.8 us: twice the staged spectrum per step), so it is
             # used there only with HOLYSHT_PARITY=2; HOLYSHT_PARITY=0 turns it off.
-            # the scalar inverse direction folds too (half the table bytes, half the FMAs)
+            # The scalar inverse direction can fold too (half the table bytes and FMAs),
+            # but with half the output rows it has half the work items and was measured
+            # slower at 512 x 1024 b4 (85 vs 77 us per InverseRealSHT.forward), so it
+            # is used only with HOLYSHT_PARITY_INV=1.
             par = os.environ.get("HOLYSHT_PARITY", "1")
-            if (stream and par != "0" and (not self.vector or (par == "2" and direction == _lib.DIR_FORWARD))
-                    and self._equatorial_symmetry()):
+            fold_inv = os.environ.get("HOLYSHT_PARITY_INV", "0") == "1"
+            if direction == _lib.DIR_FORWARD:
+                want = par != "0" and (not self.vector or par == "2")
+            else:
+                want = fold_inv and not self.vector
+            if stream and want and self._equatorial_symmetry():
                 layout = "parity"
         if layout == "parity":
             pname = "_grouped8p_fwd" if direction == _lib.DIR_FORWARD else "_grouped8p_inv"

@@ -411,13 +411,14 @@ def test_parity_layout_is_skipped_for_asymmetric_tables():
 
 @pytest.mark.parametrize("nlat,nlon,grid", [(33, 64, "equiangular"), (48, 96, "legendre-gauss"),
                                             (31, 64, "lobatto"), (512, 1024, "equiangular")])
-def test_parity_folded_scalar_inverse_matches_oracle(nlat, nlon, grid):
+def test_parity_folded_scalar_inverse_matches_oracle(monkeypatch, nlat, nlon, grid):
     """The scalar inverse on the parity fold (northern output rows, their mirrors
     written from the even/odd-degree sums; irfft preparation and zero columns on
     both halves) against the float64 oracle, and the RealSHT gradient that runs
     the same folded inverse."""
     import holysht_b200 as hs
 
+    monkeypatch.setenv("HOLYSHT_PARITY_INV", "1")
     dev = torch.device("cuda")
     rng = np.random.default_rng(nlat + 3)
     inv = hs.InverseRealSHT(nlat, nlon, grid=grid).to(dev)
