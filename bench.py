@@ -37,7 +37,9 @@ NLAT, NLON, BATCH = 512, 1024, 4
 METRIC = "RealVectorSHT.forward ms @512x1024 b4 fp32"
 UNIT = "ms"
 PUBLISHED_GB10_MS = 6.855  # the published HOLYSHT RealVectorSHT.forward 512x1024 b4 time on GB10
-PROFILE = ROOT / "profiles" / "stream_vector_fwd_512x1024_b4.md"
+# committed ncu summaries of the vector kernel, per table layout of the module's forward
+PROFILES = {"parity": ROOT / "profiles" / "stream_vector_parity_fwd_512x1024_b4.md",
+            "grouped8": ROOT / "profiles" / "stream_vector_fwd_512x1024_b4.md"}
 
 
 def parse():
@@ -116,12 +118,13 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ ours
 
-def _traffic_from_profile():
-    """DRAM bytes per launch of the vector kernel from the committed ncu summary."""
+def _traffic_from_profile(layout):
+    """DRAM bytes per launch of the vector kernel from the committed ncu summary
+    of the table layout the module uses."""
     try:
-        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", PROFILE.read_text())
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", PROFILES[layout].read_text())
         return float(m.group(1)) if m else None
-    except OSError:
+    except (OSError, KeyError):
         return None
 
 
@@ -355,7 +358,7 @@ def run_ours(args, rank, world, local_rank):
 
     peaks, peak_kind = _peaks()
     achieved = abytes / (kernel_ms * 1e-3) / 1e9
-    traffic = _traffic_from_profile()
+    traffic = _traffic_from_profile(layout)
 
     cpu = ref_cuda = None
     if rank == 0 and world == 1:

@@ -233,10 +233,9 @@ class _GroupedTablesMixin:
 
             stream = os.environ.get("HOLYSHT_TABLE_LAYOUT", "grouped8") != "grouped"
             layout = "grouped8" if stream else "grouped"
-            # the folded layout halves the table bytes; it is the scalar default
-            # (61.5 -> 55.3 us at 512 x 1024 b4).  For the vector map it was measured
-            # slower (124.9 vs 118.8 us: twice the staged spectrum per step), so it is
-            # used there only with HOLYSHT_PARITY=2; HOLYSHT_PARITY=0 turns it off.
+            # the folded layout halves the table bytes; it is the forward default
+            # (512 x 1024 b4: scalar 61.5 -> 57.3 us, vector 118.8 -> 98.3 us);
+            # HOLYSHT_PARITY=0 turns it off.
             # The scalar inverse direction can fold too (half the table bytes and FMAs),
             # but with half the output rows it has half the work items and was measured
             # slower at 512 x 1024 b4 (85 vs 77 us per InverseRealSHT.forward), so it
@@ -244,7 +243,7 @@ class _GroupedTablesMixin:
             par = os.environ.get("HOLYSHT_PARITY", "1")
             fold_inv = os.environ.get("HOLYSHT_PARITY_INV", "0") == "1"
             if direction == _lib.DIR_FORWARD:
-                want = par != "0" and (not self.vector or par == "2")
+                want = par != "0"
             else:
                 want = fold_inv and not self.vector
             if stream and want and self._equatorial_symmetry():
@@ -256,8 +255,13 @@ class _GroupedTablesMixin:
             if t is None or t.device != dense[0].device:
                 half = (self.nlat + 1) // 2
                 north = [d[:, :half, :].contiguous() for d in dense]
-                if self.vector and direction != self._hot_direction:
-                    north[1] = -north[1]  # the conjugate map (autograd of an inverse transform)
+                if self.vector:
+                    # (Wp, Wn) = (W0 + c W1, -(-1)^l (W0 - c W1)), c = -1 for the
+                    # conjugate map (autograd of an inverse transform)
+                    c = -1.0 if direction != self._hot_direction else 1.0
+                    w0, w1 = north
+                    lsign = 1.0 - 2.0 * (torch.arange(w0.shape[0], device=w0.device) % 2).float()
+                    north = [w0 + c * w1, -lsign[:, None, None] * (w0 - c * w1)]
                 t = ops.group_table8(tuple(north) if self.vector else north[0], direction, combine=False)
                 setattr(self, pname, t)
                 self.__dict__.pop("_contract_plans", None)

@@ -58,11 +58,15 @@ namespace cg = cooperative_groups;
 #define HSB_STREAM_SPLIT 1
 #endif
 constexpr int kCons = 8;                       // row groups of 8 (one table ring each) per CTA
-constexpr int kSplit = HSB_STREAM_SPLIT;       // warps sharing one row group (1 or 2)
+// warps sharing one row group (1 or 2): each reads the group's whole table
+// stage and accumulates all 8 rows for its share of the CTA's batches (twice
+// the warps per SM to hide latency, half the registers per thread; the
+// spectrum is not read twice)
+constexpr int kSplit = HSB_STREAM_SPLIT;
 constexpr int kWarps = kCons * kSplit;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRowsPerWarp = 8;                // rows of a table group
-constexpr int kWRows = kRowsPerWarp / kSplit;  // rows one warp accumulates
+constexpr int kWRows = kRowsPerWarp;           // rows one warp accumulates
 constexpr int kRows = kCons * kRowsPerWarp;    // 64 output rows per CTA
 constexpr int kMTile = 32;
 #ifndef HSB_STREAM_CHUNK_V
@@ -93,11 +97,30 @@ constexpr int kMaxChunk = HSB_STREAM_CHUNK_V > HSB_STREAM_CHUNK_S ? HSB_STREAM_C
 #ifndef HSB_STREAM_SPEC_AHEAD_V
 #define HSB_STREAM_SPEC_AHEAD_V HSB_STREAM_SPEC_AHEAD
 #endif
+// the parity-folded vector forward: 4 steps per chunk; its spectrum stage is
+// twice the unfolded one, and the 4-stage spectrum ring (3 ahead) leaves room
+// for 2 table stages.  Measured at 512 x 1024 b4: spectrum depth matters more
+// than table depth (2 stages 1 ahead with 3 table stages: 114 vs 98 us)
+#ifndef HSB_STREAM_PAR_CHUNK_V
+#define HSB_STREAM_PAR_CHUNK_V 4
+#endif
+#ifndef HSB_STREAM_PAR_SPEC_STAGES_V
+#define HSB_STREAM_PAR_SPEC_STAGES_V 4
+#endif
+#ifndef HSB_STREAM_PAR_SPEC_AHEAD_V
+#define HSB_STREAM_PAR_SPEC_AHEAD_V 3
+#endif
+#ifndef HSB_STREAM_PAR_TAB_STAGES_V
+#define HSB_STREAM_PAR_TAB_STAGES_V 2
+#endif
 // spectrum ring depth and chunks staged ahead of the one being read, per kind
-template <int KIND>
+template <int KIND, int FOLD = 0>
 struct SpecRing {
-  static constexpr int kStages = KIND == 1 ? HSB_STREAM_SPEC_STAGES_V : HSB_STREAM_SPEC_STAGES;
-  static constexpr int kAhead = KIND == 1 ? HSB_STREAM_SPEC_AHEAD_V : HSB_STREAM_SPEC_AHEAD;
+  static constexpr bool kParV = KIND == 1 && FOLD == 1;
+  static constexpr int kStages =
+      kParV ? HSB_STREAM_PAR_SPEC_STAGES_V : KIND == 1 ? HSB_STREAM_SPEC_STAGES_V : HSB_STREAM_SPEC_STAGES;
+  static constexpr int kAhead =
+      kParV ? HSB_STREAM_PAR_SPEC_AHEAD_V : KIND == 1 ? HSB_STREAM_SPEC_AHEAD_V : HSB_STREAM_SPEC_AHEAD;
   static_assert(kStages >= kAhead + 1 && kAhead >= 1, "spectrum ring too shallow");
   static_assert((kStages & (kStages - 1)) == 0, "spectrum ring depth is a power of two");
 };
@@ -204,23 +227,32 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src, bool ok) {
 // PAR (equatorial parity, forward direction): the reduction runs over the
 // northern latitudes k < ceil(K/2) only, with the table's southern half
 // folded in by symmetry, W(K-1-k) = s W(k) (W1 and the scalar table) and
-// W0(K-1-k) = -s W0(k), s = (-1)^(l+m), which every grid here has.  The
-// staged spectrum then holds, per step, batch and lane, the combinations of
-// rows k and K-1-k that even-l and odd-l rows multiply (two sets).
+// W0(K-1-k) = -s W0(k), s = (-1)^(l+m), which every grid here has.
+//   scalar: the staged spectrum holds, per step, batch and lane, the
+//     combinations X(k) + X(K-1-k) and X(k) - X(K-1-k) that even-l and odd-l
+//     rows multiply (two sets);
+//   vector: with Wp = W0 + W1, Wm = W0 - W1 (the unfolded kernel's tables),
+//     Wp(K-1-k) = -s Wm(k) and Wm(K-1-k) = -s Wp(k).  The table stores
+//     (Wp, Wn) with Wn = -(-1)^l Wm, and the staged spectrum holds
+//     (u, t u') and (v, t v'), u = c0 + i c1, v = c0 - i c1 of row k, u', v'
+//     of row K-1-k, t = (-1)^m; then, per row,
+//       pu = sum_k Wp u + Wn (t u'),   mv = -(-1)^l sum_k Wn v + Wp (t v')
+//     are the unfolded kernel's two sums, with no sign in the inner loop.
 template <int KIND, int FOLD = 0>
 struct Shape {
   static constexpr int P = KIND == 1 ? 2 : 1;  // components (KIND_VECTOR = 1)
   static constexpr int T = KIND == 1 ? 2 : 1;  // interleaved tables
   static constexpr int kStepFloats = 32 * kRowsPerWarp * T;  // one warp's step
   static constexpr int kQuads = kRowsPerWarp * T / 4;
-  static constexpr int kChunk = FOLD == 1 ? (KIND == 1 ? 2 : 4) : (KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S);
+  static constexpr int kChunk =
+      FOLD == 1 ? (KIND == 1 ? HSB_STREAM_PAR_CHUNK_V : 4) : (KIND == 1 ? HSB_STREAM_CHUNK_V : HSB_STREAM_CHUNK_S);
 };
 
-// staged spectrum float2 per lane per step: the planes, or with PAR two
-// parity sets per batch of (A, iB, iC, -D) (vector) / one value (scalar)
+// staged spectrum float2 per lane per step: the planes, or with PAR per
+// batch (u, t u', v, t v') (vector) / two parity sets of one value (scalar)
 template <int KIND, int NB, int FOLD>
 constexpr int spec_per_step() {
-  return FOLD == 1 ? (KIND == 1 ? 8 * NB : 2 * NB) : NB * Shape<KIND>::P;
+  return FOLD == 1 ? (KIND == 1 ? 4 * NB : 2 * NB) : NB * Shape<KIND>::P;
 }
 
 // FOLD: 0 none, 1 forward parity fold, 2 inverse parity fold (scalar: every
@@ -231,10 +263,11 @@ struct Smem {
   static constexpr int PB = NB * P;
   static constexpr int SX = spec_per_step<KIND, NB, FOLD>();
   static constexpr int NA = (FOLD == 2 ? 2 : 1) * NB * P;  // complex accumulators per row
-  static constexpr int kSpecBytes = SpecRing<KIND>::kStages * Shape<KIND, FOLD>::kChunk * SX * 32 * 8;
+  static constexpr int kSpecBytes = SpecRing<KIND, FOLD>::kStages * Shape<KIND, FOLD>::kChunk * SX * 32 * 8;
   static constexpr int kStageBytes = kCons * Shape<KIND, FOLD>::kChunk * Shape<KIND>::kStepFloats * 4;  // all warps
   // table ring depth: the configured one, or as many as fit next to the spectrum ring
-  static constexpr int kWant = FOLD == 1 ? 3 : (KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S);
+  static constexpr int kWant = FOLD == 1 ? (KIND == 1 ? HSB_STREAM_PAR_TAB_STAGES_V : 3)
+                                         : (KIND == 1 ? HSB_STREAM_TAB_STAGES_V : HSB_STREAM_TAB_STAGES_S);
   static constexpr int kFit = (kSmemLimit - kSpecBytes) / kStageBytes;
   static constexpr int kTabStages = kWant < kFit ? kWant : kFit;
   static_assert(kTabStages >= 2, "table ring needs two stages");
@@ -315,9 +348,13 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   constexpr bool IPAR = FOLD == 2;  // inverse fold
   static_assert(!PAR || DIR == 0, "the forward parity fold is for the forward direction");
   static_assert(!IPAR || (DIR == 1 && KIND == 0), "the inverse parity fold is for the scalar inverse direction");
-  static_assert(!PAR || kSplit == 1, "parity folding needs whole row groups per warp (row parity = index parity)");
   using S = Smem<KIND, NB, FOLD>;
   constexpr int P = S::P, PB = S::PB, NA = S::NA, SX = S::SX;
+  // batches of this warp: NBW of the CTA's NB, from bh * NBW (a CTA of one
+  // batch leaves its second warps idle)
+  constexpr int NBW = NB >= kSplit ? NB / kSplit : NB;
+  static_assert(NB % NBW == 0, "batch split");
+  constexpr int NAW = (FOLD == 2 ? 2 : 1) * NBW * P;  // this warp's accumulators per row
   constexpr int T = Shape<KIND>::T;
   constexpr int kStepFloats = Shape<KIND>::kStepFloats;
   constexpr int kTabStages = S::kTabStages;
@@ -325,8 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   static_assert(!IPAR || kChunk % 2 == 0, "the inverse fold alternates accumulators by step");
   constexpr int kStageFloats = kChunk * kStepFloats;  // one warp's table stage
   constexpr int kSpecStageElems = kChunk * SX * 32;   // float2 per spectrum stage
-  constexpr int kSpecStages = SpecRing<KIND>::kStages;
-  constexpr int kSpecAhead = SpecRing<KIND>::kAhead;
+  constexpr int kSpecStages = SpecRing<KIND, FOLD>::kStages;
+  constexpr int kSpecAhead = SpecRing<KIND, FOLD>::kAhead;
 
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float2* spec = reinterpret_cast<float2*>(smem_raw);               // [stage][step][plane][lane]
@@ -385,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
   const bool sync_stage = PAR || KIND == 1 || p.round_bf16 != 0;
   auto bf16 = [](float v) { return __bfloat162float(__float2bfloat16_rn(v)); };
   auto rnd = [&](float2 c) { return p.round_bf16 ? make_float2(bf16(c.x), bf16(c.y)) : c; };
+  int m0g_cur = 0;  // first global order of the current item (parity of m)
   auto cadd = [](float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); };
   auto csub = [](float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); };
   auto ci = [](float2 a) { return make_float2(-a.y, a.x); };  // i * a
@@ -396,27 +434,19 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         if constexpr (PAR) {
           // step s of the chunk; the equator row (odd K) pairs with itself
           const bool eq = (p.kfull & 1) && c_first_step + st_ls0 + it * kLsStep == p.S - 1;
-          const bool odd_lane = (lane & 1) != 0;  // m = m0 + lane with m0 even
+          const bool odd_lane = ((m0g_cur + lane) & 1) != 0;  // odd order m
           if constexpr (KIND == 1) {
             float4* e = reinterpret_cast<float4*>(d + it * kLsStep * SX * 32);
-            // raw: [set 0][pair 0] = (c0, c1) at row k, [set 0][pair 1] = (c0, c1) at row K-1-k
+            // raw: e[0] = (c0, c1) at row k, e[32] = (c0, c1) at row K-1-k
             const float4 r0 = e[0], r1 = e[32];
             const float2 c0 = rnd(make_float2(r0.x, r0.y)), c1 = rnd(make_float2(r0.z, r0.w));
-            const float2 d0 = eq ? make_float2(0.f, 0.f) : rnd(make_float2(r1.x, r1.y));
-            const float2 d1 = eq ? make_float2(0.f, 0.f) : rnd(make_float2(r1.z, r1.w));
-            const float2 P0 = cadd(c0, d0), M0 = eq ? make_float2(0.f, 0.f) : csub(c0, d0);
-            const float2 P1 = cadd(c1, d1), M1 = eq ? make_float2(0.f, 0.f) : csub(c1, d1);
-            // even l + m: (A, iB, iC, -D) = (M0, iP1, iP0, -M1); odd: (P0, iM1, iM0, -P1)
-            const float2 nM1 = make_float2(-M1.x, -M1.y), nP1 = make_float2(-P1.x, -P1.y);
-            const float4 e_ab = make_float4(M0.x, M0.y, ci(P1).x, ci(P1).y);
-            const float4 e_cd = make_float4(ci(P0).x, ci(P0).y, nM1.x, nM1.y);
-            const float4 o_ab = make_float4(P0.x, P0.y, ci(M1).x, ci(M1).y);
-            const float4 o_cd = make_float4(ci(M0).x, ci(M0).y, nP1.x, nP1.y);
-            // set 0 is what even rows (even l) read: E where m is even, O where m is odd
-            e[0] = odd_lane ? o_ab : e_ab;
-            e[32] = odd_lane ? o_cd : e_cd;
-            e[NB * 64] = odd_lane ? e_ab : o_ab;
-            e[NB * 64 + 32] = odd_lane ? e_cd : o_cd;
+            // t = (-1)^m on the mirror row, which the equator (odd K) does not have
+            const float t = eq ? 0.f : (odd_lane ? -1.f : 1.f);
+            const float2 d0 = rnd(make_float2(r1.x, r1.y)), d1 = rnd(make_float2(r1.z, r1.w));
+            const float2 u = cadd(c0, ci(c1)), v = csub(c0, ci(c1));
+            const float2 uq = cadd(d0, ci(d1)), vq = csub(d0, ci(d1));
+            e[0] = make_float4(u.x, u.y, t * uq.x, t * uq.y);
+            e[32] = make_float4(v.x, v.y, t * vq.x, t * vq.y);
           } else {
             float2* e = d + it * kLsStep * SX * 32;
             const float2 x = rnd(e[0]);
@@ -447,7 +477,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(&full_bar[slot]))
                  : "memory");
   };
-  const int grp = warp / kSplit, half = warp % kSplit;  // row group, and which rows of it this warp takes
+  const int grp = warp / kSplit, bh = warp % kSplit;  // row group, and which batches of it this warp takes
+  const bool bact = bh * NBW < NB;                    // the warp has batches
+  const int bw0 = bh * NBW;                           // its first batch (CTA-local)
   float* my = tab + grp * kTabStages * kStageFloats;
 
   // running ring positions over all tiles of this CTA: spectrum chunks staged
@@ -468,6 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     const int b0 = bg * NB;
     const int m0 = j * kMTile;
     const int m0g = m0 + p.m_off;
+    m0g_cur = m0g;
     const int s_begin = DIR == 0 ? 0 : min(m0g, p.S);
     const int nsteps = p.S - s_begin;
     const int per = ((nsteps + ks * kChunk - 1) / (ks * kChunk)) * kChunk;
@@ -476,11 +509,11 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     const int nchunks = (r_end - r_begin + kChunk - 1) / kChunk;
     const int n_valid = min(kCons, (r1 - r0 + kRowsPerWarp - 1) / kRowsPerWarp);  // row groups with rows
 
-    float2 acc[kWRows][NA];
+    float2 acc[kWRows][NAW];
 #pragma unroll
     for (int i = 0; i < kWRows; ++i)
 #pragma unroll
-      for (int a = 0; a < NA; ++a) acc[i][a] = make_float2(0.f, 0.f);
+      for (int a = 0; a < NAW; ++a) acc[i][a] = make_float2(0.f, 0.f);
 
     const bool st_ok = m0 + lane < p.M && b0 + st_b < p.B;
     const float2* st_src = p.in + (st_ok ? (long long)(b0 + st_b) * p.in_bs + m0 + lane : 0);
@@ -537,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       bulk_load(my + slot * kStageFloats, tsrc + (long long)q * kChunk * kStepFloats,
                 (unsigned)(n * kStepFloats * 4), &tab_bar[grp][slot]);
     };
-    if (half == 0 && lane == 0 && alive && nst > 0) {
+    if (bh == 0 && lane == 0 && alive && nst > 0) {
       // the ring memory was last written by the generic proxy (partial sums)
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       for (int q = 0; q < kTabStages && q < nst; ++q) issue_tab(q);
@@ -549,70 +582,63 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
       constexpr int H = decltype(hc)::value;
       // ts: this step's table block; xs: this step's staged spectrum planes
       // (vector: planes 2b, 2b+1 hold u, v of batch b)
-      constexpr int kQW = Shape<KIND>::kQuads / kSplit;  // quads of this warp's rows
+      constexpr int kQW = Shape<KIND>::kQuads;  // quads of this warp's rows
       float w[kWRows * T];
 #pragma unroll
       for (int q = 0; q < kQW; ++q) {
-        const float4 v = reinterpret_cast<const float4*>(ts)[(half * kQW + q) * 32 + lane];
+        const float4 v = reinterpret_cast<const float4*>(ts)[q * 32 + lane];
         w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+      }
+      if constexpr (PAR && KIND == 1) {
+        // per batch (u, t u') and (v, t v'); rows hold (Wp, Wn)
+        const float4* xv = reinterpret_cast<const float4*>(xs) + bw0 * 64 + lane;
+#pragma unroll
+        for (int b = 0; b < NBW; ++b) {
+          const float4 uu = xv[b * 64], vv = xv[b * 64 + 32];
+#pragma unroll
+          for (int i = 0; i < kWRows; ++i) {
+            const float wp = w[2 * i], wn = w[2 * i + 1];
+            acc[i][2 * b] = __ffma2_rn(make_float2(wp, wp), make_float2(uu.x, uu.y), acc[i][2 * b]);
+            acc[i][2 * b] = __ffma2_rn(make_float2(wn, wn), make_float2(uu.z, uu.w), acc[i][2 * b]);
+            acc[i][2 * b + 1] = __ffma2_rn(make_float2(wn, wn), make_float2(vv.x, vv.y), acc[i][2 * b + 1]);
+            acc[i][2 * b + 1] = __ffma2_rn(make_float2(wp, wp), make_float2(vv.z, vv.w), acc[i][2 * b + 1]);
+          }
+        }
+        return;
       }
       if constexpr (PAR) {
         // set 0 feeds the warp's even rows, set 1 its odd rows (kWRows == 8)
 #pragma unroll
         for (int set = 0; set < 2; ++set) {
-          if constexpr (KIND == 1) {
-            const float4* xv = reinterpret_cast<const float4*>(xs) + set * NB * 64 + lane;
-            float4 ab[NB], cd[NB];
+          float2 xv[NBW];
 #pragma unroll
-            for (int b = 0; b < NB; ++b) {
-              ab[b] = xv[b * 64];
-              cd[b] = xv[b * 64 + 32];
-            }
+          for (int b = 0; b < NBW; ++b) xv[b] = xs[(set * NB + bw0 + b) * 32 + lane];
 #pragma unroll
-            for (int i = set; i < kWRows; i += 2) {
-              const float w0 = w[2 * i], w1 = w[2 * i + 1];
+          for (int i = set; i < kWRows; i += 2) {
 #pragma unroll
-              for (int b = 0; b < NB; ++b) {
-                // sph += W0 A + W1 (i B),  tor += W1 (i C) + W0 (-D)
-                acc[i][2 * b] = __ffma2_rn(make_float2(w0, w0), make_float2(ab[b].x, ab[b].y), acc[i][2 * b]);
-                acc[i][2 * b] = __ffma2_rn(make_float2(w1, w1), make_float2(ab[b].z, ab[b].w), acc[i][2 * b]);
-                acc[i][2 * b + 1] =
-                    __ffma2_rn(make_float2(w1, w1), make_float2(cd[b].x, cd[b].y), acc[i][2 * b + 1]);
-                acc[i][2 * b + 1] =
-                    __ffma2_rn(make_float2(w0, w0), make_float2(cd[b].z, cd[b].w), acc[i][2 * b + 1]);
-              }
-            }
-          } else {
-            float2 xv[NB];
-#pragma unroll
-            for (int b = 0; b < NB; ++b) xv[b] = xs[(set * NB + b) * 32 + lane];
-#pragma unroll
-            for (int i = set; i < kWRows; i += 2) {
-#pragma unroll
-              for (int b = 0; b < NB; ++b) acc[i][b] = __ffma2_rn(make_float2(w[i], w[i]), xv[b], acc[i][b]);
-            }
+            for (int b = 0; b < NBW; ++b) acc[i][b] = __ffma2_rn(make_float2(w[i], w[i]), xv[b], acc[i][b]);
           }
         }
         return;
       }
-      float2 x[PB];
+      float2 x[NBW * P];
 #pragma unroll
-      for (int a = 0; a < PB; ++a) x[a] = xs[a * 32 + lane];
+      for (int a = 0; a < NBW * P; ++a) x[a] = xs[(bw0 * P + a) * 32 + lane];
 #pragma unroll
       for (int i = 0; i < kWRows; ++i) {
         if constexpr (KIND == 1) {
           const float wp = w[2 * i], wm = w[2 * i + 1];
 #pragma unroll
-          for (int b = 0; b < NB; ++b) {
+          for (int b = 0; b < NBW; ++b) {
             acc[i][2 * b] = __ffma2_rn(make_float2(wp, wp), x[2 * b], acc[i][2 * b]);
             acc[i][2 * b + 1] = __ffma2_rn(make_float2(wm, wm), x[2 * b + 1], acc[i][2 * b + 1]);
           }
         } else {
           const float wv = w[i];
 #pragma unroll
-          for (int b = 0; b < NB; ++b)
-            acc[i][(IPAR ? H * NB : 0) + b] =
-                __ffma2_rn(make_float2(wv, wv), x[b], acc[i][(IPAR ? H * NB : 0) + b]);
+          for (int b = 0; b < NBW; ++b)
+            acc[i][(IPAR ? H * NBW : 0) + b] =
+                __ffma2_rn(make_float2(wv, wv), x[b], acc[i][(IPAR ? H * NBW : 0) + b]);
         }
       }
     };
@@ -666,7 +692,9 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         const float2* xs = spec + cs * kSpecStageElems;
         const float* tsb = my + ts_ * kStageFloats;
         const int s0 = r_begin + c * kChunk;
-        if (s0 + kChunk <= r_end) {
+        if (!bact) {
+          // no batches for this warp: it only releases the table stage below
+        } else if (s0 + kChunk <= r_end) {
 #pragma unroll
           for (int ls = 0; ls < kChunk; ls += 2) {
             step(tsb + ls * kStepFloats, xs + ls * SX * 32, std::integral_constant<int, 0>{});
@@ -687,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
         // with chunk c + kTabStages
         __syncwarp();
         if constexpr (kSplit > 1) mbar_arrive(&tab_free[grp][ts_]);
-        if (half == 0 && lane == 0 && issued < nst) {
+        if (bh == 0 && lane == 0 && issued < nst) {
           if (kSplit == 1 || mbar_wait(&tab_free[grp][ts_], (h / kTabStages) & 1)) {
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
             issue_tab(issued);
@@ -701,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     }
     // nothing may still be writing into the rings when they become the partial-sum buffer
     asm volatile("cp.async.wait_all;\n" ::: "memory");
-    if (!alive && half == 0 && lane == 0 && has_rows) {
+    if (!alive && bh == 0 && lane == 0 && has_rows) {
       // a wait gave up: let this warp's table copies still in flight land first
       const int done = min(issued, nst);
       for (int q = consumed; q < done; ++q) {
@@ -721,19 +749,22 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
 #pragma unroll
       for (int i = 0; i < kWRows; ++i)
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          const float2 A = acc[i][b], Bv = acc[i][NB + b];
+        for (int b = 0; b < NBW; ++b) {
+          const float2 A = acc[i][b], Bv = acc[i][NBW + b];
           acc[i][b] = make_float2(A.x + Bv.x, A.y + Bv.y);
-          acc[i][NB + b] = a_is_even ? make_float2(A.x - Bv.x, A.y - Bv.y) : make_float2(Bv.x - A.x, Bv.y - A.y);
+          acc[i][NBW + b] = a_is_even ? make_float2(A.x - Bv.x, A.y - Bv.y) : make_float2(Bv.x - A.x, Bv.y - A.y);
         }
     }
-    if constexpr (KIND == 1 && !PAR) {
+    if constexpr (KIND == 1) {
       // sph = (Wm v + Wp u) / 2,  tor = -i (Wm v - Wp u) / 2
+      // (PAR: the mv sum carries the factor -(-1)^l; tile rows start even)
 #pragma unroll
       for (int i = 0; i < kWRows; ++i)
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          const float2 pu = acc[i][2 * b], mv = acc[i][2 * b + 1];
+        for (int b = 0; b < NBW; ++b) {
+          const float2 pu = acc[i][2 * b];
+          float2 mv = acc[i][2 * b + 1];
+          if (PAR && ((r0 + grp * kRowsPerWarp + i) & 1) == 0) mv = make_float2(-mv.x, -mv.y);
           acc[i][2 * b] = make_float2(0.5f * (mv.x + pu.x), 0.5f * (mv.y + pu.y));
           acc[i][2 * b + 1] = make_float2(0.5f * (mv.y - pu.y), -0.5f * (mv.x - pu.x));
         }
@@ -746,14 +777,19 @@ __global__ void __launch_bounds__(kThreads, 1) stream_kernel(const Params p) {
     const int rpr = kRows / ks;  // rows per owner rank, a multiple of 8
     cluster.sync();              // every CTA of the cluster is done with its rings
     {
-      const int row_local = grp * kRowsPerWarp + half * kWRows;  // first row of this warp in the tile
+      const int row_local = grp * kRowsPerWarp;  // first row of this warp in the tile
       const int owner = row_local / rpr;
       const int rl0 = row_local - owner * rpr;
       float2* dst = cluster.map_shared_rank(part, owner) + ((rank * rpr + rl0) * NA) * 32 + lane;
+      // local accumulator a -> the CTA's index: batch-major (b * P + plane), or
+      // with the inverse fold half h of batch b at h * NB + b
+      auto gidx = [&](int a) { return IPAR ? (a / NBW) * NB + bw0 + a % NBW : bw0 * P + a; };
+      if (bact) {
 #pragma unroll
-      for (int i = 0; i < kWRows; ++i)
+        for (int i = 0; i < kWRows; ++i)
 #pragma unroll
-        for (int a = 0; a < NA; ++a) dst[(i * NA + a) * 32] = acc[i][a];
+          for (int a = 0; a < NAW; ++a) dst[(i * NA + gidx(a)) * 32] = acc[i][a];
+      }
     }
     cluster.sync();
 

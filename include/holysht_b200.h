@@ -195,10 +195,11 @@ typedef struct holysht_contract_desc {
  * layout of the northern rows k < ceil(nlat/2) only (S = ceil(nlat/2) steps),
  * for grids symmetric about the equator, where the table obeys
  * W(nlat-1-k) = (-1)^(l+m) W(k) (scalar, and W1 of the vector map) and
- * W0(nlat-1-k) = -(-1)^(l+m) W0(k).  The vector tables are stored as they are
- * (t0 = W0, t1 = W1, not their sum and difference).  The kernel reads input
- * rows k and nlat-1-k together (half the table bytes, and for the scalar
- * kind half the multiply-adds).  No counterpart in the reference. */
+ * W0(nlat-1-k) = -(-1)^(l+m) W0(k).  The vector tables are stored as
+ * t0 = W0 + W1, t1 = -(-1)^l (W0 - W1) (row l; the conjugate map: W1 -> -W1).
+ * The kernel reads input rows k and nlat-1-k together (half the table bytes,
+ * and for the scalar kind half the multiply-adds).  No counterpart in the
+ * reference. */
 #define HOLYSHT_TABLE_GROUPED8_PARITY 3
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);

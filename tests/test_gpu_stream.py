@@ -374,7 +374,7 @@ def test_parity_folded_forward_matches_oracle(monkeypatch, vector, nlat, nlon, g
     against the float64 oracle, for both kinds and every grid family."""
     import holysht_b200 as hs
 
-    monkeypatch.setenv("HOLYSHT_PARITY", "2")
+    monkeypatch.delenv("HOLYSHT_PARITY", raising=False)  # the forward default
     dev = torch.device("cuda")
     rng = np.random.default_rng(nlat + 7 * vector)
     shape = (5, 2, nlat, nlon) if vector else (5, nlat, nlon)
