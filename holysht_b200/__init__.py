@@ -389,9 +389,11 @@ def _legendre_forward_planned(spec, src, round_bf16: bool, scale: float):
         # on-the-fly Legendre functions: no table stream
         seeds, coef, ct = src.recurrence_tables()
         if vector:
-            ops.legendre_vector_forward_recurrence(out, spec, seeds, coef, ct, scale)
+            ops.legendre_vector_forward_recurrence(out, spec, seeds, coef, ct, scale,
+                                                   parity=getattr(src, "rec_parity", False))
         else:
-            ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale)
+            ops.legendre_forward_recurrence(out, spec, seeds, coef, ct, scale,
+                                            parity=getattr(src, "rec_parity", False))
     elif _dense_tc_eligible(src, B, _lib.DIR_FORWARD):
         # large batch: the per-order contraction is a dense GEMM -> tcgen05
         ops.legendre_dense_tc(_lib.DIR_FORWARD, out, spec, src.dense_table_split(_lib.DIR_FORWARD), nlat=K,
@@ -797,6 +799,8 @@ class RealSHT(_GroupedTablesMixin, nn.Module):
         self._init_tables(("weight_t",), _lib.DIR_FORWARD)
         if variant == "recurrence":
             seeds, coef, ct = _weights.scalar_recurrence_tables(nlat, nlon, lmax, mmax, grid, norm, csphase)
+            self.rec_parity = _weights.recurrence_seeds_symmetric(seeds, ct)
+            seeds = _weights.compact_recurrence_seeds(seeds, coef.shape[1])
             self.register_buffer("rec_seeds", torch.from_numpy(seeds), persistent=False)
             self.register_buffer("rec_coef", torch.from_numpy(coef), persistent=False)
             self.register_buffer("rec_cos_theta", torch.from_numpy(ct), persistent=False)
@@ -870,6 +874,8 @@ class RealVectorSHT(_GroupedTablesMixin, nn.Module):
         self._init_tables(("w0_t", "w1_t"), _lib.DIR_FORWARD)
         if variant == "recurrence":
             seeds, coef, ct = _weights.vector_recurrence_tables(nlat, nlon, lmax, mmax, grid, norm, csphase)
+            self.rec_parity = _weights.recurrence_seeds_symmetric(seeds, ct)
+            seeds = _weights.compact_recurrence_seeds(seeds, coef.shape[1])
             self.register_buffer("rec_seeds", torch.from_numpy(seeds), persistent=False)
             self.register_buffer("rec_coef", torch.from_numpy(coef), persistent=False)
             self.register_buffer("rec_cos_theta", torch.from_numpy(ct), persistent=False)

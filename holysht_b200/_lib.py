@@ -22,6 +22,7 @@ DTYPE_C64, DTYPE_F32, DTYPE_BF16 = 0, 1, 2
 KIND_SCALAR, KIND_VECTOR, KIND_REAL = 0, 1, 2
 DIR_FORWARD, DIR_INVERSE = 0, 1
 FLAG_CONJ_W1, FLAG_ROUND_BF16, FLAG_IRFFT_PREP, FLAG_TABLE_SPLIT = 1, 2, 4, 16
+FLAG_EQUATORIAL_PARITY, FLAG_SEEDS_COMPACT = 32, 64
 TABLE_STRIDED, TABLE_GROUPED, TABLE_GROUPED8, TABLE_GROUPED8_PARITY = 0, 1, 2, 3
 
 # every symbol include/holysht_b200.h declares
@@ -50,7 +51,9 @@ EXPORTS = (
     "holysht_stream_launch_plan",
     "holysht_legendre_dense_tc_noalloc",
     "holysht_legendre_forward_recurrence",
+    "holysht_legendre_forward_recurrence_ex",
     "holysht_legendre_vector_forward_recurrence",
+    "holysht_legendre_vector_forward_recurrence_ex",
 )
 
 
@@ -136,8 +139,12 @@ def load() -> ctypes.CDLL:
                                             ctypes.POINTER(ctypes.c_int)], i32),
             "holysht_legendre_forward_recurrence": ([vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64,
                                                      ctypes.c_float, vp], i32),
+            "holysht_legendre_forward_recurrence_ex": ([vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64,
+                                                        ctypes.c_float, i32, vp], i32),
             "holysht_legendre_vector_forward_recurrence": ([vp, vp, i64, i64, i64, vp, vp, vp, i64, i64, i64, i64,
                                                             ctypes.c_float, vp], i32),
+            "holysht_legendre_vector_forward_recurrence_ex": ([vp, vp, i64, i64, i64, vp, vp, vp, i64, i64, i64,
+                                                               i64, ctypes.c_float, i32, vp], i32),
             "holysht_legendre_dense_tc_noalloc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,
                                                    ctypes.c_float, i32, i64, vp], i32),
         }

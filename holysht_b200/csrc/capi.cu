@@ -847,16 +847,25 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
                                         int64_t spec_row_stride, const float* seeds, const float* coef,
                                         const float* cos_theta, int64_t batch, int64_t nlat, int64_t lmax,
                                         int64_t mmax, float scale, void* stream) {
+  return holysht_legendre_forward_recurrence_ex(out, spec, spec_batch_stride, spec_row_stride, seeds, coef,
+                                                cos_theta, batch, nlat, lmax, mmax, scale, 0, stream);
+}
+
+int holysht_legendre_forward_recurrence_ex(void* out, const void* spec, int64_t spec_batch_stride,
+                                           int64_t spec_row_stride, const float* seeds, const float* coef,
+                                           const float* cos_theta, int64_t batch, int64_t nlat, int64_t lmax,
+                                           int64_t mmax, float scale, int flags, void* stream) {
   const long long B = batch, K = nlat, L = lmax, M = mmax;
   if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  if ((flags & ~(HOLYSHT_FLAG_EQUATORIAL_PARITY | HOLYSHT_FLAG_SEEDS_COMPACT)) != 0)
+    return fail(HOLYSHT_ERR_INVALID, "unknown flag");
   if (B == 0 || L == 0 || M == 0) return ok();
   if (!out || !spec || !seeds || !coef || !cos_theta) return fail(HOLYSHT_ERR_INVALID, "null pointer");
-  if (K > (long long)hsb::rec::kMaxWarps * 32 * 16)
-    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d", hsb::rec::kMaxWarps * 32 * 16);
-  if (!fits_int(B) || !fits_int(L) || !fits_int(M) || (B + 3) / 4 > 65535)
+  if (K < 1 || !fits_int(B) || !fits_int(K) || !fits_int(L) || !fits_int(M) || (B + 3) / 4 > 65535)
     return fail(HOLYSHT_ERR_INVALID, "extent out of range");
   if (spec_row_stride < M || spec_batch_stride < K * spec_row_stride)
     return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
+  if ((reinterpret_cast<uintptr_t>(seeds) & 7) != 0) return fail(HOLYSHT_ERR_INVALID, "seeds must be 8-byte aligned");
   hsb::rec::RecParams p;
   p.spec = static_cast<const float2*>(spec);
   p.sbs = spec_batch_stride;
@@ -871,20 +880,38 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
   p.M = (int)M;
   p.nseg = (int)((L + hsb::rec::kSeg - 1) / hsb::rec::kSeg);
   p.scale = scale;
-  // latitudes per thread: 8 (measured faster than 16 at 512 x 1024: more
-  // resident warps); HSB_REC_KPT16=1 selects 16 (needed above 2048 latitudes)
-  const int kpt = (K > 2048 || (K > 256 && env_int("HSB_REC_KPT16", 0))) ? 16 : 8;
-  const int threads = (int)(((K + kpt - 1) / kpt + 31) / 32 * 32);
-  const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
-  dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
-  if (env_int("HSB_REC_LEGACY", 0) && K <= (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt) {
-    const int t4 = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
-    hsb::rec::recurrence_forward_kernel<<<grid, t4 < 32 ? 32 : t4, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  } else if (kpt == 8) {
-    hsb::rec::recurrence_forward_pair_kernel<8><<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  } else {
-    hsb::rec::recurrence_forward_pair_kernel<16><<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool par = (flags & HOLYSHT_FLAG_EQUATORIAL_PARITY) != 0;
+  const int compact = (flags & HOLYSHT_FLAG_SEEDS_COMPACT) ? 1 : 0;
+  if (env_int("HSB_REC_PAIR", 0) && !par && !compact) {
+    // the earlier latitude-pair kernel (per-degree shuffle reductions), kept for comparison
+    if (K > (long long)hsb::rec::kMaxWarps * 32 * 16)
+      return fail(HOLYSHT_ERR_UNSUPPORTED, "the pair kernel supports nlat <= %d", hsb::rec::kMaxWarps * 32 * 16);
+    const int kpt = K > 2048 ? 16 : 8;
+    const int threads = (int)(((K + kpt - 1) / kpt + 31) / 32 * 32);
+    const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
+    dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
+    if (kpt == 8) hsb::rec::recurrence_forward_pair_kernel<8><<<grid, threads, 0, st>>>(p);
+    else hsb::rec::recurrence_forward_pair_kernel<16><<<grid, threads, 0, st>>>(p);
+    return check_launch("recurrence forward kernel");
   }
+  // segment-per-thread kernel: degree block (16, or 8 for more resident warps)
+  // and latitude chunks per item (warps per CTA)
+  const int mlim = (int)std::min(M, L);
+  const long long nsegs = hsb::rec::segs_before(mlim, (int)L);
+  const int db = env_int("HSB_REC_DB", 16) == 8 ? 8 : 16;
+  const int nkc = env_int("HSB_REC_NKC", 4);
+  if (!fits_int(nsegs) || (nsegs + 31) / 32 * (16 / db) > 0x7fffffffLL)
+    return fail(HOLYSHT_ERR_INVALID, "extent out of range");
+  dim3 grid((unsigned)((nsegs + 31) / 32 * (16 / db)), (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
+  cudaError_t e;
+  if (db == 16)
+    e = par ? hsb::rec::launch_seg_forward<16, true>(p, nkc, grid, mlim, (int)nsegs, compact, st)
+            : hsb::rec::launch_seg_forward<16, false>(p, nkc, grid, mlim, (int)nsegs, compact, st);
+  else
+    e = par ? hsb::rec::launch_seg_forward<8, true>(p, nkc, grid, mlim, (int)nsegs, compact, st)
+            : hsb::rec::launch_seg_forward<8, false>(p, nkc, grid, mlim, (int)nsegs, compact, st);
+  if (e != cudaSuccess) return fail(HOLYSHT_ERR_CUDA, "recurrence forward: %s", cudaGetErrorString(e));
   return check_launch("recurrence forward kernel");
 }
 
@@ -892,18 +919,29 @@ int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int6
                                                int64_t spec_comp_stride, int64_t spec_row_stride, const float* seeds,
                                                const float* coef, const float* cos_theta, int64_t batch,
                                                int64_t nlat, int64_t lmax, int64_t mmax, float scale, void* stream) {
+  return holysht_legendre_vector_forward_recurrence_ex(out, spec, spec_batch_stride, spec_comp_stride,
+                                                       spec_row_stride, seeds, coef, cos_theta, batch, nlat, lmax,
+                                                       mmax, scale, 0, stream);
+}
+
+int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, int64_t spec_batch_stride,
+                                                  int64_t spec_comp_stride, int64_t spec_row_stride,
+                                                  const float* seeds, const float* coef, const float* cos_theta,
+                                                  int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
+                                                  float scale, int flags, void* stream) {
   const long long B = batch, K = nlat, L = lmax, M = mmax;
   if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  if ((flags & ~(HOLYSHT_FLAG_EQUATORIAL_PARITY | HOLYSHT_FLAG_SEEDS_COMPACT)) != 0)
+    return fail(HOLYSHT_ERR_INVALID, "unknown flag");
   if (B == 0 || L == 0 || M == 0) return ok();
   if (!out || !spec || !seeds || !coef || !cos_theta) return fail(HOLYSHT_ERR_INVALID, "null pointer");
-  if (K > (long long)hsb::rec::kMaxWarps * 32 * 8)
-    return fail(HOLYSHT_ERR_UNSUPPORTED, "the recurrence kernel supports nlat <= %d", hsb::rec::kMaxWarps * 32 * 8);
-  if (!fits_int(B) || !fits_int(L) || !fits_int(M) || (B + hsb::rec::kNB - 1) / hsb::rec::kNB > 65535)
+  if (K < 1 || !fits_int(B) || !fits_int(K) || !fits_int(L) || !fits_int(M) ||
+      (B + hsb::rec::kNB - 1) / hsb::rec::kNB > 65535)
     return fail(HOLYSHT_ERR_INVALID, "extent out of range");
   if (spec_row_stride < M || spec_comp_stride < K * spec_row_stride || spec_batch_stride < 2 * spec_comp_stride)
     return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
-  if ((reinterpret_cast<uintptr_t>(seeds) & 15) != 0)
-    return fail(HOLYSHT_ERR_INVALID, "seeds must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(seeds) & 15) != 0 || (reinterpret_cast<uintptr_t>(coef) & 15) != 0)
+    return fail(HOLYSHT_ERR_INVALID, "seeds and coef must be 16-byte aligned");
   hsb::rec::VecRecParams p;
   p.spec = static_cast<const float2*>(spec);
   p.sbs = spec_batch_stride;
@@ -919,17 +957,28 @@ int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int6
   p.M = (int)M;
   p.nseg = (int)((L + hsb::rec::kSeg - 1) / hsb::rec::kSeg);
   p.scale = scale;
-  const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
-  dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
-  if (!env_int("HSB_REC_LEGACY", 0) || K > (long long)hsb::rec::kMaxWarps * 32 * hsb::rec::kKpt) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool par = (flags & HOLYSHT_FLAG_EQUATORIAL_PARITY) != 0;
+  const int compact = (flags & HOLYSHT_FLAG_SEEDS_COMPACT) ? 1 : 0;
+  if (env_int("HSB_REC_PAIR", 0) && !par && !compact) {
+    // the earlier latitude-pair kernel (per-degree shuffle reductions), kept for comparison
+    if (K > (long long)hsb::rec::kMaxWarps * 32 * 8)
+      return fail(HOLYSHT_ERR_UNSUPPORTED, "the pair kernel supports nlat <= %d", hsb::rec::kMaxWarps * 32 * 8);
+    const long long seg_blocks = (p.nseg + hsb::rec::kSegPerCta - 1) / hsb::rec::kSegPerCta;
+    dim3 grid((unsigned)M, (unsigned)seg_blocks, (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
     const int t8 = (int)(((K + 7) / 8 + 31) / 32 * 32);
-    hsb::rec::recurrence_vector_forward_pair_kernel<8><<<grid, t8, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    hsb::rec::recurrence_vector_forward_pair_kernel<8><<<grid, t8, 0, st>>>(p);
     return check_launch("recurrence_vector_forward");
   }
-  const int threads = (int)(((K + hsb::rec::kKpt - 1) / hsb::rec::kKpt + 31) / 32 * 32);
-  hsb::rec::recurrence_vector_forward_kernel<<<grid, threads < 32 ? 32 : threads, 0,
-                                               static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch("vector recurrence forward kernel");
+  const int mlim = (int)std::min(M, L);
+  const long long nsegs = hsb::rec::segs_before(mlim, (int)L);
+  const int nkc = env_int("HSB_REC_NKC", 4);
+  if (!fits_int(nsegs) || (nsegs + 31) / 32 * 2 > 0x7fffffffLL) return fail(HOLYSHT_ERR_INVALID, "extent out of range");
+  dim3 grid((unsigned)((nsegs + 31) / 32 * 2), (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
+  const cudaError_t e = par ? hsb::rec::launch_vseg_forward<true>(p, nkc, grid, mlim, (int)nsegs, compact, st)
+                            : hsb::rec::launch_vseg_forward<false>(p, nkc, grid, mlim, (int)nsegs, compact, st);
+  if (e != cudaSuccess) return fail(HOLYSHT_ERR_CUDA, "recurrence vector forward: %s", cudaGetErrorString(e));
+  return check_launch("recurrence vector forward kernel");
 }
 
 int holysht_tc_error_word(unsigned* value) {

@@ -22,6 +22,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 namespace hsb {
 namespace rec {
 
@@ -639,6 +641,561 @@ __global__ void __launch_bounds__(kMaxWarps * 32) recurrence_vector_forward_pair
       if (nwarps > 1) __syncthreads();
     }
   }
+}
+
+
+// ---------------------------------------------------------------------------
+// Segment-per-thread kernels: the default recurrence variant.
+//
+// A work item is one (order m, checkpoint segment c, degree block j): degrees
+// l = m + 16c + j*DB .. m + 16c + (j+1)*DB - 1.  A thread owns one item for a
+// group of kNB batches and walks its latitudes one at a time: it re-seeds the
+// recurrence from the segment's float64-built checkpoints, runs it up the
+// segment, and adds P * X for every degree of its block into DB x kNB complex
+// partial sums held in registers.  The partial sums never cross lanes inside
+// the latitude loop (the per-degree shuffle reductions of the pair kernels
+// cost as many issue slots as their FMAs); the NKC warps of a CTA share the
+// same 32 items, split the latitudes into NKC chunks, and meet once, in shared
+// memory, at the end.  Items are uniform work (one segment x one latitude
+// chunk), so the triangular l >= m structure needs no balancing.
+//
+// PAR (grids symmetric about the equator, x_{K-1-k} = -x_k and w_{K-1-k} =
+// w_k): P_l^m(-x) = (-1)^(l+m) P_l^m(x), so only the northern latitudes are
+// visited and they are contracted with E = X_k + X_{K-1-k} (l + m even) or
+// O = X_k - X_{K-1-k} (l + m odd).  Since l - m = 16c + q, the parity is that
+// of the degree's offset q inside the segment, known at compile time.  This
+// halves both the recurrence and the contraction.  The equatorial row of an
+// odd nlat is its own mirror and is used once (E = O = X).
+
+// sum_{d=1}^{n} ceil(d / 16)
+__host__ __device__ __forceinline__ long long seg_prefix(long long n) {
+  const long long q = n / kSeg, r = n % kSeg;
+  return (long long)kSeg * q * (q + 1) / 2 + r * (q + 1);
+}
+// number of (order, segment) pairs of the orders below m: order m' has
+// ceil((L - m') / 16) segments.
+__host__ __device__ __forceinline__ long long segs_before(int m, int L) {
+  return seg_prefix(L) - seg_prefix((long long)L - m);
+}
+
+// the item's order and segment from its index among all (order, segment) pairs
+__device__ __forceinline__ void decode_segment(int seg, int mlim, int L, int& m, int& c) {
+  int lo = 0, hi = mlim - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (segs_before(mid, L) <= seg) lo = mid;
+    else hi = mid - 1;
+  }
+  m = lo;
+  c = (int)(seg - segs_before(lo, L));
+}
+
+// exact zeros of every row (b, l) of this CTA's batch group for m > l,
+// rows spread over the grid's CTAs
+__device__ __forceinline__ void zero_upper(float2* out, long long plane_stride, int planes, int B, int L,
+                                           int M, int b0) {
+  const int rows = kNB * planes * L;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int bp = r / L, l = r % L;
+    const int b = b0 + bp / planes;
+    if (b >= B) break;
+    float2* row = out + ((long long)b * planes + bp % planes) * plane_stride + (long long)l * M;
+    for (int mm = l + 1 + (int)threadIdx.x; mm < M; mm += blockDim.x) row[mm] = make_float2(0.f, 0.f);
+  }
+}
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* g, bool valid) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(sa), "l"(g), "r"(valid ? 8 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* g) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* g) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Latitude ring: per warp and latitude, one stage holds the 32 lanes'
+// checkpoints, cos theta, and the spectrum rows the latitude needs (each batch's
+// row at k and, with PAR, at the mirror; c0 and c1 for the vector map) for the
+// 32 consecutive orders m_lo .. m_lo + 31 starting at the warp's first item's
+// order (32 consecutive segments span at most 32 orders).  Lane i copies order
+// m_lo + i of every row and the checkpoint of its own item, so every cp.async
+// reads and writes contiguous runs (copies in which many lanes read one address
+// split into one shared-memory wavefront per lane); the checkpoints are
+// contiguous across lanes in the latitude-major compact layout.  Stages are
+// filled kDepth latitudes ahead of use: an iteration is a few hundred cycles and
+// a first touch after the L2 is cold is on the order of a microsecond.  The ring
+// is reused for the final reduction.
+template <bool PAR, bool VEC, int NKC>
+struct SegRing {
+  static constexpr int kRows = (PAR ? 2 : 1) * (VEC ? 2 : 1) * kNB;  // spectrum rows per latitude
+  static constexpr int kSeedBytes = VEC ? 16 : 8;
+  static constexpr int kDepth = VEC ? 4 : 8;
+  static constexpr int kWarpStage = 32 * kSeedBytes + 16 + kRows * 32 * 8;
+  static constexpr int kBytes = kDepth * NKC * kWarpStage;
+  static constexpr int kRedBytes = NKC * 32 * 33 * 4;
+  static constexpr int kSmem = kBytes > kRedBytes ? kBytes : kRedBytes;
+};
+
+// dynamic shared memory of the scalar segment kernel
+template <bool PAR, int NKC>
+__host__ __device__ constexpr int seg_smem_bytes() {
+  return SegRing<PAR, false, NKC>::kSmem;
+}
+
+template <int DB, bool PAR, int NKC, int J0>
+__device__ __forceinline__ void seg_forward_body(const RecParams& p, int m, int c, int m_lo, bool live, int b0,
+                                                 const float2* sdl, long long sd_kstride, unsigned char* smem) {
+  using R = SegRing<PAR, false, NKC>;
+  constexpr int Q0 = J0 * DB;  // first contracted offset inside the segment
+  constexpr int QN = Q0 + DB;  // one past the last
+  constexpr int D = R::kDepth;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lseg = m + c * kSeg;
+  float ca[QN], cb[QN];  // a_l and -b_l of the steps q = 2 .. QN-1 (zero past lmax)
+  const float* cm = p.coef + (long long)m * p.L * 2;
+#pragma unroll
+  for (int q = 2; q < QN; ++q) {
+    const int l = lseg + q;
+    const bool ok = l < p.L;
+    ca[q] = ok ? cm[2 * l] : 0.f;
+    cb[q] = ok ? -cm[2 * l + 1] : 0.f;
+  }
+  const int Kh = PAR ? (p.K + 1) / 2 : p.K;
+  const int chunk = (Kh + NKC - 1) / NKC;
+  const int kb = warp * chunk, ke = min(Kh, kb + chunk);
+  const bool mok = m_lo + lane < p.M;
+  bool bok[kNB];
+  const float2* rows[kNB];  // this lane's column (order m_lo + lane) of each batch's spectrum
+#pragma unroll
+  for (int b = 0; b < kNB; ++b) {
+    bok[b] = b0 + b < p.B && mok;
+    rows[b] = p.spec + (long long)(b0 + b < p.B ? b0 + b : b0) * p.sbs + (mok ? m_lo + lane : m_lo);
+  }
+  const int mi = m - m_lo;  // this item's column in a stage
+
+  // stage s of this warp: checkpoints [32] float2, cos theta, spectrum [kRows][32] float2
+  auto stage = [&](int s) { return smem + (s * NKC + warp) * R::kWarpStage; };
+  auto issue = [&](int k, int s) {
+    unsigned char* st = stage(s);
+    float2* sp = reinterpret_cast<float2*>(st + 32 * 8 + 16);
+    const int km = p.K - 1 - k;
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      cp_async8(sp + b * 32 + lane, bok[b] ? rows[b] + (long long)k * p.srs : p.spec, bok[b]);
+      if (PAR) {
+        const bool v = bok[b] && km != k;
+        cp_async8(sp + (kNB + b) * 32 + lane, v ? rows[b] + (long long)km * p.srs : p.spec, v);
+      }
+    }
+    cp_async8(reinterpret_cast<float2*>(st) + lane, sdl + k * sd_kstride, true);
+    if (lane == 0) cp_async4(st + 32 * 8, p.x + k);
+  };
+
+  float2 acc[DB][kNB];
+#pragma unroll
+  for (int q = 0; q < DB; ++q)
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) acc[q][b] = make_float2(0.f, 0.f);
+
+#pragma unroll
+  for (int s = 0; s < D - 1; ++s) {
+    if (kb + s < ke) issue(kb + s, s);
+    cp_async_commit();
+  }
+  for (int k = kb, s = 0; k < ke; ++k, s = (s + 1 == D) ? 0 : s + 1) {
+    __syncwarp();  // every lane is done reading the stage about to be refilled
+    if (k + D - 1 < ke) issue(k + D - 1, (s == 0) ? D - 1 : s - 1);
+    cp_async_commit();
+    cp_async_wait<D - 1>();  // latitude k's copies have landed
+    __syncwarp();            // and so have the other lanes' (each lane reads all columns)
+    const unsigned char* st = stage(s);
+    const float x = *reinterpret_cast<const float*>(st + 32 * 8);
+    const float2 sk = reinterpret_cast<const float2*>(st)[lane];
+    float p2 = sk.x, p1 = sk.y;  // degrees lseg and lseg + 1
+    const float2* cur = reinterpret_cast<const float2*>(st + 32 * 8 + 16) + mi;
+    float2 E[kNB], O[kNB];
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      const float2 X = cur[b * 32];
+      if (PAR) {
+        const float2 Xm = cur[(kNB + b) * 32];  // zero for the equatorial row of an odd nlat
+        E[b] = make_float2(X.x + Xm.x, X.y + Xm.y);
+        O[b] = make_float2(X.x - Xm.x, X.y - Xm.y);
+      } else {
+        E[b] = O[b] = X;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < QN; ++q) {
+      float pl;
+      if (q == 0) {
+        pl = p2;
+      } else if (q == 1) {
+        pl = p1;
+      } else {
+        pl = fmaf(ca[q], __fmul_rn(x, p1), __fmul_rn(cb[q], p2));
+        p2 = p1;
+        p1 = pl;
+      }
+      if (q >= Q0) {
+        const float2 pp = make_float2(pl, pl);
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) acc[q - Q0][b] = __ffma2_rn(pp, (q & 1) ? O[b] : E[b], acc[q - Q0][b]);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  __syncthreads();  // every warp is done with the ring the reduction reuses
+
+  // the NKC latitude chunks meet in shared memory, 4 degrees at a time
+  constexpr int NV = 32 / NKC;  // values summed and written per thread per round
+  float* red = reinterpret_cast<float*>(smem);
+  float* mine = red + tid * 33;
+#pragma unroll
+  for (int r = 0; r < DB / 4; ++r) {
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+      for (int b = 0; b < kNB; ++b) {
+        mine[qq * 8 + b * 2] = acc[4 * r + qq][b].x;
+        mine[qq * 8 + b * 2 + 1] = acc[4 * r + qq][b].y;
+      }
+    __syncthreads();
+    const int v0 = warp * NV;
+    float sum[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) sum[i] = 0.f;
+#pragma unroll
+    for (int w = 0; w < NKC; ++w)
+#pragma unroll
+      for (int i = 0; i < NV; ++i) sum[i] += red[(w * 32 + lane) * 33 + v0 + i];
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < NV; i += 2) {
+        const int v = v0 + i, qq = v >> 3, b = (v >> 1) & 3;
+        const int l = lseg + Q0 + 4 * r + qq;
+        if (l < p.L && b0 + b < p.B)
+          p.out[((long long)(b0 + b) * p.L + l) * p.M + m] = make_float2(sum[i] * p.scale, sum[i + 1] * p.scale);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// The item's order, segment and checkpoint pointer.  Lanes past the last
+// segment take the last segment (they compute and write nothing), so every
+// lane's order lies in m_lo .. m_lo + 31.  Checkpoints: compact layout
+// [K][nsegs][S] (consecutive lanes contiguous) or [M][nseg][K][S].
+template <int S>
+__device__ __forceinline__ void seg_item(const float* seeds, bool compact, int nseg, int K, int mlim, int L,
+                                         int nsegs, int seg, int& m, int& c, int& m_lo, const float*& sdl,
+                                         long long& kstride) {
+  const int sg = seg < nsegs ? seg : nsegs - 1;
+  decode_segment(sg, mlim, L, m, c);
+  m_lo = __shfl_sync(0xffffffffu, m, 0);
+  if (compact) {
+    sdl = seeds + (long long)sg * S;
+    kstride = (long long)nsegs;
+  } else {
+    sdl = seeds + ((long long)m * nseg + c) * K * S;
+    kstride = 1;
+  }
+}
+
+// grid: x = J x ceil(nsegs / 32) (degree block j = x % J), y = batch group of kNB;
+// dynamic shared memory seg_smem_bytes<PAR, NKC>()
+template <int DB, bool PAR, int NKC>
+__global__ void __launch_bounds__(NKC * 32) recurrence_forward_seg_kernel(const RecParams p, int mlim, int nsegs,
+                                                                          int compact) {
+  static_assert(DB == 8 || DB == 16, "degree block of 8 or 16");
+  static_assert(NKC == 2 || NKC == 4 || NKC == 8, "2, 4 or 8 latitude chunks");
+  constexpr int J = kSeg / DB;
+  extern __shared__ __align__(16) unsigned char ssmem[];
+  const int b0 = blockIdx.y * kNB;
+  zero_upper(p.out, (long long)p.L * p.M, 1, p.B, p.L, p.M, b0);
+  const int seg = (int)(blockIdx.x / J) * 32 + (int)(threadIdx.x & 31);
+  int m, c, m_lo;
+  const float* sdl;
+  long long ks;
+  seg_item<2>(p.seeds, compact != 0, p.nseg, p.K, mlim, p.L, nsegs, seg, m, c, m_lo, sdl, ks);
+  const float2* sd2 = reinterpret_cast<const float2*>(sdl);
+  const bool live = seg < nsegs;
+  if constexpr (J == 2) {
+    if (blockIdx.x % 2) seg_forward_body<DB, PAR, NKC, 1>(p, m, c, m_lo, live, b0, sd2, ks, ssmem);
+    else seg_forward_body<DB, PAR, NKC, 0>(p, m, c, m_lo, live, b0, sd2, ks, ssmem);
+  } else {
+    seg_forward_body<DB, PAR, NKC, 0>(p, m, c, m_lo, live, b0, sd2, ks, ssmem);
+  }
+}
+
+// Vector form.  Per degree the thread forms W0 = alpha Q^{m-1}_l + beta Q^{m+1}_l
+// and W1 = gamma Q^{m-1}_{l+1} + delta Q^{m+1}_{l+1} from the two recurrences
+// and accumulates S = sum (W0 + W1) u and D = sum (W0 - W1) v, u = c0 + i c1,
+// v = c0 - i c1 (sph = (S + D) / 2, tor = i (S - D) / 2).  With PAR, W0 is odd
+// and W1 even under the mirror times s = (-1)^(l+m) (Q^{m +/- 1}_l has parity
+// (-1)^(l+m+1)), so a northern latitude k and its mirror k' give
+//   S += (W0 + W1) u - s (W0 - W1) u',   D += (W0 - W1) v - s (W0 + W1) v'
+// and the recurrences run for the northern half only.  Degree blocks of 8
+// (J = 2 per segment) keep the 8 x 4 batches x (S, D) sums in 128 registers;
+// the block j = 1 runs the recurrences through the segment's first 8 degrees
+// without contracting them.  The per-degree coefficients of the CTA's 32 items
+// sit in shared memory, lane-innermost (conflict-free 16-byte loads).
+constexpr int kVDB = 8;
+constexpr int kCoefBytes = 2 * kSeg * 32 * 16;  // [2 * 16 degrees][32 lanes] float4
+
+// dynamic shared memory of the vector segment kernel: coefficients, then the ring
+template <bool PAR, int NKC>
+__host__ __device__ constexpr int vseg_smem_bytes() {
+  return kCoefBytes + SegRing<PAR, true, NKC>::kSmem;
+}
+
+template <bool PAR, int NKC, int J0>
+__device__ __forceinline__ void vseg_forward_body(const VecRecParams& p, int m, int c, int m_lo, bool live, int b0,
+                                                  const float4* sdl, long long sd_kstride, unsigned char* smem) {
+  using R = SegRing<PAR, true, NKC>;
+  constexpr int Q0 = J0 * kVDB, QN = Q0 + kVDB;
+  constexpr int D = R::kDepth;
+  float4* cfs = reinterpret_cast<float4*>(smem);
+  unsigned char* ring = smem + kCoefBytes;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lseg = m + c * kSeg;
+  // coefficients of degrees lseg + q, q < QN: (am, -bm, ap, -bp), (alpha, beta, gamma, delta)
+  for (int e = warp; e < QN * 2; e += NKC) {
+    const int q = e >> 1, h = e & 1, l = lseg + q;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live && l < p.L) {
+      const float4 raw = reinterpret_cast<const float4*>(p.coef + ((long long)m * p.L + l) * 8)[h];
+      v = h ? raw : make_float4(raw.x, -raw.y, raw.z, -raw.w);
+    }
+    cfs[e * 32 + lane] = v;
+  }
+  __syncthreads();
+  const int Kh = PAR ? (p.K + 1) / 2 : p.K;
+  const int chunk = (Kh + NKC - 1) / NKC;
+  const int kb = warp * chunk, ke = min(Kh, kb + chunk);
+  const bool mok = m_lo + lane < p.M;
+  bool bok[kNB];
+  const float2* rows[kNB];  // this lane's column (order m_lo + lane) of each batch's c0 spectrum
+#pragma unroll
+  for (int b = 0; b < kNB; ++b) {
+    bok[b] = b0 + b < p.B && mok;
+    rows[b] = p.spec + (long long)(b0 + b < p.B ? b0 + b : b0) * p.sbs + (mok ? m_lo + lane : m_lo);
+  }
+  const int mi = m - m_lo;  // this item's column in a stage
+
+  // stage s of this warp: checkpoints [32] float4, cos theta, spectrum [kRows][32] float2;
+  // rows of batch b: c0, c1 at k (and c0, c1 at the mirror with PAR)
+  constexpr int PB = PAR ? 4 : 2;
+  auto stage = [&](int s) { return ring + (s * NKC + warp) * R::kWarpStage; };
+  auto issue = [&](int k, int s) {
+    unsigned char* st = stage(s);
+    float2* sp = reinterpret_cast<float2*>(st + 32 * 16 + 16);
+    const int km = p.K - 1 - k;
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      const float2* r0 = rows[b] + (long long)k * p.srs;
+      cp_async8(sp + (PB * b + 0) * 32 + lane, bok[b] ? r0 : p.spec, bok[b]);
+      cp_async8(sp + (PB * b + 1) * 32 + lane, bok[b] ? r0 + p.sps : p.spec, bok[b]);
+      if (PAR) {
+        const bool v = bok[b] && km != k;
+        const float2* r1 = rows[b] + (long long)km * p.srs;
+        cp_async8(sp + (PB * b + 2) * 32 + lane, v ? r1 : p.spec, v);
+        cp_async8(sp + (PB * b + 3) * 32 + lane, v ? r1 + p.sps : p.spec, v);
+      }
+    }
+    cp_async16(reinterpret_cast<float4*>(st) + lane, sdl + k * sd_kstride);
+    if (lane == 0) cp_async4(st + 32 * 16, p.x + k);
+  };
+
+  float2 S[kVDB][kNB], Dd[kVDB][kNB];
+#pragma unroll
+  for (int q = 0; q < kVDB; ++q)
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) S[q][b] = Dd[q][b] = make_float2(0.f, 0.f);
+
+#pragma unroll
+  for (int s = 0; s < D - 1; ++s) {
+    if (kb + s < ke) issue(kb + s, s);
+    cp_async_commit();
+  }
+  for (int k = kb, s = 0; k < ke; ++k, s = (s + 1 == D) ? 0 : s + 1) {
+    __syncwarp();  // every lane is done reading the stage about to be refilled
+    if (k + D - 1 < ke) issue(k + D - 1, (s == 0) ? D - 1 : s - 1);
+    cp_async_commit();
+    cp_async_wait<D - 1>();  // latitude k's copies have landed
+    __syncwarp();            // and so have the other lanes' (each lane reads all columns)
+    const unsigned char* st = stage(s);
+    const float x = *reinterpret_cast<const float*>(st + 32 * 16);
+    const float4 sk = reinterpret_cast<const float4*>(st)[lane];
+    float qm0 = sk.x, qm1 = sk.y, qp0 = sk.z, qp1 = sk.w;
+    const float2* cur = reinterpret_cast<const float2*>(st + 32 * 16 + 16) + mi;
+    float2 u[kNB], v[kNB], um[kNB], vm[kNB];
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      const float2 c0 = cur[(PB * b + 0) * 32], c1 = cur[(PB * b + 1) * 32];
+      u[b] = make_float2(c0.x - c1.y, c0.y + c1.x);
+      v[b] = make_float2(c0.x + c1.y, c0.y - c1.x);
+      if (PAR) {  // zero for the equatorial row of an odd nlat
+        const float2 d0 = cur[(PB * b + 2) * 32], d1 = cur[(PB * b + 3) * 32];
+        um[b] = make_float2(d0.x - d1.y, d0.y + d1.x);
+        vm[b] = make_float2(d0.x + d1.y, d0.y - d1.x);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < QN; ++q) {
+      const float4 ab = cfs[(2 * q) * 32 + lane];
+      if (q >= Q0) {
+        const float4 g = cfs[(2 * q + 1) * 32 + lane];
+        const float w0 = fmaf(g.x, qm0, __fmul_rn(g.y, qp0));
+        const float w1 = fmaf(g.z, qm1, __fmul_rn(g.w, qp1));
+        const float wp = w0 + w1, wm = w0 - w1;
+        const float2 pp = make_float2(wp, wp), mm = make_float2(wm, wm);
+#pragma unroll
+        for (int b = 0; b < kNB; ++b) {
+          S[q - Q0][b] = __ffma2_rn(pp, u[b], S[q - Q0][b]);
+          Dd[q - Q0][b] = __ffma2_rn(mm, v[b], Dd[q - Q0][b]);
+        }
+        if (PAR) {
+          // s = (-1)^q: even q subtracts the mirror terms, odd q adds them
+          const float2 ms = (q & 1) ? mm : make_float2(-wm, -wm);
+          const float2 ps = (q & 1) ? pp : make_float2(-wp, -wp);
+#pragma unroll
+          for (int b = 0; b < kNB; ++b) {
+            S[q - Q0][b] = __ffma2_rn(ms, um[b], S[q - Q0][b]);
+            Dd[q - Q0][b] = __ffma2_rn(ps, vm[b], Dd[q - Q0][b]);
+          }
+        }
+      }
+      if (q + 1 < QN) {  // both recurrences to degree l + 2
+        const float nm = fmaf(ab.x, __fmul_rn(x, qm1), __fmul_rn(ab.y, qm0));
+        const float np = fmaf(ab.z, __fmul_rn(x, qp1), __fmul_rn(ab.w, qp0));
+        qm0 = qm1;
+        qm1 = nm;
+        qp0 = qp1;
+        qp1 = np;
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  __syncthreads();  // every warp is done with the ring the reduction reuses
+
+  // the latitude chunks meet in shared memory, 2 degrees (32 values) at a time
+  constexpr int NV = 32 / NKC;
+  const long long plane = (long long)p.L * p.M;
+  float* red = reinterpret_cast<float*>(ring);
+  float* mine = red + tid * 33;
+#pragma unroll
+  for (int r = 0; r < kVDB / 2; ++r) {
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+      for (int b = 0; b < kNB; ++b) {
+        float* o = mine + qq * 16 + b * 4;
+        o[0] = S[2 * r + qq][b].x;
+        o[1] = S[2 * r + qq][b].y;
+        o[2] = Dd[2 * r + qq][b].x;
+        o[3] = Dd[2 * r + qq][b].y;
+      }
+    __syncthreads();
+    const int v0 = warp * NV;
+    float sum[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) sum[i] = 0.f;
+#pragma unroll
+    for (int w = 0; w < NKC; ++w)
+#pragma unroll
+      for (int i = 0; i < NV; ++i) sum[i] += red[(w * 32 + lane) * 33 + v0 + i];
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < NV; i += 4) {
+        const int vv = v0 + i, qq = vv >> 4, b = (vv >> 2) & 3;
+        const int l = lseg + Q0 + 2 * r + qq;
+        if (l < p.L && b0 + b < p.B) {
+          const float h = 0.5f * p.scale;
+          float2* o = p.out + (long long)(b0 + b) * 2 * plane + (long long)l * p.M + m;
+          o[0] = make_float2(h * (sum[i] + sum[i + 2]), h * (sum[i + 1] + sum[i + 3]));
+          o[plane] = make_float2(h * (sum[i + 3] - sum[i + 1]), h * (sum[i] - sum[i + 2]));
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// grid: x = 2 x ceil(nsegs / 32) (degree block j = x % 2), y = batch group of kNB;
+// dynamic shared memory vseg_smem_bytes<PAR, NKC>()
+template <bool PAR, int NKC>
+__global__ void __launch_bounds__(NKC * 32) recurrence_vector_forward_seg_kernel(const VecRecParams p, int mlim,
+                                                                                 int nsegs, int compact) {
+  static_assert(NKC == 2 || NKC == 4 || NKC == 8, "2, 4 or 8 latitude chunks");
+  extern __shared__ __align__(16) unsigned char vsmem[];
+  const int b0 = blockIdx.y * kNB;
+  zero_upper(p.out, (long long)p.L * p.M, 2, p.B, p.L, p.M, b0);
+  const int seg = (int)(blockIdx.x >> 1) * 32 + (int)(threadIdx.x & 31);
+  int m, c, m_lo;
+  const float* sdl;
+  long long ks;
+  seg_item<4>(p.seeds, compact != 0, p.nseg, p.K, mlim, p.L, nsegs, seg, m, c, m_lo, sdl, ks);
+  const float4* sd4 = reinterpret_cast<const float4*>(sdl);
+  const bool live = seg < nsegs;
+  if (blockIdx.x & 1) vseg_forward_body<PAR, NKC, 1>(p, m, c, m_lo, live, b0, sd4, ks, vsmem);
+  else vseg_forward_body<PAR, NKC, 0>(p, m, c, m_lo, live, b0, sd4, ks, vsmem);
+}
+
+// sets the kernel's dynamic shared-memory limit once per device, then launches
+template <typename Kern, typename Params>
+inline cudaError_t launch_with_smem(Kern kernel, int bytes, std::atomic<unsigned long long>& configured, dim3 grid,
+                                    int threads, cudaStream_t st, const Params& p, int mlim, int nsegs, int compact) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  kernel<<<grid, threads, bytes, st>>>(p, mlim, nsegs, compact);
+  return cudaSuccess;
+}
+
+template <int DB, bool PAR, int NKC>
+inline cudaError_t launch_seg(const RecParams& p, dim3 grid, int mlim, int nsegs, int compact, cudaStream_t st) {
+  static std::atomic<unsigned long long> configured{0};
+  return launch_with_smem(recurrence_forward_seg_kernel<DB, PAR, NKC>, seg_smem_bytes<PAR, NKC>(), configured, grid,
+                          NKC * 32, st, p, mlim, nsegs, compact);
+}
+
+template <int DB, bool PAR>
+inline cudaError_t launch_seg_forward(const RecParams& p, int nkc, dim3 grid, int mlim, int nsegs, int compact,
+                                      cudaStream_t st) {
+  if (nkc == 2) return launch_seg<DB, PAR, 2>(p, grid, mlim, nsegs, compact, st);
+  if (nkc == 8) return launch_seg<DB, PAR, 8>(p, grid, mlim, nsegs, compact, st);
+  return launch_seg<DB, PAR, 4>(p, grid, mlim, nsegs, compact, st);
+}
+
+template <bool PAR, int NKC>
+inline cudaError_t launch_vseg(const VecRecParams& p, dim3 grid, int mlim, int nsegs, int compact, cudaStream_t st) {
+  static std::atomic<unsigned long long> configured{0};
+  return launch_with_smem(recurrence_vector_forward_seg_kernel<PAR, NKC>, vseg_smem_bytes<PAR, NKC>(), configured,
+                          grid, NKC * 32, st, p, mlim, nsegs, compact);
+}
+
+template <bool PAR>
+inline cudaError_t launch_vseg_forward(const VecRecParams& p, int nkc, dim3 grid, int mlim, int nsegs,
+                                       int compact, cudaStream_t st) {
+  if (nkc == 2) return launch_vseg<PAR, 2>(p, grid, mlim, nsegs, compact, st);
+  if (nkc == 8) return launch_vseg<PAR, 8>(p, grid, mlim, nsegs, compact, st);
+  return launch_vseg<PAR, 4>(p, grid, mlim, nsegs, compact, st);
 }
 
 }  // namespace rec

@@ -518,45 +518,74 @@ def stream_error_word() -> int:
     return int(v.value)
 
 
+def _nsegs(L: int, M: int) -> int:
+    """Number of 16-degree checkpoint segments of the orders m < min(M, L)."""
+    return sum((L - m + 15) // 16 for m in range(min(M, L)))
+
+
 def legendre_vector_forward_recurrence(output: torch.Tensor, spec: torch.Tensor, seeds: torch.Tensor,
-                                       coef: torch.Tensor, cos_theta: torch.Tensor, scale: float = 1.0) -> None:
-    """Vector forward with on-the-fly tables (``holysht_legendre_vector_forward_recurrence``):
+                                       coef: torch.Tensor, cos_theta: torch.Tensor, scale: float = 1.0,
+                                       parity: bool = False) -> None:
+    """Vector forward with on-the-fly tables (``holysht_legendre_vector_forward_recurrence_ex``):
     output [B, 2, L, M] complex64 from an rfft-layout spectrum [B, 2, K, W >= M];
     ``seeds``, ``coef`` and ``cos_theta`` from
-    :func:`holysht_b200.weights.vector_recurrence_tables`."""
+    :func:`holysht_b200.weights.vector_recurrence_tables`.  ``parity`` folds the
+    grid's equatorial symmetry (see :func:`holysht_b200.weights.recurrence_seeds_symmetric`).
+    Seeds [K, nsegs, 4] are the compact layout
+    (:func:`holysht_b200.weights.compact_recurrence_seeds`)."""
     dev = _cuda(output, spec, seeds, coef, cos_theta)
     _require(spec.dtype == torch.complex64 and output.dtype == torch.complex64, "spectrum and output are complex64")
     _require(spec.dim() == 4 and spec.size(1) == 2 and spec.stride(3) == 1,
              "spectrum must be [B, 2, K, W] with contiguous orders")
     _contig(output, seeds, coef, cos_theta)
-    M, nseg, K, four = seeds.shape
-    L = coef.size(1)
+    flags = _lib.FLAG_EQUATORIAL_PARITY if parity else 0
+    M, L = coef.size(0), coef.size(1)
+    if seeds.dim() == 3:
+        K, nsegs, four = seeds.shape
+        _require(nsegs == _nsegs(L, M), "compact seeds do not match lmax / mmax")
+        flags |= _lib.FLAG_SEEDS_COMPACT
+    else:
+        _require(seeds.dim() == 4 and seeds.size(0) == M, "seeds must be [M, nseg, K, 4] or [K, nsegs, 4]")
+        _, nseg, K, four = seeds.shape
+        _require(nseg == (L + 15) // 16, "seeds must hold ceil(lmax / 16) segments per order")
     B = spec.size(0)
     _require(four == 4 and tuple(coef.shape) == (M, L, 8) and cos_theta.numel() == K, "inconsistent tables")
     _require(spec.size(2) == K and spec.size(3) >= M, "spectrum must be [B, 2, nlat, >= mmax]")
     _require(tuple(output.shape) == (B, 2, L, M), "output must be [B, 2, lmax, mmax]")
     with torch.cuda.device(dev):
-        _lib.check(_lib.load().holysht_legendre_vector_forward_recurrence(
+        _lib.check(_lib.load().holysht_legendre_vector_forward_recurrence_ex(
             _p(output), _p(spec), spec.stride(0), spec.stride(1), spec.stride(2), _p(seeds), _p(coef),
-            _p(cos_theta), B, K, L, M, float(scale), _stream(dev)))
+            _p(cos_theta), B, K, L, M, float(scale), flags, _stream(dev)))
 
 
 def legendre_forward_recurrence(output: torch.Tensor, spec: torch.Tensor, seeds: torch.Tensor, coef: torch.Tensor,
-                                cos_theta: torch.Tensor, scale: float = 1.0) -> None:
-    """Scalar forward with on-the-fly Legendre functions (``holysht_legendre_forward_recurrence``):
+                                cos_theta: torch.Tensor, scale: float = 1.0, parity: bool = False) -> None:
+    """Scalar forward with on-the-fly Legendre functions (``holysht_legendre_forward_recurrence_ex``):
     output [B, L, M] complex64 from an rfft-layout spectrum [B, K, W >= M]; ``seeds``,
-    ``coef`` and ``cos_theta`` from :func:`holysht_b200.weights.scalar_recurrence_tables`."""
+    ``coef`` and ``cos_theta`` from :func:`holysht_b200.weights.scalar_recurrence_tables`.
+    ``parity`` folds the grid's equatorial symmetry (the seeds must come from a
+    grid symmetric about the equator; see :func:`holysht_b200.weights.recurrence_seeds_symmetric`).
+    Seeds [K, nsegs, 2] are the compact layout
+    (:func:`holysht_b200.weights.compact_recurrence_seeds`)."""
     dev = _cuda(output, spec, seeds, coef, cos_theta)
     _require(spec.dtype == torch.complex64 and output.dtype == torch.complex64, "spectrum and output are complex64")
     _require(spec.dim() == 3 and spec.stride(2) == 1, "spectrum must be [B, K, W] with contiguous orders")
     _contig(output, seeds, coef, cos_theta)
-    M, nseg, K, two = seeds.shape
-    L = coef.size(1)
+    flags = _lib.FLAG_EQUATORIAL_PARITY if parity else 0
+    M, L = coef.size(0), coef.size(1)
+    if seeds.dim() == 3:
+        K, nsegs, two = seeds.shape
+        _require(nsegs == _nsegs(L, M), "compact seeds do not match lmax / mmax")
+        flags |= _lib.FLAG_SEEDS_COMPACT
+    else:
+        _require(seeds.dim() == 4 and seeds.size(0) == M, "seeds must be [M, nseg, K, 2] or [K, nsegs, 2]")
+        _, nseg, K, two = seeds.shape
+        _require(nseg == (L + 15) // 16, "seeds must hold ceil(lmax / 16) segments per order")
     B = spec.size(0)
     _require(two == 2 and tuple(coef.shape) == (M, L, 2) and cos_theta.numel() == K, "inconsistent tables")
     _require(spec.size(1) == K and spec.size(2) >= M, "spectrum must be [B, nlat, >= mmax]")
     _require(tuple(output.shape) == (B, L, M), "output must be [B, lmax, mmax]")
     with torch.cuda.device(dev):
-        _lib.check(_lib.load().holysht_legendre_forward_recurrence(
+        _lib.check(_lib.load().holysht_legendre_forward_recurrence_ex(
             _p(output), _p(spec), spec.stride(0), spec.stride(1), _p(seeds), _p(coef), _p(cos_theta),
-            B, K, L, M, float(scale), _stream(dev)))
+            B, K, L, M, float(scale), flags, _stream(dev)))

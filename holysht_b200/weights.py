@@ -342,6 +342,40 @@ def scalar_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular
     return seeds, coef, x.astype(np.float32)
 
 
+def recurrence_seeds_symmetric(seeds, cos_theta, tol=1e-6) -> bool:
+    """True when recurrence checkpoints obey the equatorial parity the
+    ``HOLYSHT_FLAG_EQUATORIAL_PARITY`` kernels rely on: cos_theta mirrored
+    (x_{K-1-k} = -x_k) and, for every checkpoint degree pair (l0, l0 + 1) of an
+    order, the mirrored latitude's value equal to +/- this one's, the sign
+    (-1)^(l+m') of the Legendre function's order m' (scalar seeds [..., 2]: orders
+    m, signs (+, -); vector seeds [..., 4]: orders m -/+ 1, signs (-, +, -, +)).
+    Checked to ``tol`` of the largest seed."""
+    s = np.asarray(seeds, dtype=np.float32)
+    x = np.asarray(cos_theta, dtype=np.float64)
+    if x.size == 0 or np.abs(x + x[::-1]).max() > 1e-6:
+        return False
+    sign = np.array([1.0, -1.0] if s.shape[-1] == 2 else [-1.0, 1.0, -1.0, 1.0], dtype=np.float32)
+    scale = max(float(np.abs(s).max()), 1e-30)
+    err = 0.0
+    for m in range(s.shape[0]):  # one order at a time: bounded temporaries
+        d = s[m, :, ::-1, :] - sign * s[m]
+        err = max(err, float(np.abs(d).max()) if d.size else 0.0)
+    return err <= tol * scale
+
+
+def compact_recurrence_seeds(seeds, lmax: int):
+    """Checkpoints in the compact latitude-major layout of
+    ``HOLYSHT_FLAG_SEEDS_COMPACT``: [nlat, nsegs, S] from [mmax, nseg, nlat, S],
+    keeping for each order m < min(mmax, lmax) its ceil((lmax - m) / 16)
+    segments, orders in turn.  A warp of the recurrence kernels owns 32
+    consecutive segments, so one latitude's checkpoints are contiguous."""
+    s = np.asarray(seeds)
+    mlim = min(s.shape[0], lmax)
+    parts = [s[m, : (lmax - m + SEGMENT - 1) // SEGMENT] for m in range(mlim)]
+    flat = np.concatenate(parts, axis=0) if parts else np.zeros((0,) + s.shape[2:], s.dtype)
+    return np.ascontiguousarray(flat.transpose(1, 0, 2))
+
+
 def vector_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True):
     """Inputs of the vector recurrence kernel (float64 built, float32 returned).
 

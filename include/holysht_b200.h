@@ -292,13 +292,39 @@ int holysht_legendre_dense_tc(int direction, void* out, int64_t out_batch_stride
  *   coef      float32 [mmax][lmax][2]: the recurrence coefficients (a_lm, b_lm);
  *   cos_theta float32 [nlat].
  * spec: complex64, element (b,k,m) at spec + b*spec_batch_stride + k*spec_row_stride + m;
- * out: complex64 [B][lmax][mmax].  nlat <= 2048.  (holysht_b200.weights builds
+ * out: complex64 [B][lmax][mmax].  (holysht_b200.weights builds
  * the three inputs.) */
 int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spec_batch_stride,
                                         int64_t spec_row_stride, const float* seeds,
                                         const float* coef, const float* cos_theta, int64_t batch,
                                         int64_t nlat, int64_t lmax, int64_t mmax, float scale,
                                         void* stream);
+
+/* HOLYSHT_FLAG_EQUATORIAL_PARITY (recurrence entries): the grid is symmetric
+ * about the equator (cos theta_{nlat-1-k} = -cos theta_k, equal quadrature
+ * weights), so P_l^m(-x) = (-1)^(l+m) P_l^m(x): only the northern latitudes'
+ * Legendre functions are generated, contracted with the sum (l + m even) or
+ * difference (l + m odd) of each latitude's spectrum and its mirror's.  Every
+ * grid holysht_b200.weights builds is symmetric; the result is undefined for
+ * seeds of an asymmetric grid. */
+#define HOLYSHT_FLAG_EQUATORIAL_PARITY 32
+
+/* HOLYSHT_FLAG_SEEDS_COMPACT (recurrence entries): `seeds` is in the compact,
+ * latitude-major layout [nlat][nsegs][S] (S = 2 scalar, 4 vector) holding only
+ * the segments that exist: for each order m < min(mmax, lmax) in turn, its
+ * segments c = 0 .. ceil((lmax - m) / 16) - 1, nsegs their total
+ * (holysht_b200.weights.compact_recurrence_seeds builds it).  The default
+ * layout is [mmax][ceil(lmax/16)][nlat][S]. */
+#define HOLYSHT_FLAG_SEEDS_COMPACT 64
+
+/* holysht_legendre_forward_recurrence with flags (HOLYSHT_FLAG_EQUATORIAL_PARITY,
+ * HOLYSHT_FLAG_SEEDS_COMPACT); the plain entry is flags = 0.  seeds must be
+ * 8-byte aligned; any nlat. */
+int holysht_legendre_forward_recurrence_ex(void* out, const void* spec, int64_t spec_batch_stride,
+                                           int64_t spec_row_stride, const float* seeds,
+                                           const float* coef, const float* cos_theta, int64_t batch,
+                                           int64_t nlat, int64_t lmax, int64_t mmax, float scale,
+                                           int flags, void* stream);
 
 /* Vector forward (RealVectorSHT's contraction) with on-the-fly tables: the
  * orders m - 1 and m + 1 Legendre recurrences run in fp32 from float64
@@ -308,11 +334,21 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
  * c*spec_comp_stride + k*spec_row_stride + m (the rfft layout), seeds
  * [mmax][ceil(lmax/16)][nlat][4] (16-byte aligned), coef [mmax][lmax][8],
  * cos_theta [nlat], all from holysht_b200.weights.vector_recurrence_tables.
- * Output = scale * contraction; exact zeros for m > l.  nlat <= 1024. */
+ * Output = scale * contraction; exact zeros for m > l. */
 int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int64_t spec_batch_stride,
                                                int64_t spec_comp_stride, int64_t spec_row_stride, const float* seeds,
                                                const float* coef, const float* cos_theta, int64_t batch,
                                                int64_t nlat, int64_t lmax, int64_t mmax, float scale, void* stream);
+
+/* holysht_legendre_vector_forward_recurrence with flags
+ * (HOLYSHT_FLAG_EQUATORIAL_PARITY, HOLYSHT_FLAG_SEEDS_COMPACT); the plain entry
+ * is flags = 0.  seeds and coef 16-byte aligned; any nlat. */
+int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, int64_t spec_batch_stride,
+                                                  int64_t spec_comp_stride, int64_t spec_row_stride,
+                                                  const float* seeds, const float* coef,
+                                                  const float* cos_theta, int64_t batch, int64_t nlat,
+                                                  int64_t lmax, int64_t mmax, float scale, int flags,
+                                                  void* stream);
 
 /* Same contraction as holysht_legendre_dense_tc, for callers that cannot
  * allocate device memory (a host whose own allocator owns the GPU memory, a

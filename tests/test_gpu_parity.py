@@ -493,3 +493,48 @@ def test_vector_recurrence_variant_matches_oracle(nlat, nlon, grid, norm, cs):
     ref = t(torch.from_numpy(x).to(DEV)).cpu().numpy().astype(np.complex128)
     got = out.cpu().numpy().astype(np.complex128)
     assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-6
+
+
+@pytest.mark.parametrize("vector", [False, True])
+@pytest.mark.parametrize("nlat,nlon,grid", [(47, 96, "equiangular"), (64, 128, "legendre-gauss")])
+def test_recurrence_ops_every_fold_and_block_shape(vector, nlat, nlon, grid, monkeypatch):
+    """The recurrence ops with and without the equatorial fold, for every
+    degree-block and latitude-chunk shape of the segment kernels, odd and even
+    nlat, 6 batches (a partial batch group), against the float64 oracle."""
+    rng = np.random.default_rng(nlat + 7 * vector)
+    B = 6
+    if vector:
+        seeds, coef, ct = hs.weights.vector_recurrence_tables(nlat, nlon, grid=grid)
+        mod = hs.RealVectorSHT(nlat, nlon, grid=grid)
+    else:
+        seeds, coef, ct = hs.weights.scalar_recurrence_tables(nlat, nlon, grid=grid)
+        mod = hs.RealSHT(nlat, nlon, grid=grid)
+    assert hs.weights.recurrence_seeds_symmetric(seeds, ct)
+    M, _, K, _ = seeds.shape
+    L = coef.shape[1]
+    shape = (B, 2, K, M + 3) if vector else (B, K, M + 3)  # row stride wider than mmax
+    spec = (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)).astype(np.complex64)
+    if vector:
+        w0 = mod.w0_t.cpu().numpy().astype(np.float64)
+        w1 = mod.w1_t.cpu().numpy().astype(np.float64)
+        ref = orc.vector_legendre_forward(spec[..., :M].astype(np.complex128), w0, w1)
+    else:
+        ref = orc.legendre_forward(spec[..., :M].astype(np.complex128),
+                                      mod.weight_t.cpu().numpy().astype(np.float64))
+    layouts = [torch.from_numpy(seeds).to(DEV),
+               torch.from_numpy(hs.weights.compact_recurrence_seeds(seeds, L)).to(DEV)]
+    cf, x = (torch.from_numpy(a).to(DEV) for a in (coef, ct))
+    sp = torch.from_numpy(spec).to(DEV)
+    shapes = [("8", "4"), ("16", "2"), ("16", "8"), ("8", "8")]
+    for db, nkc in shapes:
+        monkeypatch.setenv("HSB_REC_DB", db)
+        monkeypatch.setenv("HSB_REC_NKC", nkc)
+        for parity in (False, True):
+            for sd in layouts:
+                out = torch.full((B, 2, L, M) if vector else (B, L, M), float("nan"), dtype=torch.complex64,
+                                 device=DEV)
+                if vector:
+                    ops.legendre_vector_forward_recurrence(out, sp, sd, cf, x, 1.0, parity=parity)
+                else:
+                    ops.legendre_forward_recurrence(out, sp, sd, cf, x, 1.0, parity=parity)
+                assert_fp32_close(out, ref)

@@ -326,3 +326,35 @@ def test_reference_backend_flags_map_onto_the_paths(monkeypatch):
     hs_mod._REF_FLAGS_WARNED.discard("HOLYSHT_AUTOTUNE")
     with pytest.warns(UserWarning, match="HOLYSHT_AUTOTUNE"):
         hs_mod._dense_tc_eligible(m, 1, _lib.DIR_FORWARD)
+
+
+def test_compact_recurrence_seeds_order_and_symmetry():
+    """The compact checkpoint layout keeps each order's existing segments, orders
+    in turn, latitude-major; the grids this package builds pass the equatorial
+    symmetry check and a perturbed one does not."""
+    nlat, nlon, L = 21, 40, 19
+    seeds, coef, ct = weights.scalar_recurrence_tables(nlat, nlon, lmax=L, mmax=15)
+    comp = weights.compact_recurrence_seeds(seeds, L)
+    per = [(L - m + 15) // 16 for m in range(15)]
+    assert comp.shape == (nlat, sum(per), 2)
+    i = 0
+    for m, n in enumerate(per):
+        for c in range(n):
+            np.testing.assert_array_equal(comp[:, i], seeds[m, c])
+            i += 1
+    assert weights.recurrence_seeds_symmetric(seeds, ct)
+    bad = seeds.copy()
+    bad[3, 0, 2, 0] += 1e-3 * np.abs(seeds).max()
+    assert not weights.recurrence_seeds_symmetric(bad, ct)
+    vs, _, vct = weights.vector_recurrence_tables(nlat, nlon, grid="legendre-gauss")
+    assert weights.recurrence_seeds_symmetric(vs, vct)
+
+
+def test_recurrence_flags_are_checked_without_gpu():
+    lib = _lib.load()
+    st = lib.holysht_legendre_forward_recurrence_ex(None, None, 0, 0, None, None, None, 1, 4, 4, 4,
+                                                    ctypes.c_float(1.0), 1 << 10, None)
+    assert st == _lib.HOLYSHT_ERR_INVALID and b"flag" in lib.holysht_last_error()
+    st = lib.holysht_legendre_vector_forward_recurrence_ex(None, None, 0, 0, 0, None, None, None, 1, 4, 4, 4,
+                                                           ctypes.c_float(1.0), _lib.FLAG_SEEDS_COMPACT, None)
+    assert st == _lib.HOLYSHT_ERR_INVALID and b"null" in lib.holysht_last_error()
