@@ -417,9 +417,11 @@ class _FastForward:
         self.final_shape, self.device = final_shape, device
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        spec = _rfft(x).view(self.spec_shape)
+        # the output is allocated before the rfft is enqueued, so only the
+        # pointer hand-off runs on the host between the two launches
         out = torch.empty(self.out_shape, dtype=torch.complex64, device=self.device)
-        self.plan.launch(spec, out)
+        spec = _rfft(x).view(self.spec_shape)
+        self.plan.launch_ptrs(spec.data_ptr(), out.data_ptr())
         return out.view(self.final_shape)
 
 

@@ -352,6 +352,22 @@ class ContractPlan:
                     _lib.check(lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev)))
 
 
+    def launch_ptrs(self, in_ptr: int, out_ptr: int) -> None:
+        """:meth:`launch` for a caller that has already matched the tensors to
+        the plan (the modules' cached forward: same input shape, its own rfft
+        output and a fresh output of the planned shape): pointers only."""
+        lib = _lib.load()
+        with self._lock:
+            d = self._desc
+            d.in_, d.out = in_ptr, out_ptr
+            if torch.cuda.current_device() == self._dev:
+                st = lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev))
+            else:
+                with torch.cuda.device(self._dev):
+                    st = lib.holysht_legendre_contract(ctypes.byref(d), _current_stream_handle(self._dev))
+        _lib.check(st)
+
+
 def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,
                       w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,
