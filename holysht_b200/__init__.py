@@ -408,18 +408,32 @@ class _FastForward:
     """The module forward for one input shape, once it has run through the
     general path: rfft, output allocation and the prepared contraction (no
     table lookups, checks or autograd).  Used only when no gradient is
-    wanted, for FP32 modules on the table path; dropped with the tables."""
+    wanted, for FP32 modules on the table path; dropped with the tables.
+    For a contiguous input the rfft and the contraction are one library call
+    (``holysht_rfft_contract``: cuFFT's R2C, then the Legendre kernel, on the
+    current stream); otherwise torch's rfft feeds the prepared launch."""
 
-    __slots__ = ("plan", "spec_shape", "out_shape", "final_shape", "device")
+    __slots__ = ("plan", "spec_shape", "out_shape", "final_shape", "device", "rows", "nlon", "fft_work")
 
-    def __init__(self, plan, spec_shape, out_shape, final_shape, device):
+    def __init__(self, plan, spec_shape, out_shape, final_shape, device, nlon):
         self.plan, self.spec_shape, self.out_shape = plan, spec_shape, out_shape
         self.final_shape, self.device = final_shape, device
+        self.nlon = nlon
+        self.rows = 1
+        for d in spec_shape[:-1]:
+            self.rows *= d
+        self.fft_work = ops.rfft_workspace(self.rows, nlon, device) if self.rows > 0 else None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         # the output is allocated before the rfft is enqueued, so only the
         # pointer hand-off runs on the host between the two launches
         out = torch.empty(self.out_shape, dtype=torch.complex64, device=self.device)
+        if self.fft_work is not None and x.is_contiguous():
+            spec = torch.empty(self.spec_shape, dtype=torch.complex64, device=self.device)
+            work = torch.empty(self.fft_work, dtype=torch.uint8, device=self.device) if self.fft_work else None
+            self.plan.launch_rfft(x.data_ptr(), self.rows, self.nlon, spec.data_ptr(),
+                                  0 if work is None else work.data_ptr(), self.fft_work, out.data_ptr())
+            return out.view(self.final_shape)
         spec = _rfft(x).view(self.spec_shape)
         self.plan.launch_ptrs(spec.data_ptr(), out.data_ptr())
         return out.view(self.final_shape)
@@ -449,7 +463,8 @@ def _module_forward(module, x: torch.Tensor, comp_dims: int) -> torch.Tensor:
         cache = module.__dict__.setdefault("_fast_forward", {})
         if len(cache) >= _MAX_PLANS:
             cache.clear()
-        cache[(x.shape, x.dtype, x.device)] = _FastForward(plan, tuple(flat.shape), tuple(out.shape), final, x.device)
+        cache[(x.shape, x.dtype, x.device)] = _FastForward(plan, tuple(flat.shape), tuple(out.shape), final, x.device,
+                                                           module.nlon)
     return out.reshape(final)
 
 

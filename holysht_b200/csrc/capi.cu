@@ -4,6 +4,7 @@
 // non-negative extents, table/input extents that agree, and extents that fit
 // the kernels' 32-bit tile arithmetic.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 
 #include <atomic>
 #include <climits>
@@ -670,6 +671,80 @@ long long tc_workspace(long long B, long long R, long long S, long long M, bool 
 
 }  // namespace
 
+// ---- longitude rFFT through cuFFT (loaded at run time) ----------------------
+// The library does not link cuFFT: it opens libcufft.so.11 on first use,
+// preferring a copy the process has already loaded (torch's), so both share one
+// cuFFT.  Plans are cached per (device, rows, nlon) with auto-allocation off:
+// every execution takes its work area from the caller, as torch's own rFFT
+// does, so a plan may run on several streams at once.
+namespace {
+typedef int cufft_handle;
+struct CufftApi {
+  int (*create)(cufft_handle*) = nullptr;
+  int (*set_auto_alloc)(cufft_handle, int) = nullptr;
+  int (*make_plan_many)(cufft_handle, int, int*, int*, int, int, int*, int, int, int, int, size_t*) = nullptr;
+  int (*set_stream)(cufft_handle, cudaStream_t) = nullptr;
+  int (*set_work_area)(cufft_handle, void*) = nullptr;
+  int (*exec_r2c)(cufft_handle, float*, float2*) = nullptr;
+  bool ok = false;
+};
+constexpr int kCufftR2C = 0x2a;  // CUFFT_R2C
+
+const CufftApi& cufft_api() {
+  static CufftApi api = [] {
+    CufftApi a;
+    void* h = dlopen("libcufft.so.11", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libcufft.so.11", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libcufft.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return a;
+    a.create = reinterpret_cast<decltype(a.create)>(dlsym(h, "cufftCreate"));
+    a.set_auto_alloc = reinterpret_cast<decltype(a.set_auto_alloc)>(dlsym(h, "cufftSetAutoAllocation"));
+    a.make_plan_many = reinterpret_cast<decltype(a.make_plan_many)>(dlsym(h, "cufftMakePlanMany"));
+    a.set_stream = reinterpret_cast<decltype(a.set_stream)>(dlsym(h, "cufftSetStream"));
+    a.set_work_area = reinterpret_cast<decltype(a.set_work_area)>(dlsym(h, "cufftSetWorkArea"));
+    a.exec_r2c = reinterpret_cast<decltype(a.exec_r2c)>(dlsym(h, "cufftExecR2C"));
+    a.ok = a.create && a.set_auto_alloc && a.make_plan_many && a.set_stream && a.set_work_area && a.exec_r2c;
+    return a;
+  }();
+  return api;
+}
+
+struct RfftPlan {
+  cufft_handle h;
+  size_t work;
+};
+std::mutex g_fft_mu;
+std::map<std::array<long long, 3>, RfftPlan> g_fft_plans;  // (device, rows, nlon)
+constexpr size_t kMaxFftPlans = 64;  // plans live until exit (a plan in flight is never destroyed)
+
+// plan for `rows` transforms of nlon points (contiguous rows in, rows of
+// nlon/2+1 complex out) on the current device; call with g_fft_mu held
+int rfft_plan(long long rows, long long nlon, RfftPlan* out) {
+  const CufftApi& api = cufft_api();
+  if (!api.ok) return fail(HOLYSHT_ERR_UNSUPPORTED, "libcufft.so.11 could not be loaded");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(HOLYSHT_ERR_CUDA, "no current CUDA device");
+  const std::array<long long, 3> key = {dev, rows, nlon};
+  auto it = g_fft_plans.find(key);
+  if (it != g_fft_plans.end()) {
+    *out = it->second;
+    return ok();
+  }
+  if (g_fft_plans.size() >= kMaxFftPlans) return fail(HOLYSHT_ERR_UNSUPPORTED, "too many rFFT shapes");
+  RfftPlan p{};
+  if (api.create(&p.h) != 0) return fail(HOLYSHT_ERR_CUDA, "cufftCreate failed");
+  int n[1] = {(int)nlon};
+  int onembed[1] = {(int)(nlon / 2 + 1)};
+  if (api.set_auto_alloc(p.h, 0) != 0 ||
+      api.make_plan_many(p.h, 1, n, n, 1, (int)nlon, onembed, 1, (int)(nlon / 2 + 1), kCufftR2C, (int)rows,
+                         &p.work) != 0)
+    return fail(HOLYSHT_ERR_CUDA, "cufftMakePlanMany failed for %lld x %lld", rows, nlon);
+  g_fft_plans[key] = p;
+  *out = p;
+  return ok();
+}
+}  // namespace
+
 extern "C" {
 
 int holysht_legendre_dense_tc_workspace_ex(int direction, int64_t batch, int64_t nlat, int64_t lmax, int64_t mmax,
@@ -1134,6 +1209,39 @@ int contract_impl(const holysht_contract_desc* d, void* const* peers, int n_peer
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream) {
   return contract_impl(desc, nullptr, 0, 0, nullptr, stream);
+}
+
+int holysht_rfft_workspace(int64_t rows, int64_t nlon, int64_t* bytes) {
+  if (!bytes) return fail(HOLYSHT_ERR_INVALID, "bytes pointer is null");
+  if (rows < 1 || nlon < 2 || !fits_int(rows) || !fits_int(nlon)) return fail(HOLYSHT_ERR_INVALID, "bad rFFT extents");
+  std::lock_guard<std::mutex> g(g_fft_mu);
+  RfftPlan p;
+  if (int st = rfft_plan(rows, nlon, &p)) return st;
+  *bytes = (int64_t)p.work;
+  return ok();
+}
+
+int holysht_rfft_contract(const float* field, int64_t rows, int64_t nlon, void* spec, void* fft_work,
+                          int64_t fft_work_bytes, const holysht_contract_desc* desc, void* stream) {
+  if (!field || !spec || !desc) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  if (rows < 1 || nlon < 2 || !fits_int(rows) || !fits_int(nlon)) return fail(HOLYSHT_ERR_INVALID, "bad rFFT extents");
+  if (desc->direction != HOLYSHT_DIR_FORWARD || desc->in_dtype != HOLYSHT_DTYPE_C64)
+    return fail(HOLYSHT_ERR_INVALID, "the rFFT feeds a forward contraction of complex input");
+  {
+    std::lock_guard<std::mutex> g(g_fft_mu);
+    RfftPlan p;
+    if (int st = rfft_plan(rows, nlon, &p)) return st;
+    if (p.work > 0 && (!fft_work || fft_work_bytes < (int64_t)p.work))
+      return fail(HOLYSHT_ERR_INVALID, "rFFT work area of %lld bytes needed", (long long)p.work);
+    const CufftApi& api = cufft_api();
+    if (api.set_stream(p.h, static_cast<cudaStream_t>(stream)) != 0 ||
+        (p.work > 0 && api.set_work_area(p.h, fft_work) != 0) ||
+        api.exec_r2c(p.h, const_cast<float*>(field), static_cast<float2*>(spec)) != 0)
+      return fail(HOLYSHT_ERR_CUDA, "cufftExecR2C failed");
+  }
+  holysht_contract_desc d = *desc;
+  d.in = spec;
+  return contract_impl(&d, nullptr, 0, 0, nullptr, stream);
 }
 
 int holysht_legendre_contract_peers(const holysht_contract_desc* desc, void* const* peer_out, int n_peers,

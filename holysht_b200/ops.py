@@ -368,6 +368,39 @@ class ContractPlan:
         _lib.check(st)
 
 
+    def launch_rfft(self, field_ptr: int, rows: int, nlon: int, spec_ptr: int, work_ptr: int, work_bytes: int,
+                    out_ptr: int) -> None:
+        """The longitude rFFT of ``rows`` contiguous float32 rows into the
+        spectrum buffer ``spec_ptr`` (this plan's input layout), then this
+        contraction, in one library call (``holysht_rfft_contract``); for a caller
+        that has matched the buffers to the plan, like :meth:`launch_ptrs`."""
+        lib = _lib.load()
+        with self._lock:
+            d = self._desc
+            d.out = out_ptr
+            if torch.cuda.current_device() == self._dev:
+                st = lib.holysht_rfft_contract(field_ptr, rows, nlon, spec_ptr, work_ptr, work_bytes,
+                                               ctypes.byref(d), _current_stream_handle(self._dev))
+            else:
+                with torch.cuda.device(self._dev):
+                    st = lib.holysht_rfft_contract(field_ptr, rows, nlon, spec_ptr, work_ptr, work_bytes,
+                                                   ctypes.byref(d), _current_stream_handle(self._dev))
+        _lib.check(st)
+
+
+def rfft_workspace(rows: int, nlon: int, device) -> Optional[int]:
+    """Work-area bytes of the library's cuFFT plan for ``rows`` transforms of
+    ``nlon`` points on ``device`` (``holysht_rfft_workspace``), or None when
+    cuFFT cannot be opened."""
+    v = ctypes.c_int64(0)
+    with torch.cuda.device(device):
+        st = _lib.load().holysht_rfft_workspace(rows, nlon, ctypes.byref(v))
+    if st == _lib.HOLYSHT_ERR_UNSUPPORTED:
+        return None
+    _lib.check(st)
+    return int(v.value)
+
+
 def legendre_contract(*, kind: int, direction: int, input: torch.Tensor, output: torch.Tensor,
                       w0: torch.Tensor, w1: Optional[torch.Tensor] = None, batch: int, nlat: int,
                       lmax: int, mmax: int, in_strides, out_strides, out_cols: int,

@@ -204,6 +204,21 @@ typedef struct holysht_contract_desc {
 
 int holysht_legendre_contract(const holysht_contract_desc* desc, void* stream);
 
+/* Forward transform from the real field in one call: the longitude rFFT of
+ * `rows` contiguous rows of `nlon` float32 (unnormalised, cuFFT R2C on
+ * `stream`) into `spec` (caller-allocated, rows x (nlon/2+1) complex64), then
+ * holysht_legendre_contract(desc) with desc->in replaced by `spec` (desc's
+ * input strides describe `spec`; forward direction, complex input).  cuFFT is
+ * opened at run time (libcufft.so.11, the process's copy when one is loaded);
+ * HOLYSHT_ERR_UNSUPPORTED when it cannot be.  No counterpart operator in the
+ * reference, whose module calls torch.fft.rfft and then the Legendre operator
+ * (torch-ext/holysht/__init__.py:1288-1389, :1504-1693): this entry is those
+ * two steps.  fft_work: at least holysht_rfft_workspace() bytes (may be NULL
+ * when that is 0), from the caller's allocator on the same stream. */
+int holysht_rfft_workspace(int64_t rows, int64_t nlon, int64_t* bytes);
+int holysht_rfft_contract(const float* field, int64_t rows, int64_t nlon, void* spec, void* fft_work,
+                          int64_t fft_work_bytes, const holysht_contract_desc* desc, void* stream);
+
 /* The same contraction (HOLYSHT_TABLE_GROUPED8 layout only) with its output
  * stored on several GPUs at once: no counterpart in the reference, which has
  * no multi-GPU code; it is the fused "contract + all-gather" step of the

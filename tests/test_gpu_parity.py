@@ -538,3 +538,30 @@ def test_recurrence_ops_every_fold_and_block_shape(vector, nlat, nlon, grid, mon
                 else:
                     ops.legendre_forward_recurrence(out, sp, sd, cf, x, 1.0, parity=parity)
                 assert_fp32_close(out, ref)
+
+
+@pytest.mark.parametrize("vector", [False, True])
+def test_cached_forward_runs_rfft_and_contraction_in_one_call(vector):
+    """From the second call on, a no-grad FP32 forward runs cuFFT's R2C and the
+    Legendre kernel in one library call (holysht_rfft_contract); it gives the
+    first call's result (torch's rfft + the contraction) and the oracle's, and a
+    non-contiguous input of the same shape takes torch's rfft instead."""
+    rng = np.random.default_rng(11 + vector)
+    nlat, nlon = 96, 192
+    shape = (3, 2, nlat, nlon) if vector else (3, nlat, nlon)
+    x = rng.standard_normal(shape).astype(np.float32)
+    m = (hs.RealVectorSHT if vector else hs.RealSHT)(nlat, nlon).to(DEV)
+    xt = torch.from_numpy(x).to(DEV)
+    with torch.no_grad():
+        first = m(xt)
+        fast = next(iter(m.__dict__["_fast_forward"].values()))
+        assert fast.fft_work is not None, "the library could not open cuFFT"
+        second = m(xt)
+        wide = torch.zeros(shape[:-1] + (2 * nlon,), device=DEV)
+        wide[..., :nlon] = xt
+        third = m(wide[..., :nlon])  # same shape, rows not contiguous
+    assert not wide[..., :nlon].is_contiguous()
+    assert rel_l2(second.cpu().numpy(), first.cpu().numpy()) <= 1e-7
+    assert rel_l2(third.cpu().numpy(), first.cpu().numpy()) <= 1e-7
+    ref = (_module_oracle_vector if vector else _module_oracle_scalar)(m, x.astype(np.float64))
+    assert_fp32_close(second, ref)
