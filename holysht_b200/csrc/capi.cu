@@ -723,7 +723,11 @@ int rfft_plan(long long rows, long long nlon, RfftPlan* out) {
   const CufftApi& api = cufft_api();
   if (!api.ok) return fail(HOLYSHT_ERR_UNSUPPORTED, "libcufft.so.11 could not be loaded");
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(HOLYSHT_ERR_CUDA, "no current CUDA device");
+  // cuFFT needs the device's context current on this thread; a thread that
+  // has made no runtime call yet has none (cudaSetDevice makes the primary
+  // context current)
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess)
+    return fail(HOLYSHT_ERR_CUDA, "no current CUDA device");
   const std::array<long long, 3> key = {dev, rows, nlon};
   auto it = g_fft_plans.find(key);
   if (it != g_fft_plans.end()) {
