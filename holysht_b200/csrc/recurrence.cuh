@@ -1,5 +1,5 @@
-// Scalar forward Legendre transform with on-the-fly associated Legendre
-// functions (the "recurrence" variant): no table stream.
+// Forward Legendre transforms with on-the-fly associated Legendre functions
+// (the "recurrence" variant): no table stream.
 //
 //   out[b, l, m] = scale * sum_k X[b, k, m] * w_k P_l^m(x_k)        (l >= m)
 //
@@ -9,15 +9,14 @@
 // computed in float64 on the host (quadrature weight folded in; values below
 // fp32 range are exact zeros, which is what they contribute).  Re-seeding
 // bounds the fp32 drift of the recurrence: with 16-degree segments the
-// coefficients stay within ~5e-7 relative L2 of the float64 transform at
-// lmax = 512.
+// coefficients stay within ~6e-7 relative L2 of the float64 transform at
+// lmax = 512.  The vector form runs the recurrences of orders m - 1 and m + 1
+// and combines them by the ladder identities.
 //
-// CTA: one order m, 4 checkpoint segments (64 degrees), a group of 4 batches,
-// threads over latitude (kKpt latitudes per thread, in registers with the
-// kKpt x 4 complex spectrum values they multiply).  Per degree each thread forms 8 partial sums (4 batches x re/im);
-// every 4 degrees a warp transposes-and-reduces its 32 values with shuffles
-// (lane j ends with value j summed over the warp's latitudes) and the warps'
-// results are summed through shared memory.
+// Two kernel families: the segment-per-thread kernels (the default; one
+// thread per order and checkpoint segment, partial sums in registers, see
+// below) and the earlier paired-latitude kernels (threads over latitude with
+// warp transpose-reductions every few degrees), kept for comparison.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -28,10 +27,6 @@ namespace hsb {
 namespace rec {
 
 constexpr int kSeg = 16;      // degrees per checkpoint segment
-#ifndef HSB_REC_KPT
-#define HSB_REC_KPT 4
-#endif
-constexpr int kKpt = HSB_REC_KPT;  // latitudes per thread
 constexpr int kNB = 4;        // batches per CTA
 constexpr int kMaxWarps = 8;  // nlat <= 8 * 32 * 8 = 2048
 
@@ -51,133 +46,9 @@ struct RecParams {
 #endif
 constexpr int kSegPerCta = HSB_REC_SEGS_PER_CTA;  // checkpoint segments per CTA
 
-// grid: x = order m, y = block of kSegPerCta segments, z = batch group
-__global__ void __launch_bounds__(kMaxWarps * 32) recurrence_forward_kernel(const RecParams p) {
-  __shared__ float red[kMaxWarps][32];
-  const int m = blockIdx.x;
-  const int b0 = blockIdx.z * kNB;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
-  const int lm = p.L - m;  // degrees l = m .. L-1
-  const int nseg = lm > 0 ? (lm + kSeg - 1) / kSeg : 0;
-  const int c_begin = blockIdx.y * kSegPerCta;
-
-  if (blockIdx.y == 0) {
-    // rows l < m (and every row of an order without degrees) are exact zeros
-    const int zrows = lm > 0 ? m : p.L;
-    for (int e = tid; e < zrows * kNB; e += blockDim.x) {
-      const int l = e / kNB, b = b0 + e % kNB;
-      if (b < p.B) p.out[((long long)b * p.L + l) * p.M + m] = make_float2(0.f, 0.f);
-    }
-  }
-  if (c_begin >= nseg) return;  // uniform per CTA
-  const int c_end = min(nseg, c_begin + kSegPerCta);
-
-  // this thread's latitudes, their cos(theta) and scaled spectrum values
-  const int k0 = tid * kKpt;
-  float xk[kKpt];
-  float2 X[kKpt][kNB];
-#pragma unroll
-  for (int i = 0; i < kKpt; ++i) {
-    const int k = k0 + i;
-    xk[i] = k < p.K ? p.x[k] : 0.f;
-#pragma unroll
-    for (int b = 0; b < kNB; ++b) {
-      float2 v = make_float2(0.f, 0.f);
-      if (k < p.K && b0 + b < p.B) v = p.spec[(long long)(b0 + b) * p.sbs + (long long)k * p.srs + m];
-      X[i][b] = make_float2(v.x * p.scale, v.y * p.scale);
-    }
-  }
-
-  const float* coef_m = p.coef + (long long)m * p.L * 2;
-  for (int c = c_begin; c < c_end; ++c) {
-    const int lseg = m + c * kSeg;
-    // the segment's seeds and recurrence coefficients, loaded up front
-    const float* sd = p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 2;
-    float p1[kKpt], p2[kKpt];
-    float ca[kSeg], cb[kSeg];
-#pragma unroll
-    for (int q = 2; q < kSeg; ++q) {
-      const int l = lseg + q;
-      ca[q] = l < p.L ? coef_m[2 * l] : 0.f;
-      cb[q] = l < p.L ? coef_m[2 * l + 1] : 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < kKpt; ++i) {
-      const bool ok = k0 + i < p.K;
-      p2[i] = ok ? sd[2 * i] : 0.f;      // P at lseg
-      p1[i] = ok ? sd[2 * i + 1] : 0.f;  // P at lseg + 1
-    }
-#pragma unroll
-    for (int qb = 0; qb < kSeg; qb += 4) {
-      float v[32];  // 4 degrees x (4 batches x re/im)
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int q = qb + q4;
-        float pl[kKpt];
-        if (q == 0) {
-#pragma unroll
-          for (int i = 0; i < kKpt; ++i) pl[i] = p2[i];
-        } else if (q == 1) {
-#pragma unroll
-          for (int i = 0; i < kKpt; ++i) pl[i] = p1[i];
-        } else {
-#pragma unroll
-          for (int i = 0; i < kKpt; ++i) {
-            pl[i] = fmaf(ca[q] * xk[i], p1[i], -cb[q] * p2[i]);
-            p2[i] = p1[i];
-            p1[i] = pl[i];
-          }
-        }
-        float2 acc[kNB];
-#pragma unroll
-        for (int b = 0; b < kNB; ++b) acc[b] = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < kKpt; ++i)
-#pragma unroll
-          for (int b = 0; b < kNB; ++b) acc[b] = __ffma2_rn(make_float2(pl[i], pl[i]), X[i][b], acc[b]);
-#pragma unroll
-        for (int b = 0; b < kNB; ++b) {
-          v[q4 * 8 + 2 * b] = acc[b].x;
-          v[q4 * 8 + 2 * b + 1] = acc[b].y;
-        }
-      }
-      // warp transpose-reduce: lane j ends with value j summed over the warp
-#pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) {
-        const bool upper = (lane & d) != 0;
-#pragma unroll
-        for (int i = 0; i < d; ++i) {
-          const float send = upper ? v[i] : v[i + d];
-          const float keep = upper ? v[i + d] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
-        }
-      }
-      if (nwarps == 1) {
-        const int q4 = lane >> 3, b = (lane >> 1) & 3, ri = lane & 1;
-        const int l = lseg + qb + q4;
-        if (l < p.L && b0 + b < p.B)
-          reinterpret_cast<float*>(p.out)[(((long long)(b0 + b) * p.L + l) * p.M + m) * 2 + ri] = v[0];
-      } else {
-        red[warp][lane] = v[0];
-        __syncthreads();
-        if (warp == 0) {
-          float sum = 0.f;
-          for (int w = 0; w < nwarps; ++w) sum += red[w][lane];
-          const int q4 = lane >> 3, b = (lane >> 1) & 3, ri = lane & 1;
-          const int l = lseg + qb + q4;
-          if (l < p.L && b0 + b < p.B)
-            reinterpret_cast<float*>(p.out)[(((long long)(b0 + b) * p.L + l) * p.M + m) * 2 + ri] = sum;
-        }
-        __syncthreads();
-      }
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
-// Paired-latitude scalar kernel (the one the library launches).  Same maths
-// and checkpoints as recurrence_forward_kernel, organised for the FP32 pipe:
+// Paired-latitude scalar kernel (HSB_REC_PAIR=1, kept for comparison with the
+// segment-per-thread kernel below, which the library launches by default):
 //   * each thread holds KPT latitudes as KPT/2 pairs; the recurrence and the
 //     contraction run on packed f32x2 operations whose two halves are the two
 //     latitudes of a pair (fma.rn.f32x2 with no operand duplication: the
@@ -350,150 +221,10 @@ struct VecRecParams {
   float scale;
 };
 
-// grid: x = order m, y = block of kSegPerCta segments, z = batch group of kNB
-__global__ void __launch_bounds__(kMaxWarps * 32) recurrence_vector_forward_kernel(const VecRecParams p) {
-  __shared__ float red[kMaxWarps][32];
-  __shared__ float cf[kSegPerCta * kSeg][8];
-  const int m = blockIdx.x;
-  const int b0 = blockIdx.z * kNB;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
-  const int lm = p.L - m;
-  const int nseg = lm > 0 ? (lm + kSeg - 1) / kSeg : 0;
-  const int c_begin = blockIdx.y * kSegPerCta;
-  const long long plane = (long long)p.L * p.M;
-
-  if (blockIdx.y == 0) {
-    // rows l < m of both components (every row of an order without degrees) are exact zeros
-    const int zrows = lm > 0 ? m : p.L;
-    for (int e = tid; e < zrows * kNB * 2; e += blockDim.x) {
-      const int l = e / (kNB * 2), r = e % (kNB * 2), b = b0 + r / 2, pc = r % 2;
-      if (b < p.B) p.out[((long long)b * 2 + pc) * plane + (long long)l * p.M + m] = make_float2(0.f, 0.f);
-    }
-  }
-  if (c_begin >= nseg) return;  // uniform per CTA
-  const int c_end = min(nseg, c_begin + kSegPerCta);
-  const int l_first = m + c_begin * kSeg;
-  const int ndeg = min(p.L, m + c_end * kSeg) - l_first;
-  for (int e = tid; e < kSegPerCta * kSeg * 8; e += blockDim.x) {
-    const int dl = e / 8, f = e % 8;
-    cf[dl][f] = dl < ndeg ? p.coef[((long long)m * p.L + l_first + dl) * 8 + f] : 0.f;
-  }
-
-  // this thread's latitudes and u, v of its kNB batches (scaled)
-  const int k0 = tid * kKpt;
-  float xk[kKpt];
-  float2 U[kKpt][kNB], V[kKpt][kNB];
-#pragma unroll
-  for (int i = 0; i < kKpt; ++i) {
-    const int k = k0 + i;
-    xk[i] = k < p.K ? p.x[k] : 0.f;
-#pragma unroll
-    for (int b = 0; b < kNB; ++b) {
-      float2 c0 = make_float2(0.f, 0.f), c1 = c0;
-      if (k < p.K && b0 + b < p.B) {
-        const float2* s = p.spec + (long long)(b0 + b) * p.sbs + (long long)k * p.srs + m;
-        c0 = s[0];
-        c1 = s[p.sps];
-      }
-      U[i][b] = make_float2((c0.x - c1.y) * p.scale, (c0.y + c1.x) * p.scale);
-      V[i][b] = make_float2((c0.x + c1.y) * p.scale, (c0.y - c1.x) * p.scale);
-    }
-  }
-  __syncthreads();  // coefficients staged
-
-  for (int c = c_begin; c < c_end; ++c) {
-    const int lseg = m + c * kSeg;
-    const float* sd = p.seeds + (((long long)m * p.nseg + c) * p.K + k0) * 4;
-    float qm0[kKpt], qm1[kKpt], qp0[kKpt], qp1[kKpt];
-#pragma unroll
-    for (int i = 0; i < kKpt; ++i) {
-      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + i < p.K) s4 = reinterpret_cast<const float4*>(sd)[i];
-      qm0[i] = s4.x;
-      qm1[i] = s4.y;
-      qp0[i] = s4.z;
-      qp1[i] = s4.w;
-    }
-#pragma unroll
-    for (int qb = 0; qb < kSeg; qb += 2) {
-      float v[32];  // 2 degrees x (4 batches x (u, v) x re/im)
-#pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const float* k8 = cf[lseg + qb + q2 - l_first];
-        const float am = k8[0], bm = k8[1], ap = k8[2], bp = k8[3];
-        const float al = k8[4], be = k8[5], ga = k8[6], de = k8[7];
-        float2 au[kNB], av[kNB];
-#pragma unroll
-        for (int b = 0; b < kNB; ++b) au[b] = av[b] = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < kKpt; ++i) {
-          const float w0 = fmaf(al, qm0[i], be * qp0[i]);
-          const float w1 = fmaf(ga, qm1[i], de * qp1[i]);
-          const float wp = w0 + w1, wm = w0 - w1;
-#pragma unroll
-          for (int b = 0; b < kNB; ++b) {
-            au[b] = __ffma2_rn(make_float2(wp, wp), U[i][b], au[b]);
-            av[b] = __ffma2_rn(make_float2(wm, wm), V[i][b], av[b]);
-          }
-          // both recurrences to degree l + 2
-          const float nm = fmaf(am * xk[i], qm1[i], -bm * qm0[i]);
-          const float np = fmaf(ap * xk[i], qp1[i], -bp * qp0[i]);
-          qm0[i] = qm1[i];
-          qm1[i] = nm;
-          qp0[i] = qp1[i];
-          qp1[i] = np;
-        }
-#pragma unroll
-        for (int b = 0; b < kNB; ++b) {
-          v[q2 * 16 + b * 4 + 0] = au[b].x;
-          v[q2 * 16 + b * 4 + 1] = au[b].y;
-          v[q2 * 16 + b * 4 + 2] = av[b].x;
-          v[q2 * 16 + b * 4 + 3] = av[b].y;
-        }
-      }
-      // warp transpose-reduce: lane j ends with value j summed over the warp
-#pragma unroll
-      for (int d = 16; d >= 1; d >>= 1) {
-        const bool upper = (lane & d) != 0;
-#pragma unroll
-        for (int i = 0; i < d; ++i) {
-          const float send = upper ? v[i] : v[i + d];
-          const float keep = upper ? v[i + d] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
-        }
-      }
-      float sum = v[0];
-      if (nwarps > 1) {
-        red[warp][lane] = sum;
-        __syncthreads();
-        sum = 0.f;
-        if (warp == 0)
-          for (int w = 0; w < nwarps; ++w) sum += red[w][lane];
-      }
-      if (warp == 0) {
-        // lane j: degree qb + (j >> 4), batch (j >> 2) & 3, (u, v) product (j >> 1) & 1, re/im j & 1
-        const float other = __shfl_xor_sync(0xffffffffu, sum, 2);
-        const int q2 = lane >> 4, b = (lane >> 2) & 3, which = (lane >> 1) & 1, ri = lane & 1;
-        const int l = lseg + qb + q2;
-        if (which == 0 && l < p.L && b0 + b < p.B) {
-          const float pu = sum, mv = other;  // Wp u and Wm v, component ri
-          float* o = reinterpret_cast<float*>(p.out + (long long)(b0 + b) * 2 * plane + (long long)l * p.M + m);
-          o[ri] = 0.5f * (mv + pu);  // sph = (Wm v + Wp u) / 2
-          // tor = -i (Wm v - Wp u) / 2: re from the imaginary parts, im from the real parts
-          o[2 * plane + (1 - ri)] = ri ? 0.5f * (mv - pu) : -0.5f * (mv - pu);
-        }
-      }
-      if (nwarps > 1) __syncthreads();
-    }
-  }
-}
-
-// Paired-latitude vector kernel (the one the library launches): the maths of
-// recurrence_vector_forward_kernel with both recurrences, the table
-// combinations and the contraction on packed f32x2 operations over latitude
-// pairs (no operand duplication) and KPT latitudes per thread, which halves the
-// share of the per-degree warp reductions relative to 4 latitudes per thread.
+// Paired-latitude vector kernel (HSB_REC_PAIR=1, kept for comparison): both
+// recurrences, the table combinations and the contraction on packed f32x2
+// operations over latitude pairs (no operand duplication), KPT latitudes per
+// thread, a transpose-reduce over the warp every 2 degrees.
 template <int KPT>
 __global__ void __launch_bounds__(kMaxWarps * 32) recurrence_vector_forward_pair_kernel(const VecRecParams p) {
   constexpr int NP = KPT / 2;
