@@ -358,3 +358,13 @@ def test_recurrence_flags_are_checked_without_gpu():
     st = lib.holysht_legendre_vector_forward_recurrence_ex(None, None, 0, 0, 0, None, None, None, 1, 4, 4, 4,
                                                            ctypes.c_float(1.0), _lib.FLAG_SEEDS_COMPACT, None)
     assert st == _lib.HOLYSHT_ERR_INVALID and b"null" in lib.holysht_last_error()
+
+
+def test_rfft_entries_check_arguments_without_gpu():
+    lib = _lib.load()
+    v = ctypes.c_int64(0)
+    assert lib.holysht_rfft_workspace(0, 64, ctypes.byref(v)) == _lib.HOLYSHT_ERR_INVALID
+    assert lib.holysht_rfft_workspace(4, 64, None) == _lib.HOLYSHT_ERR_INVALID
+    d = _lib.ContractDesc()
+    assert lib.holysht_rfft_contract(None, 4, 64, None, None, 0, ctypes.byref(d), None) == _lib.HOLYSHT_ERR_INVALID
+    assert b"null" in lib.holysht_last_error()
