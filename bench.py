@@ -539,7 +539,10 @@ def run_c5(rank, world, dev, barrier, max_over_ranks):
         ms = _timed(lambda: m(x), 3, dev, barrier, max_over_ranks)
     res["C5_RealSHT_batch_split"] = {"ms": round(ms, 4), "slices_per_rank": n,
                                      "transforms_per_s": round(16 * 64 / (ms * 1e-3), 1),
-                                     "path": "tcgen05 dense" if n >= 128 else "streaming"}
+                                     "path": "tcgen05 dense" if n >= 128 else "streaming",
+                                     "limiter": ("no collective: each rank's own rfft, operand transposes and "
+                                                 "split-TF32 GEMM over its slices against a full table replica "
+                                                 "(2.15 GB per rank); time falls with the slices per rank")}
     del m, x
     torch.cuda.empty_cache()
     # -- vector, order partition (replicated input: the same seed on every rank)
@@ -551,7 +554,10 @@ def run_c5(rank, world, dev, barrier, max_over_ranks):
             ms = _timed(lambda: v(xv), 5, dev, barrier, max_over_ranks)
         key = "C5_RealVectorSHT_order_split" + ("" if comm == "auto" else "_nccl")
         res[key] = {"ms": round(ms, 4), "comm": v.comm, "orders": list(v.ranges[rank]),
-                    "transforms_per_s": round(16 / (ms * 1e-3), 1)}
+                    "transforms_per_s": round(16 / (ms * 1e-3), 1),
+                    "limiter": ("every rank runs the rfft of the whole replicated input and streams its "
+                                "1/world table slice once per 4-batch group; the exchange moves "
+                                "(world-1)/world of the 268 MB of coefficients to every rank")}
         del v
         torch.cuda.empty_cache()
     return res
