@@ -555,8 +555,8 @@ def run_c5(rank, world, dev, barrier, max_over_ranks):
         key = "C5_RealVectorSHT_order_split" + ("" if comm == "auto" else "_nccl")
         res[key] = {"ms": round(ms, 4), "comm": v.comm, "orders": list(v.ranges[rank]),
                     "transforms_per_s": round(16 / (ms * 1e-3), 1),
-                    "limiter": ("every rank runs the rfft of the whole replicated input and streams its "
-                                "1/world table slice once per 4-batch group; the exchange moves "
+                    "limiter": ("every rank runs the rfft of the whole replicated input and its 1/world "
+                                "of the orders' contraction (FP32 multiply-adds); the exchange moves "
                                 "(world-1)/world of the 268 MB of coefficients to every rank")}
         del v
         torch.cuda.empty_cache()
