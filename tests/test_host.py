@@ -368,3 +368,91 @@ def test_rfft_entries_check_arguments_without_gpu():
     d = _lib.ContractDesc()
     assert lib.holysht_rfft_contract(None, 4, 64, None, None, 0, ctypes.byref(d), None) == _lib.HOLYSHT_ERR_INVALID
     assert b"null" in lib.holysht_last_error()
+
+
+def _fold_scalar(spec, seeds, coef, x, L, M, par):
+    """The scalar segment kernels' algebra in float64 loops: per order and
+    16-degree segment, the recurrence from the checkpoints over (northern, with
+    ``par``) latitudes, contracted with X_k +/- X_{K-1-k} by the parity of the
+    degree's offset in the segment."""
+    B, K, _ = spec.shape
+    out = np.zeros((B, L, M), complex)
+    for m in range(min(M, L)):
+        for c in range((L - m + 15) // 16):
+            lseg = m + 16 * c
+            for k in range((K + 1) // 2 if par else K):
+                km = K - 1 - k
+                xm = spec[:, km, m] if (par and km != k) else 0
+                e, o = spec[:, k, m] + xm, (spec[:, k, m] - xm) if par else spec[:, k, m]
+                p2, p1 = seeds[m, c, k]
+                for q in range(16):
+                    l = lseg + q
+                    if q == 0:
+                        pl = p2
+                    elif q == 1:
+                        pl = p1
+                    else:
+                        a, b = coef[m, l] if l < L else (0.0, 0.0)
+                        pl = a * x[k] * p1 - b * p2
+                        p2, p1 = p1, pl
+                    if l < L:
+                        out[:, l, m] += pl * (o if q & 1 else e)
+    return out
+
+
+def _fold_vector(spec, seeds, coef, x, L, M, par):
+    """The vector segment kernels' algebra: both recurrences, the ladder
+    combinations, S = sum (W0+W1) u and D = sum (W0-W1) v with the mirror terms
+    -s (W0-W1) u' and -s (W0+W1) v' under ``par``, sph = (S+D)/2, tor = i(S-D)/2."""
+    B, _, K, _ = spec.shape
+    out = np.zeros((B, 2, L, M), complex)
+    for m in range(min(M, L)):
+        for c in range((L - m + 15) // 16):
+            lseg = m + 16 * c
+            S = np.zeros((16, B), complex)
+            D = np.zeros((16, B), complex)
+            for k in range((K + 1) // 2 if par else K):
+                km = K - 1 - k
+                u, v = spec[:, 0, k, m] + 1j * spec[:, 1, k, m], spec[:, 0, k, m] - 1j * spec[:, 1, k, m]
+                mir = par and km != k
+                um = spec[:, 0, km, m] + 1j * spec[:, 1, km, m] if mir else 0
+                vm = spec[:, 0, km, m] - 1j * spec[:, 1, km, m] if mir else 0
+                qm0, qm1, qp0, qp1 = seeds[m, c, k]
+                for q in range(16):
+                    l = lseg + q
+                    cf = coef[m, l] if l < L else np.zeros(8)
+                    w0 = cf[4] * qm0 + cf[5] * qp0
+                    w1 = cf[6] * qm1 + cf[7] * qp1
+                    s = 1 if q & 1 else -1  # -(-1)^(l+m), l - m = 16c + q
+                    S[q] += (w0 + w1) * u + (s * (w0 - w1) * um if par else 0)
+                    D[q] += (w0 - w1) * v + (s * (w0 + w1) * vm if par else 0)
+                    qm0, qm1 = qm1, cf[0] * x[k] * qm1 - cf[1] * qm0
+                    qp0, qp1 = qp1, cf[2] * x[k] * qp1 - cf[3] * qp0
+            for q in range(16):
+                if lseg + q < L:
+                    out[:, 0, lseg + q, m] = 0.5 * (S[q] + D[q])
+                    out[:, 1, lseg + q, m] = 0.5j * (S[q] - D[q])
+    return out
+
+
+@pytest.mark.parametrize("nlat,nlon,grid", [(12, 24, "equiangular"), (11, 22, "legendre-gauss")])
+def test_recurrence_fold_algebra_matches_oracle(nlat, nlon, grid):
+    """The segment kernels' algebra (checkpoints, recurrences, equatorial fold,
+    vector ladder and u/v form), run in float64 on the package's checkpoint
+    tables, reproduces the oracle's contraction with and without the fold, for
+    even and odd nlat (the tables are float32, hence 1e-6)."""
+    rng = np.random.default_rng(nlat)
+    seeds, coef, x = (a.astype(np.float64) for a in weights.scalar_recurrence_tables(nlat, nlon, grid=grid))
+    M, L = coef.shape[0], coef.shape[1]
+    spec = rng.standard_normal((2, nlat, M)) + 1j * rng.standard_normal((2, nlat, M))
+    ref = orc.legendre_forward(spec, orc.scalar_forward_table(nlat, nlon, grid=grid).transpose(1, 2, 0))
+    for par in (False, True):
+        got = _fold_scalar(spec, seeds, coef, x, L, M, par)
+        assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
+    seeds, coef, x = (a.astype(np.float64) for a in weights.vector_recurrence_tables(nlat, nlon, grid=grid))
+    spec = rng.standard_normal((2, 2, nlat, M)) + 1j * rng.standard_normal((2, 2, nlat, M))
+    w = orc.vector_forward_tables(nlat, nlon, grid=grid)
+    ref = orc.vector_legendre_forward(spec, w[0].transpose(1, 2, 0), w[1].transpose(1, 2, 0))
+    for par in (False, True):
+        got = _fold_vector(spec, seeds, coef, x, L, M, par)
+        assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
