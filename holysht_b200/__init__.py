@@ -520,7 +520,11 @@ class _SpectrumLegendreInverse(torch.autograd.Function):
         c = coef.contiguous()
         shape = (B, 2, K, W) if vector else (B, K, W)
         spec = torch.empty(shape, device=c.device, dtype=torch.complex64)
-        if _dense_tc_eligible(src, B, _lib.DIR_INVERSE):
+        if getattr(src, "variant", "table") == "recurrence" and not vector:
+            seeds, rc, ct = src.recurrence_tables()
+            ops.legendre_inverse_recurrence(spec, c, seeds, rc, ct, 1.0, parity=getattr(src, "rec_parity", False),
+                                            irfft_prep=True, nlon=nlon)
+        elif _dense_tc_eligible(src, B, _lib.DIR_INVERSE):
             ops.legendre_dense_tc(_lib.DIR_INVERSE, spec, c, src.dense_table_split(_lib.DIR_INVERSE), nlat=K, lmax=L,
                                   mmax=M, scale=1.0, flags=_lib.FLAG_IRFFT_PREP, nlon=nlon)
         else:
@@ -833,8 +837,12 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
     """Drop-in ``InverseRealSHT``: [..., lmax, mmax] complex -> [..., nlat, nlon] real."""
 
     def __init__(self, nlat: int, nlon: int, lmax: Optional[int] = None, mmax: Optional[int] = None,
-                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True, table_device=None):
+                 grid: str = "equiangular", norm: str = "ortho", csphase: bool = True, table_device=None,
+                 variant: str = "table"):
         super().__init__()
+        if variant not in ("table", "recurrence"):
+            raise ValueError(f"variant must be 'table' or 'recurrence', got {variant!r}")
+        self.variant = variant
         p, L, M = _weights.scalar_inverse(nlat, nlon, lmax, mmax, grid, norm, csphase, dtype=np.float32,
                                           device=table_device)
         _check_mmax(M, nlon)
@@ -845,6 +853,18 @@ class InverseRealSHT(_GroupedTablesMixin, nn.Module):
         self.register_buffer("pct_t", pt.permute(1, 2, 0).contiguous())
         self._mlk_name = "pct"
         self._init_tables(("pct_t",), _lib.DIR_INVERSE)
+        if variant == "recurrence":
+            # the synthesis from functions generated in registers (the gradient
+            # keeps to the table path)
+            seeds, coef, ct = _weights.scalar_recurrence_tables(nlat, nlon, lmax, mmax, grid, norm, csphase,
+                                                                inverse=True, segment=8)
+            self.rec_parity = _weights.recurrence_seeds_symmetric(seeds, ct)
+            self.register_buffer("rec_seeds", torch.from_numpy(seeds), persistent=False)
+            self.register_buffer("rec_coef", torch.from_numpy(coef), persistent=False)
+            self.register_buffer("rec_cos_theta", torch.from_numpy(ct), persistent=False)
+
+    def recurrence_tables(self):
+        return self.rec_seeds, self.rec_coef, self.rec_cos_theta
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x, "InverseRealSHT")

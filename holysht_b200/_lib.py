@@ -54,6 +54,7 @@ EXPORTS = (
     "holysht_legendre_forward_recurrence_ex",
     "holysht_legendre_vector_forward_recurrence",
     "holysht_legendre_vector_forward_recurrence_ex",
+    "holysht_legendre_inverse_recurrence",
     "holysht_rfft_workspace",
     "holysht_rfft_contract",
 )
@@ -147,6 +148,8 @@ def load() -> ctypes.CDLL:
                                                             ctypes.c_float, vp], i32),
             "holysht_legendre_vector_forward_recurrence_ex": ([vp, vp, i64, i64, i64, vp, vp, vp, i64, i64, i64,
                                                                i64, ctypes.c_float, i32, vp], i32),
+            "holysht_legendre_inverse_recurrence": ([vp, i64, i64, i64, vp, i64, i64, vp, vp, vp, i64, i64, i64,
+                                                     i64, ctypes.c_float, i32, i64, vp], i32),
             "holysht_rfft_workspace": ([i64, i64, ctypes.POINTER(ctypes.c_int64)], i32),
             "holysht_rfft_contract": ([vp, i64, i64, vp, vp, i64, ctypes.POINTER(ContractDesc), vp], i32),
             "holysht_legendre_dense_tc_noalloc": ([i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, i64, i64,

@@ -1060,6 +1060,58 @@ int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, i
   return check_launch("recurrence vector forward kernel");
 }
 
+int holysht_legendre_inverse_recurrence(void* out, int64_t out_batch_stride, int64_t out_row_stride,
+                                        int64_t out_cols, const void* spec, int64_t spec_batch_stride,
+                                        int64_t spec_row_stride, const float* seeds, const float* coef,
+                                        const float* cos_theta, int64_t batch, int64_t nlat, int64_t lmax,
+                                        int64_t mmax, float scale, int flags, int64_t nlon, void* stream) {
+  const long long B = batch, K = nlat, L = lmax, M = mmax;
+  if (B < 0 || K < 0 || L < 0 || M < 0) return fail(HOLYSHT_ERR_INVALID, "negative extent");
+  if ((flags & ~(HOLYSHT_FLAG_EQUATORIAL_PARITY | HOLYSHT_FLAG_IRFFT_PREP)) != 0)
+    return fail(HOLYSHT_ERR_INVALID, "unknown flag");
+  if (out_cols < M) return fail(HOLYSHT_ERR_INVALID, "out_cols (%lld) < mmax (%lld)", (long long)out_cols, M);
+  if (B == 0 || K == 0 || out_cols == 0) return ok();
+  if (!out || !seeds || !coef || !cos_theta || (M > 0 && L > 0 && !spec)) return fail(HOLYSHT_ERR_INVALID, "null pointer");
+  if (!fits_int(B) || !fits_int(K) || !fits_int(L) || !fits_int(M) || !fits_int(out_cols) ||
+      (B + hsb::rec::kNB - 1) / hsb::rec::kNB > 65535)
+    return fail(HOLYSHT_ERR_INVALID, "extent out of range");
+  if ((flags & HOLYSHT_FLAG_IRFFT_PREP) && (nlon <= 0 || out_cols > nlon / 2 + 1))
+    return fail(HOLYSHT_ERR_INVALID, "irfft preparation needs out_cols <= nlon/2+1");
+  if (spec_row_stride < M || spec_batch_stride < L * spec_row_stride || out_row_stride < out_cols ||
+      out_batch_stride < K * out_row_stride)
+    return fail(HOLYSHT_ERR_INVALID, "input or output strides too small");
+  if ((reinterpret_cast<uintptr_t>(seeds) & 7) || (reinterpret_cast<uintptr_t>(coef) & 7))
+    return fail(HOLYSHT_ERR_INVALID, "seeds and coef must be 8-byte aligned");
+  const bool par = (flags & HOLYSHT_FLAG_EQUATORIAL_PARITY) != 0;
+  hsb::rec::RecInvParams p;
+  p.spec = static_cast<const float2*>(spec);
+  p.sbs = spec_batch_stride;
+  p.srs = spec_row_stride;
+  p.seeds = seeds;
+  p.coef = coef;
+  p.x = cos_theta;
+  p.out = static_cast<float2*>(out);
+  p.obs = out_batch_stride;
+  p.ors = out_row_stride;
+  p.B = (int)B;
+  p.K = (int)K;
+  p.L = (int)L;
+  p.M = (int)M;
+  p.nseg = (int)((L + hsb::rec::kInvSeg - 1) / hsb::rec::kInvSeg);
+  p.out_cols = (int)out_cols;
+  p.prep = (flags & HOLYSHT_FLAG_IRFFT_PREP) ? 1 : 0;
+  p.nyq = (p.prep && nlon % 2 == 0) ? (int)(nlon / 2) : -1;
+  p.scale = scale;
+  const long long Kh = par ? (K + 1) / 2 : K;
+  dim3 grid((unsigned)((out_cols + hsb::rec::kInvOrders - 1) / hsb::rec::kInvOrders), (unsigned)((Kh + 63) / 64),
+            (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
+  if (grid.y > 65535) return fail(HOLYSHT_ERR_INVALID, "nlat out of range");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (par) hsb::rec::recurrence_inverse_kernel<true><<<grid, hsb::rec::kInvOrders * 32, 0, st>>>(p);
+  else hsb::rec::recurrence_inverse_kernel<false><<<grid, hsb::rec::kInvOrders * 32, 0, st>>>(p);
+  return check_launch("recurrence inverse kernel");
+}
+
 int holysht_tc_error_word(unsigned* value) {
   if (!value) return fail(HOLYSHT_ERR_INVALID, "null pointer");
   unsigned zero = 0;

@@ -882,6 +882,185 @@ __global__ void __launch_bounds__(NKC * 32) recurrence_vector_forward_seg_kernel
   else vseg_forward_body<PAR, NKC, 0>(p, m, c, m_lo, live, b0, sd4, ks, vsmem);
 }
 
+// ---------------------------------------------------------------------------
+// Inverse direction (InverseRealSHT's contraction) with on-the-fly functions:
+//
+//   out[b, k, m] = scale * sum_{l >= m} P_l^m(x_k) c[b, l, m]
+//
+// The reduction runs over the degree, which is the recurrence's own direction,
+// so one thread owns one (order, latitude) and accumulates while it runs the
+// recurrence up through the order's 8-degree checkpoint segments: no reduction across
+// threads.  CTA = 8 consecutive orders (one warp each) x 64 latitudes (two per lane) x
+// a group of kNB batches.  Each warp stages its order's coefficients and the
+// recurrence coefficients of the next segment in shared memory (cp.async, one
+// segment ahead); every lane reads them as broadcasts.  With PAR the lanes are
+// northern latitudes and keep even- and odd-(l + m) sums apart: row k gets
+// e + o, row K-1-k gets e - o.  The tile's results go through shared memory so
+// each (batch, row) is written as one run of 8 orders.  Orders m >= mmax up to
+// out_cols are written as zeros; IRFFT_PREP zeroes Im at m = 0 and m = nlon/2.
+struct RecInvParams {
+  const float2* spec;  // c[b, l, m] at b*sbs + l*srs + m
+  long long sbs, srs;
+  const float* seeds;  // [M][nseg][K][2]: P at l = m + 8c and m + 8c + 1 (inverse normalisation)
+  const float* coef;   // [M][L][2]
+  const float* x;      // [K]
+  float2* out;         // out[b, k, m] at b*obs + k*ors + m
+  long long obs, ors;
+  int B, K, L, M, nseg, out_cols, nyq;  // nyq: the Nyquist column to clear, or -1
+  int prep;
+  float scale;
+};
+
+constexpr int kInvOrders = 8;  // orders (warps) per CTA
+constexpr int kInvSeg = 8;     // degrees between the inverse kernel's checkpoints
+constexpr int kInvStages = 3;  // staged segments in flight per warp
+
+// the checkpoints of this kernel are 8 degrees apart: over a white spectrum the
+// synthesis weighs the high degrees, and the fp32 drift over 16 steps reached
+// 1.1e-6 relative L2 at lmax 512 (8 steps: half of it)
+// each lane runs two latitudes, k and k + 32 of a 64-latitude tile: the
+// staged coefficients are read once for both (half the shared-memory loads per
+// multiply-add) and the two recurrences are independent chains
+template <bool PAR>
+__global__ void __launch_bounds__(kInvOrders * 32, 2) recurrence_inverse_kernel(const RecInvParams p) {
+  __shared__ __align__(16) float2 cst[kInvOrders][kInvStages][kInvSeg][kNB];  // staged c of a segment, per warp
+  __shared__ __align__(16) float2 cab[kInvOrders][kInvStages][kInvSeg];       // staged (a_l, b_l), per warp
+  __shared__ __align__(16) float2 csd[kInvOrders][kInvStages][2][32];         // staged checkpoints, per latitude
+  __shared__ float2 obuf[kNB][64][kInvOrders + 1];                            // rows of one latitude half
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kInvOrders, m = m0 + warp;
+  const int kc = blockIdx.y * 64;
+  const int Kh = PAR ? (p.K + 1) / 2 : p.K;
+  bool kv[2];
+  float x[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    kv[h] = kc + 32 * h + lane < Kh;
+    x[h] = kv[h] ? p.x[kc + 32 * h + lane] : 0.f;
+  }
+  const int b0 = blockIdx.z * kNB;
+  const int nseg = (m < p.M && m < p.L) ? (p.L - m + kInvSeg - 1) / kInvSeg : 0;
+  const float2* sd = reinterpret_cast<const float2*>(p.seeds) + (long long)m * p.nseg * p.K + kc + lane;
+
+  // lane i stages entry i of the segment's kInvSeg x kNB coefficients (32 of
+  // them) and the checkpoints of its two latitudes, lanes 0 .. kInvSeg-1 the
+  // recurrence coefficients
+  static_assert(kInvSeg * kNB == 32, "one staged coefficient per lane");
+  auto stage = [&](int c, int slot) {
+    const int lseg = m + c * kInvSeg;
+    const int q = lane / kNB, b = lane % kNB;
+    const bool v = b0 + b < p.B && lseg + q < p.L;
+    cp_async8(&cst[warp][slot][q][b],
+              v ? p.spec + (long long)(b0 + b) * p.sbs + (long long)(lseg + q) * p.srs + m : p.spec, v);
+    if (lane < kInvSeg) {
+      const bool w = lseg + lane < p.L;
+      cp_async8(&cab[warp][slot][lane], w ? p.coef + ((long long)m * p.L + lseg + lane) * 2 : p.coef, w);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      cp_async8(&csd[warp][slot][h][lane],
+                kv[h] ? static_cast<const void*>(sd + (long long)c * p.K + 32 * h) : static_cast<const void*>(p.seeds),
+                kv[h]);
+  };
+  float2 e[2][kNB], o[2][kNB];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) e[h][b] = o[h][b] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int s = 0; s < kInvStages - 1; ++s) {
+    if (s < nseg) stage(s, s);
+    cp_async_commit();
+  }
+  for (int c = 0, slot = 0; c < nseg; ++c, slot = (slot + 1 == kInvStages) ? 0 : slot + 1) {
+    __syncwarp();  // every lane is done with the slot the next stage refills
+    if (c + kInvStages - 1 < nseg) stage(c + kInvStages - 1, slot == 0 ? kInvStages - 1 : slot - 1);
+    cp_async_commit();
+    cp_async_wait<kInvStages - 1>();
+    __syncwarp();
+    float p2[2], p1[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 sk = csd[warp][slot][h][lane];  // zero for a latitude past the tile
+      p2[h] = sk.x;
+      p1[h] = sk.y;
+    }
+    const float4* cs4 = reinterpret_cast<const float4*>(&cst[warp][slot][0][0]);
+    const float4* ab4 = reinterpret_cast<const float4*>(&cab[warp][slot][0]);
+#pragma unroll
+    for (int q = 0; q < kInvSeg; ++q) {
+      const float4 c01 = cs4[2 * q], c23 = cs4[2 * q + 1];  // batches 0, 1 and 2, 3 (zero past lmax / B)
+      float a = 0.f, bb = 0.f;
+      if (q >= 2) {
+        // (a, b) as staged: P_l = a x P_{l-1} - b P_{l-2}; both 0 beyond lmax
+        const float4 ab2 = ab4[q >> 1];
+        a = (q & 1) ? ab2.z : ab2.x;
+        bb = (q & 1) ? ab2.w : ab2.y;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float pl;
+        if (q == 0) {
+          pl = p2[h];
+        } else if (q == 1) {
+          pl = p1[h];
+        } else {
+          pl = fmaf(a, __fmul_rn(x[h], p1[h]), -__fmul_rn(bb, p2[h]));
+          p2[h] = p1[h];
+          p1[h] = pl;
+        }
+        const float2 pp = make_float2(pl, pl);
+        static_assert(kNB == 4, "four batches per group");
+        if (q & 1) {
+          o[h][0] = __ffma2_rn(pp, make_float2(c01.x, c01.y), o[h][0]);
+          o[h][1] = __ffma2_rn(pp, make_float2(c01.z, c01.w), o[h][1]);
+          o[h][2] = __ffma2_rn(pp, make_float2(c23.x, c23.y), o[h][2]);
+          o[h][3] = __ffma2_rn(pp, make_float2(c23.z, c23.w), o[h][3]);
+        } else {
+          e[h][0] = __ffma2_rn(pp, make_float2(c01.x, c01.y), e[h][0]);
+          e[h][1] = __ffma2_rn(pp, make_float2(c01.z, c01.w), e[h][1]);
+          e[h][2] = __ffma2_rn(pp, make_float2(c23.x, c23.y), e[h][2]);
+          e[h][3] = __ffma2_rn(pp, make_float2(c23.z, c23.w), e[h][3]);
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+
+  // rows k (e + o) and K-1-k (e - o), the irfft preparation, the scale; one
+  // latitude half at a time through shared memory
+  const bool clear_im = p.prep && (m == 0 || m == p.nyq);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (h) __syncthreads();  // the first half's rows are written out
+#pragma unroll
+    for (int b = 0; b < kNB; ++b) {
+      float2 y = make_float2((e[h][b].x + o[h][b].x) * p.scale, (e[h][b].y + o[h][b].y) * p.scale);
+      float2 ym = make_float2((e[h][b].x - o[h][b].x) * p.scale, (e[h][b].y - o[h][b].y) * p.scale);
+      if (clear_im) y.y = ym.y = 0.f;
+      obuf[b][lane][warp] = y;
+      obuf[b][32 + lane][warp] = ym;
+    }
+    __syncthreads();
+    const int kh = kc + 32 * h;
+    for (int idx = threadIdx.x; idx < kNB * 64 * kInvOrders; idx += blockDim.x) {
+      const int j = idx % kInvOrders, r = (idx / kInvOrders) % 64, b = idx / (64 * kInvOrders);
+      const int mm = m0 + j;
+      if (mm >= p.out_cols || b0 + b >= p.B) continue;
+      int row;
+      if (r < 32) {
+        if (kh + r >= Kh) continue;
+        row = kh + r;
+      } else {
+        if (!PAR || kh + r - 32 >= Kh) continue;
+        row = p.K - 1 - (kh + r - 32);
+        if (row == kh + r - 32) continue;  // the equator of an odd nlat is its own mirror
+      }
+      p.out[(long long)(b0 + b) * p.obs + (long long)row * p.ors + mm] = obuf[b][r][j];
+    }
+  }
+}
+
 // sets the kernel's dynamic shared-memory limit once per device, then launches
 template <typename Kern, typename Params>
 inline cudaError_t launch_with_smem(Kern kernel, int bytes, std::atomic<unsigned long long>& configured, dim3 grid,

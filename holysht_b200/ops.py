@@ -44,6 +44,7 @@ __all__ = [
     "tc_error_word",
     "legendre_forward_recurrence",
     "legendre_vector_forward_recurrence",
+    "legendre_inverse_recurrence",
 ]
 
 
@@ -386,6 +387,35 @@ class ContractPlan:
                     st = lib.holysht_rfft_contract(field_ptr, rows, nlon, spec_ptr, work_ptr, work_bytes,
                                                    ctypes.byref(d), _current_stream_handle(self._dev))
         _lib.check(st)
+
+
+def legendre_inverse_recurrence(output: torch.Tensor, coef_in: torch.Tensor, seeds: torch.Tensor,
+                                coef: torch.Tensor, cos_theta: torch.Tensor, scale: float = 1.0,
+                                parity: bool = False, irfft_prep: bool = False, nlon: int = 0) -> None:
+    """Scalar inverse contraction with on-the-fly Legendre functions
+    (``holysht_legendre_inverse_recurrence``): output [B, nlat, W >= mmax]
+    complex64 (columns >= mmax written as zeros; ``irfft_prep`` drops Im at m = 0
+    and m = nlon/2) from coefficients ``coef_in`` [B, lmax, mmax]; ``seeds``,
+    ``coef`` and ``cos_theta`` from
+    :func:`holysht_b200.weights.scalar_recurrence_tables` with ``inverse=True, segment=8``."""
+    dev = _cuda(output, coef_in, seeds, coef, cos_theta)
+    _require(coef_in.dtype == torch.complex64 and output.dtype == torch.complex64, "coefficients and output are complex64")
+    _require(coef_in.dim() == 3 and coef_in.stride(2) == 1 and output.dim() == 3 and output.stride(2) == 1,
+             "coefficients [B, lmax, mmax] and output [B, nlat, W] with contiguous orders")
+    _contig(seeds, coef, cos_theta)
+    M, nseg, K, two = seeds.shape
+    L = coef.size(1)
+    B = coef_in.size(0)
+    _require(two == 2 and nseg == (L + 7) // 8 and tuple(coef.shape) == (M, L, 2) and cos_theta.numel() == K,
+             "inconsistent tables (the inverse kernel's checkpoints are 8 degrees apart)")
+    _require(tuple(coef_in.shape) == (B, L, M), "coefficients must be [B, lmax, mmax]")
+    _require(output.size(0) == B and output.size(1) == K and output.size(2) >= M, "output must be [B, nlat, >= mmax]")
+    flags = (_lib.FLAG_EQUATORIAL_PARITY if parity else 0) | (_lib.FLAG_IRFFT_PREP if irfft_prep else 0)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().holysht_legendre_inverse_recurrence(
+            _p(output), output.stride(0), output.stride(1), output.size(2), _p(coef_in), coef_in.stride(0),
+            coef_in.stride(1), _p(seeds), _p(coef), _p(cos_theta), B, K, L, M, float(scale), flags, int(nlon),
+            _stream(dev)))
 
 
 def rfft_workspace(rows: int, nlon: int, device) -> Optional[int]:

@@ -301,7 +301,8 @@ def vector_inverse(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="o
 SEGMENT = 16  # degrees between recurrence checkpoints (matches the kernel)
 
 
-def scalar_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True):
+def scalar_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular", norm="ortho", csphase=True,
+                             inverse=False, segment=SEGMENT):
     """Inputs of the recurrence kernel, built in float64, returned as float32:
 
     * seeds [mmax, ceil(lmax/16), nlat, 2]: w_k * P_l^m(x_k) at l = m + 16c and
@@ -311,31 +312,36 @@ def scalar_recurrence_tables(nlat, nlon, lmax=None, mmax=None, grid="equiangular
       normalised (and, for ``schmidt``, rescaled) functions, for l >= m + 2;
     * cos_theta [nlat].
 
-    The same functions as ``scalar_forward``'s table (which is w_k P_l^m)."""
+    The same functions as ``scalar_forward``'s table (which is w_k P_l^m); with
+    ``inverse``, those of ``scalar_inverse``'s ``pct`` (the inverse
+    normalisation, no quadrature weight).  ``segment``: degrees between
+    checkpoints (16 for the forward kernels, 8 for the inverse kernel)."""
     lmax, mmax = _resolve(nlat, nlon, lmax, mmax, grid, norm)
     theta, w = nodes_and_weights(nlat, grid)
+    if inverse:
+        w = np.ones_like(w)
     x = np.cos(theta)
-    nseg = (lmax + SEGMENT - 1) // SEGMENT
+    nseg = (lmax + segment - 1) // segment
     seeds = np.zeros((mmax, nseg, nlat, 2), dtype=np.float32)
     coef = np.zeros((mmax, lmax, 2), dtype=np.float32)
     sign = np.ones(mmax)
     if csphase:
         sign[1::2] = -1.0
     m_all = np.arange(mmax)
-    for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, False)):
+    for l, row in _legendre_rows(mmax, lmax, x, _norm_seed(norm, inverse)):
         row = row.numpy()
-        f = _schmidt(norm, False, l)
+        f = _schmidt(norm, inverse, l)
         vals = row * (sign * f)[:, None] * w[None, :]          # [mmax, K]
         d = l - m_all
-        sel = (d >= 0) & (d % SEGMENT < 2)
+        sel = (d >= 0) & (d % segment < 2)
         ms = m_all[sel]
-        seeds[ms, d[sel] // SEGMENT, :, d[sel] % SEGMENT] = vals[sel].astype(np.float32)
+        seeds[ms, d[sel] // segment, :, d[sel] % segment] = vals[sel].astype(np.float32)
         if l >= 2:
             mm = m_all[(m_all <= l - 2)].astype(np.float64)
             a = np.sqrt((4.0 * l * l - 1.0) / (l * l - mm * mm))
             b = np.sqrt(((l - 1.0) ** 2 - mm * mm) * (2.0 * l + 1.0) / ((2.0 * l - 3.0) * (l * l - mm * mm)))
-            a *= f / _schmidt(norm, False, l - 1)
-            b *= f / _schmidt(norm, False, l - 2)
+            a *= f / _schmidt(norm, inverse, l - 1)
+            b *= f / _schmidt(norm, inverse, l - 2)
             k = mm.astype(np.int64)
             coef[k, l, 0] = a
             coef[k, l, 1] = b

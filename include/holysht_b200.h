@@ -365,6 +365,25 @@ int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, i
                                                   int64_t lmax, int64_t mmax, float scale, int flags,
                                                   void* stream);
 
+/* Scalar inverse contraction (InverseRealSHT's) with on-the-fly Legendre
+ * functions (the recurrence variant; no counterpart operator in the reference):
+ *   out[b,k,m] = scale * sum_{l >= m} P_l^m(cos theta_k) * spec[b,l,m],  m < mmax;
+ * columns mmax .. out_cols-1 are written as zeros.  One thread per (order,
+ * latitude) runs the recurrence through the order's 8-degree checkpoint
+ * segments; the reduction over l needs no exchange between threads.
+ *   seeds float32 [mmax][ceil(lmax/8)][nlat][2]: P at l = m + 8c, m + 8c + 1
+ *         in the inverse normalisation (holysht_b200.weights.scalar_recurrence_tables(
+ *         ..., inverse=True, segment=8)); coef [mmax][lmax][2]; cos_theta [nlat];
+ *   flags: HOLYSHT_FLAG_EQUATORIAL_PARITY (symmetric grids), HOLYSHT_FLAG_IRFFT_PREP
+ *         (Im = 0 at m = 0 and, even nlon, at m = nlon/2; out_cols <= nlon/2+1).
+ * spec: complex64, element (b,l,m) at spec + b*spec_batch_stride + l*spec_row_stride + m;
+ * out: complex64, element (b,k,m) at out + b*out_batch_stride + k*out_row_stride + m. */
+int holysht_legendre_inverse_recurrence(void* out, int64_t out_batch_stride, int64_t out_row_stride,
+                                        int64_t out_cols, const void* spec, int64_t spec_batch_stride,
+                                        int64_t spec_row_stride, const float* seeds, const float* coef,
+                                        const float* cos_theta, int64_t batch, int64_t nlat, int64_t lmax,
+                                        int64_t mmax, float scale, int flags, int64_t nlon, void* stream);
+
 /* Same contraction as holysht_legendre_dense_tc, for callers that cannot
  * allocate device memory (a host whose own allocator owns the GPU memory, a
  * loop that must not allocate per call, a plugin handed no allocator).  No

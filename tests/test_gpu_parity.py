@@ -565,3 +565,43 @@ def test_cached_forward_runs_rfft_and_contraction_in_one_call(vector):
     assert rel_l2(third.cpu().numpy(), first.cpu().numpy()) <= 1e-7
     ref = (_module_oracle_vector if vector else _module_oracle_scalar)(m, x.astype(np.float64))
     assert_fp32_close(second, ref)
+
+
+@pytest.mark.parametrize("nlat,nlon,grid,norm,cs,lmax,mmax", [
+    (512, 1024, "equiangular", "ortho", True, None, None),
+    (96, 192, "legendre-gauss", "schmidt", False, None, None),
+    (33, 64, "lobatto", "four-pi", True, None, None),
+    (47, 96, "equiangular", "ortho", True, 40, 30),
+])
+def test_inverse_recurrence_variant_matches_oracle(nlat, nlon, grid, norm, cs, lmax, mmax):
+    """InverseRealSHT(variant="recurrence"): the synthesis from functions
+    generated in registers (one thread per order and latitude) against the
+    float64 oracle and the table variant, 5 batches (two batch groups), odd
+    nlat and truncated lmax / mmax (zero columns up to nlon/2+1); the op with
+    and without the equatorial fold; gradients through the table backward."""
+    rng = np.random.default_rng(nlat + 3)
+    m = hs.InverseRealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=cs,
+                          variant="recurrence").to(DEV)
+    t = hs.InverseRealSHT(nlat, nlon, lmax=lmax, mmax=mmax, grid=grid, norm=norm, csphase=cs).to(DEV)
+    L, M = m.lmax, m.mmax
+    c = (rng.standard_normal((5, L, M)) + 1j * rng.standard_normal((5, L, M))).astype(np.complex64)
+    c *= (np.arange(M)[None, :] <= np.arange(L)[:, None])
+    ct = torch.from_numpy(c).to(DEV)
+    got = m(ct)
+    ref = orc.sht_inverse(c.astype(np.complex128), m.pct.double().cpu().numpy(), nlon)
+    assert_fp32_close(got, ref)
+    assert rel_l2(got.detach().cpu().numpy(), t(ct).detach().cpu().numpy()) <= 1e-6
+    seeds, coef, cth = m.recurrence_tables()
+    W = nlon // 2 + 1
+    ref_spec = np.einsum("blm,mlk->bkm", c.astype(np.complex128), m.pct.double().cpu().numpy())
+    for parity in (False, True):
+        spec = torch.full((5, nlat, W), float("nan"), dtype=torch.complex64, device=DEV)
+        ops.legendre_inverse_recurrence(spec, ct, seeds, coef, cth, 1.0, parity=parity)
+        s = spec.cpu().numpy()
+        assert np.all(s[..., M:] == 0)
+        assert_fp32_close(s[..., :M], ref_spec)
+    cg = ct.clone().requires_grad_(True)
+    cg2 = ct.clone().requires_grad_(True)
+    (m(cg) ** 2).sum().backward()
+    (t(cg2) ** 2).sum().backward()
+    assert rel_l2(cg.grad.cpu().numpy(), cg2.grad.cpu().numpy()) <= 1e-6
