@@ -456,3 +456,38 @@ def test_recurrence_fold_algebra_matches_oracle(nlat, nlon, grid):
     for par in (False, True):
         got = _fold_vector(spec, seeds, coef, x, L, M, par)
         assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-6
+
+
+@pytest.mark.parametrize("grid,norm,cs", [("equiangular", "ortho", True), ("legendre-gauss", "schmidt", False),
+                                          ("equiangular", "four-pi", True)])
+def test_inverse_recurrence_tables_reproduce_the_inverse_table(grid, norm, cs):
+    """The inverse kernel's inputs (8-degree checkpoints in the inverse
+    normalisation, no quadrature weight, and the recurrence coefficients),
+    advanced in float64 by P_l = a_l x P_{l-1} - b_l P_{l-2} from each
+    checkpoint, reproduce InverseRealSHT's pct table; the synthesis from them
+    matches the oracle's inverse contraction."""
+    nlat, nlon = 13, 26
+    seeds, coef, x = (a.astype(np.float64) for a in
+                      weights.scalar_recurrence_tables(nlat, nlon, grid=grid, norm=norm, csphase=cs,
+                                                       inverse=True, segment=8))
+    pct = orc.scalar_inverse_table(nlat, nlon, grid=grid, norm=norm, csphase=cs)
+    M, L = coef.shape[0], coef.shape[1]
+    assert seeds.shape == (M, (L + 7) // 8, nlat, 2)
+    got = np.zeros_like(pct)
+    for m in range(M):
+        for c in range((L - m + 7) // 8):
+            l0 = m + 8 * c
+            p0, p1 = seeds[m, c, :, 0], seeds[m, c, :, 1]
+            got[m, l0] = p0
+            if l0 + 1 < L:
+                got[m, l0 + 1] = p1
+            for l in range(l0 + 2, min(l0 + 8, L)):
+                p0, p1 = p1, coef[m, l, 0] * x * p1 - coef[m, l, 1] * p0
+                got[m, l] = p1
+    scale = np.abs(pct).max()
+    np.testing.assert_allclose(got, pct, rtol=0, atol=1e-6 * scale)
+    rng = np.random.default_rng(3)
+    spec = rng.standard_normal((2, L, M)) + 1j * rng.standard_normal((2, L, M))
+    ref = orc.legendre_inverse(spec, pct.transpose(1, 2, 0))
+    syn = orc.legendre_inverse(spec, got.transpose(1, 2, 0))
+    assert np.linalg.norm(syn - ref) / np.linalg.norm(ref) < 1e-6
