@@ -8,8 +8,9 @@ Legendre kernel) over a (4, 2, 512, 1024) float32 batch resident in HBM.
 Multi-GPU: batch partition with no collective (every rank transforms its own
 batch of 4, weak scaling); the timing is device time (CUDA events), the max
 over ranks.  The L2 is flushed (256 MiB write, then 256 MiB read) before
-every timed step.  Secondary fields: the scalar, inverse and recurrence
-forwards, the 1024 x 2048 configuration under both multi-GPU partitions, and
+every timed step.  Secondary fields: the scalar and inverse forwards (scalar and
+vector), the recurrence variants (scalar and vector forward, scalar inverse),
+the 1024 x 2048 configuration under both multi-GPU partitions, and
 (N = 1) the reference's own CUDA path timed in a child process.
 
 Prints one JSON line (rank 0).  ``--impl reference`` times the reference's
@@ -304,6 +305,24 @@ def run_ours(args, rank, world, local_rank):
     inv_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(is_, ie)))
     del isht, coef
 
+    def time_forward(mod, inp):
+        for _ in range(3):
+            mod(inp)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(sn)]
+        for s, e in ev:
+            flush_l2()
+            s.record(stream)
+            mod(inp)
+            e.record(stream)
+        torch.cuda.synchronize(dev)
+        return max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in ev))
+
+    # InverseRealSHT.forward (irfft included): the table path and the recurrence variant
+    scoef = hs.RealSHT(NLAT, NLON, table_device=dev)(xs)
+    sinv_ms = time_forward(hs.InverseRealSHT(NLAT, NLON, table_device=dev), scoef)
+    sinv_rec_ms = time_forward(hs.InverseRealSHT(NLAT, NLON, variant="recurrence").to(dev), scoef)
+    del scoef
+
     # ---- the 1024 x 2048 configuration on all ranks (both partitions) ----
     c5 = run_c5(rank, world, dev, barrier, max_over_ranks) if not args.skip_c5 else {}
 
@@ -394,7 +413,9 @@ def run_ours(args, rank, world, local_rank):
         "secondary": {"RealSHT.forward_ms": round(scalar_ms, 5),
                       "RealSHT.forward_recurrence_variant_ms": round(rec_ms, 5),
                       "RealVectorSHT.forward_recurrence_variant_ms": round(vrec_ms, 5),
-                      "InverseRealVectorSHT.forward_ms": round(inv_ms, 5), **c5},
+                      "InverseRealVectorSHT.forward_ms": round(inv_ms, 5),
+                      "InverseRealSHT.forward_ms": round(sinv_ms, 5),
+                      "InverseRealSHT.forward_recurrence_variant_ms": round(sinv_rec_ms, 5), **c5},
         "e2e": {"value": round(e2e_ms, 5), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "how": (f"{K} steps through holysht_b200.pipeline.HostStream (pinned host in/out; upload, transform "
                         "and download of consecutive steps overlap on three streams), total / K"),
