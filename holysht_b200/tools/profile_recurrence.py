@@ -1,9 +1,10 @@
 """Run the recurrence-variant forward (512x1024, batch 4) for profilers.
 
-    python -m holysht_b200.tools.profile_recurrence [reps] [vector]
+    python -m holysht_b200.tools.profile_recurrence [reps] [vector|inverse]
 
 RealSHT(variant="recurrence") by default, RealVectorSHT(variant="recurrence")
-with ``vector``.
+with ``vector``, InverseRealSHT(variant="recurrence") on a (4, 512, 513)
+spectrum with ``inverse``.
 """
 from __future__ import annotations
 
@@ -17,8 +18,12 @@ import holysht_b200 as hs
 def main(argv):
     reps = int(argv[1]) if len(argv) > 1 else 3
     vector = "vector" in argv
+    inverse = "inverse" in argv
     dev = torch.device("cuda")
-    if vector:
+    if inverse:
+        m = hs.InverseRealSHT(512, 1024, variant="recurrence").to(dev)
+        x = torch.randn(4, 512, 513, dtype=torch.complex64, device=dev)
+    elif vector:
         m = hs.RealVectorSHT(512, 1024, variant="recurrence").to(dev)
         x = torch.randn(4, 2, 512, 1024, device=dev)
     else:
@@ -34,7 +39,8 @@ def main(argv):
             m(x)
         e[1].record()
         torch.cuda.synchronize()
-    print("recurrence", "RealVectorSHT" if vector else "RealSHT", "512x1024 b4 ms",
+    name = "InverseRealSHT" if inverse else "RealVectorSHT" if vector else "RealSHT"
+    print("recurrence", name, "512x1024 b4 ms",
           round(e[0].elapsed_time(e[1]) / 10, 4))
 
 
