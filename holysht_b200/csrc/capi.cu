@@ -1103,9 +1103,14 @@ int holysht_legendre_inverse_recurrence(void* out, int64_t out_batch_stride, int
   p.nyq = (p.prep && nlon % 2 == 0) ? (int)(nlon / 2) : -1;
   p.scale = scale;
   const long long Kh = par ? (K + 1) / 2 : K;
-  dim3 grid((unsigned)((out_cols + hsb::rec::kInvOrders - 1) / hsb::rec::kInvOrders), (unsigned)((Kh + 63) / 64),
-            (unsigned)((B + hsb::rec::kNB - 1) / hsb::rec::kNB));
-  if (grid.y > 65535) return fail(HOLYSHT_ERR_INVALID, "nlat out of range");
+  // x runs over (latitude tile, batch group) and y over the order blocks, so the
+  // block scheduler issues every tile of the long low-order blocks first
+  const long long ntile = (Kh + 63) / 64, ngroup = (B + hsb::rec::kNB - 1) / hsb::rec::kNB;
+  const long long nblk = (out_cols + hsb::rec::kInvOrders - 1) / hsb::rec::kInvOrders;
+  if (nblk > 65535) return fail(HOLYSHT_ERR_INVALID, "out_cols out of range");
+  if (ntile * ngroup > 0x7fffffffLL) return fail(HOLYSHT_ERR_INVALID, "nlat x batch out of range");
+  p.ntile = (int)ntile;
+  dim3 grid((unsigned)(ntile * ngroup), (unsigned)nblk, 1);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (par) hsb::rec::recurrence_inverse_kernel<true><<<grid, hsb::rec::kInvOrders * 32, 0, st>>>(p);
   else hsb::rec::recurrence_inverse_kernel<false><<<grid, hsb::rec::kInvOrders * 32, 0, st>>>(p);

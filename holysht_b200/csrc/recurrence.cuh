@@ -891,7 +891,8 @@ __global__ void __launch_bounds__(NKC * 32) recurrence_vector_forward_seg_kernel
 // so one thread owns one (order, latitude) and accumulates while it runs the
 // recurrence up through the order's 8-degree checkpoint segments: no reduction across
 // threads.  CTA = 8 consecutive orders (one warp each) x 64 latitudes (two per lane) x
-// a group of kNB batches.  Each warp stages its order's coefficients and the
+// a group of kNB batches; blockIdx.y is the order block, so the long low-order blocks
+// are issued first.  Each warp stages its order's coefficients and the
 // recurrence coefficients of the next segment in shared memory (cp.async, one
 // segment ahead); every lane reads them as broadcasts.  With PAR the lanes are
 // northern latitudes and keep even- and odd-(l + m) sums apart: row k gets
@@ -908,6 +909,7 @@ struct RecInvParams {
   long long obs, ors;
   int B, K, L, M, nseg, out_cols, nyq;  // nyq: the Nyquist column to clear, or -1
   int prep;
+  int ntile;  // 64-latitude tiles per batch group (blockIdx.x = tile + ntile * group)
   float scale;
 };
 
@@ -928,8 +930,8 @@ __global__ void __launch_bounds__(kInvOrders * 32, 2) recurrence_inverse_kernel(
   __shared__ __align__(16) float2 csd[kInvOrders][kInvStages][2][32];         // staged checkpoints, per latitude
   __shared__ float2 obuf[kNB][64][kInvOrders + 1];                            // rows of one latitude half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kInvOrders, m = m0 + warp;
-  const int kc = blockIdx.y * 64;
+  const int m0 = blockIdx.y * kInvOrders, m = m0 + warp;
+  const int kc = (blockIdx.x % p.ntile) * 64;
   const int Kh = PAR ? (p.K + 1) / 2 : p.K;
   bool kv[2];
   float x[2];
@@ -938,7 +940,7 @@ __global__ void __launch_bounds__(kInvOrders * 32, 2) recurrence_inverse_kernel(
     kv[h] = kc + 32 * h + lane < Kh;
     x[h] = kv[h] ? p.x[kc + 32 * h + lane] : 0.f;
   }
-  const int b0 = blockIdx.z * kNB;
+  const int b0 = (blockIdx.x / p.ntile) * kNB;
   const int nseg = (m < p.M && m < p.L) ? (p.L - m + kInvSeg - 1) / kInvSeg : 0;
   const float2* sd = reinterpret_cast<const float2*>(p.seeds) + (long long)m * p.nseg * p.K + kc + lane;
 
