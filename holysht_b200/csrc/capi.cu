@@ -1082,6 +1082,9 @@ int holysht_legendre_inverse_recurrence(void* out, int64_t out_batch_stride, int
     return fail(HOLYSHT_ERR_INVALID, "input or output strides too small");
   if ((reinterpret_cast<uintptr_t>(seeds) & 7) || (reinterpret_cast<uintptr_t>(coef) & 7))
     return fail(HOLYSHT_ERR_INVALID, "seeds and coef must be 8-byte aligned");
+  // spec is copied and out written as 8-byte complex values
+  if ((reinterpret_cast<uintptr_t>(spec) & 7) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return fail(HOLYSHT_ERR_INVALID, "spec and out must be 8-byte aligned");
   const bool par = (flags & HOLYSHT_FLAG_EQUATORIAL_PARITY) != 0;
   hsb::rec::RecInvParams p;
   p.spec = static_cast<const float2*>(spec);

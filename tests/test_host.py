@@ -491,3 +491,27 @@ def test_inverse_recurrence_tables_reproduce_the_inverse_table(grid, norm, cs):
     ref = orc.legendre_inverse(spec, pct.transpose(1, 2, 0))
     syn = orc.legendre_inverse(spec, got.transpose(1, 2, 0))
     assert np.linalg.norm(syn - ref) / np.linalg.norm(ref) < 1e-6
+
+
+def test_inverse_recurrence_arguments_are_checked_without_gpu():
+    """The inverse recurrence entry rejects bad flags, extents, strides and
+    misaligned pointers before touching the device (the addresses below are
+    never dereferenced)."""
+    lib = _lib.load()
+    f = lib.holysht_legendre_inverse_recurrence
+    B, K, L, M = 2, 8, 8, 8
+    good, odd = 0x10000, 0x10004
+    one = ctypes.c_float(1.0)
+
+    def call(out=good, spec=good, seeds=good, flags=0, obs=K * M, ors=M, cols=M, sbs=L * M, srs=M, nlon=16):
+        return f(out, obs, ors, cols, spec, sbs, srs, seeds, good, good, B, K, L, M, one, flags, nlon, None)
+
+    assert call(flags=1 << 12) == _lib.HOLYSHT_ERR_INVALID and b"flag" in lib.holysht_last_error()
+    assert call(cols=M - 1) == _lib.HOLYSHT_ERR_INVALID and b"out_cols" in lib.holysht_last_error()
+    assert call(srs=M - 1) == _lib.HOLYSHT_ERR_INVALID and b"strides" in lib.holysht_last_error()
+    assert call(flags=_lib.FLAG_IRFFT_PREP, nlon=8) == _lib.HOLYSHT_ERR_INVALID
+    assert b"irfft" in lib.holysht_last_error()
+    assert call(seeds=odd) == _lib.HOLYSHT_ERR_INVALID and b"seeds" in lib.holysht_last_error()
+    assert call(spec=odd) == _lib.HOLYSHT_ERR_INVALID and b"aligned" in lib.holysht_last_error()
+    assert call(out=odd) == _lib.HOLYSHT_ERR_INVALID and b"aligned" in lib.holysht_last_error()
+    assert call(out=None) == _lib.HOLYSHT_ERR_INVALID and b"null" in lib.holysht_last_error()
