@@ -945,6 +945,9 @@ int holysht_legendre_forward_recurrence_ex(void* out, const void* spec, int64_t 
   if (spec_row_stride < M || spec_batch_stride < K * spec_row_stride)
     return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
   if ((reinterpret_cast<uintptr_t>(seeds) & 7) != 0) return fail(HOLYSHT_ERR_INVALID, "seeds must be 8-byte aligned");
+  // the spectrum is copied and the output written as 8-byte complex values
+  if ((reinterpret_cast<uintptr_t>(spec) & 7) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return fail(HOLYSHT_ERR_INVALID, "spec and out must be 8-byte aligned");
   hsb::rec::RecParams p;
   p.spec = static_cast<const float2*>(spec);
   p.sbs = spec_batch_stride;
@@ -1021,6 +1024,8 @@ int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, i
     return fail(HOLYSHT_ERR_INVALID, "spectrum strides too small");
   if ((reinterpret_cast<uintptr_t>(seeds) & 15) != 0 || (reinterpret_cast<uintptr_t>(coef) & 15) != 0)
     return fail(HOLYSHT_ERR_INVALID, "seeds and coef must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(spec) & 7) || (reinterpret_cast<uintptr_t>(out) & 7))
+    return fail(HOLYSHT_ERR_INVALID, "spec and out must be 8-byte aligned");
   hsb::rec::VecRecParams p;
   p.spec = static_cast<const float2*>(spec);
   p.sbs = spec_batch_stride;

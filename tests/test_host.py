@@ -515,3 +515,18 @@ def test_inverse_recurrence_arguments_are_checked_without_gpu():
     assert call(spec=odd) == _lib.HOLYSHT_ERR_INVALID and b"aligned" in lib.holysht_last_error()
     assert call(out=odd) == _lib.HOLYSHT_ERR_INVALID and b"aligned" in lib.holysht_last_error()
     assert call(out=None) == _lib.HOLYSHT_ERR_INVALID and b"null" in lib.holysht_last_error()
+
+
+def test_forward_recurrence_entries_reject_misaligned_spectra_without_gpu():
+    """Both forward recurrence entries refuse a spectrum or output that is not
+    8-byte aligned (the addresses are never dereferenced)."""
+    lib = _lib.load()
+    good, odd = 0x10000, 0x10004
+    one = ctypes.c_float(1.0)
+    for spec, out in ((odd, good), (good, odd)):
+        st = lib.holysht_legendre_forward_recurrence_ex(out, spec, 64, 8, good, good, good, 1, 8, 8, 8, one, 0,
+                                                        None)
+        assert st == _lib.HOLYSHT_ERR_INVALID and b"aligned" in lib.holysht_last_error()
+        st = lib.holysht_legendre_vector_forward_recurrence_ex(out, spec, 128, 64, 8, good, good, good, 1, 8, 8, 8,
+                                                               one, 0, None)
+        assert st == _lib.HOLYSHT_ERR_INVALID and b"aligned" in lib.holysht_last_error()
