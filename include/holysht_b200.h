@@ -333,8 +333,8 @@ int holysht_legendre_forward_recurrence(void* out, const void* spec, int64_t spe
 #define HOLYSHT_FLAG_SEEDS_COMPACT 64
 
 /* holysht_legendre_forward_recurrence with flags (HOLYSHT_FLAG_EQUATORIAL_PARITY,
- * HOLYSHT_FLAG_SEEDS_COMPACT); the plain entry is flags = 0.  seeds must be
- * 8-byte aligned; any nlat. */
+ * HOLYSHT_FLAG_SEEDS_COMPACT); the plain entry is flags = 0.  seeds, spec and
+ * out must be 8-byte aligned; any nlat. */
 int holysht_legendre_forward_recurrence_ex(void* out, const void* spec, int64_t spec_batch_stride,
                                            int64_t spec_row_stride, const float* seeds,
                                            const float* coef, const float* cos_theta, int64_t batch,
@@ -357,7 +357,8 @@ int holysht_legendre_vector_forward_recurrence(void* out, const void* spec, int6
 
 /* holysht_legendre_vector_forward_recurrence with flags
  * (HOLYSHT_FLAG_EQUATORIAL_PARITY, HOLYSHT_FLAG_SEEDS_COMPACT); the plain entry
- * is flags = 0.  seeds and coef 16-byte aligned; any nlat. */
+ * is flags = 0.  seeds and coef 16-byte aligned, spec and out 8-byte aligned;
+ * any nlat. */
 int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, int64_t spec_batch_stride,
                                                   int64_t spec_comp_stride, int64_t spec_row_stride,
                                                   const float* seeds, const float* coef,
@@ -377,7 +378,8 @@ int holysht_legendre_vector_forward_recurrence_ex(void* out, const void* spec, i
  *   flags: HOLYSHT_FLAG_EQUATORIAL_PARITY (symmetric grids), HOLYSHT_FLAG_IRFFT_PREP
  *         (Im = 0 at m = 0 and, even nlon, at m = nlon/2; out_cols <= nlon/2+1).
  * spec: complex64, element (b,l,m) at spec + b*spec_batch_stride + l*spec_row_stride + m;
- * out: complex64, element (b,k,m) at out + b*out_batch_stride + k*out_row_stride + m. */
+ * out: complex64, element (b,k,m) at out + b*out_batch_stride + k*out_row_stride + m.
+ * spec, out, seeds and coef must be 8-byte aligned. */
 int holysht_legendre_inverse_recurrence(void* out, int64_t out_batch_stride, int64_t out_row_stride,
                                         int64_t out_cols, const void* spec, int64_t spec_batch_stride,
                                         int64_t spec_row_stride, const float* seeds, const float* coef,
